@@ -1,0 +1,306 @@
+// The C ABI of include/vdbgpu.h over the C++ runtime. No exception or C++ type crosses it;
+// every failure becomes a vdbgpu_status code plus a message readable with vdbgpu_last_error.
+#include "../../include/vdbgpu.h"
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "formats.h"
+#include "runtime.h"
+
+struct vdbgpu_ctx {
+  std::unique_ptr<vdbgpu::Context> c;
+  std::string open_error;
+};
+
+struct vdbgpu_index {
+  vdbgpu_ctx* ctx;
+  std::unique_ptr<vdbgpu::GpuIndex> idx;
+};
+
+namespace {
+
+using vdbgpu::Status;
+
+int Fail(vdbgpu_ctx* ctx, const Status& s) {
+  if (ctx != nullptr && ctx->c) ctx->c->set_error(s.message());
+  return static_cast<int>(s.code());
+}
+
+bool IsDevicePtr(const void* p) {
+  if (p == nullptr) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
+
+}  // namespace
+
+extern "C" {
+
+int vdbgpu_abi_version(void) { return VDBGPU_ABI_VERSION; }
+
+int vdbgpu_device_count(int* out) {
+  if (out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  *out = n;
+  return VDBGPU_OK;
+}
+
+int vdbgpu_open(int device, vdbgpu_ctx** out) {
+  if (out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = nullptr;
+  auto* h = new (std::nothrow) vdbgpu_ctx;
+  if (h == nullptr) return VDBGPU_RESOURCE_EXHAUSTED;
+  Status s = vdbgpu::Context::Open(device, &h->c);
+  if (!s.ok()) {
+    delete h;
+    return static_cast<int>(s.code());
+  }
+  *out = h;
+  return VDBGPU_OK;
+}
+
+void vdbgpu_close(vdbgpu_ctx* ctx) { delete ctx; }
+
+size_t vdbgpu_last_error(const vdbgpu_ctx* ctx, char* buf, size_t cap) {
+  const std::string empty;
+  const std::string& e = (ctx != nullptr && ctx->c) ? ctx->c->last_error() : empty;
+  if (buf != nullptr && cap > 0) {
+    const size_t n = std::min(cap - 1, e.size());
+    std::memcpy(buf, e.data(), n);
+    buf[n] = '\0';
+  }
+  return e.size();
+}
+
+int vdbgpu_set_stream(vdbgpu_ctx* ctx, void* stream) {
+  if (ctx == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  ctx->c->set_user_stream(static_cast<cudaStream_t>(stream));
+  return VDBGPU_OK;
+}
+
+int vdbgpu_set_timing(vdbgpu_ctx* ctx, int enable) {
+  if (ctx == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  Status s = ctx->c->EnableTiming(enable != 0);
+  return s.ok() ? VDBGPU_OK : Fail(ctx, s);
+}
+
+int vdbgpu_stage_times(vdbgpu_ctx* ctx, float* out, int cap) {
+  if (ctx == nullptr || out == nullptr) return 0;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  return ctx->c->StageTimes(out, cap);
+}
+
+int vdbgpu_synchronize(vdbgpu_ctx* ctx) {
+  if (ctx == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  Status s = ctx->c->Sync("synchronize");
+  return s.ok() ? VDBGPU_OK : Fail(ctx, s);
+}
+
+void vdbgpu_search_params_default(vdbgpu_search_params* p) {
+  if (p == nullptr) return;
+  p->ef = 64;
+  p->nprobe = 16;
+  p->rerank = -1;
+  p->strategy = 0;
+  p->prefilter_threshold = 10000;
+  p->post_filter_alpha = 10;
+}
+
+int vdbgpu_index_load(vdbgpu_ctx* ctx, const void* file_bytes, size_t nbytes, int metric,
+                      const float* rows, uint64_t nrows, uint32_t dim, uint32_t padded_dim,
+                      vdbgpu_index** out) {
+  if (ctx == nullptr || out == nullptr || file_bytes == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = nullptr;
+  if (metric < 0 || metric > 2 || dim == 0 || dim > padded_dim || padded_dim % 16 != 0 ||
+      (nrows > 0 && rows == nullptr))
+    return Fail(ctx, Status(Status::kInvalidArgument, "bad index geometry or metric"));
+  if (nrows > 0xFFFFFFFFull)
+    return Fail(ctx, Status(Status::kInvalidArgument, "a segment holds at most 2^32 - 1 rows"));
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  std::unique_ptr<vdbgpu::GpuIndex> idx;
+  Status s = vdbgpu::LoadIndexFile(*ctx->c, file_bytes, nbytes, metric, rows, nrows, dim,
+                                   padded_dim, &idx);
+  if (!s.ok()) return Fail(ctx, s);
+  *out = new vdbgpu_index{ctx, std::move(idx)};
+  return VDBGPU_OK;
+}
+
+int vdbgpu_index_create(vdbgpu_ctx* ctx, int type, int metric, const float* rows, uint64_t nrows,
+                        uint32_t dim, uint32_t padded_dim, vdbgpu_index** out) {
+  if (ctx == nullptr || out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = nullptr;
+  if (metric < 0 || metric > 2 || dim == 0 || dim > padded_dim || padded_dim % 16 != 0 ||
+      (nrows > 0 && rows == nullptr))
+    return Fail(ctx, Status(Status::kInvalidArgument, "bad index geometry or metric"));
+  if (nrows > 0xFFFFFFFFull)
+    return Fail(ctx, Status(Status::kInvalidArgument, "a segment holds at most 2^32 - 1 rows"));
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  std::unique_ptr<vdbgpu::GpuIndex> idx;
+  Status s;
+  if (type == VDBGPU_INDEX_FLAT) {
+    s = vdbgpu::CreateFlatIndex(*ctx->c, metric, rows, nrows, dim, padded_dim, &idx);
+  } else if (type == VDBGPU_INDEX_SQ8_FLAT) {
+    s = vdbgpu::CreateSq8FlatIndex(*ctx->c, metric, rows, nrows, dim, padded_dim, nullptr, nullptr,
+                                   nullptr, &idx);
+  } else {
+    s = Status(Status::kNotSupported,
+               "only FLAT and SQ8_FLAT are built on the GPU; load other types from index files");
+  }
+  if (!s.ok()) return Fail(ctx, s);
+  *out = new vdbgpu_index{ctx, std::move(idx)};
+  return VDBGPU_OK;
+}
+
+void vdbgpu_index_free(vdbgpu_index* index) {
+  if (index == nullptr) return;
+  if (index->ctx != nullptr && index->ctx->c) {
+    std::lock_guard<std::mutex> g(index->ctx->c->mu());
+    cudaSetDevice(index->ctx->c->device());
+    cudaStreamSynchronize(index->ctx->c->stream());
+    index->idx.reset();
+  }
+  delete index;
+}
+
+int vdbgpu_index_get_info(const vdbgpu_index* index, vdbgpu_index_info* out) {
+  if (index == nullptr || out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  out->type = index->idx->type();
+  out->metric = index->idx->metric;
+  out->rows = index->idx->rows();
+  out->dim = index->idx->dim;
+  out->padded_dim = index->idx->pd;
+  out->device_bytes = index->idx->device_bytes();
+  return VDBGPU_OK;
+}
+
+int vdbgpu_index_search(vdbgpu_index* index, const float* queries, uint64_t nq, uint32_t k,
+                        const vdbgpu_search_params* params, const uint64_t* allow_bits,
+                        float* out_dist, uint32_t* out_row, uint64_t* out_dist_comps) {
+  if (index == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  vdbgpu_ctx* ctx = index->ctx;
+  if (nq == 0 || k == 0) return VDBGPU_OK;
+  if (queries == nullptr || out_dist == nullptr || out_row == nullptr)
+    return Fail(ctx, Status(Status::kInvalidArgument, "null query or output buffer"));
+  if (k > 10000) return Fail(ctx, Status(Status::kInvalidArgument, "k must be in 1..10000"));
+  vdbgpu::Context& c = *ctx->c;
+  std::lock_guard<std::mutex> g(c.mu());
+  cudaSetDevice(c.device());
+  vdbgpu::GpuIndex& idx = *index->idx;
+  const uint32_t pd = idx.pd;
+  const cudaStream_t st = c.stream();
+
+  vdbgpu::SearchBatch b{};
+  b.nq = nq;
+  b.k = k;
+  if (params != nullptr) {
+    b.params.ef = params->ef;
+    b.params.nprobe = params->nprobe;
+    b.params.rerank = params->rerank;
+    b.params.strategy = params->strategy;
+    b.params.prefilter_threshold = params->prefilter_threshold;
+    b.params.post_filter_alpha = params->post_filter_alpha;
+  }
+  Status s;
+  auto check = [&](const Status& x) { s = x; return x.ok(); };
+  auto cuda = [&](cudaError_t e, const char* what) { return check(vdbgpu::CudaStatus(e, what)); };
+
+  // Queries.
+  void* p = nullptr;
+  if (IsDevicePtr(queries)) {
+    b.queries = queries;
+  } else {
+    if (!check(c.workspace(vdbgpu::kWsQueries, nq * pd * sizeof(float), &p))) return Fail(ctx, s);
+    if (!cuda(cudaMemcpyAsync(p, queries, nq * pd * sizeof(float), cudaMemcpyHostToDevice, st), "copy queries"))
+      return Fail(ctx, s);
+    b.queries = static_cast<const float*>(p);
+  }
+  // Filter bitset: 64-bit words (little-endian) seen as 32-bit words, padded to 256 rows.
+  if (allow_bits != nullptr) {
+    const uint64_t n = idx.rows();
+    const uint64_t words64 = (n + 63) / 64;
+    const uint64_t bytes = RoundUp(std::max<uint64_t>(n, 1), 256) / 8 + 64;
+    if (!check(c.workspace(vdbgpu::kWsAllow, bytes, &p))) return Fail(ctx, s);
+    if (!cuda(cudaMemsetAsync(p, 0, bytes, st), "clear filter")) return Fail(ctx, s);
+    if (words64 > 0 &&
+        !cuda(cudaMemcpyAsync(p, allow_bits, words64 * 8, cudaMemcpyDefault, st), "copy filter"))
+      return Fail(ctx, s);
+    b.allow = static_cast<const uint32_t*>(p);
+  }
+  // Outputs.
+  const bool dev_out = IsDevicePtr(out_dist) && IsDevicePtr(out_row);
+  if (dev_out) {
+    b.out_dist = out_dist;
+    b.out_row = out_row;
+  } else {
+    void* od = nullptr;
+    void* orow = nullptr;
+    if (!check(c.workspace(vdbgpu::kWsOutDist, nq * k * sizeof(float), &od)) ||
+        !check(c.workspace(vdbgpu::kWsOutRow, nq * k * sizeof(uint32_t), &orow)))
+      return Fail(ctx, s);
+    b.out_dist = static_cast<float*>(od);
+    b.out_row = static_cast<uint32_t*>(orow);
+  }
+  const bool dev_dc = out_dist_comps != nullptr && IsDevicePtr(out_dist_comps);
+  if (out_dist_comps != nullptr) {
+    if (dev_dc) {
+      b.dist_comps = out_dist_comps;
+    } else {
+      if (!check(c.workspace(vdbgpu::kWsDistComps, nq * sizeof(uint64_t), &p))) return Fail(ctx, s);
+      b.dist_comps = static_cast<uint64_t*>(p);
+    }
+  }
+  if (!check(idx.Search(c, b))) return Fail(ctx, s);
+  if (!dev_out) {
+    if (!cuda(cudaMemcpyAsync(out_dist, b.out_dist, nq * k * sizeof(float), cudaMemcpyDeviceToHost, st), "copy distances") ||
+        !cuda(cudaMemcpyAsync(out_row, b.out_row, nq * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "copy rows"))
+      return Fail(ctx, s);
+  }
+  if (out_dist_comps != nullptr && !dev_dc) {
+    if (!cuda(cudaMemcpyAsync(out_dist_comps, b.dist_comps, nq * sizeof(uint64_t), cudaMemcpyDeviceToHost, st), "copy stats"))
+      return Fail(ctx, s);
+  }
+  if (!check(c.Sync("search"))) return Fail(ctx, s);
+  return VDBGPU_OK;
+}
+
+int vdbgpu_index_sq8_export(const vdbgpu_index* index, float* vmin, float* scale, uint8_t* codes) {
+  if (index == nullptr || vmin == nullptr || scale == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  vdbgpu_ctx* ctx = index->ctx;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  Status s = index->idx->ExportSq8(*ctx->c, vmin, scale, codes);
+  return s.ok() ? VDBGPU_OK : Fail(ctx, s);
+}
+
+int vdbgpu_index_file_inspect(const void* file_bytes, size_t nbytes, int* type) {
+  if (file_bytes == nullptr || type == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::string_view magic, body;
+  Status s = vdbgpu::CheckIndexFile(std::string_view(static_cast<const char*>(file_bytes), nbytes),
+                                    &magic, &body);
+  if (!s.ok()) return static_cast<int>(s.code());
+  *type = vdbgpu::IndexTypeForMagic(magic);
+  return *type < 0 ? VDBGPU_CORRUPTION : VDBGPU_OK;
+}
+
+}  // extern "C"

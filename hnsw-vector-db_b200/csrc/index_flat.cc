@@ -1,0 +1,359 @@
+// Exact flat search (FlatIndex, src/index/flat_index.h:24-44) and the exhaustive SQ8 scan with
+// an fp32 re-rank on the GPU. Both run the same pipeline (ScanSearch):
+//   prep_queries -> tensor-core scan with fused top-C (scan_mma.cu) -> exact finalize (select.cu)
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "kernels.cuh"
+#include "runtime.h"
+#include "scan_mma.cuh"
+
+namespace vdbgpu {
+namespace {
+
+uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
+
+uint32_t Pow2Ceil(uint32_t x) {
+  uint32_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Row slices per 128-query tile: minimises waves * (tiles per slice + a fixed per-slice cost)
+// for a grid of one CTA per SM.
+void ChooseUnits(uint64_t qtiles, uint64_t ntiles, int sms, int* upq, int* tiles_per_unit) {
+  double best = 1e300;
+  *upq = 1;
+  *tiles_per_unit = static_cast<int>(ntiles);
+  const uint64_t max_u = std::min<uint64_t>(ntiles, 512);
+  for (uint64_t u = 1; u <= max_u; ++u) {
+    const uint64_t tpu = (ntiles + u - 1) / u;
+    const uint64_t real_u = (ntiles + tpu - 1) / tpu;
+    const uint64_t units = qtiles * real_u;
+    const uint64_t waves = (units + sms - 1) / sms;
+    const double t = static_cast<double>(waves) * (static_cast<double>(tpu) + 3.0);
+    if (t < best) {
+      best = t;
+      *upq = static_cast<int>(real_u);
+      *tiles_per_unit = static_cast<int>(tpu);
+    }
+  }
+}
+
+// Copies n x pd floats from host or device memory to a new device buffer.
+Status UploadRows(Context& ctx, const float* rows, uint64_t n, uint32_t pd, DeviceBuffer* out) {
+  VDBGPU_RETURN_IF_ERROR(out->alloc(std::max<uint64_t>(1, n * pd) * sizeof(float)));
+  if (n > 0)
+    VDBGPU_CUDA(cudaMemcpyAsync(out->get(), rows, n * pd * sizeof(float), cudaMemcpyDefault,
+                                ctx.stream()));
+  return Status::OK();
+}
+
+class FlatGpuIndex final : public GpuIndex {
+ public:
+  int type() const override { return kIndexFlat; }
+  uint64_t rows() const override { return n_; }
+  uint64_t device_bytes() const override {
+    return rows_.size() + operand_.size() + norms_.size();
+  }
+
+  Status Build(Context& ctx, const float* rows, uint64_t n) {
+    n_ = n;
+    const uint64_t npad = RoundUp(std::max<uint64_t>(n, 1), kScanBN);
+    const uint32_t kpad = static_cast<uint32_t>(RoundUp(pd, kScanBK));
+    VDBGPU_RETURN_IF_ERROR(UploadRows(ctx, rows, n, pd, &rows_));
+    // fp16 when the rows fit its range (scaled by a power of two into [2^14, 2^15)), else bf16.
+    DeviceBuffer amax;
+    VDBGPU_RETURN_IF_ERROR(amax.alloc(sizeof(uint32_t)));
+    VDBGPU_CUDA(cudaMemsetAsync(amax.get(), 0, sizeof(uint32_t), ctx.stream()));
+    if (n > 0) VDBGPU_CUDA(LaunchAbsMax(rows_.as<float>(), n * pd, amax.as<uint32_t>(), ctx.stream()));
+    uint32_t bits = 0;
+    VDBGPU_CUDA(cudaMemcpyAsync(&bits, amax.get(), 4, cudaMemcpyDeviceToHost, ctx.stream()));
+    VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    float m;
+    std::memcpy(&m, &bits, 4);
+    if (!std::isfinite(m)) return Status(Status::kInvalidArgument, "rows contain NaN or infinity");
+    op_.ab_format = m > 60000.f ? 1 : 0;
+    op_.row_scale_log2 = (op_.ab_format == 0 && m > 0.f) ? 14 - std::ilogb(m) : 0;
+    VDBGPU_RETURN_IF_ERROR(operand_.alloc(npad * kpad * 2));
+    VDBGPU_CUDA(cudaMemsetAsync(operand_.get(), 0, npad * kpad * 2, ctx.stream()));
+    VDBGPU_RETURN_IF_ERROR(norms_.alloc(npad * sizeof(float)));
+    VDBGPU_CUDA(cudaMemsetAsync(norms_.get(), 0, npad * sizeof(float), ctx.stream()));
+    if (n > 0)
+      VDBGPU_CUDA(LaunchPrepRows(rows_.as<float>(), n, pd, kpad, op_.ab_format, op_.row_scale_log2,
+                                 operand_.get(), norms_.as<float>(), ctx.stream()));
+    op_.b_operand = operand_.get();
+    op_.rows = n;
+    op_.kpad = kpad;
+    op_.rowterm = metric == 0 ? norms_.as<float>() : nullptr;
+    op_.prep_kind = kPrepFlat;
+    op_.key_factor = metric == 0 ? 2 : 1;
+    op_.rows_f32 = rows_.as<float>();
+    VDBGPU_RETURN_IF_ERROR(
+        ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, op_.ab_format));
+    return ctx.Sync("flat index build");
+  }
+
+  // FlatIndex::search (src/index/flat_index.cc:73-77): exact top-k over allowed rows; counts
+  // every row as a distance computation.
+  Status Search(Context& ctx, const SearchBatch& b) override {
+    if (b.k > 256) return Status(Status::kNotSupported, "k > 256 is not supported by the GPU flat path");
+    const int cpre = static_cast<int>(std::max<uint32_t>(32, Pow2Ceil(2 * b.k)));
+    VDBGPU_RETURN_IF_ERROR(ScanSearch(ctx, op_, metric, pd, b, cpre, 0));
+    if (b.dist_comps != nullptr) {
+      std::vector<uint64_t> dc(b.nq, n_);
+      VDBGPU_CUDA(cudaMemcpyAsync(b.dist_comps, dc.data(), b.nq * 8, cudaMemcpyHostToDevice, ctx.stream()));
+      VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    }
+    return Status::OK();
+  }
+
+ private:
+  uint64_t n_ = 0;
+  DeviceBuffer rows_, operand_, norms_;
+  ScanOperands op_;
+};
+
+class Sq8FlatGpuIndex final : public GpuIndex {
+ public:
+  int type() const override { return kIndexSq8Flat; }
+  uint64_t rows() const override { return n_; }
+  uint64_t device_bytes() const override {
+    return rows_.size() + codes_.size() + operand_.size() + rowterm_.size() + vmin_.size() +
+           scale_.size();
+  }
+
+  // Sq8Quantizer::train + encode (src/index/quant/sq8.cc:9-37) on the GPU, or loads a trained
+  // quantiser and its codes (vmin/scale/codes non-null, host or device memory).
+  Status Build(Context& ctx, const float* rows, uint64_t n, const float* vmin, const float* scale,
+               const uint8_t* codes) {
+    n_ = n;
+    const uint64_t npad = RoundUp(std::max<uint64_t>(n, 1), kScanBN);
+    const uint32_t kpad = static_cast<uint32_t>(RoundUp(pd, kScanBK));
+    VDBGPU_RETURN_IF_ERROR(UploadRows(ctx, rows, n, pd, &rows_));
+    VDBGPU_RETURN_IF_ERROR(vmin_.alloc(pd * sizeof(float)));
+    VDBGPU_RETURN_IF_ERROR(scale_.alloc(pd * sizeof(float)));
+    VDBGPU_RETURN_IF_ERROR(codes_.alloc(std::max<uint64_t>(1, n * pd)));
+    VDBGPU_RETURN_IF_ERROR(operand_.alloc(npad * kpad * 2));
+    VDBGPU_CUDA(cudaMemsetAsync(operand_.get(), 0, npad * kpad * 2, ctx.stream()));
+    VDBGPU_RETURN_IF_ERROR(rowterm_.alloc(npad * sizeof(float)));
+    VDBGPU_CUDA(cudaMemsetAsync(rowterm_.get(), 0, npad * sizeof(float), ctx.stream()));
+    if (vmin != nullptr) {
+      VDBGPU_CUDA(cudaMemcpyAsync(vmin_.get(), vmin, pd * 4, cudaMemcpyDefault, ctx.stream()));
+      VDBGPU_CUDA(cudaMemcpyAsync(scale_.get(), scale, pd * 4, cudaMemcpyDefault, ctx.stream()));
+      if (n > 0) {
+        VDBGPU_CUDA(cudaMemcpyAsync(codes_.get(), codes, n * pd, cudaMemcpyDefault, ctx.stream()));
+        VDBGPU_CUDA(LaunchSq8Operand(codes_.as<uint8_t>(), n, pd, kpad, scale_.as<float>(),
+                                     operand_.as<__half>(), rowterm_.as<float>(), ctx.stream()));
+      }
+    } else {
+      // train: per-dimension min/max, then scale = (max - min) / 255 in IEEE fp32 on the host.
+      std::vector<float> hmin(pd, 0.f), hscale(pd, 0.f);
+      if (n > 0) {
+        DeviceBuffer kmm;
+        VDBGPU_RETURN_IF_ERROR(kmm.alloc(2 * dim * sizeof(uint32_t)));
+        uint32_t* kmin = kmm.as<uint32_t>();
+        uint32_t* kmax = kmin + dim;
+        VDBGPU_CUDA(cudaMemsetAsync(kmin, 0xFF, dim * 4, ctx.stream()));
+        VDBGPU_CUDA(cudaMemsetAsync(kmax, 0x00, dim * 4, ctx.stream()));
+        VDBGPU_CUDA(LaunchSq8MinMax(rows_.as<float>(), n, dim, pd, kmin, kmax, ctx.stream()));
+        std::vector<uint32_t> h(2 * dim);
+        VDBGPU_CUDA(cudaMemcpyAsync(h.data(), kmin, 2 * dim * 4, cudaMemcpyDeviceToHost, ctx.stream()));
+        VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+        for (uint32_t i = 0; i < dim; ++i) {
+          const float lo = KeyToFloat(h[i]), hi = KeyToFloat(h[dim + i]);
+          hmin[i] = lo;
+          hscale[i] = (hi - lo) / 255.f;
+        }
+      }
+      VDBGPU_CUDA(cudaMemcpyAsync(vmin_.get(), hmin.data(), pd * 4, cudaMemcpyHostToDevice, ctx.stream()));
+      VDBGPU_CUDA(cudaMemcpyAsync(scale_.get(), hscale.data(), pd * 4, cudaMemcpyHostToDevice, ctx.stream()));
+      if (n > 0)
+        VDBGPU_CUDA(LaunchSq8Encode(rows_.as<float>(), n, dim, pd, kpad, vmin_.as<float>(),
+                                    scale_.as<float>(), codes_.as<uint8_t>(), operand_.as<__half>(),
+                                    rowterm_.as<float>(), ctx.stream()));
+      VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    }
+    op_.b_operand = operand_.get();
+    op_.rows = n;
+    op_.kpad = kpad;
+    op_.ab_format = 0;
+    op_.row_scale_log2 = 0;
+    op_.rowterm = metric == 0 ? rowterm_.as<float>() : nullptr;
+    op_.prep_kind = metric == 0 ? kPrepSq8L2 : kPrepSq8Ip;
+    op_.key_factor = metric == 0 ? 2 : 1;
+    op_.rows_f32 = rows_.as<float>();
+    op_.codes = codes_.as<uint8_t>();
+    op_.vmin = vmin_.as<float>();
+    op_.scale = scale_.as<float>();
+    VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, 0));
+    return ctx.Sync("sq8 index build");
+  }
+
+  // Exhaustive SQ8 scan: SQ8 distances to every code pick the `depth` best, which are re-ranked
+  // on fp32 rows (Rerank, src/index/index.cc:89-95). depth follows RerankDepth
+  // (src/index/quant/ivf_pq.cc:16-19): rerank < 0 -> max(10k, 100), 0 -> SQ8 distances only.
+  Status Search(Context& ctx, const SearchBatch& b) override {
+    const int32_t rr = b.params.rerank;
+    const uint32_t depth = rr < 0 ? std::max<uint32_t>(10 * b.k, 100) : static_cast<uint32_t>(rr);
+    const uint32_t need = std::max(depth, b.k);
+    const uint32_t cpre = Pow2Ceil(need + need / 4);
+    if (cpre > 256)
+      return Status(Status::kNotSupported, "re-rank depth above 204 is not supported on the GPU");
+    VDBGPU_RETURN_IF_ERROR(ScanSearch(ctx, op_, metric, pd, b, static_cast<int>(cpre),
+                                      static_cast<int>(depth)));
+    if (b.dist_comps != nullptr) {
+      std::vector<uint64_t> dc(b.nq, n_ + (depth > 0 ? std::min<uint64_t>(depth, n_) : 0));
+      VDBGPU_CUDA(cudaMemcpyAsync(b.dist_comps, dc.data(), b.nq * 8, cudaMemcpyHostToDevice, ctx.stream()));
+      VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    }
+    return Status::OK();
+  }
+
+  Status ExportSq8(Context& ctx, float* vmin, float* scale, uint8_t* codes) const override {
+    VDBGPU_CUDA(cudaMemcpyAsync(vmin, vmin_.get(), pd * 4, cudaMemcpyDefault, ctx.stream()));
+    VDBGPU_CUDA(cudaMemcpyAsync(scale, scale_.get(), pd * 4, cudaMemcpyDefault, ctx.stream()));
+    if (codes != nullptr && n_ > 0)
+      VDBGPU_CUDA(cudaMemcpyAsync(codes, codes_.get(), n_ * pd, cudaMemcpyDefault, ctx.stream()));
+    VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    return Status::OK();
+  }
+
+ private:
+  static float KeyToFloat(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  }
+
+  uint64_t n_ = 0;
+  DeviceBuffer rows_, codes_, operand_, rowterm_, vmin_, scale_;
+  ScanOperands op_;
+};
+
+}  // namespace
+
+Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
+                  const SearchBatch& b, int cpre, int depth) {
+  if (b.nq == 0) return Status::OK();
+  if (op.rows == 0) {
+    // Nothing to scan: every slot is a miss.
+    std::vector<float> d(b.nq * b.k, INFINITY);
+    std::vector<uint32_t> r(b.nq * b.k, UINT32_MAX);
+    VDBGPU_CUDA(cudaMemcpyAsync(b.out_dist, d.data(), d.size() * 4, cudaMemcpyHostToDevice, ctx.stream()));
+    VDBGPU_CUDA(cudaMemcpyAsync(b.out_row, r.data(), r.size() * 4, cudaMemcpyHostToDevice, ctx.stream()));
+    return ctx.Sync("empty scan");
+  }
+  if (cpre > kScanCap - 64) return Status(Status::kNotSupported, "candidate depth too large");
+  if (op.kpad > kScanMaxKB * kScanBK)
+    return Status(Status::kNotSupported, "padded dimension above 256 is not supported by the scan");
+  const uint64_t nq = b.nq;
+  const uint64_t nq_pad = RoundUp(nq, kScanBM);
+  void *a_op, *qscale, *qtau, *cand, *cnt;
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsOperandA, nq_pad * op.kpad * 2, &a_op));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsQScale, nq * sizeof(float), &qscale));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsQTau, nq * sizeof(uint32_t), &qtau));
+  VDBGPU_CUDA(cudaMemsetAsync(qtau, 0xFF, nq * sizeof(uint32_t), ctx.stream()));
+
+  ctx.Mark(0);
+  PrepArgs pa{};
+  pa.nq = static_cast<int>(nq);
+  pa.nq_pad = static_cast<int>(nq_pad);
+  pa.pd = static_cast<int>(pd);
+  pa.kpad = static_cast<int>(op.kpad);
+  pa.kind = op.prep_kind;
+  pa.ab_format = op.ab_format;
+  pa.key_factor = op.key_factor;
+  pa.row_scale_log2 = op.row_scale_log2;
+  pa.queries = b.queries;
+  pa.vmin = op.vmin;
+  pa.scale = op.scale;
+  pa.operand = a_op;
+  pa.qscale = static_cast<float*>(qscale);
+  VDBGPU_CUDA(LaunchPrepQueries(pa, ctx.stream()));
+
+  CUtensorMap amap;
+  VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&amap, a_op, nq_pad, op.kpad, kScanBM, op.ab_format));
+  const uint64_t qtiles = nq_pad / kScanBM;
+  const uint64_t ntiles = (op.rows + kScanBN - 1) / kScanBN;
+  int upq = 1, tpu = 1;
+  ChooseUnits(qtiles, ntiles, ctx.sm_count(), &upq, &tpu);
+  const uint64_t nunits = qtiles * static_cast<uint64_t>(upq);
+  VDBGPU_RETURN_IF_ERROR(
+      ctx.workspace(kWsCand, nunits * kScanBM * kScanCap * sizeof(uint2), &cand));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, nunits * kScanBM * sizeof(int), &cnt));
+
+  ScanArgs sa{};
+  sa.nq = static_cast<int>(nq);
+  sa.nrows = static_cast<int>(op.rows);
+  sa.kblocks = static_cast<int>(op.kpad / kScanBK);
+  sa.mode = op.rowterm != nullptr ? kKeyRowTerm : kKeyScaled;
+  sa.ab_format = op.ab_format;
+  sa.keep = cpre;
+  sa.units_per_qtile = upq;
+  sa.rows_per_unit = tpu * kScanBN;
+  sa.nunits = static_cast<int>(nunits);
+  sa.qscale = static_cast<const float*>(qscale);
+  sa.rowterm = op.rowterm;
+  sa.allow = b.allow;
+  sa.cand = static_cast<uint2*>(cand);
+  sa.cand_count = static_cast<int*>(cnt);
+  sa.qtau = static_cast<uint32_t*>(qtau);
+  sa.status = ctx.status_word();
+  const int grid = static_cast<int>(std::min<uint64_t>(nunits, static_cast<uint64_t>(ctx.sm_count())));
+  ctx.Mark(1);
+  VDBGPU_CUDA(LaunchScan(amap, op.b_map, sa, grid, ctx.stream()));
+  ctx.Mark(2);
+
+  FinalizeArgs fa{};
+  fa.nq = static_cast<int>(nq);
+  fa.pd = static_cast<int>(pd);
+  fa.k = static_cast<int>(b.k);
+  fa.cpre = cpre;
+  fa.depth = depth;
+  fa.metric = metric;
+  fa.order = ctx.order();
+  fa.units_per_qtile = upq;
+  fa.cand = static_cast<const uint2*>(cand);
+  fa.cand_count = static_cast<const int*>(cnt);
+  fa.qtau = static_cast<const uint32_t*>(qtau);
+  fa.queries = b.queries;
+  fa.rows = op.rows_f32;
+  fa.codes = op.codes;
+  fa.vmin = op.vmin;
+  fa.scale = op.scale;
+  fa.out_dist = b.out_dist;
+  fa.out_row = b.out_row;
+  VDBGPU_CUDA(LaunchFinalize(fa, ctx.stream()));
+  ctx.Mark(3);
+  return Status::OK();
+}
+
+Status CreateFlatIndex(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim,
+                       uint32_t pd, std::unique_ptr<GpuIndex>* out) {
+  auto idx = std::make_unique<FlatGpuIndex>();
+  idx->metric = metric;
+  idx->dim = dim;
+  idx->pd = pd;
+  VDBGPU_RETURN_IF_ERROR(idx->Build(ctx, rows, n));
+  *out = std::move(idx);
+  return Status::OK();
+}
+
+Status CreateSq8FlatIndex(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim,
+                          uint32_t pd, const float* vmin, const float* scale, const uint8_t* codes,
+                          std::unique_ptr<GpuIndex>* out) {
+  if (dim > 1024) return Status(Status::kNotSupported, "SQ8 training supports dim <= 1024");
+  auto idx = std::make_unique<Sq8FlatGpuIndex>();
+  idx->metric = metric;
+  idx->dim = dim;
+  idx->pd = pd;
+  VDBGPU_RETURN_IF_ERROR(idx->Build(ctx, rows, n, vmin, scale, codes));
+  *out = std::move(idx);
+  return Status::OK();
+}
+
+}  // namespace vdbgpu

@@ -1,0 +1,388 @@
+// Tensor-core pre-rank scan for flat and SQ8 search (sm_100a).
+//
+// Replaces the reference's per-row distance loop (FlatSearch, src/index/flat_index.cc:11-27, and
+// the SQ8 distance loop over codes, src/distance/avx512.cc:48-65) with a Q x N x K contraction on
+// the 5th-generation tensor cores, fused with a streaming top-C selection so the Q x N distance
+// matrix never reaches HBM.
+//
+// One persistent CTA per SM walks "units": a 128-query tile against a contiguous slice of rows.
+//   warp 0      TMA producer: loads the query tile once per unit (resident), then streams row
+//               k-blocks (256 rows x 64 fp16) through a 4-stage mbarrier ring.
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one thread issues
+//               tcgen05.mma (M=128, N=256, K=16) into alternating accumulators.
+//   warps 2..5  epilogue: each thread owns one query (one TMEM lane) and reads its 256 columns in
+//               chunks of 32 (tcgen05.ld). A chunk whose best key does not beat the thread's
+//               threshold costs one min per value; otherwise qualifying (key, row) pairs are
+//               appended to the query's candidate buffer in global memory. A full buffer is
+//               compacted by the whole warp to its C best (by key, then row) and the C-th key
+//               becomes the new threshold, also published to every unit of the same query.
+// Rows inside one unit arrive in increasing order, so a strict "key < threshold" test keeps
+// ties exactly as the reference's (dist, id) order does. Thresholds from other units are
+// applied as "key <= their C-th key", which can never drop a member of the global top C.
+#include "common.cuh"
+#include "scan_mma.cuh"
+
+#include <cuda_runtime.h>
+
+namespace vdbgpu {
+namespace {
+
+constexpr uint32_t kABytesPerKB = kScanBM * 128;  // 16 KB
+constexpr uint32_t kBBytesPerStage = kScanBN * 128;  // 32 KB
+constexpr uint32_t kTmemCols = 512;
+
+struct __align__(8) ScanBarriers {
+  uint64_t full[kScanStages];
+  uint64_t empty[kScanStages];
+  uint64_t a_full;
+  uint64_t a_empty;
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_slot;
+};
+
+__device__ __forceinline__ void unit_rows(const ScanArgs& a, int unit, int* qtile, int* r0,
+                                          int* r1) {
+  *qtile = unit / a.units_per_qtile;
+  const int part = unit - *qtile * a.units_per_qtile;
+  *r0 = part * a.rows_per_unit;
+  int e = *r0 + a.rows_per_unit;
+  *r1 = e < a.nrows ? e : a.nrows;
+}
+
+// Warp-cooperative compaction of lane `src`'s candidate buffer (n entries, in row order) to
+// its `keep` best by (key, row). Returns the keep-th key (ordered) to every lane.
+__device__ uint32_t compact_buffer(uint2* buf, int n, int keep) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kT = kScanCap / 32;
+  uint32_t keys[kT];
+  uint2 ent[kT];
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    const int e = lane + 32 * t;
+    ent[t] = e < n ? buf[e] : make_uint2(0xFFFFFFFFu, 0xFFFFFFFFu);
+    keys[t] = e < n ? float_key(__uint_as_float(ent[t].x)) : 0xFFFFFFFFu;
+  }
+  // Largest value v with #{key < v} < keep: the keep-th smallest key.
+  uint32_t ans = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = ans | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int t = 0; t < kT; ++t) c += keys[t] < cand ? 1 : 0;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    if (c < keep) ans = cand;
+  }
+  int less = 0;
+#pragma unroll
+  for (int t = 0; t < kT; ++t) less += keys[t] < ans ? 1 : 0;
+  less = __reduce_add_sync(0xFFFFFFFFu, less);
+  const int need_eq = keep - less;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  int w = 0, eq_seen = 0;
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    const bool is_less = keys[t] < ans;
+    const bool is_eq = keys[t] == ans && (lane + 32 * t) < n;
+    const uint32_t eqm = __ballot_sync(0xFFFFFFFFu, is_eq);
+    const int eq_before = eq_seen + __popc(eqm & lt_mask);
+    const bool keep_it = is_less || (is_eq && eq_before < need_eq);
+    const uint32_t km = __ballot_sync(0xFFFFFFFFu, keep_it);
+    if (keep_it) buf[w + __popc(km & lt_mask)] = ent[t];
+    w += __popc(km);
+    eq_seen += __popc(eqm);
+  }
+  __syncwarp();
+  return ans;
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kScanThreads, 1)
+    scan_mma_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b, const ScanArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzle atoms.
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + a.kblocks * kABytesPerKB;
+  ScanBarriers* bars =
+      reinterpret_cast<ScanBarriers*>(smem_b + kScanStages * kBBytesPerStage);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kScanStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->a_full, 1);
+    mbar_init(&bars->a_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 128);
+    }
+    mbar_init(&bars->mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, a_phase = 0;
+      uint32_t issued = 0, last_parity = 0;  // per-stage bit masks of loads in flight
+      bool a_issued = false;
+      uint32_t a_parity = 0;
+      bool ok = true;
+      bool first = true;
+      for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
+        int qtile, r0, r1;
+        unit_rows(a, unit, &qtile, &r0, &r1);
+        if (!first) {
+          if (!mbar_wait(&bars->a_empty, a_phase, a.status, kDevTimeoutEmpty)) break;
+          a_phase ^= 1u;
+        }
+        first = false;
+        mbar_arrive_expect_tx(&bars->a_full, a.kblocks * kABytesPerKB);
+        a_issued = true;
+        a_parity = a_phase;
+        for (int kb = 0; kb < a.kblocks; ++kb)
+          tma_load_2d(smem_a + kb * kABytesPerKB, &tmap_a, &bars->a_full, kb * kScanBK,
+                      qtile * kScanBM);
+        for (int row0 = r0; ok && row0 < r1; row0 += kScanBN) {
+          for (int kb = 0; kb < a.kblocks; ++kb) {
+            if (!mbar_wait(&bars->empty[stage], phase ^ 1u, a.status, kDevTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars->full[stage], kBBytesPerStage);
+            tma_load_2d(smem_b + stage * kBBytesPerStage, &tmap_b, &bars->full[stage],
+                        kb * kScanBK, row0);
+            issued |= 1u << stage;
+            last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == kScanStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+      // Every copy this thread issued lands before the CTA may exit (bounded): the last load
+      // into each stage completes the phase recorded for it.
+      for (int s = 0; s < kScanStages; ++s)
+        if ((issued >> s) & 1u)
+          mbar_wait(&bars->full[s], (last_parity >> s) & 1u, nullptr, 0);
+      if (a_issued) mbar_wait(&bars->a_full, a_parity, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kScanBM, kScanBN, static_cast<uint32_t>(a.ab_format));
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0, a_phase = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(smem_a), b_base = smem_u32(smem_b);
+      for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
+        int qtile, r0, r1;
+        unit_rows(a, unit, &qtile, &r0, &r1);
+        if (!mbar_wait(&bars->a_full, a_phase, a.status, kDevTimeoutFull)) break;
+        a_phase ^= 1u;
+        tc_fence_after();
+        for (int row0 = r0; ok && row0 < r1; row0 += kScanBN) {
+          if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, a.status, kDevTimeoutAccFree)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kScanBN);
+          for (int kb = 0; kb < a.kblocks; ++kb) {
+            if (!mbar_wait(&bars->full[stage], phase, a.status, kDevTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_kb = a_base + kb * kABytesPerKB;
+            const uint32_t b_st = b_base + stage * kBBytesPerStage;
+#pragma unroll
+            for (int kk = 0; kk < kScanBK / 16; ++kk) {
+              umma_f16(d_tmem, umma_desc_sw128(a_kb + kk * 32), umma_desc_sw128(b_st + kk * 32),
+                       idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
+            umma_commit(&bars->empty[stage]);
+            if (++stage == kScanStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          umma_commit(&bars->acc_full[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+        umma_commit(&bars->a_empty);
+      }
+      // Every MMA this thread issued retires before TMEM is released (bounded wait).
+      umma_commit(&bars->mma_done);
+      mbar_wait(&bars->mma_done, 0, nullptr, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
+      int qtile, r0, r1;
+      unit_rows(a, unit, &qtile, &r0, &r1);
+      const int q = qtile * kScanBM + row_in_tile;
+      const bool valid_q = q < a.nq;
+      const float qs = valid_q ? a.qscale[q] : 0.f;
+      float tau = valid_q ? INFINITY : -INFINITY;
+      int count = 0;
+      uint2* buf = a.cand + (static_cast<size_t>(unit) * kScanBM + row_in_tile) * kScanCap;
+      for (int row0 = r0; row0 < r1; row0 += kScanBN) {
+        if (valid_q) {
+          const uint32_t g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
+          if (g != 0xFFFFFFFFu) tau = fminf(tau, key_float(g));
+        }
+        if (!mbar_wait(&bars->acc_full[acc], acc_phase, a.status, kDevTimeoutAcc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                static_cast<uint32_t>(acc * kScanBN);
+#pragma unroll 1
+        for (int ch = 0; ch < kScanBN / 32; ++ch) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(t_addr + ch * 32, v);
+          tmem_ld_wait();
+          const int c0 = row0 + ch * 32;
+          uint32_t allow_bits = 0xFFFFFFFFu;
+          if (a.allow != nullptr) allow_bits = __ldg(&a.allow[c0 >> 5]);
+          const int nvalid = r1 - c0;  // columns < nvalid are real rows of this unit
+          float kmin = INFINITY;
+          float rt[32];
+          if constexpr (kMode == kKeyRowTerm) {
+            const float4* rt4 = reinterpret_cast<const float4*>(a.rowterm + c0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 x = __ldg(&rt4[j]);
+              rt[4 * j] = x.x;
+              rt[4 * j + 1] = x.y;
+              rt[4 * j + 2] = x.z;
+              rt[4 * j + 3] = x.w;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float key;
+            if constexpr (kMode == kKeyRowTerm) {
+              key = fmaf(qs, __uint_as_float(v[j]), rt[j]);
+            } else {
+              key = qs * __uint_as_float(v[j]);
+            }
+            v[j] = __float_as_uint(key);
+          }
+          if (nvalid >= 32 && allow_bits == 0xFFFFFFFFu) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) kmin = fminf(kmin, __uint_as_float(v[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j >= nvalid || !((allow_bits >> j) & 1u)) v[j] = __float_as_uint(INFINITY);
+              kmin = fminf(kmin, __uint_as_float(v[j]));
+            }
+          }
+          if (__any_sync(0xFFFFFFFFu, kmin < tau)) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float key = __uint_as_float(v[j]);
+              if (key < tau) {
+                buf[count] = make_uint2(v[j], static_cast<uint32_t>(c0 + j));
+                ++count;
+              }
+            }
+            uint32_t need = __ballot_sync(0xFFFFFFFFu, count > kScanCap - 32);
+            while (need != 0u) {
+              const int src = __ffs(need) - 1;
+              need &= need - 1u;
+              const int n = __shfl_sync(0xFFFFFFFFu, count, src);
+              const int src_row = quad * 32 + src;
+              uint2* sbuf = a.cand + (static_cast<size_t>(unit) * kScanBM + src_row) * kScanCap;
+              __syncwarp();
+              const uint32_t kth = compact_buffer(sbuf, n, a.keep);
+              if (lane == src) {
+                count = a.keep;
+                tau = fminf(tau, key_float(kth));
+                // Other units of this query may drop keys above the keep-th key of this one.
+                atomicMin(&a.qtau[q], kth + 1u);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->acc_empty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      a.cand_count[static_cast<size_t>(unit) * kScanBM + row_in_tile] = valid_q ? count : 0;
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace
+
+size_t ScanSmemBytes(int kblocks) {
+  return 1024 + static_cast<size_t>(kblocks) * kABytesPerKB +
+         static_cast<size_t>(kScanStages) * kBBytesPerStage + sizeof(ScanBarriers);
+}
+
+cudaError_t LaunchScan(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
+                       int grid, cudaStream_t stream) {
+  const size_t smem = ScanSmemBytes(a.kblocks);
+  cudaError_t e;
+  if (a.mode == kKeyRowTerm) {
+    e = cudaFuncSetAttribute(scan_mma_kernel<kKeyRowTerm>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    scan_mma_kernel<kKeyRowTerm><<<grid, kScanThreads, smem, stream>>>(tmap_a, tmap_b, a);
+  } else {
+    e = cudaFuncSetAttribute(scan_mma_kernel<kKeyScaled>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    scan_mma_kernel<kKeyScaled><<<grid, kScanThreads, smem, stream>>>(tmap_a, tmap_b, a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace vdbgpu

@@ -1,0 +1,50 @@
+// Tensor-core scan with a fused streaming top-C selection: the pre-rank stage of exact flat
+// search and of the exhaustive SQ8 scan.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+namespace vdbgpu {
+
+constexpr int kScanBM = 128;      // queries per tile: TMEM lanes, M of the MMA
+constexpr int kScanBN = 256;      // rows per tile: TMEM columns of one accumulator, N of the MMA
+constexpr int kScanBK = 64;       // fp16 elements per k-block (one 128-byte swizzle atom)
+constexpr int kScanStages = 4;    // B k-block stages in flight
+constexpr int kScanMaxKB = 4;     // padded dims up to 256
+constexpr int kScanCap = 512;     // candidate slots per (unit, query)
+constexpr int kScanThreads = 192; // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2..5 epilogue
+
+// Key transform applied to the fp32 accumulator acc = sum_i A[q,i] * B[r,i]:
+//   kKeyScaled:  key = qscale[q] * acc
+//   kKeyRowTerm: key = fma(qscale[q], acc, rowterm[r])
+// Smaller key = closer. Keys of one query are comparable across rows and units.
+enum ScanKeyMode : int { kKeyScaled = 0, kKeyRowTerm = 1 };
+
+struct ScanArgs {
+  int nq;               // valid queries
+  int nrows;            // valid rows
+  int kblocks;          // ceil(padded_dim / 64)
+  int mode;             // ScanKeyMode
+  int ab_format;        // 0 = fp16, 1 = bf16 (both operands)
+  int keep;             // candidates kept per compaction (C), < kScanCap - 32
+  int units_per_qtile;  // row slices per 128-query tile
+  int rows_per_unit;    // multiple of kScanBN
+  int nunits;           // qtiles * units_per_qtile
+  const float* qscale;  // [nq]
+  const float* rowterm; // [round_up(nrows, 256)] (kKeyRowTerm) or null
+  const uint32_t* allow;// allowed-row bitset, 32 rows per word, padded to 256 rows; null = all
+  uint2* cand;          // [nunits][128][kScanCap] (float key bits, row)
+  int* cand_count;      // [nunits][128]
+  uint32_t* qtau;       // [nq] shared per-query threshold (ordered-key space), 0xFFFFFFFF = none
+  int* status;          // device status word
+};
+
+// Launches the scan on `stream`. tmap_a: queries operand [qpad x kpad] K-major, box {64, 128};
+// tmap_b: rows operand [nrows x kpad] K-major, box {64, 256}; both SWIZZLE_128B.
+cudaError_t LaunchScan(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
+                       int grid, cudaStream_t stream);
+
+size_t ScanSmemBytes(int kblocks);
+
+}  // namespace vdbgpu

@@ -1,0 +1,417 @@
+// Selection, exact re-rank and operand preparation kernels for flat and SQ8 search.
+//
+//   finalize_kernel  one warp per query: merges the candidate buffers that the tensor-core scan
+//                    left for that query (every row slice), keeps the C best by (pre-rank key,
+//                    row), recomputes their distances exactly in fp32 in the reference kernel
+//                    set's summation order, and writes the k best by (dist, id). For SQ8 the
+//                    exact SQ8 distances pick the re-rank depth first, then the fp32 rows decide
+//                    (Rerank, src/index/index.cc:89-95; TopK order, src/util/topk.h:13-54).
+//   prep_queries     fp32 queries -> fp16/bf16 tensor-core operand with a per-query power-of-two
+//                    scale, plus the per-query key multiplier.
+//   rows/codes prep  fp32 rows -> fp16/bf16 operand (+ squared norms); SQ8 codes -> fp16.
+//   sq8 train/encode Sq8Quantizer::train / encode (src/index/quant/sq8.cc:9-37), bit-exact.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "scan_mma.cuh"
+#include "warp_ops.cuh"
+
+namespace vdbgpu {
+namespace {
+
+constexpr int kFinWarps = 4;
+constexpr int kMaxSurvivors = 1024;
+constexpr uint64_t kNoNeighbor = ~0ull;  // packs (+NaN-ordered, UINT32_MAX): sorts last
+
+template <int E>
+__device__ void sort_into_smem(uint64_t* s, int n) {
+  const int lane = threadIdx.x & 31;
+  uint64_t x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    x[e] = i < n ? s[i] : kNoNeighbor;
+  }
+  warp_sort<E>(x);
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < E; ++e) s[e * 32 + lane] = x[e];
+  __syncwarp();
+}
+
+// Sorts s[0..n) (n <= 1024) ascending in place, padding to the sort size with kNoNeighbor.
+__device__ void sort_small(uint64_t* s, int n) {
+  if (n <= 32) sort_into_smem<1>(s, n);
+  else if (n <= 64) sort_into_smem<2>(s, n);
+  else if (n <= 128) sort_into_smem<4>(s, n);
+  else if (n <= 256) sort_into_smem<8>(s, n);
+  else if (n <= 512) sort_into_smem<16>(s, n);
+  else sort_into_smem<32>(s, n);
+}
+
+// The c-th smallest packed key (1-based) among entries passing `thr`, by bitwise search over
+// every entry of the query's buffers. Used only when more than kMaxSurvivors entries pass.
+__device__ uint64_t global_kth(const FinalizeArgs& a, int qtile, int row_in_tile, uint32_t thr,
+                               int c) {
+  uint64_t ans = 0;
+  for (int bit = 63; bit >= 0; --bit) {
+    const uint64_t cand = ans | (1ull << bit);
+    int cnt = 0;
+    for (int p = 0; p < a.units_per_qtile; ++p) {
+      const size_t slot = (static_cast<size_t>(qtile) * a.units_per_qtile + p) * kScanBM + row_in_tile;
+      const int n = a.cand_count[slot];
+      const uint2* b = a.cand + slot * kScanCap;
+      for (int e = threadIdx.x & 31; e < n; e += 32) {
+        const uint2 v = b[e];
+        const uint32_t key = float_key(__uint_as_float(v.x));
+        const uint64_t pk = (static_cast<uint64_t>(key) << 32) | v.y;
+        cnt += (key < thr && pk < cand) ? 1 : 0;
+      }
+    }
+    cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+    if (cnt < c) ans = cand;
+  }
+  return ans;
+}
+
+__global__ void __launch_bounds__(kFinWarps * 32)
+    finalize_kernel(const FinalizeArgs a) {
+  extern __shared__ __align__(16) uint8_t fsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pd = a.pd;
+  // Block-shared: vmin, scale (SQ8). Per warp: query, survivors / candidates.
+  float* vmin_s = reinterpret_cast<float*>(fsm);
+  float* scale_s = vmin_s + pd;
+  uint8_t* wbase = fsm + 2 * pd * sizeof(float) +
+                   warp * (pd * sizeof(float) + kMaxSurvivors * sizeof(uint64_t));
+  float* q_s = reinterpret_cast<float*>(wbase);
+  uint64_t* surv = reinterpret_cast<uint64_t*>(wbase + pd * sizeof(float));
+  if (a.codes != nullptr) {
+    for (int i = threadIdx.x; i < pd; i += blockDim.x) {
+      vmin_s[i] = a.vmin[i];
+      scale_s[i] = a.scale[i];
+    }
+  }
+  __syncthreads();
+  const int q = blockIdx.x * kFinWarps + warp;
+  if (q >= a.nq) return;
+  for (int i = lane; i < pd; i += 32) q_s[i] = a.queries[static_cast<size_t>(q) * pd + i];
+  const int qtile = q / kScanBM, row_in_tile = q % kScanBM;
+  const uint32_t thr = a.qtau[q];  // keep key < thr (ordered); 0xFFFFFFFF keeps all
+  const uint32_t lt = (1u << lane) - 1u;
+
+  // 1. Gather the entries that can still be among the C best.
+  int nsurv = 0;
+  for (int p = 0; p < a.units_per_qtile; ++p) {
+    const size_t slot = (static_cast<size_t>(qtile) * a.units_per_qtile + p) * kScanBM + row_in_tile;
+    const int n = a.cand_count[slot];
+    const uint2* b = a.cand + slot * kScanCap;
+    for (int e0 = 0; e0 < n; e0 += 32) {
+      const int e = e0 + lane;
+      uint2 v = make_uint2(0, 0);
+      bool pass = false;
+      if (e < n) {
+        v = b[e];
+        pass = float_key(__uint_as_float(v.x)) < thr;
+      }
+      const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
+      const int pos = nsurv + __popc(m & lt);
+      if (pass && pos < kMaxSurvivors)
+        surv[pos] = (static_cast<uint64_t>(float_key(__uint_as_float(v.x))) << 32) | v.y;
+      nsurv += __popc(m);
+    }
+  }
+  __syncwarp();
+  int ncand;
+  if (nsurv <= kMaxSurvivors) {
+    sort_small(surv, nsurv);
+    ncand = nsurv < a.cpre ? nsurv : a.cpre;
+  } else {
+    // Rare: select the cpre-th key over all entries, then gather exactly those <= it.
+    const uint64_t kth = global_kth(a, qtile, row_in_tile, thr, a.cpre);
+    int w = 0;
+    for (int p = 0; p < a.units_per_qtile; ++p) {
+      const size_t slot = (static_cast<size_t>(qtile) * a.units_per_qtile + p) * kScanBM + row_in_tile;
+      const int n = a.cand_count[slot];
+      const uint2* b = a.cand + slot * kScanCap;
+      for (int e0 = 0; e0 < n; e0 += 32) {
+        const int e = e0 + lane;
+        uint64_t pk = kNoNeighbor;
+        bool pass = false;
+        if (e < n) {
+          const uint2 v = b[e];
+          const uint32_t key = float_key(__uint_as_float(v.x));
+          pk = (static_cast<uint64_t>(key) << 32) | v.y;
+          pass = key < thr && pk <= kth;
+        }
+        const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
+        const int pos = w + __popc(m & lt);
+        if (pass && pos < a.cpre) surv[pos] = pk;
+        w += __popc(m);
+      }
+    }
+    __syncwarp();
+    ncand = w < a.cpre ? w : a.cpre;
+    sort_small(surv, ncand);
+  }
+
+  // 2. Exact distances of the candidates (stored back as packed (dist, row)).
+  const bool l2 = a.metric == 0;
+  if (a.codes == nullptr) {
+    for (int i = 0; i < ncand; ++i) {
+      const uint32_t row = neighbor_id(surv[i]);
+      const float d = warp_exact_dist(q_s, a.rows + static_cast<size_t>(row) * pd, pd, l2, a.order);
+      __syncwarp();
+      if (lane == 0) surv[i] = pack_neighbor(d, row);
+    }
+    __syncwarp();
+    sort_small(surv, ncand);
+  } else {
+    for (int i = 0; i < ncand; i += 2) {
+      const int my = i + (lane >> 4);
+      const uint32_t row = my < ncand ? neighbor_id(surv[my]) : neighbor_id(surv[i]);
+      const float d = halfwarp_sq8_dist(q_s, a.codes + static_cast<size_t>(row) * pd, vmin_s,
+                                        scale_s, pd, l2, a.order);
+      __syncwarp();
+      if ((lane & 15) == 0 && my < ncand) surv[my] = pack_neighbor(d, row);
+    }
+    __syncwarp();
+    sort_small(surv, ncand);
+    if (a.depth > 0) {
+      const int nr = ncand < a.depth ? ncand : a.depth;
+      for (int i = 0; i < nr; ++i) {
+        const uint32_t row = neighbor_id(surv[i]);
+        const float d = warp_exact_dist(q_s, a.rows + static_cast<size_t>(row) * pd, pd, l2, a.order);
+        __syncwarp();
+        if (lane == 0) surv[i] = pack_neighbor(d, row);
+      }
+      __syncwarp();
+      ncand = nr;
+      sort_small(surv, ncand);
+    }
+  }
+
+  // 3. The k best, closest first; missing slots are (+inf, UINT32_MAX).
+  for (int i = lane; i < a.k; i += 32) {
+    const size_t o = static_cast<size_t>(q) * a.k + i;
+    if (i < ncand) {
+      a.out_dist[o] = neighbor_dist(surv[i]);
+      a.out_row[o] = neighbor_id(surv[i]);
+    } else {
+      a.out_dist[o] = INFINITY;
+      a.out_row[o] = UINT32_MAX;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ operand preparation
+
+__global__ void prep_queries_kernel(const PrepArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= a.nq_pad) return;
+  const int q = warp;
+  const bool valid = q < a.nq;
+  // Operand values a_i of this query.
+  float amax = 0.f;
+  for (int i = lane; i < a.pd; i += 32) {
+    float v = 0.f;
+    if (valid) {
+      const float x = a.queries[static_cast<size_t>(q) * a.pd + i];
+      if (a.kind == kPrepFlat) v = x;
+      else if (a.kind == kPrepSq8Ip) v = x * a.scale[i];
+      else v = (x - a.vmin[i]) * a.scale[i];
+    }
+    amax = fmaxf(amax, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  // Power-of-two scale bringing max|a| into [2^14, 2^15) for fp16 (exact rescaling).
+  int s = 0;
+  if (a.ab_format == 0 && amax > 0.f) {
+    s = 14 - ilogbf(amax);
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+  }
+  const float up = ldexpf(1.f, s);
+  for (int i = lane; i < a.kpad; i += 32) {
+    float v = 0.f;
+    if (valid && i < a.pd) {
+      const float x = a.queries[static_cast<size_t>(q) * a.pd + i];
+      if (a.kind == kPrepFlat) v = x;
+      else if (a.kind == kPrepSq8Ip) v = x * a.scale[i];
+      else v = (x - a.vmin[i]) * a.scale[i];
+      v *= up;
+    }
+    const size_t o = static_cast<size_t>(q) * a.kpad + i;
+    if (a.ab_format == 0) reinterpret_cast<__half*>(a.operand)[o] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(a.operand)[o] = __float2bfloat16_rn(v);
+  }
+  if (lane == 0 && valid) {
+    // key = qscale * acc (+ row term): acc = 2^s * <a, b>.
+    const float down = ldexpf(1.f, -s - a.row_scale_log2);
+    a.qscale[q] = (a.key_factor == 2 ? -2.f : -1.f) * down;
+  }
+}
+
+__global__ void prep_rows_kernel(const float* __restrict__ rows, uint64_t n, int pd, int kpad,
+                                 int ab_format, int scale_log2, void* operand, float* norms) {
+  const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n) return;
+  const float up = ldexpf(1.f, scale_log2);
+  float ss = 0.f;
+  for (int i = lane; i < kpad; i += 32) {
+    const float x = i < pd ? rows[warp * pd + i] : 0.f;
+    ss = fmaf(x, x, ss);
+    const size_t o = warp * kpad + i;
+    if (ab_format == 0) reinterpret_cast<__half*>(operand)[o] = __float2half_rn(x * up);
+    else reinterpret_cast<__nv_bfloat16*>(operand)[o] = __float2bfloat16_rn(x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  if (norms != nullptr && lane == 0) norms[warp] = ss;
+}
+
+__global__ void absmax_kernel(const float* __restrict__ x, uint64_t count, uint32_t* out) {
+  float m = 0.f;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(x[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// Per-dimension min/max over all rows (Sq8Quantizer::train, sq8.cc:9-26), in ordered-key space.
+__global__ void sq8_minmax_kernel(const float* __restrict__ rows, uint64_t n, int dim, int pd,
+                                  uint32_t* kmin, uint32_t* kmax) {
+  const int d = threadIdx.x;
+  if (d >= dim) return;
+  uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+  for (uint64_t r = blockIdx.x; r < n; r += gridDim.x) {
+    const uint32_t k = float_key(rows[r * pd + d]);
+    lo = k < lo ? k : lo;
+    hi = k > hi ? k : hi;
+  }
+  atomicMin(&kmin[d], lo);
+  atomicMax(&kmax[d], hi);
+}
+
+// Sq8Quantizer::encode (sq8.cc:28-37): nearbyint((x - vmin) / scale) with IEEE division,
+// clamped to [0, 255]; padding dimensions and scale <= 0 encode 0. Also writes the fp16 operand
+// copy of the code and, for L2, the row term sum_i (scale_i * code_i)^2.
+__global__ void sq8_encode_kernel(const float* __restrict__ rows, uint64_t n, int dim, int pd,
+                                  int kpad, const float* __restrict__ vmin,
+                                  const float* __restrict__ scale, uint8_t* codes,
+                                  __half* operand, float* rowterm) {
+  const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n) return;
+  float ss = 0.f;
+  for (int i = lane; i < kpad; i += 32) {
+    uint8_t c = 0;
+    if (i < pd && i < dim && scale[i] > 0.f) {
+      float v = rintf(__fdiv_rn(__fsub_rn(rows[warp * pd + i], vmin[i]), scale[i]));
+      v = v < 0.f ? 0.f : (255.f < v ? 255.f : v);
+      c = static_cast<uint8_t>(v);
+    }
+    if (i < pd) codes[warp * pd + i] = c;
+    const float cf = static_cast<float>(c);
+    operand[warp * kpad + i] = __float2half_rn(cf);
+    if (i < pd) {
+      const float t = scale[i] * cf;
+      ss = fmaf(t, t, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  if (rowterm != nullptr && lane == 0) rowterm[warp] = ss;
+}
+
+// fp16 operand and row term from existing codes (codes loaded from an index file).
+__global__ void sq8_operand_kernel(const uint8_t* __restrict__ codes, uint64_t n, int pd, int kpad,
+                                   const float* __restrict__ scale, __half* operand,
+                                   float* rowterm) {
+  const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n) return;
+  float ss = 0.f;
+  for (int i = lane; i < kpad; i += 32) {
+    const float cf = i < pd ? static_cast<float>(codes[warp * pd + i]) : 0.f;
+    operand[warp * kpad + i] = __float2half_rn(cf);
+    if (i < pd) {
+      const float t = scale[i] * cf;
+      ss = fmaf(t, t, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  if (rowterm != nullptr && lane == 0) rowterm[warp] = ss;
+}
+
+}  // namespace
+
+size_t FinalizeSmemBytes(int pd) {
+  return 2 * pd * sizeof(float) + kFinWarps * (pd * sizeof(float) + kMaxSurvivors * sizeof(uint64_t));
+}
+
+cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream) {
+  const size_t smem = FinalizeSmemBytes(a.pd);
+  cudaError_t e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int blocks = (a.nq + kFinWarps - 1) / kFinWarps;
+  finalize_kernel<<<blocks, kFinWarps * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchPrepQueries(const PrepArgs& a, cudaStream_t stream) {
+  const int threads = 256;
+  const int blocks = (a.nq_pad * 32 + threads - 1) / threads;
+  prep_queries_kernel<<<blocks, threads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchPrepRows(const float* rows, uint64_t n, int pd, int kpad, int ab_format,
+                           int scale_log2, void* operand, float* norms, cudaStream_t stream) {
+  const int threads = 256;
+  const uint64_t blocks = (n * 32 + threads - 1) / threads;
+  prep_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      rows, n, pd, kpad, ab_format, scale_log2, operand, norms);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchAbsMax(const float* x, uint64_t count, uint32_t* out, cudaStream_t stream) {
+  absmax_kernel<<<1184, 256, 0, stream>>>(x, count, out);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchSq8MinMax(const float* rows, uint64_t n, int dim, int pd, uint32_t* kmin,
+                            uint32_t* kmax, cudaStream_t stream) {
+  if (dim > 1024) return cudaErrorInvalidValue;
+  uint64_t blocks = n < 4096 ? (n == 0 ? 1 : n) : 4096;
+  sq8_minmax_kernel<<<static_cast<unsigned>(blocks), dim, 0, stream>>>(rows, n, dim, pd, kmin, kmax);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchSq8Encode(const float* rows, uint64_t n, int dim, int pd, int kpad,
+                            const float* vmin, const float* scale, uint8_t* codes, __half* operand,
+                            float* rowterm, cudaStream_t stream) {
+  const int threads = 256;
+  const uint64_t blocks = (n * 32 + threads - 1) / threads;
+  sq8_encode_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      rows, n, dim, pd, kpad, vmin, scale, codes, operand, rowterm);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchSq8Operand(const uint8_t* codes, uint64_t n, int pd, int kpad, const float* scale,
+                             __half* operand, float* rowterm, cudaStream_t stream) {
+  const int threads = 256;
+  const uint64_t blocks = (n * 32 + threads - 1) / threads;
+  sq8_operand_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(codes, n, pd, kpad,
+                                                                            scale, operand, rowterm);
+  return cudaGetLastError();
+}
+
+}  // namespace vdbgpu

@@ -1,0 +1,197 @@
+// Warp-level building blocks shared by the selection kernels: a register bitonic sort of packed
+// (distance, id) keys and exact fp32 distances that sum in the same order as the reference's
+// runtime-selected CPU kernels.
+#pragma once
+
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace vdbgpu {
+
+// Sorts 32*E packed keys held striped across the warp (element i = e*32 + lane) ascending.
+template <int E>
+__device__ __forceinline__ void warp_sort(uint64_t (&x)[E]) {
+  constexpr int N = 32 * E;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int je = j >> 5;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int p = e ^ je;
+          if (p > e) {
+            const bool up = (((e * 32) & k) == 0);
+            const uint64_t a = x[e], b = x[p];
+            const bool swap = up ? (a > b) : (a < b);
+            x[e] = swap ? b : a;
+            x[p] = swap ? a : b;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int i = e * 32 + lane;
+          const uint64_t other = __shfl_xor_sync(0xFFFFFFFFu, x[e], j);
+          const bool up = ((i & k) == 0);
+          const bool lower = (lane & j) == 0;
+          const bool take_min = (up == lower);
+          const uint64_t mn = x[e] < other ? x[e] : other;
+          const uint64_t mx = x[e] < other ? other : x[e];
+          x[e] = take_min ? mn : mx;
+        }
+      }
+    }
+  }
+}
+
+// Kernel-set summation orders of the reference (src/distance/cpu_features.cc:36-60).
+enum SumOrder : int { kOrderScalar = 0, kOrderAvx512 = 1, kOrderAvx2 = 2 };
+
+// Exact fp32 distance between the warp's query and one row, summed in the order of the
+// reference kernel set (all lanes receive the result). q_s and x point to pd floats; q_s may be
+// shared memory. l2 selects squared L2, otherwise minus the dot product.
+//   avx512: 16 lanes x 2 accumulators over blocks of 32, FMA, tail block of 16 into the first
+//           accumulator, then _mm512_reduce_add_ps's tree (src/distance/avx512.cc:19-46)
+//   avx2:   8 lanes x 2 accumulators over blocks of 16, FMA, then hadd (avx2.cc:11-46)
+//   scalar: one running sum, no FMA (scalar.cc:8-23)
+__device__ __forceinline__ float warp_exact_dist(const float* q_s, const float* __restrict__ x,
+                                                 int pd, bool l2, int order) {
+  const int lane = threadIdx.x & 31;
+  float r;
+  if (order == kOrderAvx512) {
+    float acc = 0.f;
+    const int nb = pd >> 5;
+    for (int t = 0; t < nb; ++t) {
+      const int e = 32 * t + lane;
+      const float qv = q_s[e], xv = __ldg(&x[e]);
+      if (l2) {
+        const float d = __fsub_rn(qv, xv);
+        acc = __fmaf_rn(d, d, acc);
+      } else {
+        acc = __fmaf_rn(qv, xv, acc);
+      }
+    }
+    if ((pd & 31) != 0 && lane < 16) {
+      const int e = 32 * nb + lane;
+      const float qv = q_s[e], xv = __ldg(&x[e]);
+      if (l2) {
+        const float d = __fsub_rn(qv, xv);
+        acc = __fmaf_rn(d, d, acc);
+      } else {
+        acc = __fmaf_rn(qv, xv, acc);
+      }
+    }
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 16));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
+    r = acc;
+  } else if (order == kOrderAvx2) {
+    // lane = 8*h + j (h: 0 = acc0, 1 = acc1 within a 16-block); lanes 16..31 idle.
+    float acc = 0.f;
+    if (lane < 16) {
+      for (int i = 0; i < pd; i += 16) {
+        const int e = i + lane;
+        const float qv = q_s[e], xv = __ldg(&x[e]);
+        if (l2) {
+          const float d = __fsub_rn(qv, xv);
+          acc = __fmaf_rn(d, d, acc);
+        } else {
+          acc = __fmaf_rn(qv, xv, acc);
+        }
+      }
+    }
+    // v[j] = acc0[j] + acc1[j]; s[j] = v[j] + v[4+j]; (s0+s1)+(s2+s3)
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
+    r = acc;
+  } else {
+    float s = 0.f;
+    if (lane == 0) {
+      for (int e = 0; e < pd; ++e) {
+        const float qv = q_s[e], xv = __ldg(&x[e]);
+        if (l2) {
+          const float d = __fsub_rn(qv, xv);
+          s = __fadd_rn(s, __fmul_rn(d, d));
+        } else {
+          s = __fadd_rn(s, __fmul_rn(qv, xv));
+        }
+      }
+    }
+    r = s;
+  }
+  r = __shfl_sync(0xFFFFFFFFu, r, 0);
+  return l2 ? r : -r;
+}
+
+// Exact SQ8 distance of the query against two codes at once (lanes 0..15: code0, lanes 16..31:
+// code1), in the reference kernel set's order. Returns the distance of the half this lane
+// belongs to. x = fma(code, scale, vmin) as in Decode16 (src/distance/avx512.cc:11-15).
+__device__ __forceinline__ float halfwarp_sq8_dist(const float* q_s, const uint8_t* __restrict__ code,
+                                                   const float* vmin_s, const float* scale_s,
+                                                   int pd, bool l2, int order) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane & 15;
+  float r;
+  if (order == kOrderAvx512) {
+    float acc = 0.f;
+    for (int i = 0; i < pd; i += 16) {
+      const int e = i + j;
+      const float xv = __fmaf_rn(static_cast<float>(code[e]), scale_s[e], vmin_s[e]);
+      if (l2) {
+        const float d = __fsub_rn(q_s[e], xv);
+        acc = __fmaf_rn(d, d, acc);
+      } else {
+        acc = __fmaf_rn(q_s[e], xv, acc);
+      }
+    }
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
+    r = acc;
+  } else if (order == kOrderAvx2) {
+    // lane j: j < 8 -> acc0 lane j over elements i + j; j >= 8 -> acc1 lane j-8 over i + j.
+    float acc = 0.f;
+    for (int i = 0; i < pd; i += 16) {
+      const int e = i + j;
+      const float xv = __fmaf_rn(static_cast<float>(code[e]), scale_s[e], vmin_s[e]);
+      if (l2) {
+        const float d = __fsub_rn(q_s[e], xv);
+        acc = __fmaf_rn(d, d, acc);
+      } else {
+        acc = __fmaf_rn(q_s[e], xv, acc);
+      }
+    }
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
+    r = acc;
+  } else {
+    float s = 0.f;
+    if (j == 0) {
+      for (int e = 0; e < pd; ++e) {
+        const float xv = __fadd_rn(vmin_s[e], __fmul_rn(static_cast<float>(code[e]), scale_s[e]));
+        if (l2) {
+          const float d = __fsub_rn(q_s[e], xv);
+          s = __fadd_rn(s, __fmul_rn(d, d));
+        } else {
+          s = __fadd_rn(s, __fmul_rn(q_s[e], xv));
+        }
+      }
+    }
+    r = s;
+  }
+  r = __shfl_sync(0xFFFFFFFFu, r, lane & 16);
+  return l2 ? r : -r;
+}
+
+}  // namespace vdbgpu

@@ -1,0 +1,294 @@
+"""vdb_b200: batched nearest-neighbour search on B200 GPUs, behind vdb's Index interface.
+
+A thin Python host over the C ABI of include/vdbgpu.h (lib/libvdbgpu.so, built in place by the
+package Makefile). It mirrors the reference's Python surface: `Index.search(queries, k, ef,
+nprobe, rerank, filter)` returns `(ids, dists)` arrays of shape (nq, k), closest first, with
+missing slots as (UINT32_MAX, +inf) like `_vdb._Collection.search` (python/bindings.cc:107-142).
+Errors map as the reference binding does (bindings.cc:27-34): invalid argument -> ValueError,
+not found -> KeyError, anything else -> RuntimeError.
+
+There is no CPU fallback: importing works without a GPU, but opening a Context raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Tuple
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_DIR = os.path.join(os.path.dirname(_HERE), "lib")
+LIB_PATH = os.path.join(LIB_DIR, "libvdbgpu.so")
+
+OK, INVALID_ARGUMENT, NOT_FOUND = 0, 1, 2
+RESOURCE_EXHAUSTED, UNAVAILABLE, NOT_SUPPORTED = 7, 8, 9
+STATUS_NAMES = {
+    0: "OK", 1: "InvalidArgument", 2: "NotFound", 3: "AlreadyExists", 4: "IOError",
+    5: "Corruption", 6: "FailedPrecondition", 7: "ResourceExhausted", 8: "Unavailable",
+    9: "NotSupported", 10: "Internal",
+}
+
+METRICS = {"l2": 0, "ip": 1, "inner_product": 1, "cosine": 2}
+INDEX_TYPES = {"flat": 0, "hnsw": 1, "hnsw_sq8": 2, "pq_flat": 3, "ivf_pq": 4, "sq8_flat": 16}
+STRATEGIES = {"auto": 0, "prefilter": 1, "graph": 2, "postfilter": 3}
+
+
+class VdbError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class SearchParams(ctypes.Structure):
+    """vdb::SearchParams (include/vdb/options.h:59-67)."""
+    _fields_ = [("ef", ctypes.c_uint64), ("nprobe", ctypes.c_uint64), ("rerank", ctypes.c_int32),
+                ("strategy", ctypes.c_int32), ("prefilter_threshold", ctypes.c_uint64),
+                ("post_filter_alpha", ctypes.c_uint64)]
+
+
+class IndexInfo(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int32), ("metric", ctypes.c_int32), ("rows", ctypes.c_uint64),
+                ("dim", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32),
+                ("device_bytes", ctypes.c_uint64)]
+
+
+# Every symbol declared in include/vdbgpu.h, with its ctypes signature.
+_P = ctypes.c_void_p
+_SIGNATURES = {
+    "vdbgpu_abi_version": (ctypes.c_int, []),
+    "vdbgpu_device_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "vdbgpu_open": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(_P)]),
+    "vdbgpu_close": (None, [_P]),
+    "vdbgpu_last_error": (ctypes.c_size_t, [_P, ctypes.c_char_p, ctypes.c_size_t]),
+    "vdbgpu_synchronize": (ctypes.c_int, [_P]),
+    "vdbgpu_set_stream": (ctypes.c_int, [_P, _P]),
+    "vdbgpu_set_timing": (ctypes.c_int, [_P, ctypes.c_int]),
+    "vdbgpu_stage_times": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
+    "vdbgpu_search_params_default": (None, [ctypes.POINTER(SearchParams)]),
+    "vdbgpu_index_load": (ctypes.c_int, [_P, _P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64,
+                                         ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_P)]),
+    "vdbgpu_index_create": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_uint64,
+                                           ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_P)]),
+    "vdbgpu_index_free": (None, [_P]),
+    "vdbgpu_index_get_info": (ctypes.c_int, [_P, ctypes.POINTER(IndexInfo)]),
+    "vdbgpu_index_search": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32,
+                                           ctypes.POINTER(SearchParams), _P, _P, _P, _P]),
+    "vdbgpu_index_file_inspect": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int)]),
+    "vdbgpu_index_sq8_export": (ctypes.c_int, [_P, _P, _P, _P]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C library; raises if it was not built (no silent fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {os.path.dirname(_HERE)}`")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def _raise(code: int, msg: str):
+    if code == INVALID_ARGUMENT:
+        raise ValueError(f"InvalidArgument: {msg}")
+    if code == NOT_FOUND:
+        raise KeyError(f"NotFound: {msg}")
+    raise VdbError(code, msg)
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    lib().vdbgpu_device_count(ctypes.byref(n))
+    return n.value
+
+
+def padded_dim(dim: int) -> int:
+    """vdb::PaddedDim (include/vdb/types.h:30-32): rows are zero-padded to 16 floats."""
+    return (dim + 15) // 16 * 16
+
+
+def _ptr(a) -> int:
+    """Address of a numpy array or a torch tensor (device or host)."""
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    raise TypeError(f"unsupported buffer type {type(a)}")
+
+
+class Context:
+    """One GPU, one stream (vdbgpu_open)."""
+
+    def __init__(self, device: int = 0):
+        h = _P()
+        code = lib().vdbgpu_open(int(device), ctypes.byref(h))
+        if code != OK:
+            _raise(code, f"cannot open device {device}")
+        self._h = h
+        self.device = device
+
+    def last_error(self) -> str:
+        buf = ctypes.create_string_buffer(4096)
+        lib().vdbgpu_last_error(self._h, buf, len(buf))
+        return buf.value.decode(errors="replace")
+
+    def check(self, code: int):
+        if code != OK:
+            _raise(code, self.last_error())
+
+    def synchronize(self):
+        self.check(lib().vdbgpu_synchronize(self._h))
+
+    def set_stream(self, stream_handle: int = 0):
+        """Launch on a caller's CUDA stream (e.g. torch.cuda.current_stream().cuda_stream)."""
+        self.check(lib().vdbgpu_set_stream(self._h, stream_handle or None))
+
+    def set_timing(self, on: bool = True):
+        self.check(lib().vdbgpu_set_timing(self._h, 1 if on else 0))
+
+    def stage_times(self):
+        """Device ms of the last search: [prep, scan/walk, select+re-rank]."""
+        buf = (ctypes.c_float * 8)()
+        n = lib().vdbgpu_stage_times(self._h, buf, 8)
+        return [buf[i] for i in range(n)]
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().vdbgpu_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _rows_f32(rows) -> Tuple[object, int, int]:
+    if isinstance(rows, np.ndarray):
+        if rows.dtype != np.float32 or not rows.flags.c_contiguous or rows.ndim != 2:
+            raise ValueError("rows must be a C-contiguous float32 matrix (n x padded_dim)")
+        return rows, rows.shape[0], rows.shape[1]
+    return rows, rows.shape[0], rows.shape[1]
+
+
+class Index:
+    """A GPU index: the counterpart of vdb::Index (src/index/index.h:36-55)."""
+
+    def __init__(self, ctx: Context, handle: _P, keep=None):
+        self.ctx = ctx
+        self._h = handle
+        self._keep = keep
+        info = IndexInfo()
+        ctx.check(lib().vdbgpu_index_get_info(self._h, ctypes.byref(info)))
+        self.type, self.metric = info.type, info.metric
+        self.rows, self.dim, self.padded_dim = info.rows, info.dim, info.padded_dim
+        self.device_bytes = info.device_bytes
+
+    @classmethod
+    def load(cls, ctx: Context, file_bytes: bytes, metric, rows, dim: int) -> "Index":
+        """LoadIndex (src/index/index.h:61-62) over the segment's rows (n x padded_dim)."""
+        m = METRICS[metric] if isinstance(metric, str) else int(metric)
+        rows, n, pd = _rows_f32(rows)
+        buf = np.frombuffer(file_bytes, dtype=np.uint8)
+        h = _P()
+        code = lib().vdbgpu_index_load(ctx._h, buf.ctypes.data, buf.size, m, _ptr(rows), n, dim, pd,
+                                       ctypes.byref(h))
+        ctx.check(code)
+        return cls(ctx, h)
+
+    @classmethod
+    def create(cls, ctx: Context, type, metric, rows, dim: int) -> "Index":
+        """CreateIndex + build for GPU-built types ("flat", "sq8_flat")."""
+        t = INDEX_TYPES[type] if isinstance(type, str) else int(type)
+        m = METRICS[metric] if isinstance(metric, str) else int(metric)
+        rows, n, pd = _rows_f32(rows)
+        h = _P()
+        ctx.check(lib().vdbgpu_index_create(ctx._h, t, m, _ptr(rows), n, dim, pd, ctypes.byref(h)))
+        return cls(ctx, h)
+
+    def search(self, queries, k: int = 10, ef: int = 64, nprobe: int = 16, rerank: int = -1,
+               filter=None, strategy: str = "auto", out=None, stats: bool = False):
+        """Batched Index::search. `queries` is (nq, padded_dim) float32 (numpy, or a CUDA tensor),
+        `filter` an optional allowed-row bitset (uint64 words, bit r of word r//64). Returns
+        (ids uint32[nq,k], dists float32[nq,k]) [, distance_computations uint64[nq]]."""
+        if isinstance(queries, np.ndarray):
+            q = np.ascontiguousarray(queries, dtype=np.float32)
+            if q.ndim == 1:
+                q = q[None, :]
+            if q.shape[1] != self.padded_dim:
+                raise ValueError("query dimension does not match the index")
+            nq = q.shape[0]
+        else:
+            q = queries
+            nq = int(q.shape[0])
+        p = SearchParams()
+        lib().vdbgpu_search_params_default(ctypes.byref(p))
+        p.ef, p.nprobe, p.rerank, p.strategy = int(ef), int(nprobe), int(rerank), STRATEGIES[strategy]
+        if out is None:
+            ids = np.empty((nq, k), dtype=np.uint32)
+            dists = np.empty((nq, k), dtype=np.float32)
+        else:
+            ids, dists = out
+        dc = np.empty(nq, dtype=np.uint64) if stats else None
+        fb = None
+        if filter is not None:
+            fb = np.ascontiguousarray(filter, dtype=np.uint64)
+            if fb.size < (self.rows + 63) // 64:
+                raise ValueError("filter bitset is shorter than the index")
+        code = lib().vdbgpu_index_search(self._h, _ptr(q), nq, int(k), ctypes.byref(p), _ptr(fb),
+                                         _ptr(dists), _ptr(ids), _ptr(dc))
+        self.ctx.check(code)
+        return (ids, dists, dc) if stats else (ids, dists)
+
+    def sq8_export(self, with_codes: bool = True):
+        """(vmin, scale, codes) of an SQ8 index (Sq8Quantizer, src/index/quant/sq8.h)."""
+        vmin = np.empty(self.padded_dim, dtype=np.float32)
+        scale = np.empty(self.padded_dim, dtype=np.float32)
+        codes = np.empty((self.rows, self.padded_dim), dtype=np.uint8) if with_codes else None
+        self.ctx.check(lib().vdbgpu_index_sq8_export(self._h, _ptr(vmin), _ptr(scale), _ptr(codes)))
+        return vmin, scale, codes
+
+    def free(self):
+        if getattr(self, "_h", None):
+            lib().vdbgpu_index_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def inspect_index_file(file_bytes: bytes) -> int:
+    """CheckIndexFile + magic dispatch without a GPU: the index type, or raises."""
+    buf = np.frombuffer(file_bytes, dtype=np.uint8)
+    t = ctypes.c_int(-1)
+    code = lib().vdbgpu_index_file_inspect(buf.ctypes.data, buf.size, ctypes.byref(t))
+    if code != OK:
+        _raise(code, "bad index file")
+    return t.value
+
+
+def unpack_bitset(words: np.ndarray, n: int) -> np.ndarray:
+    return np.unpackbits(words.view(np.uint8), bitorder="little")[:n].astype(bool)
+
+
+def pack_bitset(allowed: np.ndarray) -> np.ndarray:
+    """Dense allowed-row bitset (bit r of word r//64) from a boolean mask."""
+    n = allowed.size
+    b = np.packbits(allowed.astype(np.uint8), bitorder="little")
+    out = np.zeros((n + 63) // 64 * 8, dtype=np.uint8)
+    out[: b.size] = b
+    return out.view(np.uint64)

@@ -1,0 +1,86 @@
+"""Seeded synthetic workloads with the shapes and distributions of the benchmark configs
+(lib/libvdbsynth.so). Harness code: used by tests and bench.py, not by the search path."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import LIB_DIR, padded_dim
+
+_lib = None
+
+
+def _l():
+    global _lib
+    if _lib is None:
+        path = os.path.join(LIB_DIR, "libvdbsynth.so")
+        if not os.path.exists(path):
+            raise ImportError(f"{path} is missing: build it with make")
+        l = ctypes.CDLL(path)
+        l.synth_mixture.restype = None
+        l.synth_mixture.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                    ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                    ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
+                                    ctypes.c_int]
+        l.synth_metadata.restype = None
+        l.synth_metadata.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32,
+                                     ctypes.c_uint32, ctypes.c_double, ctypes.c_uint64, ctypes.c_void_p,
+                                     ctypes.c_void_p, ctypes.c_int]
+        l.synth_zipf.restype = None
+        l.synth_zipf.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_double, ctypes.c_uint64,
+                                 ctypes.c_void_p]
+        _lib = l
+    return _lib
+
+
+def mixture(n, dim, ncentres, centres="uniform", lo=0.0, hi=100.0, sigma=10.0, integer=False,
+            normalize=False, seed=0, stream=0, threads=0) -> np.ndarray:
+    """n rows of padded_dim(dim) float32 from a Gaussian mixture (zero padding)."""
+    pd = padded_dim(dim)
+    out = np.empty((n, pd), dtype=np.float32)
+    flags = (1 if integer else 0) | (2 if normalize else 0)
+    _l().synth_mixture(n, dim, pd, ncentres, 0 if centres == "uniform" else 1, lo, hi, sigma, flags,
+                       seed, stream, out.ctypes.data, threads)
+    return out
+
+
+# The benchmark configs (seeded; base rows use stream 0, queries stream 1).
+def flat_int(n, nq, dim=128, seed=0):
+    """Config 0 / 3: centres U[0,100]^d, sigma 10, clipped to [0,255], rounded."""
+    kw = dict(centres="uniform", lo=0.0, hi=100.0, sigma=10.0, integer=True, seed=seed)
+    return mixture(n, dim, 100, stream=0, **kw), mixture(nq, dim, 100, stream=1, **kw)
+
+
+def sq8_cosine(n, nq, dim=128, seed=1):
+    """Config 1: centres N(0,1)^d, sigma 0.3, then L2-normalised."""
+    kw = dict(centres="normal", sigma=0.3, normalize=True, seed=seed)
+    return mixture(n, dim, 1000, stream=0, **kw), mixture(nq, dim, 1000, stream=1, **kw)
+
+
+def ivfpq_l2(n, nq, dim=96, seed=2):
+    """Config 2: centres U[-1,1]^d, sigma 0.15."""
+    kw = dict(centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=seed)
+    return mixture(n, dim, 1000, stream=0, **kw), mixture(nq, dim, 1000, stream=1, **kw)
+
+
+def sharded_cosine(n, nq, dim=128, seed=4, stream_base=0):
+    """Config 4: centres U[0,100]^d, sigma 10 (not rounded), then L2-normalised."""
+    kw = dict(centres="uniform", lo=0.0, hi=100.0, sigma=10.0, normalize=True, seed=seed)
+    return (mixture(n, dim, 100, stream=stream_base, **kw),
+            mixture(nq, dim, 100, stream=stream_base + 1, **kw))
+
+
+def metadata(n, seed=4, year_lo=1990, year_hi=2024, max_tags=5, vocab=1000, zipf_s=1.1, threads=0):
+    years = np.empty(n, dtype=np.int64)
+    tags = np.empty((n, max_tags), dtype=np.uint32)
+    _l().synth_metadata(n, year_lo, year_hi, max_tags, vocab, zipf_s, seed, years.ctypes.data,
+                        tags.ctypes.data, threads)
+    return years, tags
+
+
+def zipf_tags(n, vocab=1000, zipf_s=1.1, seed=5):
+    out = np.empty(n, dtype=np.uint32)
+    _l().synth_zipf(n, vocab, zipf_s, seed, out.ctypes.data)
+    return out

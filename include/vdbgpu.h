@@ -1,0 +1,160 @@
+/* vdbgpu: B200-native batched nearest-neighbour search behind vdb's Index interface.
+ *
+ * A C ABI (plain pointers, sizes and integer status codes; no C++ types, no exceptions) over the
+ * GPU implementation of vdb's search path (KoduruChandrasekhar/HNSW-Vector-DB). Every entry point
+ * names the reference interface it replaces. Paths below are relative to the reference project.
+ *
+ * Pointer arguments that carry vectors or results may point to host memory or to device memory
+ * of the context's GPU; the library detects which and copies host buffers itself.
+ * Thread safety: a context serialises its calls; use one context per thread for concurrency.
+ */
+#ifndef VDBGPU_H_
+#define VDBGPU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VDBGPU_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VDBGPU_API __attribute__((visibility("default")))
+#else
+#define VDBGPU_API
+#endif
+
+/* Status codes: the values of vdb::Status::Code (include/vdb/status.h:14-26). */
+typedef enum vdbgpu_status {
+  VDBGPU_OK = 0,
+  VDBGPU_INVALID_ARGUMENT = 1,
+  VDBGPU_NOT_FOUND = 2,
+  VDBGPU_ALREADY_EXISTS = 3,
+  VDBGPU_IO_ERROR = 4,
+  VDBGPU_CORRUPTION = 5,
+  VDBGPU_FAILED_PRECONDITION = 6,
+  VDBGPU_RESOURCE_EXHAUSTED = 7, /* device allocation failed */
+  VDBGPU_UNAVAILABLE = 8,        /* no GPU, or a bounded device wait ran out */
+  VDBGPU_NOT_SUPPORTED = 9,
+  VDBGPU_INTERNAL = 10
+} vdbgpu_status;
+
+/* vdb::Metric (include/vdb/types.h:17): smaller distance is closer for every metric. */
+typedef enum vdbgpu_metric {
+  VDBGPU_METRIC_L2 = 0,     /* squared L2 */
+  VDBGPU_METRIC_IP = 1,     /* minus the dot product */
+  VDBGPU_METRIC_COSINE = 2  /* rows and queries normalised, minus the dot product */
+} vdbgpu_metric;
+
+/* vdb::IndexType (include/vdb/options.h:13), plus SQ8_FLAT: an exhaustive scan of SQ8 codes
+ * with an fp32 re-rank, which has no reference index type. */
+typedef enum vdbgpu_index_type {
+  VDBGPU_INDEX_FLAT = 0,
+  VDBGPU_INDEX_HNSW = 1,
+  VDBGPU_INDEX_HNSW_SQ8 = 2,
+  VDBGPU_INDEX_PQ_FLAT = 3,
+  VDBGPU_INDEX_IVF_PQ = 4,
+  VDBGPU_INDEX_SQ8_FLAT = 16
+} vdbgpu_index_type;
+
+/* vdb::SearchParams (include/vdb/options.h:59-67). */
+typedef struct vdbgpu_search_params {
+  uint64_t ef;       /* HNSW beam width; max(ef, k) is used (default 64) */
+  uint64_t nprobe;   /* IVF lists to scan (default 16) */
+  int32_t rerank;    /* candidates re-ranked on fp32 rows; -1 = auto, 0 = none */
+  int32_t strategy;  /* vdb::FilterStrategy: 0 auto, 1 prefilter, 2 graph, 3 postfilter */
+  uint64_t prefilter_threshold; /* default 10000 */
+  uint64_t post_filter_alpha;   /* default 10 */
+} vdbgpu_search_params;
+
+typedef struct vdbgpu_index_info {
+  int32_t type;
+  int32_t metric;
+  uint64_t rows;
+  uint32_t dim;
+  uint32_t padded_dim;
+  uint64_t device_bytes; /* HBM held by the index */
+} vdbgpu_index_info;
+
+typedef struct vdbgpu_ctx vdbgpu_ctx;
+typedef struct vdbgpu_index vdbgpu_index;
+
+/* Library version (VDBGPU_ABI_VERSION). */
+VDBGPU_API int vdbgpu_abi_version(void);
+
+/* Number of visible CUDA devices (0 without a GPU). */
+VDBGPU_API int vdbgpu_device_count(int* out);
+
+/* Opens a context on `device` (one stream, one workspace). No reference counterpart: the
+ * reference runs on host threads (src/util/thread_pool.h:15-44). */
+VDBGPU_API int vdbgpu_open(int device, vdbgpu_ctx** out);
+VDBGPU_API void vdbgpu_close(vdbgpu_ctx* ctx);
+
+/* Copies the context's last error message (NUL-terminated, truncated to cap) and returns its
+ * full length. Replaces vdb::Status::ToString (include/vdb/status.h). */
+VDBGPU_API size_t vdbgpu_last_error(const vdbgpu_ctx* ctx, char* buf, size_t cap);
+
+/* Launches the context's work on `stream` (a cudaStream_t of the context's device; NULL restores
+ * the context's own stream), like cublasSetStream. */
+VDBGPU_API int vdbgpu_set_stream(vdbgpu_ctx* ctx, void* stream);
+
+/* Enables (1) or disables (0) per-stage device timing of searches, read back with
+ * vdbgpu_stage_times. The counterpart of SearchExplain's micros (include/vdb/collection.h). */
+VDBGPU_API int vdbgpu_set_timing(vdbgpu_ctx* ctx, int enable);
+
+/* Device milliseconds of the last search's stages (CUDA events on the launching stream):
+ * out[0] = query preparation, out[1] = the dominant scan or walk kernel, out[2] = selection and
+ * re-rank. Returns the number of stages written (0 when timing is off). */
+VDBGPU_API int vdbgpu_stage_times(vdbgpu_ctx* ctx, float* out, int cap);
+
+/* Blocks until the context's stream is idle. */
+VDBGPU_API int vdbgpu_synchronize(vdbgpu_ctx* ctx);
+
+/* Sets vdb::SearchParams defaults (include/vdb/options.h:59-67). */
+VDBGPU_API void vdbgpu_search_params_default(vdbgpu_search_params* p);
+
+/* LoadIndex (src/index/index.h:61-62, src/index/index.cc:58-87): parses an index file written
+ * by the reference's Index::save (magic VDBFLAT1 / VDBHNSW1 / VDBHSQ81 / VDBPQFL1 / VDBIVFP1,
+ * CRC32C footer) over the segment's float rows (VectorView, src/util/aligned_buffer.h:56-63:
+ * nrows x padded_dim floats, zero padded) and copies everything the search needs to the GPU.
+ * The rows are read, not retained. */
+VDBGPU_API int vdbgpu_index_load(vdbgpu_ctx* ctx, const void* file_bytes, size_t nbytes, int metric,
+                      const float* rows, uint64_t nrows, uint32_t dim, uint32_t padded_dim,
+                      vdbgpu_index** out);
+
+/* CreateIndex + Index::build (src/index/index.h:58-59, index.cc:16-36) for index types built on
+ * the GPU: FLAT (nothing to train) and SQ8_FLAT (Sq8Quantizer::train/encode,
+ * src/index/quant/sq8.cc:9-37, bit-exact). */
+VDBGPU_API int vdbgpu_index_create(vdbgpu_ctx* ctx, int type, int metric, const float* rows, uint64_t nrows,
+                        uint32_t dim, uint32_t padded_dim, vdbgpu_index** out);
+
+VDBGPU_API void vdbgpu_index_free(vdbgpu_index* index);
+
+VDBGPU_API int vdbgpu_index_get_info(const vdbgpu_index* index, vdbgpu_index_info* out);
+
+/* Index::search for a batch (src/index/index.h:44-45): the k nearest allowed rows of each of
+ * nq queries (nq x padded_dim floats, already padded and, for cosine, normalised as
+ * CollectionImpl::PrepareQuery does, src/engine/collection_impl.cc:1023-1034), closest first,
+ * ties by row id. Missing slots are (+inf, UINT32_MAX). allow_bits (nullable) is a dense bitset
+ * of allowed rows (bit r of word r/64), the RowFilter of src/index/index.h:23-27.
+ * out_dist_comps (nullable, nq values) receives IndexSearchStats::distance_computations
+ * (src/index/index.h:29-32). params may be NULL (defaults). */
+VDBGPU_API int vdbgpu_index_search(vdbgpu_index* index, const float* queries, uint64_t nq, uint32_t k,
+                        const vdbgpu_search_params* params, const uint64_t* allow_bits,
+                        float* out_dist, uint32_t* out_row, uint64_t* out_dist_comps);
+
+/* CheckIndexFile (src/index/index.cc:46-56) + the magic dispatch of LoadIndex (index.cc:58-87)
+ * without a GPU: verifies the CRC32C footer and reports the index type of the magic. */
+VDBGPU_API int vdbgpu_index_file_inspect(const void* file_bytes, size_t nbytes, int* type);
+
+/* The SQ8 quantiser and codes of an SQ8 index (Sq8Quantizer::vmin/scale, src/index/quant/
+ * sq8.h:24-25): vmin, scale receive padded_dim floats; codes (nullable) nrows x padded_dim. */
+VDBGPU_API int vdbgpu_index_sq8_export(const vdbgpu_index* index, float* vmin, float* scale,
+                            uint8_t* codes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VDBGPU_H_ */

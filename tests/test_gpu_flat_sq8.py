@@ -1,0 +1,114 @@
+"""GPU parity for exact flat search and the exhaustive SQ8 scan (tensor-core pre-rank + exact
+fp32 re-rank) against the reference's outputs (golden fixtures) and the oracle."""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import assert_same_neighbors, golden, inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def test_flat_integer_rows_bit_exact(ctx):
+    import vdb_b200
+    g = golden("flat_int")
+    base, qs = inputs("flat_int", g)
+    idx = vdb_b200.Index.load(ctx, bytes(g["flat_file"]), "l2", base, 128)
+    ids, d, dc = idx.search(qs, k=10, stats=True)
+    # Integer rows: tensor-core keys are exact, so ids (tie order included) and distances match.
+    np.testing.assert_array_equal(ids, g["ids"])
+    np.testing.assert_array_equal(d, g["dists"])
+    assert np.all(dc == base.shape[0])  # FlatIndex::search counts every row (flat_index.cc:76)
+    odd = (np.arange(base.shape[0]) % 2) == 1
+    fi, fd = idx.search(qs, k=50, filter=vdb_b200.pack_bitset(odd))
+    np.testing.assert_array_equal(fi, g["filt_ids"])
+    np.testing.assert_array_equal(fd, g["filt_dists"])
+
+
+def test_flat_every_metric_odd_dim(ctx):
+    import vdb_b200
+    g = golden("flat_float")
+    base, qs = inputs("flat_float", g)
+    for m in (0, 1, 2):
+        idx = vdb_b200.Index.create(ctx, "flat", m, base, 100)
+        ids, d = idx.search(qs, k=20)
+        assert_same_neighbors(ids, d, g[f"ids_m{m}"], g[f"dists_m{m}"])
+        idx.free()
+
+
+def test_flat_edge_cases(ctx):
+    import vdb_b200
+    orc = oracle.Oracle()
+    from vdb_b200 import synth
+    # k larger than the rows, a batch that is not a multiple of 128, rows not a multiple of 256.
+    for n, nq, k in ((5, 3, 100), (300, 130, 7), (1, 1, 1), (513, 257, 32)):
+        base, qs = synth.flat_int(n, nq, dim=48, seed=n)
+        idx = vdb_b200.Index.create(ctx, "flat", "l2", base, 48)
+        ids, d = idx.search(qs, k=k)
+        oi, od = orc.flat_search(0, base, qs, k)
+        np.testing.assert_array_equal(ids, oi)
+        np.testing.assert_array_equal(d, od)
+        assert np.all(ids[:, n:] == np.uint32(0xFFFFFFFF)) and np.all(np.isinf(d[:, n:]))
+        idx.free()
+    # A filter that allows nothing returns only misses.
+    base, qs = synth.flat_int(1000, 10, dim=128, seed=3)
+    idx = vdb_b200.Index.create(ctx, "flat", "l2", base, 128)
+    ids, d = idx.search(qs, k=5, filter=vdb_b200.pack_bitset(np.zeros(1000, bool)))
+    assert np.all(ids == np.uint32(0xFFFFFFFF)) and np.all(np.isinf(d))
+    with pytest.raises(ValueError):
+        idx.search(qs[:, :64], k=5)
+
+
+def test_flat_full_size_config0(ctx):
+    """Config 0 at full size (100k x 128 integer rows, 1000 queries): ids and distances identical
+    to the oracle on a sample of queries, recall@10 = 1 against it."""
+    import vdb_b200
+    from vdb_b200 import synth
+    base, qs = synth.flat_int(100_000, 1000, dim=128, seed=0)
+    idx = vdb_b200.Index.create(ctx, "flat", "l2", base, 128)
+    ids, d = idx.search(qs, k=10)
+    orc = oracle.Oracle()
+    sample = np.arange(0, 1000, 50)
+    oi, od = orc.flat_search(0, base, qs[sample], 10)
+    np.testing.assert_array_equal(ids[sample], oi)
+    np.testing.assert_array_equal(d[sample], od)
+    # Sortedness for every query.
+    assert np.all(np.diff(d, axis=1) >= 0)
+
+
+def test_sq8_train_encode_bit_exact(ctx):
+    import vdb_b200
+    g = golden("sq8_scan")
+    base, qs = inputs("sq8_scan", g)
+    idx = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
+    vmin, scale, codes = idx.sq8_export()
+    np.testing.assert_array_equal(vmin, g["vmin"])
+    np.testing.assert_array_equal(scale, g["scale"])
+    np.testing.assert_array_equal(codes, g["codes"])
+
+
+def test_sq8_scan_matches_reference(ctx):
+    import vdb_b200
+    g = golden("sq8_scan")
+    base, qs = inputs("sq8_scan", g)
+    idx = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
+    ids, d = idx.search(qs, k=10, rerank=100)
+    # Final ids identical; distances are the reference's fp32 re-rank, bit for bit.
+    assert_same_neighbors(ids, d, g["ids"], g["dists"])
+    assert oracle.recall_at_k(ids, g["ids"], 10) == 1.0
+
+
+def test_sq8_scan_full_size_config1(ctx):
+    """Config 1 at full size (1M x 128, cosine): identical results to the oracle on a sample of
+    the 10k-query batch."""
+    import vdb_b200
+    from vdb_b200 import synth
+    base, qs = synth.sq8_cosine(1_000_000, 10_000, dim=128, seed=1)
+    idx = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
+    ids, d = idx.search(qs, k=10, rerank=100)
+    orc = oracle.Oracle()
+    vmin, scale, codes = idx.sq8_export()
+    sample = np.arange(0, 10_000, 500)
+    oi, od = orc.sq8_scan_search(2, base, codes, vmin, scale, qs[sample], k=10, depth=100)
+    assert_same_neighbors(ids[sample], d[sample], oi, od)
+    assert np.all(np.diff(d, axis=1) >= 0)
