@@ -42,10 +42,14 @@ struct __align__(8) ScanBarriers {
   uint32_t tmem_slot;
 };
 
+// Units are ordered slice-major: the CTAs running at the same time cover one or two row slices
+// for every query tile, so each slice is read from HBM about once and served from L2, and the
+// later slices of a query start from the threshold its earlier slices published.
 __device__ __forceinline__ void unit_rows(const ScanArgs& a, int unit, int* qtile, int* r0,
                                           int* r1) {
-  *qtile = unit / a.units_per_qtile;
-  const int part = unit - *qtile * a.units_per_qtile;
+  const int qtiles = a.nunits / a.units_per_qtile;
+  const int part = unit / qtiles;
+  *qtile = unit - part * qtiles;
   *r0 = part * a.rows_per_unit;
   int e = *r0 + a.rows_per_unit;
   *r1 = e < a.nrows ? e : a.nrows;
@@ -254,15 +258,97 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       unit_rows(a, unit, &qtile, &r0, &r1);
       const int q = qtile * kScanBM + row_in_tile;
       const bool valid_q = q < a.nq;
-      const float qs = valid_q ? a.qscale[q] : 0.f;
+      // key = qs * acc (+ row term); qs is minus a power of two, so key < tau <=> acc > tau / qs
+      // holds exactly and the scaled-key fast path compares raw accumulators.
+      const float qs = valid_q ? a.qscale[q] : -1.f;
+      const float qs_inv = 1.f / qs;
       float tau = valid_q ? INFINITY : -INFINITY;
+      float tau_acc = tau * qs_inv;
       int count = 0;
-      uint2* buf = a.cand + (static_cast<size_t>(unit) * kScanBM + row_in_tile) * kScanCap;
-      for (int row0 = r0; row0 < r1; row0 += kScanBN) {
-        if (valid_q) {
-          const uint32_t g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
-          if (g != 0xFFFFFFFFu) tau = fminf(tau, key_float(g));
+      const size_t slot = static_cast<size_t>(unit) * kScanBM + row_in_tile;
+      uint2* buf = a.cand + slot * kScanCap;
+
+      // Compacts every lane whose buffer holds more than `limit` entries to its `keep` best
+      // and publishes the keep-th key for the other units of the same query.
+      auto compact_lanes = [&](int limit) {
+        uint32_t need = __ballot_sync(0xFFFFFFFFu, count > limit);
+        while (need != 0u) {
+          const int src = __ffs(need) - 1;
+          need &= need - 1u;
+          const int n = __shfl_sync(0xFFFFFFFFu, count, src);
+          uint2* sbuf = a.cand + (static_cast<size_t>(unit) * kScanBM + quad * 32 + src) * kScanCap;
+          __syncwarp();
+          const uint32_t kth = compact_buffer(sbuf, n, a.keep);
+          if (lane == src) {
+            count = a.keep;
+            tau = fminf(tau, key_float(kth));
+            tau_acc = tau * qs_inv;
+            // Other units of this query may drop keys above the keep-th key of this one.
+            atomicMin(&a.qtau[q], kth + 1u);
+          }
         }
+      };
+
+      // One chunk of 32 accumulator columns starting at row c0.
+      auto process = [&](uint32_t (&v)[32], int c0) {
+        uint32_t allow_bits = 0xFFFFFFFFu;
+        if (a.allow != nullptr) allow_bits = __ldg(&a.allow[c0 >> 5]);
+        const int nvalid = r1 - c0;  // columns < nvalid are real rows of this unit
+        const bool full = nvalid >= 32 && allow_bits == 0xFFFFFFFFu;
+        bool hit;
+        if constexpr (kMode == kKeyRowTerm) {
+          float rt[32];
+          const float4* rt4 = reinterpret_cast<const float4*>(a.rowterm + c0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = __ldg(&rt4[j]);
+            rt[4 * j] = x.x;
+            rt[4 * j + 1] = x.y;
+            rt[4 * j + 2] = x.z;
+            rt[4 * j + 3] = x.w;
+          }
+          float kmin = INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float key = fmaf(qs, __uint_as_float(v[j]), rt[j]);
+            if (!full && (j >= nvalid || !((allow_bits >> j) & 1u))) key = INFINITY;
+            v[j] = __float_as_uint(key);
+            kmin = fminf(kmin, key);
+          }
+          hit = kmin < tau;
+        } else {
+          float amax = -INFINITY;
+          if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, __uint_as_float(v[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j >= nvalid || !((allow_bits >> j) & 1u)) v[j] = __float_as_uint(-INFINITY);
+              amax = fmaxf(amax, __uint_as_float(v[j]));
+            }
+          }
+          hit = amax > tau_acc;
+        }
+        if (__any_sync(0xFFFFFFFFu, hit)) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float key;
+            if constexpr (kMode == kKeyRowTerm) key = __uint_as_float(v[j]);
+            else key = qs * __uint_as_float(v[j]);
+            if (key < tau) {
+              buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c0 + j));
+              ++count;
+            }
+          }
+          compact_lanes(kScanCap - 32);
+        }
+      };
+
+      for (int row0 = r0; row0 < r1; row0 += kScanBN) {
+        // The shared threshold is read now and applied after the first chunk (hides latency).
+        uint32_t g = 0xFFFFFFFFu;
+        if (valid_q) g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
         if (!mbar_wait(&bars->acc_full[acc], acc_phase, a.status, kDevTimeoutAcc)) {
           ok = false;
           break;
@@ -270,75 +356,26 @@ __global__ void __launch_bounds__(kScanThreads, 1)
         tc_fence_after();
         const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                 static_cast<uint32_t>(acc * kScanBN);
+        uint32_t va[32], vb[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(t_addr, va);
+        tmem_ld_wait_regs(va);
 #pragma unroll 1
-        for (int ch = 0; ch < kScanBN / 32; ++ch) {
-          uint32_t v[32];
+        for (int ch = 0; ch < kScanBN / 32; ch += 2) {
           __syncwarp();
-          tmem_ld_32x32b_x32(t_addr + ch * 32, v);
-          tmem_ld_wait();
-          const int c0 = row0 + ch * 32;
-          uint32_t allow_bits = 0xFFFFFFFFu;
-          if (a.allow != nullptr) allow_bits = __ldg(&a.allow[c0 >> 5]);
-          const int nvalid = r1 - c0;  // columns < nvalid are real rows of this unit
-          float kmin = INFINITY;
-          float rt[32];
-          if constexpr (kMode == kKeyRowTerm) {
-            const float4* rt4 = reinterpret_cast<const float4*>(a.rowterm + c0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 x = __ldg(&rt4[j]);
-              rt[4 * j] = x.x;
-              rt[4 * j + 1] = x.y;
-              rt[4 * j + 2] = x.z;
-              rt[4 * j + 3] = x.w;
-            }
+          tmem_ld_32x32b_x32(t_addr + (ch + 1) * 32, vb);  // in flight while va is processed
+          process(va, row0 + ch * 32);
+          if (ch == 0 && g != 0xFFFFFFFFu) {
+            tau = fminf(tau, key_float(g));
+            tau_acc = tau * qs_inv;
           }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float key;
-            if constexpr (kMode == kKeyRowTerm) {
-              key = fmaf(qs, __uint_as_float(v[j]), rt[j]);
-            } else {
-              key = qs * __uint_as_float(v[j]);
-            }
-            v[j] = __float_as_uint(key);
+          tmem_ld_wait_regs(vb);
+          if (ch + 2 < kScanBN / 32) {
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_addr + (ch + 2) * 32, va);
           }
-          if (nvalid >= 32 && allow_bits == 0xFFFFFFFFu) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) kmin = fminf(kmin, __uint_as_float(v[j]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j >= nvalid || !((allow_bits >> j) & 1u)) v[j] = __float_as_uint(INFINITY);
-              kmin = fminf(kmin, __uint_as_float(v[j]));
-            }
-          }
-          if (__any_sync(0xFFFFFFFFu, kmin < tau)) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float key = __uint_as_float(v[j]);
-              if (key < tau) {
-                buf[count] = make_uint2(v[j], static_cast<uint32_t>(c0 + j));
-                ++count;
-              }
-            }
-            uint32_t need = __ballot_sync(0xFFFFFFFFu, count > kScanCap - 32);
-            while (need != 0u) {
-              const int src = __ffs(need) - 1;
-              need &= need - 1u;
-              const int n = __shfl_sync(0xFFFFFFFFu, count, src);
-              const int src_row = quad * 32 + src;
-              uint2* sbuf = a.cand + (static_cast<size_t>(unit) * kScanBM + src_row) * kScanCap;
-              __syncwarp();
-              const uint32_t kth = compact_buffer(sbuf, n, a.keep);
-              if (lane == src) {
-                count = a.keep;
-                tau = fminf(tau, key_float(kth));
-                // Other units of this query may drop keys above the keep-th key of this one.
-                atomicMin(&a.qtau[q], kth + 1u);
-              }
-            }
-          }
+          process(vb, row0 + (ch + 1) * 32);
+          tmem_ld_wait_regs(va);
         }
         tc_fence_before();
         mbar_arrive(&bars->acc_empty[acc]);
@@ -347,7 +384,9 @@ __global__ void __launch_bounds__(kScanThreads, 1)
           acc_phase ^= 1u;
         }
       }
-      a.cand_count[static_cast<size_t>(unit) * kScanBM + row_in_tile] = valid_q ? count : 0;
+      // Leave at most `keep` entries per query and publish this unit's keep-th key.
+      if (ok) compact_lanes(a.keep);
+      a.cand_count[slot] = valid_q ? count : 0;
     }
   }
 

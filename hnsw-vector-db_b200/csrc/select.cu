@@ -50,6 +50,14 @@ __device__ void sort_small(uint64_t* s, int n) {
   else sort_into_smem<32>(s, n);
 }
 
+// Candidate slot of (query tile, row slice, query row): units are numbered slice-major
+// (scan_mma.cu unit_rows), so unit = slice * qtiles + qtile.
+__device__ __forceinline__ size_t unit_slot(const FinalizeArgs& a, int qtile, int slice,
+                                            int row_in_tile) {
+  const size_t qtiles = (static_cast<size_t>(a.nq) + kScanBM - 1) / kScanBM;
+  return (static_cast<size_t>(slice) * qtiles + qtile) * kScanBM + row_in_tile;
+}
+
 // The c-th smallest packed key (1-based) among entries passing `thr`, by bitwise search over
 // every entry of the query's buffers. Used only when more than kMaxSurvivors entries pass.
 __device__ uint64_t global_kth(const FinalizeArgs& a, int qtile, int row_in_tile, uint32_t thr,
@@ -59,7 +67,7 @@ __device__ uint64_t global_kth(const FinalizeArgs& a, int qtile, int row_in_tile
     const uint64_t cand = ans | (1ull << bit);
     int cnt = 0;
     for (int p = 0; p < a.units_per_qtile; ++p) {
-      const size_t slot = (static_cast<size_t>(qtile) * a.units_per_qtile + p) * kScanBM + row_in_tile;
+      const size_t slot = unit_slot(a, qtile, p, row_in_tile);
       const int n = a.cand_count[slot];
       const uint2* b = a.cand + slot * kScanCap;
       for (int e = threadIdx.x & 31; e < n; e += 32) {
@@ -104,7 +112,7 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   // 1. Gather the entries that can still be among the C best.
   int nsurv = 0;
   for (int p = 0; p < a.units_per_qtile; ++p) {
-    const size_t slot = (static_cast<size_t>(qtile) * a.units_per_qtile + p) * kScanBM + row_in_tile;
+    const size_t slot = unit_slot(a, qtile, p, row_in_tile);
     const int n = a.cand_count[slot];
     const uint2* b = a.cand + slot * kScanCap;
     for (int e0 = 0; e0 < n; e0 += 32) {
@@ -132,7 +140,7 @@ __global__ void __launch_bounds__(kFinWarps * 32)
     const uint64_t kth = global_kth(a, qtile, row_in_tile, thr, a.cpre);
     int w = 0;
     for (int p = 0; p < a.units_per_qtile; ++p) {
-      const size_t slot = (static_cast<size_t>(qtile) * a.units_per_qtile + p) * kScanBM + row_in_tile;
+      const size_t slot = unit_slot(a, qtile, p, row_in_tile);
       const int n = a.cand_count[slot];
       const uint2* b = a.cand + slot * kScanCap;
       for (int e0 = 0; e0 < n; e0 += 32) {
@@ -158,35 +166,63 @@ __global__ void __launch_bounds__(kFinWarps * 32)
 
   // 2. Exact distances of the candidates (stored back as packed (dist, row)).
   const bool l2 = a.metric == 0;
-  if (a.codes == nullptr) {
-    for (int i = 0; i < ncand; ++i) {
-      const uint32_t row = neighbor_id(surv[i]);
-      const float d = warp_exact_dist(q_s, a.rows + static_cast<size_t>(row) * pd, pd, l2, a.order);
+  // Exact fp32 distances of surv[0..n) on the float rows, 4 gathers in flight at a time.
+  auto exact_rows = [&](int n) {
+    for (int i = 0; i < n; i += 4) {
+      uint32_t r[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) r[c] = neighbor_id(surv[i + c < n ? i + c : i]);
+      float d[4];
+      if (a.order == kOrderAvx512 && pd <= 8 * 32 + 16) {
+        warp_exact_dist4_avx512<8>(q_s, a.rows, r, n - i, pd, l2, d);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          d[c] = warp_exact_dist(q_s, a.rows + static_cast<size_t>(r[c]) * pd, pd, l2, a.order);
+      }
       __syncwarp();
-      if (lane == 0) surv[i] = pack_neighbor(d, row);
+      if (lane < 4 && i + lane < n) {
+        float dl = d[0];
+        uint32_t rl = r[0];
+#pragma unroll
+        for (int c = 1; c < 4; ++c) {
+          dl = lane == c ? d[c] : dl;
+          rl = lane == c ? r[c] : rl;
+        }
+        surv[i + lane] = pack_neighbor(dl, rl);
+      }
+      __syncwarp();
     }
-    __syncwarp();
+  };
+  if (a.codes == nullptr) {
+    exact_rows(ncand);
     sort_small(surv, ncand);
   } else {
-    for (int i = 0; i < ncand; i += 2) {
-      const int my = i + (lane >> 4);
-      const uint32_t row = my < ncand ? neighbor_id(surv[my]) : neighbor_id(surv[i]);
-      const float d = halfwarp_sq8_dist(q_s, a.codes + static_cast<size_t>(row) * pd, vmin_s,
-                                        scale_s, pd, l2, a.order);
+    for (int i = 0; i < ncand; i += 8) {
+      // Four pairs of codes per iteration: half-warp h takes candidates i+2c+h, c = 0..3.
+      float d[4];
+      uint32_t row[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int my = i + 2 * c + (lane >> 4);
+        row[c] = neighbor_id(surv[my < ncand ? my : i]);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        d[c] = halfwarp_sq8_dist(q_s, a.codes + static_cast<size_t>(row[c]) * pd, vmin_s, scale_s,
+                                 pd, l2, a.order);
       __syncwarp();
-      if ((lane & 15) == 0 && my < ncand) surv[my] = pack_neighbor(d, row);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int my = i + 2 * c + (lane >> 4);
+        if ((lane & 15) == 0 && my < ncand) surv[my] = pack_neighbor(d[c], row[c]);
+      }
+      __syncwarp();
     }
-    __syncwarp();
     sort_small(surv, ncand);
     if (a.depth > 0) {
       const int nr = ncand < a.depth ? ncand : a.depth;
-      for (int i = 0; i < nr; ++i) {
-        const uint32_t row = neighbor_id(surv[i]);
-        const float d = warp_exact_dist(q_s, a.rows + static_cast<size_t>(row) * pd, pd, l2, a.order);
-        __syncwarp();
-        if (lane == 0) surv[i] = pack_neighbor(d, row);
-      }
-      __syncwarp();
+      exact_rows(nr);
       ncand = nr;
       sort_small(surv, ncand);
     }

@@ -194,4 +194,56 @@ __device__ __forceinline__ float halfwarp_sq8_dist(const float* q_s, const uint8
   return l2 ? r : -r;
 }
 
+// AVX-512-order exact distances of up to 4 rows at once (ids r[0..nc)), all lanes receive them.
+// Same arithmetic as warp_exact_dist with kOrderAvx512; the loads of the 4 rows are issued
+// together so the gathers overlap. pd <= 32 * kMaxT + 16.
+template <int kMaxT>
+__device__ __forceinline__ void warp_exact_dist4_avx512(const float* q_s, const float* __restrict__ rows,
+                                                        const uint32_t (&r)[4], int nc, int pd,
+                                                        bool l2, float (&out)[4]) {
+  const int lane = threadIdx.x & 31;
+  const int nb = pd >> 5;
+  const bool tail = (pd & 31) != 0 && lane < 16;
+  float x[4][kMaxT + 1];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float* row = rows + static_cast<size_t>(r[c < nc ? c : 0]) * pd;
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) x[c][t] = t < nb ? __ldg(&row[32 * t + lane]) : 0.f;
+    x[c][kMaxT] = tail ? __ldg(&row[32 * nb + lane]) : 0.f;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float acc = 0.f;
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t < nb) {
+        const float qv = q_s[32 * t + lane];
+        if (l2) {
+          const float d = __fsub_rn(qv, x[c][t]);
+          acc = __fmaf_rn(d, d, acc);
+        } else {
+          acc = __fmaf_rn(qv, x[c][t], acc);
+        }
+      }
+    }
+    if (tail) {
+      const float qv = q_s[32 * nb + lane];
+      if (l2) {
+        const float d = __fsub_rn(qv, x[c][kMaxT]);
+        acc = __fmaf_rn(d, d, acc);
+      } else {
+        acc = __fmaf_rn(qv, x[c][kMaxT], acc);
+      }
+    }
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 16));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
+    acc = __shfl_sync(0xFFFFFFFFu, acc, 0);
+    out[c] = l2 ? acc : -acc;
+  }
+}
+
 }  // namespace vdbgpu
