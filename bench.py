@@ -204,7 +204,7 @@ def run_ours(args):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks = Clocks(local)
-    scan_ms, stage = [], np.zeros(3)
+    scan_ms, stage, counters = [], np.zeros(3), np.zeros(4)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
@@ -212,6 +212,7 @@ def run_ours(args):
         st = ctx.stage_times()
         scan_ms.append(st[1])
         stage += np.array(st[:3])
+        counters += np.array(ctx.stage_counters()[:4], dtype=np.float64)
     ev1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -269,6 +270,10 @@ def run_ours(args):
             "roofline": roof,
             "stage_ms": {"prep": stage[0] / args.steps, "scan": stage[1] / args.steps,
                          "select_rerank": stage[2] / args.steps},
+            "scan_counters_per_step": {"chunks": counters[0] / args.steps,
+                                       "chunks_with_candidates": counters[1] / args.steps,
+                                       "candidates_per_query": counters[2] / args.steps / nq,
+                                       "compactions_per_query": counters[3] / args.steps / nq},
             "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": nq * DIM * 4,
                     "d2h_bytes_per_step": nq * K * 8},
             "gpu_launches": launches_per_step * args.steps,

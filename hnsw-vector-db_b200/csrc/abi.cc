@@ -107,6 +107,16 @@ int vdbgpu_stage_times(vdbgpu_ctx* ctx, float* out, int cap) {
   return ctx->c->StageTimes(out, cap);
 }
 
+int vdbgpu_stage_counters(vdbgpu_ctx* ctx, uint64_t* out, int cap) {
+  if (ctx == nullptr || out == nullptr) return 0;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  unsigned long long tmp[8];
+  const int n = ctx->c->Counters(tmp, cap < 8 ? cap : 8);
+  for (int i = 0; i < n; ++i) out[i] = tmp[i];
+  return n;
+}
+
 int vdbgpu_synchronize(vdbgpu_ctx* ctx) {
   if (ctx == nullptr) return VDBGPU_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> g(ctx->c->mu());

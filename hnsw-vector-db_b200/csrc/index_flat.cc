@@ -282,9 +282,11 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   int upq = 1, tpu = 1;
   ChooseUnits(qtiles, ntiles, ctx.sm_count(), &upq, &tpu);
   const uint64_t nunits = qtiles * static_cast<uint64_t>(upq);
+  // One candidate list per (unit, epilogue warpgroup, query).
+  const uint64_t wgs = static_cast<uint64_t>(ctx.scan_wgs());
   VDBGPU_RETURN_IF_ERROR(
-      ctx.workspace(kWsCand, nunits * kScanBM * kScanCap * sizeof(uint2), &cand));
-  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, nunits * kScanBM * sizeof(int), &cnt));
+      ctx.workspace(kWsCand, nunits * wgs * kScanBM * kScanCap * sizeof(uint2), &cand));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, nunits * wgs * kScanBM * sizeof(int), &cnt));
 
   ScanArgs sa{};
   sa.nq = static_cast<int>(nq);
@@ -299,6 +301,10 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   sa.qscale = static_cast<const float*>(qscale);
   sa.rowterm = op.rowterm;
   sa.allow = b.allow;
+  sa.wgs = static_cast<int>(wgs);
+  sa.counters = ctx.timing() ? ctx.counters() : nullptr;
+  if (sa.counters != nullptr)
+    VDBGPU_CUDA(cudaMemsetAsync(sa.counters, 0, 8 * sizeof(unsigned long long), ctx.stream()));
   sa.cand = static_cast<uint2*>(cand);
   sa.cand_count = static_cast<int*>(cnt);
   sa.qtau = static_cast<uint32_t*>(qtau);
@@ -317,6 +323,7 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   fa.metric = metric;
   fa.order = ctx.order();
   fa.units_per_qtile = upq;
+  fa.wgs = static_cast<int>(wgs);
   fa.cand = static_cast<const uint2*>(cand);
   fa.cand_count = static_cast<const int*>(cnt);
   fa.qtau = static_cast<const uint32_t*>(qtau);

@@ -17,6 +17,7 @@ struct FinalizeArgs {
   int metric;           // 0 = L2, else minus the dot product
   int order;            // SumOrder of the reference kernel set
   int units_per_qtile;
+  int wgs;              // candidate lists per unit (scan epilogue warpgroups)
   const uint2* cand;
   const int* cand_count;
   const uint32_t* qtau;

@@ -87,6 +87,8 @@ Status Context::Open(int device, std::unique_ptr<Context>* out) {
   if (q != cudaDriverEntryPointSuccess || c->encode_fn_ == nullptr)
     return Status(Status::kUnavailable, "cuTensorMapEncodeTiled is not available");
   c->order_ = DetectKernelOrder();
+  if (const char* w = std::getenv("VDB_SCAN_WARPGROUPS"); w != nullptr && std::strcmp(w, "2") == 0)
+    c->scan_wgs_ = 2;
   *out = std::move(c);
   return Status::OK();
 }
@@ -94,8 +96,24 @@ Status Context::Open(int device, std::unique_ptr<Context>* out) {
 Status Context::EnableTiming(bool on) {
   if (on && marks_[0] == nullptr)
     for (int i = 0; i < kMaxMarks; ++i) VDBGPU_CUDA(cudaEventCreate(&marks_[i]));
+  if (on && counters_.get() == nullptr) {
+    VDBGPU_RETURN_IF_ERROR(counters_.alloc(8 * sizeof(unsigned long long)));
+    VDBGPU_CUDA(cudaMemset(counters_.get(), 0, 8 * sizeof(unsigned long long)));
+  }
   timing_ = on;
   return Status::OK();
+}
+
+int Context::Counters(unsigned long long* out, int cap) {
+  if (!timing_ || counters_.get() == nullptr) return 0;
+  unsigned long long h[8] = {};
+  if (cudaMemcpy(h, counters_.get(), sizeof(h), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  const int n = cap < 8 ? cap : 8;
+  for (int i = 0; i < n; ++i) out[i] = h[i];
+  return n;
 }
 
 int Context::StageTimes(float* out, int cap) {

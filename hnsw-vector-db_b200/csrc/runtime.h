@@ -105,6 +105,13 @@ class Context {
   }
   int StageTimes(float* out, int cap);
   static constexpr int kMaxMarks = 4;
+  bool timing() const { return timing_; }
+  // Device counters of the last scan (chunks, triggered chunks, inserts, compactions), kept
+  // only while timing is enabled.
+  unsigned long long* counters() const { return counters_.as<unsigned long long>(); }
+  int Counters(unsigned long long* out, int cap);
+  // Epilogue warpgroups of the scan (VDB_SCAN_WARPGROUPS, default 1).
+  int scan_wgs() const { return scan_wgs_; }
   int sm_count() const { return sm_count_; }
   int order() const { return order_; }
   int* status_word() const { return status_.as<int>(); }
@@ -131,6 +138,8 @@ class Context {
   cudaStream_t user_stream_ = nullptr;
   bool timing_ = false;
   cudaEvent_t marks_[kMaxMarks] = {};
+  DeviceBuffer counters_;
+  int scan_wgs_ = 1;
   int sm_count_ = 0;
   int order_ = 1;
   DeviceBuffer status_;

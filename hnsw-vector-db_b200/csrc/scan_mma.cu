@@ -101,8 +101,8 @@ __device__ uint32_t compact_buffer(uint2* buf, int n, int keep) {
   return ans;
 }
 
-template <int kMode>
-__global__ void __launch_bounds__(kScanThreads, 1)
+template <int kMode, int kWgs>
+__global__ void __launch_bounds__(ScanThreads(kWgs), 1)
     scan_mma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const ScanArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     mbar_init(&bars->a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
+      // Two epilogue warpgroups: warpgroup b drains accumulator b alone (128 threads). One
+      // warpgroup drains both.
       mbar_init(&bars->acc_empty[b], 128);
     }
     mbar_init(&bars->mma_done, 1);
@@ -248,10 +250,14 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue
+    // Two warpgroups; warpgroup w takes the tiles that land in accumulator w (every other tile
+    // of the CTA's sequence), keeping its own threshold and candidate list per query.
+    const int wg = kWgs == 1 ? 0 : (warp - 2) >> 2;
+    unsigned long long n_chunks = 0, n_trig = 0, n_ins = 0, n_comp = 0;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t tcount = 0;  // tiles of this CTA so far (both warpgroups count all of them)
     bool ok = true;
     for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
       int qtile, r0, r1;
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       float tau = valid_q ? INFINITY : -INFINITY;
       float tau_acc = tau * qs_inv;
       int count = 0;
-      const size_t slot = static_cast<size_t>(unit) * kScanBM + row_in_tile;
+      const size_t slot = (static_cast<size_t>(unit) * kWgs + wg) * kScanBM + row_in_tile;
       uint2* buf = a.cand + slot * kScanCap;
 
       // Compacts every lane whose buffer holds more than `limit` entries to its `keep` best
@@ -276,7 +282,9 @@ __global__ void __launch_bounds__(kScanThreads, 1)
           const int src = __ffs(need) - 1;
           need &= need - 1u;
           const int n = __shfl_sync(0xFFFFFFFFu, count, src);
-          uint2* sbuf = a.cand + (static_cast<size_t>(unit) * kScanBM + quad * 32 + src) * kScanCap;
+          uint2* sbuf = a.cand + ((static_cast<size_t>(unit) * kWgs + wg) * kScanBM + quad * 32 + src) *
+                                     kScanCap;
+          ++n_comp;
           __syncwarp();
           const uint32_t kth = compact_buffer(sbuf, n, a.keep);
           if (lane == src) {
@@ -289,73 +297,74 @@ __global__ void __launch_bounds__(kScanThreads, 1)
         }
       };
 
-      // One chunk of 32 accumulator columns starting at row c0.
+      // One chunk of 32 accumulator columns starting at row c0. Scores: raw accumulators
+      // (larger is closer, scaled-key mode) or keys (smaller is closer, row-term mode); masked
+      // columns get the worst score. A max/min tree over the 32 scores is the fast path's
+      // filter; when some lane of the warp has a hit, the warp descends the tree with votes and
+      // each lane appends only its qualifying columns, in column order.
       auto process = [&](uint32_t (&v)[32], int c0) {
         uint32_t allow_bits = 0xFFFFFFFFu;
         if (a.allow != nullptr) allow_bits = __ldg(&a.allow[c0 >> 5]);
-        const int nvalid = r1 - c0;  // columns < nvalid are real rows of this unit
+        const int nvalid = r1 - c0;
         const bool full = nvalid >= 32 && allow_bits == 0xFFFFFFFFu;
-        bool hit;
+        constexpr bool kMin = kMode == kKeyRowTerm;
+        const float worst = kMin ? INFINITY : -INFINITY;
+        const float bound = kMin ? tau : tau_acc;
         if constexpr (kMode == kKeyRowTerm) {
-          float rt[32];
           const float4* rt4 = reinterpret_cast<const float4*>(a.rowterm + c0);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 x = __ldg(&rt4[j]);
-            rt[4 * j] = x.x;
-            rt[4 * j + 1] = x.y;
-            rt[4 * j + 2] = x.z;
-            rt[4 * j + 3] = x.w;
+            v[4 * j + 0] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 0]), x.x));
+            v[4 * j + 1] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 1]), x.y));
+            v[4 * j + 2] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 2]), x.z));
+            v[4 * j + 3] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 3]), x.w));
           }
-          float kmin = INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float key = fmaf(qs, __uint_as_float(v[j]), rt[j]);
-            if (!full && (j >= nvalid || !((allow_bits >> j) & 1u))) key = INFINITY;
-            v[j] = __float_as_uint(key);
-            kmin = fminf(kmin, key);
-          }
-          hit = kmin < tau;
-        } else {
-          float amax = -INFINITY;
-          if (full) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, __uint_as_float(v[j]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j >= nvalid || !((allow_bits >> j) & 1u)) v[j] = __float_as_uint(-INFINITY);
-              amax = fmaxf(amax, __uint_as_float(v[j]));
-            }
-          }
-          hit = amax > tau_acc;
         }
-        if (__any_sync(0xFFFFFFFFu, hit)) {
+        if (!full) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float key;
-            if constexpr (kMode == kKeyRowTerm) key = __uint_as_float(v[j]);
-            else key = qs * __uint_as_float(v[j]);
-            if (key < tau) {
-              buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c0 + j));
-              ++count;
-            }
-          }
-          compact_lanes(kScanCap - 32);
+          for (int j = 0; j < 32; ++j)
+            if (j >= nvalid || !((allow_bits >> j) & 1u)) v[j] = __float_as_uint(worst);
         }
+        auto better = [&](float x, float y) { return kMin ? fminf(x, y) : fmaxf(x, y); };
+        auto passes = [&](float x) { return kMin ? (x < bound) : (x > bound); };
+        float t1[16], t2[8], t3[4];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t1[i] = better(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t2[i] = better(t1[2 * i], t1[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t3[i] = better(t2[2 * i], t2[2 * i + 1]);
+        ++n_chunks;
+        if (!__any_sync(0xFFFFFFFFu, passes(better(better(t3[0], t3[1]), better(t3[2], t3[3]))))) return;
+        ++n_trig;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float sc = __uint_as_float(v[j]);
+          if (passes(sc)) {
+            const float key = kMin ? sc : qs * sc;
+            buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c0 + j));
+            ++count;
+            ++n_ins;
+          }
+        }
+        compact_lanes(kScanCap - 32);
       };
 
-      for (int row0 = r0; row0 < r1; row0 += kScanBN) {
+      for (int row0 = r0; row0 < r1; row0 += kScanBN, ++tcount) {
+        const int accb = static_cast<int>(tcount & 1u);
+        if (kWgs == 2 && accb != wg) continue;
         // The shared threshold is read now and applied after the first chunk (hides latency).
         uint32_t g = 0xFFFFFFFFu;
         if (valid_q) g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
-        if (!mbar_wait(&bars->acc_full[acc], acc_phase, a.status, kDevTimeoutAcc)) {
+        if (!mbar_wait(&bars->acc_full[accb], kWgs == 2 ? acc_phase : (tcount >> 1) & 1u, a.status,
+                       kDevTimeoutAcc)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                static_cast<uint32_t>(acc * kScanBN);
+                                static_cast<uint32_t>(accb * kScanBN);
         uint32_t va[32], vb[32];
         __syncwarp();
         tmem_ld_32x32b_x32(t_addr, va);
@@ -378,15 +387,23 @@ __global__ void __launch_bounds__(kScanThreads, 1)
           tmem_ld_wait_regs(va);
         }
         tc_fence_before();
-        mbar_arrive(&bars->acc_empty[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
-        }
+        mbar_arrive(&bars->acc_empty[accb]);
+        acc_phase ^= 1u;
       }
       // Leave at most `keep` entries per query and publish this unit's keep-th key.
       if (ok) compact_lanes(a.keep);
       a.cand_count[slot] = valid_q ? count : 0;
+    }
+    if (a.counters != nullptr) {
+      unsigned long long ins = n_ins;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ins += __shfl_xor_sync(0xFFFFFFFFu, ins, o);
+      if (lane == 0) {
+        atomicAdd(&a.counters[0], n_chunks);
+        atomicAdd(&a.counters[1], n_trig);
+        atomicAdd(&a.counters[2], ins);
+        atomicAdd(&a.counters[3], n_comp);
+      }
     }
   }
 
@@ -406,22 +423,25 @@ size_t ScanSmemBytes(int kblocks) {
          static_cast<size_t>(kScanStages) * kBBytesPerStage + sizeof(ScanBarriers);
 }
 
+template <int kMode, int kWgs>
+cudaError_t LaunchScanT(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
+                        int grid, cudaStream_t stream) {
+  const size_t smem = ScanSmemBytes(a.kblocks);
+  cudaError_t e = cudaFuncSetAttribute(scan_mma_kernel<kMode, kWgs>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  scan_mma_kernel<kMode, kWgs><<<grid, ScanThreads(kWgs), smem, stream>>>(tmap_a, tmap_b, a);
+  return cudaGetLastError();
+}
+
 cudaError_t LaunchScan(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
                        int grid, cudaStream_t stream) {
-  const size_t smem = ScanSmemBytes(a.kblocks);
-  cudaError_t e;
-  if (a.mode == kKeyRowTerm) {
-    e = cudaFuncSetAttribute(scan_mma_kernel<kKeyRowTerm>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    scan_mma_kernel<kKeyRowTerm><<<grid, kScanThreads, smem, stream>>>(tmap_a, tmap_b, a);
-  } else {
-    e = cudaFuncSetAttribute(scan_mma_kernel<kKeyScaled>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    scan_mma_kernel<kKeyScaled><<<grid, kScanThreads, smem, stream>>>(tmap_a, tmap_b, a);
-  }
-  return cudaGetLastError();
+  if (a.mode == kKeyRowTerm)
+    return a.wgs == 2 ? LaunchScanT<kKeyRowTerm, 2>(tmap_a, tmap_b, a, grid, stream)
+                      : LaunchScanT<kKeyRowTerm, 1>(tmap_a, tmap_b, a, grid, stream);
+  return a.wgs == 2 ? LaunchScanT<kKeyScaled, 2>(tmap_a, tmap_b, a, grid, stream)
+                    : LaunchScanT<kKeyScaled, 1>(tmap_a, tmap_b, a, grid, stream);
 }
 
 }  // namespace vdbgpu

@@ -12,8 +12,12 @@ constexpr int kScanBN = 256;      // rows per tile: TMEM columns of one accumula
 constexpr int kScanBK = 64;       // fp16 elements per k-block (one 128-byte swizzle atom)
 constexpr int kScanStages = 4;    // B k-block stages in flight
 constexpr int kScanMaxKB = 4;     // padded dims up to 256
-constexpr int kScanCap = 512;     // candidate slots per (unit, query)
-constexpr int kScanThreads = 192; // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2..5 epilogue
+#ifndef VDBGPU_SCAN_CAP
+#define VDBGPU_SCAN_CAP 512
+#endif
+constexpr int kScanCap = VDBGPU_SCAN_CAP;  // candidate slots per (unit, query)
+// warp 0 TMA, warp 1 MMA + TMEM owner, then 4 epilogue warps per epilogue warpgroup (1 or 2)
+constexpr int ScanThreads(int wgs) { return 64 + 128 * wgs; }
 
 // Key transform applied to the fp32 accumulator acc = sum_i A[q,i] * B[r,i]:
 //   kKeyScaled:  key = qscale[q] * acc
@@ -34,8 +38,10 @@ struct ScanArgs {
   const float* qscale;  // [nq]
   const float* rowterm; // [round_up(nrows, 256)] (kKeyRowTerm) or null
   const uint32_t* allow;// allowed-row bitset, 32 rows per word, padded to 256 rows; null = all
-  uint2* cand;          // [nunits][128][kScanCap] (float key bits, row)
-  int* cand_count;      // [nunits][128]
+  int wgs;              // epilogue warpgroups (1 or 2); each keeps its own candidate lists
+  uint2* cand;          // [nunits][wgs][128][kScanCap] (float key bits, row)
+  int* cand_count;      // [nunits][wgs][128]
+  unsigned long long* counters;  // optional: chunks, triggered chunks, inserts, compactions
   uint32_t* qtau;       // [nq] shared per-query threshold (ordered-key space), 0xFFFFFFFF = none
   int* status;          // device status word
 };

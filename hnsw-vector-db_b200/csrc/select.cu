@@ -50,12 +50,14 @@ __device__ void sort_small(uint64_t* s, int n) {
   else sort_into_smem<32>(s, n);
 }
 
-// Candidate slot of (query tile, row slice, query row): units are numbered slice-major
-// (scan_mma.cu unit_rows), so unit = slice * qtiles + qtile.
-__device__ __forceinline__ size_t unit_slot(const FinalizeArgs& a, int qtile, int slice,
+// Candidate slot of (query tile, list, query row). A query has `wgs` lists per row slice (one
+// per epilogue warpgroup of the scan): list p = wgs * slice + warpgroup. Units are numbered
+// slice-major (scan_mma.cu unit_rows), so unit = slice * qtiles + qtile.
+__device__ __forceinline__ size_t unit_slot(const FinalizeArgs& a, int qtile, int p,
                                             int row_in_tile) {
   const size_t qtiles = (static_cast<size_t>(a.nq) + kScanBM - 1) / kScanBM;
-  return (static_cast<size_t>(slice) * qtiles + qtile) * kScanBM + row_in_tile;
+  const size_t unit = static_cast<size_t>(p / a.wgs) * qtiles + qtile;
+  return (unit * a.wgs + (p % a.wgs)) * kScanBM + row_in_tile;
 }
 
 // The c-th smallest packed key (1-based) among entries passing `thr`, by bitwise search over
@@ -66,7 +68,7 @@ __device__ uint64_t global_kth(const FinalizeArgs& a, int qtile, int row_in_tile
   for (int bit = 63; bit >= 0; --bit) {
     const uint64_t cand = ans | (1ull << bit);
     int cnt = 0;
-    for (int p = 0; p < a.units_per_qtile; ++p) {
+    for (int p = 0; p < a.wgs * a.units_per_qtile; ++p) {
       const size_t slot = unit_slot(a, qtile, p, row_in_tile);
       const int n = a.cand_count[slot];
       const uint2* b = a.cand + slot * kScanCap;
@@ -111,7 +113,7 @@ __global__ void __launch_bounds__(kFinWarps * 32)
 
   // 1. Gather the entries that can still be among the C best.
   int nsurv = 0;
-  for (int p = 0; p < a.units_per_qtile; ++p) {
+  for (int p = 0; p < a.wgs * a.units_per_qtile; ++p) {
     const size_t slot = unit_slot(a, qtile, p, row_in_tile);
     const int n = a.cand_count[slot];
     const uint2* b = a.cand + slot * kScanCap;
@@ -139,7 +141,7 @@ __global__ void __launch_bounds__(kFinWarps * 32)
     // Rare: select the cpre-th key over all entries, then gather exactly those <= it.
     const uint64_t kth = global_kth(a, qtile, row_in_tile, thr, a.cpre);
     int w = 0;
-    for (int p = 0; p < a.units_per_qtile; ++p) {
+    for (int p = 0; p < a.wgs * a.units_per_qtile; ++p) {
       const size_t slot = unit_slot(a, qtile, p, row_in_tile);
       const int n = a.cand_count[slot];
       const uint2* b = a.cand + slot * kScanCap;

@@ -19,7 +19,7 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_DIR = os.path.join(os.path.dirname(_HERE), "lib")
-LIB_PATH = os.path.join(LIB_DIR, "libvdbgpu.so")
+LIB_PATH = os.environ.get("VDBGPU_LIB") or os.path.join(LIB_DIR, "libvdbgpu.so")
 
 OK, INVALID_ARGUMENT, NOT_FOUND = 0, 1, 2
 RESOURCE_EXHAUSTED, UNAVAILABLE, NOT_SUPPORTED = 7, 8, 9
@@ -65,6 +65,7 @@ _SIGNATURES = {
     "vdbgpu_set_stream": (ctypes.c_int, [_P, _P]),
     "vdbgpu_set_timing": (ctypes.c_int, [_P, ctypes.c_int]),
     "vdbgpu_stage_times": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
+    "vdbgpu_stage_counters": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
     "vdbgpu_search_params_default": (None, [ctypes.POINTER(SearchParams)]),
     "vdbgpu_index_load": (ctypes.c_int, [_P, _P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64,
                                          ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_P)]),
@@ -161,6 +162,12 @@ class Context:
         buf = (ctypes.c_float * 8)()
         n = lib().vdbgpu_stage_times(self._h, buf, 8)
         return [buf[i] for i in range(n)]
+
+    def stage_counters(self):
+        """Work counters of the last search's dominant kernel (timing must be on)."""
+        buf = (ctypes.c_uint64 * 8)()
+        n = lib().vdbgpu_stage_counters(self._h, buf, 8)
+        return [int(buf[i]) for i in range(n)]
 
     def close(self):
         if getattr(self, "_h", None):

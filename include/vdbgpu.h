@@ -109,6 +109,11 @@ VDBGPU_API int vdbgpu_set_timing(vdbgpu_ctx* ctx, int enable);
  * re-rank. Returns the number of stages written (0 when timing is off). */
 VDBGPU_API int vdbgpu_stage_times(vdbgpu_ctx* ctx, float* out, int cap);
 
+/* Work counters of the last search's dominant kernel, collected while timing is on. For the
+ * tensor-core scan: out[0] chunks of 32 columns filtered, out[1] chunks with a candidate,
+ * out[2] candidates appended, out[3] candidate-list compactions. Returns the count written. */
+VDBGPU_API int vdbgpu_stage_counters(vdbgpu_ctx* ctx, uint64_t* out, int cap);
+
 /* Blocks until the context's stream is idle. */
 VDBGPU_API int vdbgpu_synchronize(vdbgpu_ctx* ctx);
 
