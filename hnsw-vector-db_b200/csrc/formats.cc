@@ -94,6 +94,9 @@ Status ParseHnswGraph(Reader& r, uint64_t expected_cap, HnswGraphData* g) {
     g->upper.resize(at + n);
     std::memcpy(g->upper.data() + at, b.data(), n * 4);
   }
+  // The descent starts at the entry point on the top layer, so it must live there.
+  if (sz > 0 && cap > 0 && g->level[ep] < max_level)
+    return Status(Status::kCorruption, "hnsw entry point is below the top layer");
   // Every link must stay in range (the reference validates the same before searching).
   for (uint64_t i = 0; i < cap; ++i) {
     for (int l = 0; l <= g->level[i]; ++l) {

@@ -1,0 +1,466 @@
+// Batched HNSW search over the reference's own graphs (sm_100a), one warp per query.
+//
+// Follows HnswGraph::search (src/index/hnsw/hnsw_graph.h:286-309) step for step: greedy descent
+// over the upper layers (greedy<false>, :482-508), then the ef-beam on layer 0
+// (search_layer<false, filtered>, :513-567), then HnswSq8Index's fp32 re-rank
+// (src/index/hnsw/hnsw_index.cc:82-102). Distances are summed in the order of the reference's
+// runtime kernel set, so for the same graph and inputs the walk takes the same path and returns
+// the same neighbours, distances and distance-computation counts.
+//
+// Parallel where the reference is sequential, without changing the result:
+//   * the distances of a node's neighbours are independent: four quarter-warps compute four rows
+//     at a time (8 lanes emulate one 16-lane AVX-512 accumulator pair, same adds in the same tree);
+//   * visited marks go to a per-warp open-addressing hash in shared memory (the reference's
+//     tag array, visited_pool.h:16-41; a list never holds a node twice, so marking a whole list at
+//     once is equivalent);
+//   * the heaps are sorted arrays. (dist, id) is a total order, so popping the least candidate and
+//     evicting the greatest result pick the same elements a binary heap picks. Heap updates are
+//     applied one neighbour at a time, in list order, with the reference's
+//     "results.size() < ef || d < lower" rule.
+//   * once the result set holds ef entries its worst distance can only fall, so a candidate
+//     farther than it can never be expanded and is dropped when the candidate array is full.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "hnsw.cuh"
+#include "warp_ops.cuh"
+
+namespace vdbgpu {
+namespace {
+
+constexpr int kHnswWarps = 4;
+constexpr uint32_t kEmpty = 0u;
+
+struct WarpSmem {
+  float* q;           // pd floats
+  uint32_t* hash;     // 1 << hash_bits slots (id + 1, 0 = empty)
+  uint64_t* res;      // ef sorted ascending packed (dist, id)
+  uint64_t* cand;     // cand_cap, ascending from index head
+  uint32_t* nb_id;    // 32 neighbour ids of the current expansion (new ones, compacted)
+  float* nb_d;        // their distances
+};
+
+__device__ __forceinline__ uint32_t hash_slot(uint32_t id, int bits) {
+  return (id * 2654435761u) >> (32 - bits);
+}
+
+// Marks `id` visited; true when it was not visited before. Sets *full when the table has no
+// free slot left on the probe path (the caller reports an overflow).
+__device__ __forceinline__ bool visit(uint32_t* hash, int bits, uint32_t id, bool* full) {
+  const uint32_t mask = (1u << bits) - 1u;
+  uint32_t s = hash_slot(id, bits);
+  const uint32_t key = id + 1u;
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    const uint32_t prev = atomicCAS(&hash[s], kEmpty, key);
+    if (prev == kEmpty) return true;
+    if (prev == key) return false;
+    s = (s + 1u) & mask;
+  }
+  *full = true;
+  return false;
+}
+
+// Distance of the query (shared memory) to 4 rows at once: lanes 8g..8g+7 take row r[g].
+// Float rows: the reference kernel set's order. Returns the distance of this lane's group.
+template <bool kSq8>
+__device__ __forceinline__ float group_dist(const HnswArgs& a, const float* q_s, uint32_t row,
+                                            bool l2) {
+  const int j = threadIdx.x & 7;
+  const int pd = a.pd;
+  float r;
+  if (!kSq8) {
+    const float* x = a.rows + static_cast<size_t>(row) * pd;
+    if (a.order == kOrderAvx512) {
+      const int nb = pd >> 5;
+      float a0 = 0.f, a0b = 0.f, a1 = 0.f, a1b = 0.f;
+      for (int t = 0; t < nb; ++t) {
+        const int e = 32 * t + j;
+        const float x0 = __ldg(&x[e]), x1 = __ldg(&x[e + 8]), x2 = __ldg(&x[e + 16]), x3 = __ldg(&x[e + 24]);
+        if (l2) {
+          const float d0 = __fsub_rn(q_s[e], x0), d1 = __fsub_rn(q_s[e + 8], x1);
+          const float d2 = __fsub_rn(q_s[e + 16], x2), d3 = __fsub_rn(q_s[e + 24], x3);
+          a0 = __fmaf_rn(d0, d0, a0);
+          a0b = __fmaf_rn(d1, d1, a0b);
+          a1 = __fmaf_rn(d2, d2, a1);
+          a1b = __fmaf_rn(d3, d3, a1b);
+        } else {
+          a0 = __fmaf_rn(q_s[e], x0, a0);
+          a0b = __fmaf_rn(q_s[e + 8], x1, a0b);
+          a1 = __fmaf_rn(q_s[e + 16], x2, a1);
+          a1b = __fmaf_rn(q_s[e + 24], x3, a1b);
+        }
+      }
+      if ((pd & 31) != 0) {
+        const int e = 32 * nb + j;
+        const float x0 = __ldg(&x[e]), x1 = __ldg(&x[e + 8]);
+        if (l2) {
+          const float d0 = __fsub_rn(q_s[e], x0), d1 = __fsub_rn(q_s[e + 8], x1);
+          a0 = __fmaf_rn(d0, d0, a0);
+          a0b = __fmaf_rn(d1, d1, a0b);
+        } else {
+          a0 = __fmaf_rn(q_s[e], x0, a0);
+          a0b = __fmaf_rn(q_s[e + 8], x1, a0b);
+        }
+      }
+      // s[j] = acc0[j] + acc1[j]; T3[j] = s[j+8] + s[j]; then lanes +4, +2, +1.
+      float t3 = __fadd_rn(__fadd_rn(a0b, a1b), __fadd_rn(a0, a1));
+      t3 = __fadd_rn(t3, __shfl_xor_sync(0xFFFFFFFFu, t3, 4));
+      t3 = __fadd_rn(t3, __shfl_xor_sync(0xFFFFFFFFu, t3, 2));
+      t3 = __fadd_rn(t3, __shfl_xor_sync(0xFFFFFFFFu, t3, 1));
+      r = t3;
+    } else if (a.order == kOrderAvx2) {
+      float a0 = 0.f, a1 = 0.f;
+      for (int i = 0; i < pd; i += 16) {
+        const float x0 = __ldg(&x[i + j]), x1 = __ldg(&x[i + 8 + j]);
+        if (l2) {
+          const float d0 = __fsub_rn(q_s[i + j], x0), d1 = __fsub_rn(q_s[i + 8 + j], x1);
+          a0 = __fmaf_rn(d0, d0, a0);
+          a1 = __fmaf_rn(d1, d1, a1);
+        } else {
+          a0 = __fmaf_rn(q_s[i + j], x0, a0);
+          a1 = __fmaf_rn(q_s[i + 8 + j], x1, a1);
+        }
+      }
+      float v = __fadd_rn(a0, a1);                               // v[j]
+      v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));      // s[j] = v[j] + v[j+4]
+      v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));      // s0+s1, s2+s3
+      v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+      r = v;
+    } else {
+      float s = 0.f;
+      if (j == 0) {
+        for (int e = 0; e < pd; ++e) {
+          const float xv = __ldg(&x[e]);
+          if (l2) {
+            const float d = __fsub_rn(q_s[e], xv);
+            s = __fadd_rn(s, __fmul_rn(d, d));
+          } else {
+            s = __fadd_rn(s, __fmul_rn(q_s[e], xv));
+          }
+        }
+      }
+      r = __shfl_sync(0xFFFFFFFFu, s, threadIdx.x & 24);
+    }
+  } else {
+    const uint8_t* c = a.codes + static_cast<size_t>(row) * pd;
+    if (a.order == kOrderAvx512 || a.order == kOrderAvx2) {
+      float a0 = 0.f, a1 = 0.f;  // avx512: acc[j], acc[j+8]; avx2: acc0[j], acc1[j]
+      for (int i = 0; i < pd; i += 16) {
+        const int e0 = i + j, e1 = i + 8 + j;
+        const float x0 = __fmaf_rn(static_cast<float>(c[e0]), a.scale[e0], a.vmin[e0]);
+        const float x1 = __fmaf_rn(static_cast<float>(c[e1]), a.scale[e1], a.vmin[e1]);
+        if (l2) {
+          const float d0 = __fsub_rn(q_s[e0], x0), d1 = __fsub_rn(q_s[e1], x1);
+          a0 = __fmaf_rn(d0, d0, a0);
+          a1 = __fmaf_rn(d1, d1, a1);
+        } else {
+          a0 = __fmaf_rn(q_s[e0], x0, a0);
+          a1 = __fmaf_rn(q_s[e1], x1, a1);
+        }
+      }
+      float v = __fadd_rn(a0, a1);
+      if (a.order == kOrderAvx512) {
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+      } else {
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+      }
+      r = v;
+    } else {
+      float s = 0.f;
+      if (j == 0) {
+        for (int e = 0; e < pd; ++e) {
+          const float xv = __fadd_rn(a.vmin[e], __fmul_rn(static_cast<float>(c[e]), a.scale[e]));
+          if (l2) {
+            const float d = __fsub_rn(q_s[e], xv);
+            s = __fadd_rn(s, __fmul_rn(d, d));
+          } else {
+            s = __fadd_rn(s, __fmul_rn(q_s[e], xv));
+          }
+        }
+      }
+      r = __shfl_sync(0xFFFFFFFFu, s, threadIdx.x & 24);
+    }
+  }
+  return l2 ? r : -r;
+}
+
+// Distances of ids[0..n) (n <= 32) into d[0..n), four rows per pass.
+template <bool kSq8>
+__device__ void dists_of(const HnswArgs& a, const float* q_s, const uint32_t* ids, float* d, int n,
+                         bool l2) {
+  const int lane = threadIdx.x & 31, g = lane >> 3;
+  for (int i = 0; i < n; i += 4) {
+    const int my = i + g;
+    const uint32_t row = ids[my < n ? my : i];
+    const float v = group_dist<kSq8>(a, q_s, row, l2);
+    if ((lane & 7) == 0 && my < n) d[my] = v;
+  }
+  __syncwarp();
+}
+
+// Number of elements of the ascending arr[b..b+n) strictly below key (warp-cooperative).
+__device__ __forceinline__ int count_below(const uint64_t* arr, int b, int n, uint64_t key) {
+  const int lane = threadIdx.x & 31;
+  int c = 0;
+  for (int i = lane; i < n; i += 32) c += arr[b + i] < key ? 1 : 0;
+  return __reduce_add_sync(0xFFFFFFFFu, c);
+}
+
+// Inserts key into the ascending arr[b..b+n) keeping order; arr must have room at b + n.
+__device__ __forceinline__ void insert_sorted(uint64_t* arr, int b, int n, uint64_t key) {
+  const int lane = threadIdx.x & 31;
+  const int p = count_below(arr, b, n, key);
+  // Shift arr[b+p .. b+n) up by one, top chunk first.
+  for (int hi = n; hi > p; hi -= 32) {
+    const int i = hi - 1 - lane;
+    uint64_t v = 0;
+    const bool mv = i >= p;
+    if (mv) v = arr[b + i];
+    __syncwarp();
+    if (mv) arr[b + i + 1] = v;
+    __syncwarp();
+  }
+  if (lane == 0) arr[b + p] = key;
+  __syncwarp();
+}
+
+template <bool kSq8>
+__global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const HnswArgs a) {
+  extern __shared__ __align__(16) uint8_t hsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = blockIdx.x * kHnswWarps + warp;
+  if (q >= a.nq) return;
+  const int pd = a.pd;
+  const size_t per_warp = HnswWarpSmemBytes(pd, a.hash_bits, a.ef, a.cand_cap);
+  uint8_t* base = hsm + warp * per_warp;
+  WarpSmem s;
+  s.q = reinterpret_cast<float*>(base);
+  s.hash = reinterpret_cast<uint32_t*>(base + static_cast<size_t>(pd) * 4);
+  s.res = reinterpret_cast<uint64_t*>(s.hash + (1u << a.hash_bits));
+  s.cand = s.res + a.ef;
+  s.nb_id = reinterpret_cast<uint32_t*>(s.cand + a.cand_cap);
+  s.nb_d = reinterpret_cast<float*>(s.nb_id + 32);
+  for (int i = lane; i < pd; i += 32) s.q[i] = a.queries[static_cast<size_t>(q) * pd + i];
+  for (int i = lane; i < (1 << a.hash_bits); i += 32) s.hash[i] = kEmpty;
+  __syncwarp();
+  const bool l2 = a.metric == 0;
+  const uint64_t n = a.n;
+  uint64_t dc = 0;
+  int nres = 0;
+  bool bad = false;
+
+  if (a.max_level >= 0 && n > 0) {
+    // Entry point and greedy descent over layers max_level..1.
+    uint32_t cur = a.entry;
+    if (lane == 0) s.nb_id[0] = cur;
+    __syncwarp();
+    dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, 1, l2);
+    float curd = s.nb_d[0];
+    dc = 1;
+    for (int layer = a.max_level; layer > 0 && !bad; --layer) {
+      for (int iter = 0; iter < a.step_limit; ++iter) {
+        const uint32_t* ll = a.upper + a.upper_off[cur] + static_cast<size_t>(layer - 1) * (1 + a.M);
+        const uint32_t cnt = ll[0];
+        __syncwarp();
+        if (lane < static_cast<int>(cnt)) {
+          const uint32_t e = ll[1 + lane];
+          // A valid graph only links nodes present on this layer (HnswGraph::check).
+          const bool ok_e = e < n && a.level[e] >= layer;
+          s.nb_id[lane] = ok_e ? e : 0u;
+          if (!ok_e) bad = true;
+        }
+        bad = __any_sync(0xFFFFFFFFu, bad);
+        __syncwarp();
+        if (bad) {
+          if (lane == 0) set_error(a.status, kDevBadIndex);
+          break;
+        }
+        dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, static_cast<int>(cnt), l2);
+        dc += cnt;
+        // Strict improvements in list order end at the first occurrence of the minimum.
+        float m = lane < static_cast<int>(cnt) ? s.nb_d[lane] : INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fminf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        if (!(m < curd)) break;
+        const uint32_t at = __ballot_sync(0xFFFFFFFFu, lane < static_cast<int>(cnt) && s.nb_d[lane] == m);
+        cur = s.nb_id[__ffs(at) - 1];
+        curd = m;
+      }
+    }
+
+    // Layer 0: ef-beam.
+    const int ef = a.ef;
+    const bool filtered = a.allow != nullptr;
+    auto allowed = [&](uint32_t id) { return !filtered || ((a.allow[id >> 5] >> (id & 31)) & 1u); };
+    bool full = false;
+    if (lane == 0) visit(s.hash, a.hash_bits, cur, &full);
+    float lower = INFINITY;
+    int chead = 0, ncand = 0;
+    if (allowed(cur)) {
+      if (lane == 0) s.res[0] = pack_neighbor(curd, cur);
+      nres = 1;
+      lower = curd;
+    }
+    if (lane == 0) s.cand[0] = pack_neighbor(curd, cur);
+    ncand = 1;
+    __syncwarp();
+    int steps = 0;
+    while (ncand > 0 && !bad) {
+      const uint64_t c = s.cand[chead];
+      const float cd = neighbor_dist(c);
+      if (cd > lower && (!filtered || nres >= ef)) break;
+      ++chead;
+      --ncand;
+      if (++steps > a.step_limit) {
+        if (lane == 0) set_error(a.status, kDevStepLimit);
+        bad = true;
+        break;
+      }
+      const uint32_t cid = neighbor_id(c);
+      const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
+      const uint32_t cnt = ll[0];
+      uint32_t e = 0;
+      bool fresh = false;
+      if (lane < static_cast<int>(cnt)) {
+        e = ll[1 + lane];
+        if (e >= n) {
+          bad = true;
+        } else {
+          fresh = visit(s.hash, a.hash_bits, e, &full);
+        }
+      }
+      if (__any_sync(0xFFFFFFFFu, bad || full)) {
+        if (lane == 0) set_error(a.status, full ? kDevOverflow : kDevBadIndex);
+        bad = true;
+        break;
+      }
+      const uint32_t fm = __ballot_sync(0xFFFFFFFFu, fresh);
+      const int nf = __popc(fm);
+      if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
+      __syncwarp();
+      dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
+      dc += static_cast<uint64_t>(nf);
+      // Heap updates in list order (the fresh neighbours keep their list order).
+      for (int i = 0; i < nf; ++i) {
+        const uint32_t id = s.nb_id[i];
+        const float de = s.nb_d[i];
+        if (nres < ef || de < lower) {
+          const uint64_t key = pack_neighbor(de, id);
+          if (chead + ncand >= a.cand_cap) {
+            // Compact to the front; if still full, drop the farthest candidate when it can never
+            // be expanded again (results full and it lies beyond the current worst result).
+            for (int k0 = 0; k0 < ncand; k0 += 32) {
+              const int k = k0 + lane;
+              uint64_t v = 0;
+              if (k < ncand) v = s.cand[chead + k];
+              __syncwarp();
+              if (k < ncand) s.cand[k] = v;
+              __syncwarp();
+            }
+            chead = 0;
+            if (ncand >= a.cand_cap) {
+              if (nres >= ef && neighbor_dist(s.cand[ncand - 1]) > lower) {
+                --ncand;
+              } else {
+                if (lane == 0) set_error(a.status, kDevOverflow);
+                bad = true;
+                break;
+              }
+            }
+          }
+          insert_sorted(s.cand, chead, ncand, key);
+          ++ncand;
+          if (allowed(id)) {
+            if (nres < ef) {
+              insert_sorted(s.res, 0, nres, key);
+              ++nres;
+            } else {
+              // Push then evict the greatest: only changes anything when key is below the max.
+              if (key < s.res[ef - 1]) {
+                __syncwarp();
+                insert_sorted(s.res, 0, ef - 1, key);
+              }
+            }
+            lower = neighbor_dist(s.res[nres - 1]);
+          }
+        }
+      }
+    }
+  }
+
+  // Output: the k best results; HNSW-SQ8 re-ranks the best `depth` on fp32 rows first.
+  int nout = nres < a.k_graph ? nres : a.k_graph;
+  if (!bad && kSq8 && a.depth > 0 && nout > 0) {
+    // Rerank (src/index/index.cc:89-95): exact fp32 distances of the graph's best candidates.
+    for (int i = 0; i < nout; i += 4) {
+      uint32_t r[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) r[c] = neighbor_id(s.res[i + c < nout ? i + c : i]);
+      float d[4];
+      if (a.order == kOrderAvx512 && pd <= 8 * 32 + 16) {
+        warp_exact_dist4_avx512<8>(s.q, a.rows, r, nout - i, pd, l2, d);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          d[c] = warp_exact_dist(s.q, a.rows + static_cast<size_t>(r[c]) * pd, pd, l2, a.order);
+      }
+      __syncwarp();
+      if (lane < 4 && i + lane < nout) {
+        float dl = d[0];
+        uint32_t rl = r[0];
+#pragma unroll
+        for (int c = 1; c < 4; ++c) {
+          dl = lane == c ? d[c] : dl;
+          rl = lane == c ? r[c] : rl;
+        }
+        s.cand[i + lane] = pack_neighbor(dl, rl);
+      }
+      __syncwarp();
+    }
+    dc += static_cast<uint64_t>(nout);
+    // Sort the re-ranked candidates (insertion into res, nout <= ef).
+    for (int i = 0; i < nout; ++i) {
+      const uint64_t key = s.cand[i];
+      __syncwarp();
+      insert_sorted(s.res, 0, i, key);
+    }
+  }
+  const int kout = a.k;
+  for (int i = lane; i < kout; i += 32) {
+    const size_t o = static_cast<size_t>(q) * kout + i;
+    if (!bad && i < nout) {
+      a.out_dist[o] = neighbor_dist(s.res[i]);
+      a.out_row[o] = neighbor_id(s.res[i]);
+    } else {
+      a.out_dist[o] = INFINITY;
+      a.out_row[o] = UINT32_MAX;
+    }
+  }
+  if (lane == 0 && a.out_dc != nullptr) a.out_dc[q] = dc;
+}
+
+}  // namespace
+
+cudaError_t LaunchHnswSearch(const HnswArgs& a, cudaStream_t stream) {
+  const size_t smem = kHnswWarps * HnswWarpSmemBytes(a.pd, a.hash_bits, a.ef, a.cand_cap);
+  const int blocks = (a.nq + kHnswWarps - 1) / kHnswWarps;
+  cudaError_t e;
+  if (a.codes != nullptr) {
+    e = cudaFuncSetAttribute(hnsw_search_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    hnsw_search_kernel<true><<<blocks, kHnswWarps * 32, smem, stream>>>(a);
+  } else {
+    e = cudaFuncSetAttribute(hnsw_search_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    hnsw_search_kernel<false><<<blocks, kHnswWarps * 32, smem, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace vdbgpu

@@ -1,0 +1,50 @@
+// Batched HNSW beam search (one warp per query) over the reference's serialized graphs.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace vdbgpu {
+
+struct HnswArgs {
+  int nq, pd;
+  int k;           // results written per query
+  int k_graph;     // results the graph search keeps (HnswSq8: max(depth, k))
+  int ef;          // beam width (already max(ef, k_graph))
+  int depth;       // HNSW-SQ8 re-rank depth on fp32 rows (0 = none)
+  int metric;      // 0 = L2, else minus the dot product
+  int order;       // SumOrder of the reference kernel set
+  const float* queries;
+  const float* rows;       // fp32 rows (float space, re-rank)
+  const uint8_t* codes;    // SQ8 codes (SQ8 space) or null
+  const float* vmin;
+  const float* scale;
+  const uint32_t* links0;  // cap * (1 + M0)
+  uint32_t M0;
+  const uint32_t* upper;
+  const uint64_t* upper_off;
+  const uint8_t* level;
+  uint32_t M;
+  int max_level;
+  uint32_t entry;
+  uint64_t n;              // nodes (graph capacity = rows)
+  const uint32_t* allow;   // allowed-row bitset (32 per word) or null
+  int hash_bits;           // visited hash: 1 << hash_bits slots per warp
+  int cand_cap;            // candidate array capacity per warp
+  int step_limit;          // bounded walk: expansions per query
+  float* out_dist;
+  uint32_t* out_row;
+  uint64_t* out_dc;        // distance computations per query (device) or null
+  int* status;
+};
+
+// Shared memory of one query's warp: query, visited hash, results, candidates, neighbour scratch.
+__host__ __device__ inline size_t HnswWarpSmemBytes(int pd, int hash_bits, int ef, int cand_cap) {
+  const size_t b = static_cast<size_t>(pd) * 4 + (static_cast<size_t>(1) << hash_bits) * 4 +
+                   static_cast<size_t>(ef) * 8 + static_cast<size_t>(cand_cap) * 8 + 32 * 4 + 32 * 4;
+  return (b + 15) / 16 * 16;
+}
+cudaError_t LaunchHnswSearch(const HnswArgs& a, cudaStream_t stream);
+
+}  // namespace vdbgpu

@@ -1,13 +1,166 @@
-// Loaders for the graph (HNSW, HNSW-SQ8) and list (PQ-flat, IVF-PQ) index types.
+// GPU indexes loaded from the reference's graph and list index files:
+//   HnswIndex     (src/index/hnsw/hnsw_index.h:12-41, file body hnsw_index.cc:36-48)
+//   HnswSq8Index  (hnsw_index.h:63-96, file body hnsw_index.cc:104-129)
+//   PqFlatIndex / IvfPqIndex (src/index/quant/ivf_pq.h) in index_ivfpq.cc
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
 #include "formats.h"
+#include "hnsw.cuh"
 #include "runtime.h"
 
 namespace vdbgpu {
 
-Status LoadGraphOrListIndex(Context&, int type, std::string_view, int, const float*, uint64_t,
-                            uint32_t, uint32_t, std::unique_ptr<GpuIndex>*) {
-  return Status(Status::kNotSupported,
-                "index type " + std::to_string(type) + " is not available on the GPU yet");
+Status LoadIvfPqIndex(Context& ctx, int type, std::string_view body, int metric, const float* rows,
+                      uint64_t n, uint32_t dim, uint32_t pd, std::unique_ptr<GpuIndex>* out);
+
+namespace {
+
+template <class T>
+Status Upload(Context& ctx, const std::vector<T>& v, DeviceBuffer* out) {
+  VDBGPU_RETURN_IF_ERROR(out->alloc(std::max<size_t>(1, v.size()) * sizeof(T)));
+  if (!v.empty())
+    VDBGPU_CUDA(cudaMemcpyAsync(out->get(), v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice,
+                                ctx.stream()));
+  return Status::OK();
+}
+
+int Log2Ceil(uint64_t x) {
+  int b = 0;
+  while ((uint64_t{1} << b) < x) ++b;
+  return b;
+}
+
+class HnswGpuIndex final : public GpuIndex {
+ public:
+  explicit HnswGpuIndex(bool sq8) : sq8_(sq8) {}
+  int type() const override { return sq8_ ? kIndexHnswSq8 : kIndexHnsw; }
+  uint64_t rows() const override { return n_; }
+  uint64_t device_bytes() const override {
+    return rows_.size() + codes_.size() + links0_.size() + upper_.size() + upper_off_.size() +
+           level_.size() + vmin_.size() + scale_.size();
+  }
+
+  Status Load(Context& ctx, std::string_view body, const float* rows, uint64_t n) {
+    n_ = n;
+    Reader r(body);
+    if (!sq8_) {
+      uint32_t fpd = 0;
+      if (!r.u32(&fpd) || fpd != pd) return Status(Status::kCorruption, "hnsw dim mismatch");
+    } else {
+      uint64_t fn = 0;
+      if (!r.u64(&fn) || fn != n) return Status(Status::kCorruption, "hnsw-sq8 index does not match the segment");
+      Sq8Data q;
+      VDBGPU_RETURN_IF_ERROR(ParseSq8(r, &q));
+      if (q.pd != pd) return Status(Status::kCorruption, "hnsw-sq8 index does not match the segment");
+      std::string_view codes;
+      if (!r.bytes(n * pd, &codes)) return Status(Status::kCorruption, "truncated sq8 codes");
+      VDBGPU_RETURN_IF_ERROR(Upload(ctx, q.vmin, &vmin_));
+      VDBGPU_RETURN_IF_ERROR(Upload(ctx, q.scale, &scale_));
+      VDBGPU_RETURN_IF_ERROR(codes_.alloc(std::max<uint64_t>(1, n * pd)));
+      if (n > 0)
+        VDBGPU_CUDA(cudaMemcpyAsync(codes_.get(), codes.data(), n * pd, cudaMemcpyHostToDevice, ctx.stream()));
+    }
+    VDBGPU_RETURN_IF_ERROR(ParseHnswGraph(r, n, &g_));
+    VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.links0, &links0_));
+    VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.upper, &upper_));
+    VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.upper_off, &upper_off_));
+    VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.level, &level_));
+    VDBGPU_RETURN_IF_ERROR(rows_.alloc(std::max<uint64_t>(1, n * pd) * sizeof(float)));
+    if (n > 0)
+      VDBGPU_CUDA(cudaMemcpyAsync(rows_.get(), rows, n * pd * sizeof(float), cudaMemcpyDefault, ctx.stream()));
+    // The graph arrays on the host are no longer needed.
+    g_.links0 = {};
+    g_.upper = {};
+    g_.upper_off = {};
+    g_.level = {};
+    return ctx.Sync("hnsw index load");
+  }
+
+  // HnswIndex::search (hnsw_index.cc:22-34) / HnswSq8Index::search (hnsw_index.cc:82-102).
+  Status Search(Context& ctx, const SearchBatch& b) override {
+    const uint64_t k = b.k;
+    const uint64_t pef = b.params.ef;
+    uint64_t depth = 0, kg = k, ef = std::max(pef, k);
+    if (sq8_) {
+      depth = b.params.rerank < 0 ? std::max(pef, k) : static_cast<uint64_t>(b.params.rerank);
+      ef = std::max({pef, k, depth});
+      kg = depth == 0 ? k : std::max(depth, k);
+      ef = std::max(ef, kg);
+    }
+    if (ef > 4096) return Status(Status::kNotSupported, "ef above 4096 is not supported on the GPU");
+    HnswArgs a{};
+    a.nq = static_cast<int>(b.nq);
+    a.pd = static_cast<int>(pd);
+    a.k = static_cast<int>(k);
+    a.k_graph = static_cast<int>(kg);
+    a.ef = static_cast<int>(ef);
+    a.depth = static_cast<int>(depth);
+    a.metric = metric;
+    a.order = ctx.order();
+    a.queries = b.queries;
+    a.rows = rows_.as<float>();
+    a.codes = sq8_ ? codes_.as<uint8_t>() : nullptr;
+    a.vmin = sq8_ ? vmin_.as<float>() : nullptr;
+    a.scale = sq8_ ? scale_.as<float>() : nullptr;
+    a.links0 = links0_.as<uint32_t>();
+    a.M0 = g_.M0;
+    a.upper = upper_.as<uint32_t>();
+    a.upper_off = upper_off_.as<uint64_t>();
+    a.level = level_.as<uint8_t>();
+    a.M = g_.M;
+    a.max_level = g_.size > 0 ? g_.max_level : -1;
+    a.entry = g_.entry;
+    a.n = n_;
+    a.allow = b.allow;
+    a.cand_cap = static_cast<int>(2 * ef + 64);
+    a.step_limit = 1 << 22;
+    a.out_dist = b.out_dist;
+    a.out_row = b.out_row;
+    a.out_dc = b.dist_comps;
+    a.status = ctx.status_word();
+    // Visited hash sized for the walk; on overflow the batch reruns with a table twice as large.
+    int bits = std::max(11, Log2Ceil(32 * ef));
+    for (;;) {
+      a.hash_bits = bits;
+      const size_t smem = 4 * HnswWarpSmemBytes(a.pd, bits, a.ef, a.cand_cap);
+      if (smem > 227 * 1024)
+        return Status(Status::kResourceExhausted, "HNSW search state does not fit in shared memory");
+      ctx.Mark(0);
+      ctx.Mark(1);
+      VDBGPU_CUDA(LaunchHnswSearch(a, ctx.stream()));
+      ctx.Mark(2);
+      ctx.Mark(3);
+      Status s = ctx.Sync("hnsw search");
+      if (s.ok()) return s;
+      if (s.message().find("code 6") == std::string::npos || bits >= 16) return s;
+      ++bits;  // visited table overflow (kDevOverflow): retry larger
+    }
+  }
+
+ private:
+  bool sq8_;
+  uint64_t n_ = 0;
+  HnswGraphData g_;
+  DeviceBuffer rows_, codes_, vmin_, scale_, links0_, upper_, upper_off_, level_;
+};
+
+}  // namespace
+
+Status LoadGraphOrListIndex(Context& ctx, int type, std::string_view body, int metric,
+                            const float* rows, uint64_t n, uint32_t dim, uint32_t pd,
+                            std::unique_ptr<GpuIndex>* out) {
+  if (type == kIndexHnsw || type == kIndexHnswSq8) {
+    auto idx = std::make_unique<HnswGpuIndex>(type == kIndexHnswSq8);
+    idx->metric = metric;
+    idx->dim = dim;
+    idx->pd = pd;
+    VDBGPU_RETURN_IF_ERROR(idx->Load(ctx, body, rows, n));
+    *out = std::move(idx);
+    return Status::OK();
+  }
+  return LoadIvfPqIndex(ctx, type, body, metric, rows, n, dim, pd, out);
 }
 
 }  // namespace vdbgpu
