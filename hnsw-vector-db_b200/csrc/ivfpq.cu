@@ -1,0 +1,339 @@
+// IVF-PQ and PQ-flat ADC scan with re-rank (sm_100a): one CTA of four warps per query.
+//
+// Follows IvfPqIndex::search (src/index/quant/ivf_pq.cc:169-222) and PqFlatIndex::search
+// (:59-76) float operation for float:
+//   * the probed lists and their coarse distances come from the GPU flat search over the coarse
+//     centroids (same kernel-set summation order as the reference's dist_);
+//   * tables: precomputed L2 uses table = term2[l] + 2 * (-<q_j, C_j[c]>) (:190-205), residual L2
+//     uses L2SqAny(q_j - c_j, C_j[c]) (:206-208), inner product / cosine one shared
+//     -DotAny(q_j, C_j[c]) table with offset -DotAny(q, c) (:191, 209-211); DotAny / L2SqAny keep
+//     the reference's four accumulators (src/distance/scalar.cc:43-73);
+//   * ADC: four partial sums over the m sub-quantisers (ProductQuantizer::adc, pq.h:36-47), then
+//     offset + adc;
+//   * TopK(R) by (dist, id) over all probed rows, then Rerank on fp32 rows (index.cc:89-95).
+// The four warps share the query's tables in shared memory and split each list's rows; each warp
+// keeps its own candidate buffer and threshold (exact: a warp's threshold is the R-th best of
+// the entries it has seen, and the tighter of the warps' thresholds is shared as an inclusive
+// bound), and the buffers are merged at the end.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "ivfpq.cuh"
+#include "warp_ops.cuh"
+
+namespace vdbgpu {
+namespace {
+
+constexpr int kIvfWarps = 4;
+constexpr int kIvfCap = 512;  // candidates per warp buffer
+constexpr uint64_t kNone = ~0ull;
+
+__device__ __forceinline__ float dot_any(const float* a, const float* b, int d) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= d; i += 4) {
+    s0 = __fadd_rn(s0, __fmul_rn(a[i], b[i]));
+    s1 = __fadd_rn(s1, __fmul_rn(a[i + 1], b[i + 1]));
+    s2 = __fadd_rn(s2, __fmul_rn(a[i + 2], b[i + 2]));
+    s3 = __fadd_rn(s3, __fmul_rn(a[i + 3], b[i + 3]));
+  }
+  for (; i < d; ++i) s0 = __fadd_rn(s0, __fmul_rn(a[i], b[i]));
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+__device__ __forceinline__ float l2_any(const float* a, const float* b, int d) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= d; i += 4) {
+    const float t0 = __fsub_rn(a[i], b[i]), t1 = __fsub_rn(a[i + 1], b[i + 1]);
+    const float t2 = __fsub_rn(a[i + 2], b[i + 2]), t3 = __fsub_rn(a[i + 3], b[i + 3]);
+    s0 = __fadd_rn(s0, __fmul_rn(t0, t0));
+    s1 = __fadd_rn(s1, __fmul_rn(t1, t1));
+    s2 = __fadd_rn(s2, __fmul_rn(t2, t2));
+    s3 = __fadd_rn(s3, __fmul_rn(t3, t3));
+  }
+  for (; i < d; ++i) {
+    const float t = __fsub_rn(a[i], b[i]);
+    s0 = __fadd_rn(s0, __fmul_rn(t, t));
+  }
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+// ProductQuantizer::adc over one code (m bytes), four partial sums.
+__device__ __forceinline__ float adc(const float* table, const uint8_t* __restrict__ code, int m) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int j = 0;
+  if ((m & 3) == 0) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(code);
+    for (; j + 4 <= m; j += 4) {
+      const uint32_t c = __ldg(&w[j >> 2]);
+      s0 = __fadd_rn(s0, table[(j + 0) * 256 + (c & 0xFFu)]);
+      s1 = __fadd_rn(s1, table[(j + 1) * 256 + ((c >> 8) & 0xFFu)]);
+      s2 = __fadd_rn(s2, table[(j + 2) * 256 + ((c >> 16) & 0xFFu)]);
+      s3 = __fadd_rn(s3, table[(j + 3) * 256 + (c >> 24)]);
+    }
+  } else {
+    for (; j + 4 <= m; j += 4) {
+      s0 = __fadd_rn(s0, table[(j + 0) * 256 + code[j + 0]]);
+      s1 = __fadd_rn(s1, table[(j + 1) * 256 + code[j + 1]]);
+      s2 = __fadd_rn(s2, table[(j + 2) * 256 + code[j + 2]]);
+      s3 = __fadd_rn(s3, table[(j + 3) * 256 + code[j + 3]]);
+    }
+    for (; j < m; ++j) s0 = __fadd_rn(s0, table[j * 256 + code[j]]);
+  }
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+// Keeps the `keep` smallest packed keys of buf[0..n) (n <= kIvfCap), sorted, at the front.
+__device__ int warp_keep_best(uint64_t* buf, int n, int keep) {
+  const int lane = threadIdx.x & 31;
+  uint64_t x[kIvfCap / 32];
+#pragma unroll
+  for (int e = 0; e < kIvfCap / 32; ++e) {
+    const int i = e * 32 + lane;
+    x[e] = i < n ? buf[i] : kNone;
+  }
+  warp_sort<kIvfCap / 32>(x);
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < kIvfCap / 32; ++e) buf[e * 32 + lane] = x[e];
+  __syncwarp();
+  return n < keep ? n : keep;
+}
+
+__global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a) {
+  extern __shared__ __align__(16) uint8_t ism[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = blockIdx.x;
+  const int m = a.m, ds = a.dsub, pd = a.pd, ts = m * 256;
+  float* q_s = reinterpret_cast<float*>(ism);                 // pd
+  float* r_s = q_s + pd;                                      // pd (residual)
+  float* table = r_s + pd;                                    // ts
+  float* qtab = table + ts;                                   // ts (precomputed L2 only)
+  uint64_t* bufs = reinterpret_cast<uint64_t*>(qtab + (a.mode == kIvfPrecomputed ? ts : 0));
+  uint64_t* buf = bufs + warp * kIvfCap;
+  __shared__ uint64_t tau_shared;
+  __shared__ float offset_s;
+  __shared__ int count_s[kIvfWarps];
+
+  for (int i = threadIdx.x; i < pd; i += blockDim.x) q_s[i] = a.queries[static_cast<size_t>(q) * pd + i];
+  if (threadIdx.x == 0) tau_shared = kNone;
+  __syncthreads();
+  const bool l2 = a.metric == 0;
+  // Per-query tables.
+  if (a.mode == kIvfPrecomputed) {
+    for (int i = threadIdx.x; i < ts; i += blockDim.x) {
+      const int j = i >> 8;
+      const float d = dot_any(q_s + j * ds, a.centroids + static_cast<size_t>(i) * ds, ds);
+      qtab[i] = __fmul_rn(-d, 2.f);
+    }
+  } else if (a.mode == kIvfShared || a.mode == kPqFlat) {
+    for (int i = threadIdx.x; i < ts; i += blockDim.x) {
+      const int j = i >> 8;
+      const float* cen = a.centroids + static_cast<size_t>(i) * ds;
+      table[i] = (l2 && a.mode == kPqFlat) ? l2_any(q_s + j * ds, cen, ds) : -dot_any(q_s + j * ds, cen, ds);
+    }
+  }
+  __syncthreads();
+
+  const int R = a.depth > a.k ? a.depth : a.k;  // TopK(max(depth, k))
+  uint64_t tau = kNone;                          // this warp's R-th best so far (exclusive)
+  int count = 0;
+  uint64_t dc = 0;
+  const uint32_t lt = (1u << lane) - 1u;
+  const int nprobe = a.mode == kPqFlat ? 1 : a.nprobe;
+  for (int pi = 0; pi < nprobe; ++pi) {
+    uint32_t l = 0;
+    float offset = 0.f;
+    if (a.mode != kPqFlat) {
+      l = a.probe_ids[static_cast<size_t>(q) * a.nprobe + pi];
+      if (static_cast<uint64_t>(l) >= a.nlist) {
+        if (threadIdx.x == 0) set_error(a.status, kDevBadIndex);
+        break;
+      }
+    }
+    if (a.mode == kIvfPrecomputed) {
+      offset = a.probe_dist[static_cast<size_t>(q) * a.nprobe + pi];
+      const float* t2 = a.term2 + static_cast<size_t>(l) * ts;
+      for (int i = threadIdx.x; i < ts; i += blockDim.x) table[i] = __fadd_rn(__ldg(&t2[i]), qtab[i]);
+    } else if (a.mode == kIvfResidual) {
+      const float* c = a.coarse + static_cast<size_t>(l) * pd;
+      for (int j = threadIdx.x; j < a.dim; j += blockDim.x) r_s[j] = __fsub_rn(q_s[j], c[j]);
+      __syncthreads();
+      for (int i = threadIdx.x; i < ts; i += blockDim.x) {
+        const int j = i >> 8;
+        table[i] = l2_any(r_s + j * ds, a.centroids + static_cast<size_t>(i) * ds, ds);
+      }
+    } else if (a.mode == kIvfShared) {
+      if (threadIdx.x == 0) offset_s = -dot_any(q_s, a.coarse + static_cast<size_t>(l) * pd, a.dim);
+      __syncthreads();
+      offset = offset_s;
+    }
+    __syncthreads();
+    // The tighter shared bound (another warp's R-th best, inclusive) also prunes this warp.
+    const uint64_t tb = tau_shared;
+    const uint64_t bound = tb < tau ? tb : tau;
+    const uint64_t b0 = a.mode == kPqFlat ? 0 : a.list_off[l];
+    const uint64_t e0 = a.mode == kPqFlat ? a.n : a.list_off[l + 1];
+    dc += e0 - b0;
+    uint64_t cur_bound = bound;
+    for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += kIvfWarps * 32) {
+      const uint64_t i = base + lane;
+      uint64_t key = kNone;
+      if (i < e0) {
+        const uint32_t id = a.mode == kPqFlat ? static_cast<uint32_t>(i) : __ldg(&a.ids[i]);
+        const bool ok = a.allow == nullptr || ((__ldg(&a.allow[id >> 5]) >> (id & 31)) & 1u);
+        if (ok) {
+          const float d = __fadd_rn(offset, adc(table, a.codes + i * m, m));
+          key = pack_neighbor(d, id);
+        }
+      }
+      const bool pass = key < cur_bound;
+      const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
+      if (pm != 0u) {
+        if (pass) buf[count + __popc(pm & lt)] = key;
+        count += __popc(pm);
+        __syncwarp();
+        if (count > kIvfCap - 32) {
+          count = warp_keep_best(buf, count, R);
+          if (count == R) {
+            tau = buf[R - 1];  // R-th best: later keys must be smaller (ids are unique)
+            cur_bound = tau < cur_bound ? tau : cur_bound;
+            if (lane == 0) atomicMin(reinterpret_cast<unsigned long long*>(&tau_shared), tau + 1);
+          }
+        }
+      }
+    }
+    __syncthreads();  // table is rebuilt for the next list
+  }
+  // Merge: every warp reduces to its R best, warp 0 merges the sorted lists.
+  count = warp_keep_best(buf, count, R);
+  if (lane == 0) count_s[warp] = count;
+  __syncthreads();
+  if (warp == 0) {
+    // Gather the candidates of all warps into warp 0's buffer region after its own R entries
+    // (bufs has kIvfWarps * kIvfCap slots; R <= 256 so the total fits in 1024 <= kIvfWarps * kIvfCap).
+    uint64_t* all = bufs;  // reuse: compact all warps' lists to the front
+    int total = count_s[0];
+    for (int w = 1; w < kIvfWarps; ++w) {
+      const int cw = count_s[w];
+      for (int i = lane; i < cw; i += 32) all[total + i] = bufs[w * kIvfCap + i];
+      total += cw;
+      __syncwarp();
+    }
+    // total <= 4 * R <= 1024
+    {
+      uint64_t x[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int i = e * 32 + lane;
+        x[e] = i < total ? all[i] : kNone;
+      }
+      warp_sort<32>(x);
+      __syncwarp();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) all[e * 32 + lane] = x[e];
+      __syncwarp();
+    }
+    const int ncand = total < R ? total : R;
+    int nout;
+    if (a.depth > 0) {
+      // Rerank the R best on fp32 rows (exact, reference kernel-set order), keep k.
+      for (int i = 0; i < ncand; i += 4) {
+        uint32_t r[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r[c] = neighbor_id(all[i + c < ncand ? i + c : i]);
+        float d[4];
+        if (a.order == kOrderAvx512 && pd <= 8 * 32 + 16) {
+          warp_exact_dist4_avx512<8>(q_s, a.rows, r, ncand - i, pd, l2, d);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            d[c] = warp_exact_dist(q_s, a.rows + static_cast<size_t>(r[c]) * pd, pd, l2, a.order);
+        }
+        __syncwarp();
+        if (lane < 4 && i + lane < ncand) {
+          float dl = d[0];
+          uint32_t rl = r[0];
+#pragma unroll
+          for (int c = 1; c < 4; ++c) {
+            dl = lane == c ? d[c] : dl;
+            rl = lane == c ? r[c] : rl;
+          }
+          all[i + lane] = pack_neighbor(dl, rl);
+        }
+        __syncwarp();
+      }
+      {
+        uint64_t x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = e * 32 + lane;
+          x[e] = i < ncand ? all[i] : kNone;
+        }
+        warp_sort<8>(x);
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 8; ++e) all[e * 32 + lane] = x[e];
+        __syncwarp();
+      }
+      dc += static_cast<uint64_t>(ncand);
+      nout = ncand < a.k ? ncand : a.k;
+    } else {
+      nout = ncand < a.k ? ncand : a.k;
+    }
+    for (int i = lane; i < a.k; i += 32) {
+      const size_t o = static_cast<size_t>(q) * a.k + i;
+      if (i < nout) {
+        a.out_dist[o] = neighbor_dist(all[i]);
+        a.out_row[o] = neighbor_id(all[i]);
+      } else {
+        a.out_dist[o] = INFINITY;
+        a.out_row[o] = UINT32_MAX;
+      }
+    }
+    if (lane == 0 && a.out_dc != nullptr)
+      a.out_dc[q] = (a.mode == kPqFlat ? 0 : a.nlist) + dc;
+  }
+}
+
+// IvfPqIndex::precompute_tables (src/index/quant/ivf_pq.cc:152-167): term2[l][j][c] =
+// DotAny(C_j[c], C_j[c]) + 2 * DotAny(coarse_l + j*dsub, C_j[c]).
+__global__ void term2_kernel(const float* __restrict__ coarse, uint32_t nlist, int pd,
+                             const float* __restrict__ centroids, int m, int ds, float* term2) {
+  const uint64_t ts = static_cast<uint64_t>(m) * 256;
+  const uint64_t total = nlist * ts;
+  for (uint64_t x = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total;
+       x += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t l = x / ts, i = x % ts;
+    const int j = static_cast<int>(i >> 8);
+    const float* cen = centroids + i * ds;
+    const float norm = dot_any(cen, cen, ds);
+    term2[x] = __fadd_rn(norm, __fmul_rn(2.f, dot_any(coarse + l * pd + j * ds, cen, ds)));
+  }
+}
+
+}  // namespace
+
+size_t IvfPqSmemBytes(int pd, int m, int mode) {
+  const size_t ts = static_cast<size_t>(m) * 256;
+  return (2 * static_cast<size_t>(pd) + ts + (mode == kIvfPrecomputed ? ts : 0)) * 4 +
+         static_cast<size_t>(kIvfWarps) * kIvfCap * 8;
+}
+
+cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream) {
+  const size_t smem = IvfPqSmemBytes(a.pd, a.m, a.mode);
+  cudaError_t e = cudaFuncSetAttribute(ivfpq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  ivfpq_kernel<<<a.nq, kIvfWarps * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchTerm2(const float* coarse, uint32_t nlist, int pd, const float* centroids, int m,
+                        int ds, float* term2, cudaStream_t stream) {
+  term2_kernel<<<2048, 256, 0, stream>>>(coarse, nlist, pd, centroids, m, ds, term2);
+  return cudaGetLastError();
+}
+
+}  // namespace vdbgpu
