@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "formats.h"
+#include "noalloc.h"
 #include "runtime.h"
 
 struct vdbgpu_ctx {
@@ -300,6 +301,48 @@ int vdbgpu_index_sq8_export(const vdbgpu_index* index, float* vmin, float* scale
   std::lock_guard<std::mutex> g(ctx->c->mu());
   cudaSetDevice(ctx->c->device());
   Status s = index->idx->ExportSq8(*ctx->c, vmin, scale, codes);
+  return s.ok() ? VDBGPU_OK : Fail(ctx, s);
+}
+
+int vdbgpu_index_search_noalloc(vdbgpu_index* index, const float* queries, uint64_t nq, uint32_t k,
+                                const vdbgpu_search_params* params, float* out_dist,
+                                uint32_t* out_row, void* stream) {
+  if (index == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  vdbgpu_ctx* ctx = index->ctx;
+  if (nq == 0 || k == 0) return VDBGPU_OK;
+  if (queries == nullptr || out_dist == nullptr || out_row == nullptr)
+    return Fail(ctx, Status(Status::kInvalidArgument, "null query or output buffer"));
+  vdbgpu::Context& c = *ctx->c;
+  std::lock_guard<std::mutex> g(c.mu());
+  cudaSetDevice(c.device());
+  // Host buffers would need staging copies in allocated memory: only device pointers are taken.
+  if (!IsDevicePtr(queries) || !IsDevicePtr(out_dist) || !IsDevicePtr(out_row))
+    return Fail(ctx, Status(Status::kInvalidArgument,
+                            "the allocation-free search takes device pointers for queries and outputs"));
+  vdbgpu::SearchBatch b{};
+  b.queries = queries;
+  b.nq = nq;
+  b.k = k;
+  if (params != nullptr) {
+    b.params.ef = params->ef;
+    b.params.nprobe = params->nprobe;
+    b.params.rerank = params->rerank;
+    b.params.strategy = params->strategy;
+  }
+  b.out_dist = out_dist;
+  b.out_row = out_row;
+  const vdbgpu::ScanOperands* op = nullptr;
+  int cpre = 0, depth = 0;
+  Status s = index->idx->ScanPlan(b, &op, &cpre, &depth);
+  if (!s.ok()) return Fail(ctx, s);
+  const cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : c.stream();
+  s = vdbgpu::ScanSearchNoAlloc(c, *op, index->idx->metric, index->idx->pd, b, cpre, depth, st);
+  if (!s.ok()) return Fail(ctx, s);
+  if (cudaStreamSynchronize(st) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    return Fail(ctx, vdbgpu::CudaStatus(e == cudaSuccess ? cudaErrorUnknown : e, "allocation-free search"));
+  }
+  s = c.CheckDeviceStatus("allocation-free search");
   return s.ok() ? VDBGPU_OK : Fail(ctx, s);
 }
 

@@ -96,6 +96,14 @@ class FlatGpuIndex final : public GpuIndex {
     return ctx.Sync("flat index build");
   }
 
+  Status ScanPlan(const SearchBatch& b, const ScanOperands** op, int* cpre, int* depth) const override {
+    if (b.k > 256) return Status(Status::kNotSupported, "k > 256 is not supported by the GPU flat path");
+    *op = &op_;
+    *cpre = static_cast<int>(std::max<uint32_t>(32, Pow2Ceil(2 * b.k)));
+    *depth = 0;
+    return Status::OK();
+  }
+
   // FlatIndex::search (src/index/flat_index.cc:73-77): exact top-k over allowed rows; counts
   // every row as a distance computation.
   Status Search(Context& ctx, const SearchBatch& b) override {
@@ -190,6 +198,18 @@ class Sq8FlatGpuIndex final : public GpuIndex {
     op_.scale = scale_.as<float>();
     VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, 0));
     return ctx.Sync("sq8 index build");
+  }
+
+  Status ScanPlan(const SearchBatch& b, const ScanOperands** op, int* cpre, int* depth) const override {
+    const int32_t rr = b.params.rerank;
+    const uint32_t d = rr < 0 ? std::max<uint32_t>(10 * b.k, 100) : static_cast<uint32_t>(rr);
+    const uint32_t need = std::max(d, b.k);
+    const uint32_t c = Pow2Ceil(need + need / 4);
+    if (c > 256) return Status(Status::kNotSupported, "re-rank depth above 204 is not supported on the GPU");
+    *op = &op_;
+    *cpre = static_cast<int>(c);
+    *depth = static_cast<int>(d);
+    return Status::OK();
   }
 
   // Exhaustive SQ8 scan: SQ8 distances to every code pick the `depth` best, which are re-ranked

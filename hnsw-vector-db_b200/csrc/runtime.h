@@ -208,6 +208,11 @@ class GpuIndex {
   virtual Status ExportSq8(Context&, float*, float*, uint8_t*) const {
     return Status(Status::kNotSupported, "index has no SQ8 codes");
   }
+  // For indexes searched by the tensor-core scan (flat, SQ8-flat): the scan operands and the
+  // candidate depths a search with these parameters uses.
+  virtual Status ScanPlan(const SearchBatch&, const struct ScanOperands**, int*, int*) const {
+    return Status(Status::kNotSupported, "index is not searched by the tensor-core scan");
+  }
 
   int metric = 0;
   uint32_t dim = 0;

@@ -75,6 +75,8 @@ _SIGNATURES = {
     "vdbgpu_index_get_info": (ctypes.c_int, [_P, ctypes.POINTER(IndexInfo)]),
     "vdbgpu_index_search": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32,
                                            ctypes.POINTER(SearchParams), _P, _P, _P, _P]),
+    "vdbgpu_index_search_noalloc": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32,
+                                                   ctypes.POINTER(SearchParams), _P, _P, _P]),
     "vdbgpu_index_file_inspect": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int)]),
     "vdbgpu_index_sq8_export": (ctypes.c_int, [_P, _P, _P, _P]),
 }
@@ -257,6 +259,17 @@ class Index:
                                          _ptr(dists), _ptr(ids), _ptr(dc))
         self.ctx.check(code)
         return (ids, dists, dc) if stats else (ids, dists)
+
+    def search_noalloc(self, queries, out_ids, out_dists, k: int = 10, rerank: int = -1, stream: int = 0):
+        """The allocation-free search (vdbgpu_index_search_noalloc): `queries` (nq <= 128, padded
+        dim) and the outputs are CUDA tensors on the index's device; nothing is allocated."""
+        p = SearchParams()
+        lib().vdbgpu_search_params_default(ctypes.byref(p))
+        p.rerank = int(rerank)
+        nq = int(queries.shape[0])
+        code = lib().vdbgpu_index_search_noalloc(self._h, _ptr(queries), nq, int(k), ctypes.byref(p),
+                                                 _ptr(out_dists), _ptr(out_ids), stream or None)
+        self.ctx.check(code)
 
     def sq8_export(self, with_codes: bool = True):
         """(vmin, scale, codes) of an SQ8 index (Sq8Quantizer, src/index/quant/sq8.h)."""

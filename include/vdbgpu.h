@@ -150,6 +150,23 @@ VDBGPU_API int vdbgpu_index_search(vdbgpu_index* index, const float* queries, ui
                         const vdbgpu_search_params* params, const uint64_t* allow_bits,
                         float* out_dist, uint32_t* out_row, uint64_t* out_dist_comps);
 
+/* Index::search for FLAT and SQ8_FLAT indexes without allocating any device memory. No
+ * counterpart in the reference: it exists for callers that must not allocate device memory while
+ * they search (a host whose device memory is owned by its own allocator, or a serving loop that
+ * cannot afford cudaMalloc's synchronisation or its failure under memory pressure).
+ * Scratch comes from a fixed array of about 8.4 MB compiled into the library, which every GPU that
+ * loads the library holds until the process exits; its device address is looked up on the first
+ * call on each device, so make that first call before any stream capture.
+ * Limits: nq <= 128 queries per call, padded_dim <= 256; larger requests fail with
+ * VDBGPU_INVALID_ARGUMENT. queries, out_dist and out_row must be device memory of the index's
+ * device (nq x padded_dim, nq x k, nq x k). Work is launched on `stream` (NULL: the context's
+ * stream) and the call returns once it has finished. All calls share the one scratch array: calls
+ * whose work overlaps on the GPU race and must be serialised by the caller. Results are those of
+ * vdbgpu_index_search with the same parameters (no filter, no statistics). */
+VDBGPU_API int vdbgpu_index_search_noalloc(vdbgpu_index* index, const float* queries, uint64_t nq,
+                                           uint32_t k, const vdbgpu_search_params* params,
+                                           float* out_dist, uint32_t* out_row, void* stream);
+
 /* CheckIndexFile (src/index/index.cc:46-56) + the magic dispatch of LoadIndex (index.cc:58-87)
  * without a GPU: verifies the CRC32C footer and reports the index type of the magic. */
 VDBGPU_API int vdbgpu_index_file_inspect(const void* file_bytes, size_t nbytes, int* type);
