@@ -23,6 +23,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_LIB = os.path.join(HERE, "_ref", "libvdbref.so")
+REF_ENGINE_LIB = os.path.join(HERE, "_ref", "libvdbref_engine.so")
 ORACLE_LIB = os.path.join(HERE, "liboracle.so")
 REFERENCE_SRC = os.environ.get("VDB_REFERENCE_SRC", "/root/reference")
 
@@ -35,7 +36,7 @@ def build(ref: bool = True) -> None:
     """Builds liboracle.so, and _ref/libvdbref.so when the reference sources are present."""
     targets = ["oracle"]
     if ref and os.path.isdir(os.path.join(REFERENCE_SRC, "src")):
-        targets.append("ref")
+        targets += ["ref", "engine"]
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REFERENCE_SRC}", "-j8"] + targets, check=True)
 
 
@@ -198,6 +199,90 @@ class RefIndex:
     def __del__(self):
         try:
             self.ref.l.ref_index_free(self.h)
+        except Exception:
+            pass
+
+
+class RefCollection:
+    """The reference's Collection (oracle/_ref/libvdbref_engine.so): bulk-loaded on-disk segments
+    with year / tags metadata, filtered batched search through its planner and merge."""
+
+    def __init__(self, path: str, dim: int, metric: str = "cosine", index: Optional[dict] = None,
+                 threads: int = 0, lib_path: str = REF_ENGINE_LIB):
+        import json
+        if not os.path.exists(lib_path):
+            raise ImportError(f"{lib_path} is missing (build with `make -C oracle engine`)")
+        l = ctypes.CDLL(lib_path)
+        sig = {
+            "ref_coll_last_error": (ctypes.c_char_p, []),
+            "ref_coll_create": (_P, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int]),
+            "ref_coll_free": (None, [_P]),
+            "ref_coll_bulk_load": (ctypes.c_int, [_P, _P, _P, ctypes.c_uint64, _P, _P, ctypes.c_uint32]),
+            "ref_coll_search_batch": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64,
+                                                     ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
+                                                     _P, _P]),
+            "ref_coll_explain": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int,
+                                                ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        self.l = l
+        self.dim = dim
+        self.path = path
+        opts = {"dim": dim, "metric": metric, "sync": "none",
+                "index": index or {"type": "hnsw", "M": 16, "ef_construction": 200},
+                "schema": [{"name": "year", "type": "int64"}, {"name": "tags", "type": "keyword_list"}]}
+        self.h = l.ref_coll_create(path.encode(), json.dumps(opts).encode(), threads)
+        if not self.h:
+            raise RuntimeError(l.ref_coll_last_error().decode())
+
+    def bulk_load(self, ids: np.ndarray, vectors: np.ndarray, years=None, tags=None):
+        v = np.ascontiguousarray(vectors[:, :self.dim], dtype=np.float32)
+        ids = np.ascontiguousarray(ids, dtype=np.uint64)
+        mt = 0 if tags is None else tags.shape[1]
+        rc = self.l.ref_coll_bulk_load(self.h, _ptr(ids), _ptr(v), ids.size,
+                                       _ptr(None if years is None else np.ascontiguousarray(years, np.int64)),
+                                       _ptr(None if tags is None else np.ascontiguousarray(tags, np.uint32)), mt)
+        if rc != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+
+    def search(self, q: np.ndarray, k=10, ef=64, nprobe=16, rerank=-1, strategy=0, filter=None):
+        import json
+        q = np.ascontiguousarray(q[:, :self.dim], dtype=np.float32)
+        nq = q.shape[0]
+        ids = np.empty((nq, k), np.uint64)
+        d = np.empty((nq, k), np.float32)
+        fj = None if filter is None else json.dumps(filter).encode()
+        rc = self.l.ref_coll_search_batch(self.h, _ptr(q), nq, k, ef, nprobe, rerank, strategy, fj,
+                                          _ptr(ids), _ptr(d))
+        if rc != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+        return ids, d
+
+    def explain(self, q: np.ndarray, k=10, ef=64, strategy=0, filter=None):
+        import json
+        q = np.ascontiguousarray(q[:self.dim], dtype=np.float32)
+        buf = ctypes.create_string_buffer(1 << 20)
+        fj = None if filter is None else json.dumps(filter).encode()
+        rc = self.l.ref_coll_explain(self.h, _ptr(q), k, ef, strategy, fj, buf, len(buf))
+        if rc != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+        return json.loads(buf.value.decode())
+
+    def segment_dirs(self):
+        d = os.path.join(self.path, "segments")
+        return sorted(os.path.join(d, x) for x in os.listdir(d) if x.startswith("seg-") and not x.endswith(".tmp"))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.l.ref_coll_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
         except Exception:
             pass
 

@@ -1,0 +1,163 @@
+// Test infrastructure, not product code.
+//
+// A C ABI over the reference's Collection (include/vdb/collection.h) for the multi-segment,
+// filtered read path: Collection::Create / BulkLoad (src/engine/collection_impl.cc:926-1016) with
+// year / tags metadata, Collection::SearchBatch (:1121-1136) and Collection::Search with explain
+// (:1036-1119: PrepareQuery, the per-segment planner of src/engine/planner.cc:42-129, and the
+// merge by (dist, part, row) with dedupe by external id). Built into oracle/_ref/
+// libvdbref_engine.so with shim/roaring.hh standing in for CRoaring (same set semantics).
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <nlohmann/json.hpp>
+#include <string>
+#include <vector>
+
+#include "engine/options_json.h"
+#include "vdb/collection.h"
+
+namespace {
+std::string g_err;
+}
+
+struct ref_coll {
+  std::unique_ptr<vdb::Collection> c;
+  size_t dim = 0;
+};
+
+extern "C" {
+
+const char* ref_coll_last_error() { return g_err.c_str(); }
+
+// options_json: the reference's collection options (engine/options_json.cc). Compaction and
+// background flushing are off so every bulk load stays its own on-disk segment.
+ref_coll* ref_coll_create(const char* path, const char* options_json, int threads) {
+  auto j = nlohmann::json::parse(options_json, nullptr, false);
+  if (j.is_discarded()) {
+    g_err = "options must be JSON";
+    return nullptr;
+  }
+  vdb::CollectionOptions o;
+  vdb::Status s = vdb::OptionsFromJson(j, &o);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return nullptr;
+  }
+  vdb::OpenOptions oo;
+  oo.num_threads = static_cast<size_t>(threads);
+  oo.auto_compact = false;
+  oo.auto_flush = false;
+  auto c = vdb::Collection::Create(path, o, oo);
+  if (!c.ok()) {
+    g_err = c.status().ToString();
+    return nullptr;
+  }
+  auto* h = new ref_coll;
+  h->c = std::move(c).value();
+  h->dim = o.dim;
+  return h;
+}
+
+void ref_coll_free(ref_coll* h) {
+  if (h == nullptr) return;
+  if (h->c) (void)h->c->Close();
+  delete h;
+}
+
+// One segment: n rows (dim floats each), external ids, year (int64) and up to max_tags tags per
+// row given as word ids (UINT32_MAX = unused), stored as keyword strings "w<id>".
+int ref_coll_bulk_load(ref_coll* h, const uint64_t* ids, const float* vectors, uint64_t n,
+                       const int64_t* years, const uint32_t* tags, uint32_t max_tags) {
+  std::vector<vdb::Metadata> md;
+  if (years != nullptr) {
+    md.resize(n);
+    for (uint64_t i = 0; i < n; ++i) {
+      md[i]["year"] = years[i];
+      std::vector<std::string> t;
+      for (uint32_t j = 0; j < max_tags; ++j) {
+        const uint32_t w = tags[i * max_tags + j];
+        if (w != UINT32_MAX) t.push_back("w" + std::to_string(w));
+      }
+      md[i]["tags"] = t;
+    }
+  }
+  vdb::Status s = h->c->BulkLoad(ids, vectors, n, years != nullptr ? &md : nullptr);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  return 0;
+}
+
+// Collection::SearchBatch with an optional JSON filter. Misses: UINT64_MAX / +inf.
+int ref_coll_search_batch(ref_coll* h, const float* q, uint64_t nq, uint32_t k, uint64_t ef,
+                          uint64_t nprobe, int rerank, int strategy, const char* filter_json,
+                          uint64_t* out_ids, float* out_dist) {
+  vdb::SearchParams p;
+  p.ef = ef;
+  p.nprobe = nprobe;
+  p.rerank = rerank;
+  p.strategy = static_cast<vdb::FilterStrategy>(strategy);
+  std::unique_ptr<vdb::Filter> f;
+  if (filter_json != nullptr) {
+    auto pf = h->c->ParseFilter(filter_json);
+    if (!pf.ok()) {
+      g_err = pf.status().ToString();
+      return static_cast<int>(pf.status().code());
+    }
+    f = std::move(pf).value();
+  }
+  std::vector<std::vector<vdb::SearchHit>> hits;
+  vdb::Status s = h->c->SearchBatch(q, nq, k, p, f.get(), &hits);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  for (uint64_t i = 0; i < nq; ++i)
+    for (uint32_t j = 0; j < k; ++j) {
+      const bool have = j < hits[i].size();
+      out_ids[i * k + j] = have ? hits[i][j].id : UINT64_MAX;
+      out_dist[i * k + j] = have ? hits[i][j].distance : INFINITY;
+    }
+  return 0;
+}
+
+// Collection::Search of one query with explain: per part (mutable first, then disk segments in
+// snapshot order) the strategy name, matches and distance computations, as JSON.
+int ref_coll_explain(ref_coll* h, const float* q, uint32_t k, uint64_t ef, int strategy,
+                     const char* filter_json, char* out, size_t cap) {
+  vdb::SearchRequest req;
+  req.vector = q;
+  req.k = k;
+  req.params.ef = ef;
+  req.params.strategy = static_cast<vdb::FilterStrategy>(strategy);
+  std::unique_ptr<vdb::Filter> f;
+  if (filter_json != nullptr) {
+    auto pf = h->c->ParseFilter(filter_json);
+    if (!pf.ok()) {
+      g_err = pf.status().ToString();
+      return static_cast<int>(pf.status().code());
+    }
+    f = std::move(pf).value();
+    req.filter = f.get();
+  }
+  std::vector<vdb::SearchHit> hits;
+  vdb::SearchExplain ex;
+  vdb::Status s = h->c->Search(req, &hits, &ex);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  nlohmann::json j = nlohmann::json::array();
+  for (const auto& e : ex.segments)
+    j.push_back({{"id", e.segment_id}, {"kind", e.kind}, {"strategy", e.strategy},
+                 {"matches", e.matches}, {"live_rows", e.live_rows}, {"ef", e.ef},
+                 {"distance_computations", e.distance_computations}, {"results", e.results}});
+  const std::string str = j.dump();
+  if (str.size() + 1 > cap) return -1;
+  std::memcpy(out, str.c_str(), str.size() + 1);
+  return 0;
+}
+
+}  // extern "C"
