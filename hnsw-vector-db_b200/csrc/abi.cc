@@ -7,6 +7,8 @@
 #include <new>
 #include <vector>
 
+#include "collection.h"
+#include "filter.h"
 #include "formats.h"
 #include "noalloc.h"
 #include "runtime.h"
@@ -20,6 +22,13 @@ struct vdbgpu_index {
   vdbgpu_ctx* ctx;
   std::unique_ptr<vdbgpu::GpuIndex> idx;
 };
+
+struct vdbgpu_collection {
+  vdbgpu_ctx* ctx;
+  std::unique_ptr<vdbgpu::GpuCollection> c;
+};
+
+static_assert(sizeof(vdbgpu_hit) == sizeof(vdbgpu::HitRecord), "vdbgpu_hit layout");
 
 namespace {
 
@@ -354,6 +363,262 @@ int vdbgpu_index_file_inspect(const void* file_bytes, size_t nbytes, int* type) 
   if (!s.ok()) return static_cast<int>(s.code());
   *type = vdbgpu::IndexTypeForMagic(magic);
   return *type < 0 ? VDBGPU_CORRUPTION : VDBGPU_OK;
+}
+
+
+// ------------------------------------------------------------------------------ collections
+
+namespace {
+
+vdbgpu::SearchParams ToParams(const vdbgpu_search_params* params) {
+  vdbgpu::SearchParams p;
+  if (params != nullptr) {
+    p.ef = params->ef;
+    p.nprobe = params->nprobe;
+    p.rerank = params->rerank;
+    p.strategy = params->strategy;
+    p.prefilter_threshold = params->prefilter_threshold;
+    p.post_filter_alpha = params->post_filter_alpha;
+  }
+  return p;
+}
+
+bool BadStrategy(const vdbgpu_search_params* params) {
+  return params != nullptr && (params->strategy < 0 || params->strategy > 3);
+}
+
+}  // namespace
+
+int vdbgpu_collection_open(vdbgpu_ctx* ctx, const char* path, uint32_t shard, uint32_t nshards,
+                           vdbgpu_collection** out) {
+  if (ctx == nullptr || path == nullptr || out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = nullptr;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  std::unique_ptr<vdbgpu::GpuCollection> c;
+  Status s = vdbgpu::GpuCollection::Open(*ctx->c, path, shard, nshards, &c);
+  if (!s.ok()) return Fail(ctx, s);
+  *out = new vdbgpu_collection{ctx, std::move(c)};
+  return VDBGPU_OK;
+}
+
+int vdbgpu_collection_create(vdbgpu_ctx* ctx, const char* options_json, vdbgpu_collection** out) {
+  if (ctx == nullptr || options_json == nullptr || out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = nullptr;
+  std::unique_ptr<vdbgpu::GpuCollection> c;
+  Status s = vdbgpu::GpuCollection::Create(options_json, &c);
+  if (!s.ok()) return Fail(ctx, s);
+  *out = new vdbgpu_collection{ctx, std::move(c)};
+  return VDBGPU_OK;
+}
+
+int vdbgpu_collection_add_segment(vdbgpu_collection* c, uint32_t segment_id, uint32_t ordinal,
+                                  const float* rows, uint64_t n, const uint64_t* ids, const void* meta,
+                                  size_t meta_bytes, const void* index_file, size_t index_bytes) {
+  if (c == nullptr || index_file == nullptr || (n > 0 && (rows == nullptr || ids == nullptr)))
+    return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(c->ctx->c->mu());
+  cudaSetDevice(c->ctx->c->device());
+  Status s = c->c->AddSegment(*c->ctx->c, segment_id, ordinal, rows, n, ids,
+                              meta != nullptr ? std::string_view(static_cast<const char*>(meta), meta_bytes)
+                                              : std::string_view(),
+                              std::string_view(static_cast<const char*>(index_file), index_bytes));
+  return s.ok() ? VDBGPU_OK : Fail(c->ctx, s);
+}
+
+int vdbgpu_collection_set_deleted(vdbgpu_collection* c, uint32_t segment_id, const uint32_t* bits) {
+  if (c == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(c->ctx->c->mu());
+  cudaSetDevice(c->ctx->c->device());
+  Status s = c->c->SetDeleted(*c->ctx->c, segment_id, bits);
+  return s.ok() ? VDBGPU_OK : Fail(c->ctx, s);
+}
+
+void vdbgpu_collection_free(vdbgpu_collection* c) {
+  if (c == nullptr) return;
+  if (c->ctx != nullptr && c->ctx->c) {
+    std::lock_guard<std::mutex> g(c->ctx->c->mu());
+    cudaSetDevice(c->ctx->c->device());
+    cudaStreamSynchronize(c->ctx->c->stream());
+    c->c.reset();
+  }
+  delete c;
+}
+
+int vdbgpu_collection_get_info(const vdbgpu_collection* c, vdbgpu_collection_info* out) {
+  if (c == nullptr || out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  const auto& o = c->c->options();
+  out->dim = o.dim;
+  out->padded_dim = o.pd;
+  out->metric = o.metric;
+  out->index_type = o.index_type;
+  out->segments_total = c->c->segments_total();
+  out->segments_local = static_cast<uint32_t>(c->c->segments_local());
+  out->rows_local = c->c->rows_local();
+  out->device_bytes = c->c->device_bytes();
+  return VDBGPU_OK;
+}
+
+int vdbgpu_collection_search_grouped(vdbgpu_collection* c, const float* queries, uint64_t nq, uint32_t k,
+                                     const vdbgpu_search_params* params, const char* const* filters,
+                                     uint32_t nfilters, const int32_t* query_filter, uint64_t* out_ids,
+                                     float* out_dist, vdbgpu_hit* out_hits) {
+  if (c == nullptr || (nq > 0 && queries == nullptr) || (nfilters > 0 && filters == nullptr) ||
+      ((out_ids == nullptr) != (out_dist == nullptr)))
+    return VDBGPU_INVALID_ARGUMENT;
+  if (BadStrategy(params)) return Fail(c->ctx, Status(Status::kInvalidArgument, "bad strategy"));
+  vdbgpu::GpuCollection::Request r;
+  r.queries = queries;
+  r.nq = nq;
+  r.k = k;
+  r.params = ToParams(params);
+  for (uint32_t i = 0; i < nfilters; ++i) {
+    if (filters[i] == nullptr) return Fail(c->ctx, Status(Status::kInvalidArgument, "null filter"));
+    r.filters.emplace_back(filters[i]);
+  }
+  r.query_filter = query_filter;
+  r.out_ids = out_ids;
+  r.out_dist = out_dist;
+  r.out_records = reinterpret_cast<vdbgpu::HitRecord*>(out_hits);
+  std::lock_guard<std::mutex> g(c->ctx->c->mu());
+  cudaSetDevice(c->ctx->c->device());
+  Status s = c->c->Search(*c->ctx->c, r);
+  return s.ok() ? VDBGPU_OK : Fail(c->ctx, s);
+}
+
+int vdbgpu_collection_search(vdbgpu_collection* c, const float* queries, uint64_t nq, uint32_t k,
+                             const vdbgpu_search_params* params, const char* filter_json, uint64_t* out_ids,
+                             float* out_dist) {
+  if (out_ids == nullptr || out_dist == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  const char* f[1] = {filter_json};
+  return vdbgpu_collection_search_grouped(c, queries, nq, k, params, f, filter_json != nullptr ? 1 : 0,
+                                          nullptr, out_ids, out_dist, nullptr);
+}
+
+int vdbgpu_collection_explain(vdbgpu_collection* c, const float* query, uint32_t k,
+                              const vdbgpu_search_params* params, const char* filter_json, char* out_json,
+                              size_t cap) {
+  if (c == nullptr || query == nullptr || out_json == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  if (BadStrategy(params)) return Fail(c->ctx, Status(Status::kInvalidArgument, "bad strategy"));
+  vdbgpu::GpuCollection::Request r;
+  r.queries = query;
+  r.nq = 1;
+  r.k = k;
+  r.params = ToParams(params);
+  if (filter_json != nullptr) r.filters.emplace_back(filter_json);
+  std::vector<std::vector<vdbgpu::PartExplain>> ex;
+  r.explain = &ex;
+  std::lock_guard<std::mutex> g(c->ctx->c->mu());
+  cudaSetDevice(c->ctx->c->device());
+  Status s = c->c->Search(*c->ctx->c, r);
+  if (!s.ok()) return Fail(c->ctx, s);
+  std::string j = "[";
+  for (size_t i = 0; i < ex[0].size(); ++i) {
+    const auto& e = ex[0][i];
+    if (i > 0) j += ",";
+    j += "{\"id\":" + std::to_string(e.segment_id) + ",\"strategy\":\"" + e.strategy +
+         "\",\"matches\":" + std::to_string(e.matches) + ",\"live_rows\":" + std::to_string(e.live_rows) +
+         ",\"distance_computations\":" + std::to_string(e.dc) + ",\"results\":" + std::to_string(e.results) +
+         "}";
+  }
+  j += "]";
+  if (j.size() + 1 > cap) return Fail(c->ctx, Status(Status::kResourceExhausted, "explain buffer too small"));
+  std::memcpy(out_json, j.c_str(), j.size() + 1);
+  return VDBGPU_OK;
+}
+
+int vdbgpu_collection_filter_bitmap(vdbgpu_collection* c, const char* filter_json, uint32_t segment_id,
+                                    uint32_t* out_words, uint64_t* matches) {
+  if (c == nullptr || filter_json == nullptr || out_words == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(c->ctx->c->mu());
+  cudaSetDevice(c->ctx->c->device());
+  Status s = c->c->FilterBitmap(*c->ctx->c, filter_json, segment_id, out_words, matches);
+  return s.ok() ? VDBGPU_OK : Fail(c->ctx, s);
+}
+
+int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists, uint64_t nq, uint32_t k,
+                      uint64_t* out_ids, float* out_dist, vdbgpu_hit* out_hits) {
+  if (ctx == nullptr || (nlists > 0 && nq > 0 && lists == nullptr) ||
+      ((out_ids == nullptr) != (out_dist == nullptr)))
+    return VDBGPU_INVALID_ARGUMENT;
+  if (k == 0 || k > 240) return Fail(ctx, Status(Status::kInvalidArgument, "k must be in 1..240"));
+  if (nq == 0) return VDBGPU_OK;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  vdbgpu::Context& cx = *ctx->c;
+  cudaStream_t st = cx.stream();
+  const size_t nrec = static_cast<size_t>(nlists) * nq * k;
+  const vdbgpu_hit* in = lists;
+  void* buf;
+  Status s;
+  if (nrec > 0 && !IsDevicePtr(lists)) {
+    s = cx.workspace(vdbgpu::kWsScratch0, nrec * sizeof(vdbgpu_hit), &buf);
+    if (!s.ok()) return Fail(ctx, s);
+    if (cudaMemcpyAsync(buf, lists, nrec * sizeof(vdbgpu_hit), cudaMemcpyHostToDevice, st) != cudaSuccess)
+      return Fail(ctx, Status(Status::kInternal, "copy hit lists"));
+    in = static_cast<const vdbgpu_hit*>(buf);
+  }
+  vdbgpu::MergeArgs ma{};
+  ma.kind = 1;
+  ma.nlists = static_cast<int>(nlists);
+  ma.k = static_cast<int>(k);
+  ma.nq = nq;
+  ma.records = reinterpret_cast<const vdbgpu::HitRecord*>(in);
+  const bool ids_dev = IsDevicePtr(out_ids) && IsDevicePtr(out_dist);
+  const bool hits_dev = IsDevicePtr(out_hits);
+  void *ib = nullptr, *db = nullptr, *hb = nullptr;
+  if (out_ids != nullptr) {
+    if (ids_dev) {
+      ma.out_ids = out_ids;
+      ma.out_dist = out_dist;
+    } else {
+      if (!(s = cx.workspace(vdbgpu::kWsScratch1, nq * k * 8, &ib)).ok()) return Fail(ctx, s);
+      if (!(s = cx.workspace(vdbgpu::kWsScratch2, nq * k * 4, &db)).ok()) return Fail(ctx, s);
+      ma.out_ids = static_cast<uint64_t*>(ib);
+      ma.out_dist = static_cast<float*>(db);
+    }
+  }
+  if (out_hits != nullptr) {
+    if (hits_dev) {
+      ma.out_records = reinterpret_cast<vdbgpu::HitRecord*>(out_hits);
+    } else {
+      if (!(s = cx.workspace(vdbgpu::kWsScratch3, nq * k * sizeof(vdbgpu_hit), &hb)).ok()) return Fail(ctx, s);
+      ma.out_records = static_cast<vdbgpu::HitRecord*>(hb);
+    }
+  }
+  if (vdbgpu::LaunchMerge(ma, st) != cudaSuccess) return Fail(ctx, Status(Status::kInternal, "merge launch"));
+  if (ib != nullptr) {
+    cudaMemcpyAsync(out_ids, ib, nq * k * 8, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(out_dist, db, nq * k * 4, cudaMemcpyDeviceToHost, st);
+  }
+  if (hb != nullptr) cudaMemcpyAsync(out_hits, hb, nq * k * sizeof(vdbgpu_hit), cudaMemcpyDeviceToHost, st);
+  s = cx.Sync("merge hits");
+  return s.ok() ? VDBGPU_OK : Fail(ctx, s);
+}
+
+int vdbgpu_filter_describe(const char* schema_json, const char* filter_json, char* out, size_t cap) {
+  if (schema_json == nullptr || filter_json == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::string text;
+  int rc = VDBGPU_OK;
+  vdbgpu::JsonValue sj;
+  vdbgpu::Schema schema;
+  Status s = vdbgpu::ParseJson(schema_json, &sj) ? vdbgpu::SchemaFromJson(sj, &schema)
+                                                 : Status(Status::kInvalidArgument, "schema must be JSON");
+  if (s.ok()) {
+    std::unique_ptr<vdbgpu::FilterExpr> f;
+    s = vdbgpu::FilterExpr::Parse(filter_json, schema, &f);
+    if (s.ok()) text = f->ToString();
+  }
+  if (!s.ok()) {
+    rc = static_cast<int>(s.code());
+    text = s.message();
+  }
+  if (out != nullptr && cap > 0) {
+    const size_t n = std::min(cap - 1, text.size());
+    std::memcpy(out, text.data(), n);
+    out[n] = '\0';
+  }
+  return rc;
 }
 
 }  // extern "C"

@@ -26,8 +26,12 @@ int IndexTypeForMagic(std::string_view magic);
 class Reader {
  public:
   explicit Reader(std::string_view d) : p_(d.data()), end_(d.data() + d.size()) {}
+  bool u8(uint8_t* v) { return raw(v, 1); }
+  bool u16(uint16_t* v) { return raw(v, 2); }
   bool u32(uint32_t* v) { return raw(v, 4); }
   bool u64(uint64_t* v) { return raw(v, 8); }
+  bool i64(int64_t* v) { return raw(v, 8); }
+  bool f64(double* v) { return raw(v, 8); }
   bool bytes(size_t n, std::string_view* out) {
     if (static_cast<size_t>(end_ - p_) < n) return false;
     *out = std::string_view(p_, n);

@@ -55,6 +55,7 @@ class FlatGpuIndex final : public GpuIndex {
  public:
   int type() const override { return kIndexFlat; }
   uint64_t rows() const override { return n_; }
+  const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + operand_.size() + norms_.size();
   }
@@ -128,6 +129,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
  public:
   int type() const override { return kIndexSq8Flat; }
   uint64_t rows() const override { return n_; }
+  const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + codes_.size() + operand_.size() + rowterm_.size() + vmin_.size() +
            scale_.size();

@@ -37,6 +37,7 @@ class HnswGpuIndex final : public GpuIndex {
   explicit HnswGpuIndex(bool sq8) : sq8_(sq8) {}
   int type() const override { return sq8_ ? kIndexHnswSq8 : kIndexHnsw; }
   uint64_t rows() const override { return n_; }
+  const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + codes_.size() + links0_.size() + upper_.size() + upper_off_.size() +
            level_.size() + vmin_.size() + scale_.size();

@@ -31,6 +31,7 @@ class IvfPqGpuIndex final : public GpuIndex {
   explicit IvfPqGpuIndex(bool flat) : pqflat_(flat) {}
   int type() const override { return pqflat_ ? kIndexPqFlat : kIndexIvfPq; }
   uint64_t rows() const override { return n_; }
+  const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + coarse_.size() + cents_.size() + term2_.size() + off_.size() + ids_.size() +
            codes_.size() + (coarse_index_ ? coarse_index_->device_bytes() : 0);

@@ -45,8 +45,6 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchEnd];
 std::mutex g_mu;
 void* g_addr[kNoAllocMaxDevices] = {};
 
-uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
-
 }  // namespace
 
 const size_t kNoAllocScratchBytes = kScratchEnd;

@@ -205,6 +205,8 @@ class GpuIndex {
   virtual Status Search(Context& ctx, const SearchBatch& b) = 0;
   virtual uint64_t rows() const = 0;
   virtual uint64_t device_bytes() const = 0;
+  // The fp32 rows (rows() x pd) the index keeps on the device.
+  virtual const float* device_rows() const = 0;
   virtual Status ExportSq8(Context&, float*, float*, uint8_t*) const {
     return Status(Status::kNotSupported, "index has no SQ8 codes");
   }

@@ -31,7 +31,11 @@ STATUS_NAMES = {
 
 METRICS = {"l2": 0, "ip": 1, "inner_product": 1, "cosine": 2}
 INDEX_TYPES = {"flat": 0, "hnsw": 1, "hnsw_sq8": 2, "pq_flat": 3, "ivf_pq": 4, "sq8_flat": 16}
-STRATEGIES = {"auto": 0, "prefilter": 1, "graph": 2, "postfilter": 3}
+# ParseFilterStrategy (src/util/status.cc:115-128).
+STRATEGIES = {"auto": 0, "prefilter": 1, "exact": 1, "graph": 2, "postfilter": 3}
+
+# vdbgpu_hit: one merged collection hit (24 bytes).
+HIT_DTYPE = np.dtype([("dist", "<f4"), ("part", "<u4"), ("row", "<u4"), ("pad", "<u4"), ("id", "<u8")])
 
 
 class VdbError(RuntimeError):
@@ -50,6 +54,13 @@ class SearchParams(ctypes.Structure):
 class IndexInfo(ctypes.Structure):
     _fields_ = [("type", ctypes.c_int32), ("metric", ctypes.c_int32), ("rows", ctypes.c_uint64),
                 ("dim", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32),
+                ("device_bytes", ctypes.c_uint64)]
+
+
+class CollectionInfo(ctypes.Structure):
+    _fields_ = [("dim", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32), ("metric", ctypes.c_int32),
+                ("index_type", ctypes.c_int32), ("segments_total", ctypes.c_uint32),
+                ("segments_local", ctypes.c_uint32), ("rows_local", ctypes.c_uint64),
                 ("device_bytes", ctypes.c_uint64)]
 
 
@@ -79,6 +90,28 @@ _SIGNATURES = {
                                                    ctypes.POINTER(SearchParams), _P, _P, _P]),
     "vdbgpu_index_file_inspect": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int)]),
     "vdbgpu_index_sq8_export": (ctypes.c_int, [_P, _P, _P, _P]),
+    "vdbgpu_collection_open": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_uint32, ctypes.c_uint32,
+                                              ctypes.POINTER(_P)]),
+    "vdbgpu_collection_create": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "vdbgpu_collection_add_segment": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32, _P, ctypes.c_uint64,
+                                                     _P, _P, ctypes.c_size_t, _P, ctypes.c_size_t]),
+    "vdbgpu_collection_set_deleted": (ctypes.c_int, [_P, ctypes.c_uint32, _P]),
+    "vdbgpu_collection_free": (None, [_P]),
+    "vdbgpu_collection_get_info": (ctypes.c_int, [_P, ctypes.POINTER(CollectionInfo)]),
+    "vdbgpu_collection_search": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32,
+                                                ctypes.POINTER(SearchParams), ctypes.c_char_p, _P, _P]),
+    "vdbgpu_collection_search_grouped": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32,
+                                                        ctypes.POINTER(SearchParams),
+                                                        ctypes.POINTER(ctypes.c_char_p), ctypes.c_uint32,
+                                                        _P, _P, _P, _P]),
+    "vdbgpu_collection_explain": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.POINTER(SearchParams),
+                                                 ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "vdbgpu_collection_filter_bitmap": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_uint32, _P,
+                                                       ctypes.POINTER(ctypes.c_uint64)]),
+    "vdbgpu_merge_hits": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
+                                         _P, _P, _P]),
+    "vdbgpu_filter_describe": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                              ctypes.c_size_t]),
 }
 
 _lib = None
@@ -312,3 +345,187 @@ def pack_bitset(allowed: np.ndarray) -> np.ndarray:
     out = np.zeros((n + 63) // 64 * 8, dtype=np.uint8)
     out[: b.size] = b
     return out.view(np.uint64)
+
+
+# ------------------------------------------------------------------------------ collections
+
+def _params(ef, nprobe, rerank, strategy, prefilter_threshold, post_filter_alpha) -> SearchParams:
+    if strategy not in STRATEGIES:
+        raise ValueError("bad strategy")
+    p = SearchParams()
+    lib().vdbgpu_search_params_default(ctypes.byref(p))
+    p.ef, p.nprobe, p.rerank, p.strategy = int(ef), int(nprobe), int(rerank), STRATEGIES[strategy]
+    p.prefilter_threshold, p.post_filter_alpha = int(prefilter_threshold), int(post_filter_alpha)
+    return p
+
+
+def _filter_text(f) -> Optional[bytes]:
+    import json
+    if f is None:
+        return None
+    return (f if isinstance(f, str) else json.dumps(f)).encode()
+
+
+class Collection:
+    """A collection's on-disk segments on one GPU (or one shard of them): the read path of
+    vdb::Collection (include/vdb/collection.h). `search` mirrors `_vdb._Collection.search`
+    (python/bindings.cc:107-142): raw queries (nq, dim) float32, returns (ids uint64[nq,k],
+    dists float32[nq,k]) with misses as (UINT64_MAX, +inf)."""
+
+    def __init__(self, ctx: Context, handle: _P):
+        self.ctx = ctx
+        self._h = handle
+        self._refresh()
+
+    def _refresh(self):
+        info = CollectionInfo()
+        self.ctx.check(lib().vdbgpu_collection_get_info(self._h, ctypes.byref(info)))
+        self.dim, self.padded_dim, self.metric = info.dim, info.padded_dim, info.metric
+        self.index_type = info.index_type
+        self.segments_total, self.segments_local = info.segments_total, info.segments_local
+        self.rows_local, self.device_bytes = info.rows_local, info.device_bytes
+
+    @classmethod
+    def open(cls, ctx: Context, path: str, shard: int = 0, nshards: int = 1) -> "Collection":
+        """Loads a collection directory written by the reference (this shard's segments)."""
+        h = _P()
+        ctx.check(lib().vdbgpu_collection_open(ctx._h, path.encode(), int(shard), int(nshards), ctypes.byref(h)))
+        return cls(ctx, h)
+
+    @classmethod
+    def create(cls, ctx: Context, options) -> "Collection":
+        """An empty collection with the reference's options (dict or JSON text)."""
+        import json
+        text = options if isinstance(options, str) else json.dumps(options)
+        h = _P()
+        ctx.check(lib().vdbgpu_collection_create(ctx._h, text.encode(), ctypes.byref(h)))
+        return cls(ctx, h)
+
+    def add_segment(self, segment_id: int, ordinal: int, rows, ids: np.ndarray, meta: bytes,
+                    index_file: bytes):
+        """One segment from its files' contents: rows (n, padded_dim) float32 (numpy or a CUDA
+        tensor), external ids, the meta.bin payload and the index file."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint64)
+        mb = np.frombuffer(meta, dtype=np.uint8) if meta else None
+        ib = np.frombuffer(index_file, dtype=np.uint8)
+        n = int(rows.shape[0])
+        self.ctx.check(lib().vdbgpu_collection_add_segment(self._h, int(segment_id), int(ordinal), _ptr(rows), n,
+                                                           _ptr(ids), _ptr(mb), 0 if mb is None else mb.size,
+                                                           _ptr(ib), ib.size))
+        self._refresh()
+
+    def set_deleted(self, segment_id: int, deleted: Optional[np.ndarray]):
+        """Deleted rows of a segment as a boolean mask (None clears them)."""
+        words = None
+        if deleted is not None:
+            d = np.asarray(deleted, dtype=bool)
+            b = np.packbits(d.astype(np.uint8), bitorder="little")
+            pad = np.zeros((d.size + 31) // 32 * 4, np.uint8)
+            pad[: b.size] = b
+            words = pad.view(np.uint32)
+        self.ctx.check(lib().vdbgpu_collection_set_deleted(self._h, int(segment_id), _ptr(words)))
+
+    def _queries(self, queries):
+        if isinstance(queries, np.ndarray):
+            q = np.ascontiguousarray(queries, dtype=np.float32)
+            if q.ndim == 1:
+                q = q[None, :]
+            if q.shape[1] != self.dim:
+                raise ValueError("query dimension does not match the collection")
+            return q, q.shape[0]
+        return queries, int(queries.shape[0])
+
+    def search(self, queries, k: int = 10, ef: int = 64, nprobe: int = 16, rerank: int = -1,
+               filter=None, strategy: str = "auto", prefilter_threshold: int = 10000,
+               post_filter_alpha: int = 10, out=None):
+        """Collection::SearchBatch with one filter (JSON text or dict) for every query."""
+        q, nq = self._queries(queries)
+        p = _params(ef, nprobe, rerank, strategy, prefilter_threshold, post_filter_alpha)
+        ids, dists = out if out is not None else (np.empty((nq, k), np.uint64), np.empty((nq, k), np.float32))
+        self.ctx.check(lib().vdbgpu_collection_search(self._h, _ptr(q), nq, int(k), ctypes.byref(p),
+                                                      _filter_text(filter), _ptr(ids), _ptr(dists)))
+        return ids, dists
+
+    def search_grouped(self, queries, filters, query_filter=None, k: int = 10, ef: int = 64,
+                       nprobe: int = 16, rerank: int = -1, strategy: str = "auto",
+                       prefilter_threshold: int = 10000, post_filter_alpha: int = 10, out=None,
+                       hits=None):
+        """Several filters in one batch: query i uses filters[query_filter[i]] (-1: none).
+        `hits` (optional, (nq, k) HIT_DTYPE numpy array or a CUDA uint8 tensor of nq*k*24 bytes)
+        receives the merged hit records for a cross-GPU merge. out=False skips the ids / dists."""
+        q, nq = self._queries(queries)
+        p = _params(ef, nprobe, rerank, strategy, prefilter_threshold, post_filter_alpha)
+        texts = [_filter_text(f) for f in filters]
+        arr = (ctypes.c_char_p * max(1, len(texts)))(*texts)
+        qf = None if query_filter is None else np.ascontiguousarray(query_filter, dtype=np.int32)
+        if qf is not None and qf.size != nq:
+            raise ValueError("query_filter needs one entry per query")
+        if out is None:
+            ids, dists = np.empty((nq, k), np.uint64), np.empty((nq, k), np.float32)
+        elif out is False:
+            ids = dists = None
+        else:
+            ids, dists = out
+        self.ctx.check(lib().vdbgpu_collection_search_grouped(self._h, _ptr(q), nq, int(k), ctypes.byref(p), arr,
+                                                              len(texts), _ptr(qf), _ptr(ids), _ptr(dists),
+                                                              _ptr(hits)))
+        return ids, dists
+
+    def explain(self, query, k: int = 10, ef: int = 64, nprobe: int = 16, rerank: int = -1, filter=None,
+                strategy: str = "auto", prefilter_threshold: int = 10000, post_filter_alpha: int = 10):
+        """Per-segment plan of one query (SegmentExplain): strategy, matches, distance
+        computations, results."""
+        import json
+        q, _ = self._queries(np.asarray(query, dtype=np.float32).reshape(1, -1))
+        p = _params(ef, nprobe, rerank, strategy, prefilter_threshold, post_filter_alpha)
+        buf = ctypes.create_string_buffer(1 << 20)
+        self.ctx.check(lib().vdbgpu_collection_explain(self._h, _ptr(q), int(k), ctypes.byref(p),
+                                                       _filter_text(filter), buf, len(buf)))
+        return json.loads(buf.value.decode())
+
+    def filter_bitmap(self, filter, segment_id: int, rows: int) -> Tuple[np.ndarray, int]:
+        """The rows of one segment a filter selects: (uint32 words, bit r of word r//32; count)."""
+        words = np.zeros((rows + 31) // 32, np.uint32)
+        m = ctypes.c_uint64(0)
+        self.ctx.check(lib().vdbgpu_collection_filter_bitmap(self._h, _filter_text(filter), int(segment_id),
+                                                             _ptr(words), ctypes.byref(m)))
+        return words, int(m.value)
+
+    def free(self):
+        if getattr(self, "_h", None):
+            lib().vdbgpu_collection_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def merge_hits(ctx: Context, lists, k: int, out=None, hits=None):
+    """The collection merge over already-merged hit lists: `lists` is (nlists, nq, k) HIT_DTYPE
+    (numpy) or a CUDA uint8 tensor of nlists*nq*k*24 bytes (give nlists, nq via its shape
+    (nlists, nq, k*24)). Returns (ids uint64[nq,k], dists float32[nq,k])."""
+    if isinstance(lists, np.ndarray):
+        if lists.dtype != HIT_DTYPE or lists.ndim != 3:
+            raise ValueError("lists must be (nlists, nq, k) of HIT_DTYPE")
+        nl, nq = lists.shape[0], lists.shape[1]
+        lists = np.ascontiguousarray(lists)
+    else:
+        nl, nq = int(lists.shape[0]), int(lists.shape[1])
+    if out is None:
+        ids, dists = np.empty((nq, k), np.uint64), np.empty((nq, k), np.float32)
+    else:
+        ids, dists = out
+    ctx.check(lib().vdbgpu_merge_hits(ctx._h, _ptr(lists), nl, nq, int(k), _ptr(ids), _ptr(dists), _ptr(hits)))
+    return ids, dists
+
+
+def filter_describe(schema, filter) -> Tuple[int, str]:
+    """FilterExpr::Parse against a schema without a GPU: (0, description) or (code, message)."""
+    import json
+    st = schema if isinstance(schema, str) else json.dumps(schema)
+    buf = ctypes.create_string_buffer(1 << 16)
+    code = lib().vdbgpu_filter_describe(st.encode(), _filter_text(filter), buf, len(buf))
+    return code, buf.value.decode(errors="replace")

@@ -176,6 +176,122 @@ VDBGPU_API int vdbgpu_index_file_inspect(const void* file_bytes, size_t nbytes, 
 VDBGPU_API int vdbgpu_index_sq8_export(const vdbgpu_index* index, float* vmin, float* scale,
                             uint8_t* codes);
 
+/* ------------------------------------------------------------------ collections (read path)
+ *
+ * A collection's on-disk segments on one GPU (or this rank's share of them), searched as
+ * vdb::Collection::SearchBatch does (src/engine/collection_impl.cc:1121-1136): per segment the
+ * planner of SearchDiskSegment (src/engine/planner.cc:42-129) over the segment's filter bitmap,
+ * then the merge of CollectionImpl::Search (collection_impl.cc:1079-1108). The mutable and frozen
+ * in-memory segments stay with the host (SearchMutable); their hits merge with
+ * vdbgpu_merge_hits. */
+
+typedef struct vdbgpu_collection vdbgpu_collection;
+
+/* One merged hit (24 bytes): ordered by (dist, part, row); part = the segment's position among
+ * the collection's disk segments; id = the external id (vdb::VectorId). A miss has
+ * id UINT64_MAX, dist +inf, part and row UINT32_MAX. */
+typedef struct vdbgpu_hit {
+  float dist;
+  uint32_t part;
+  uint32_t row;
+  uint32_t pad;
+  uint64_t id;
+} vdbgpu_hit;
+
+/* Collection::Open's recovery of the on-disk state (CollectionImpl::Recover, collection_impl.cc:
+ * 95-150, Segment::Open, src/storage/segment_reader.cc:20-122): reads CURRENT, the manifest and
+ * every segment directory (vectors.f32, ids.u64, meta.bin, index.<type>). With nshards > 1 only
+ * the segments whose manifest position % nshards == shard are loaded (one shard per GPU).
+ * Segments with a persisted delete set are refused (VDBGPU_NOT_SUPPORTED); pass deletes with
+ * vdbgpu_collection_set_deleted. */
+VDBGPU_API int vdbgpu_collection_open(vdbgpu_ctx* ctx, const char* path, uint32_t shard,
+                                      uint32_t nshards, vdbgpu_collection** out);
+
+/* An empty collection with the reference's options JSON (src/engine/options_json.cc:72-104:
+ * dim, metric, index type, schema), to be filled with vdbgpu_collection_add_segment. */
+VDBGPU_API int vdbgpu_collection_create(vdbgpu_ctx* ctx, const char* options_json,
+                                        vdbgpu_collection** out);
+
+/* One segment from the contents of its files: rows = n x padded_dim floats (host or device; the
+ * body of vectors.f32), ids = n external ids (host), meta = the payload of meta.bin (u64 rows,
+ * u64 offsets[rows + 1], EncodeMetaRow rows; NULL/0 = no metadata), index_file = the whole
+ * index file. ordinal = the segment's position among the collection's disk segments. */
+VDBGPU_API int vdbgpu_collection_add_segment(vdbgpu_collection* c, uint32_t segment_id,
+                                             uint32_t ordinal, const float* rows, uint64_t n,
+                                             const uint64_t* ids, const void* meta,
+                                             size_t meta_bytes, const void* index_file,
+                                             size_t index_bytes);
+
+/* The deleted rows of a segment (Segment::deletes, src/storage/segment.h): bit r of 32-bit word
+ * r / 32 (host); NULL clears them. */
+VDBGPU_API int vdbgpu_collection_set_deleted(vdbgpu_collection* c, uint32_t segment_id,
+                                             const uint32_t* bits);
+
+VDBGPU_API void vdbgpu_collection_free(vdbgpu_collection* c);
+
+typedef struct vdbgpu_collection_info {
+  uint32_t dim;
+  uint32_t padded_dim;
+  int32_t metric;
+  int32_t index_type;
+  uint32_t segments_total;
+  uint32_t segments_local;
+  uint64_t rows_local;
+  uint64_t device_bytes;
+} vdbgpu_collection_info;
+
+VDBGPU_API int vdbgpu_collection_get_info(const vdbgpu_collection* c, vdbgpu_collection_info* out);
+
+/* Collection::SearchBatch: nq raw queries (nq x dim, host or device; prepared on the GPU as
+ * PrepareQuery does), one filter (JSON, the language of src/meta/filter.h; NULL = none) for
+ * all. out_ids (nq x k) / out_dist (nq x k), host or device: misses UINT64_MAX / +inf. Errors:
+ * VDBGPU_INVALID_ARGUMENT for a bad filter, k outside 1..10000, a non-finite or (cosine) zero
+ * query, with the reference's messages; VDBGPU_NOT_SUPPORTED for k > 240. */
+VDBGPU_API int vdbgpu_collection_search(vdbgpu_collection* c, const float* queries, uint64_t nq,
+                                        uint32_t k, const vdbgpu_search_params* params,
+                                        const char* filter_json, uint64_t* out_ids,
+                                        float* out_dist);
+
+/* Several filters in one batch: query i uses filters[query_filter[i]] (-1 = no filter);
+ * query_filter NULL = filters[0] for all. Results as nfilters separate SearchBatch calls over
+ * each filter's queries. out_hits (nq x k, host or device, nullable) receives the merged hit
+ * records (the input of vdbgpu_merge_hits on another rank). */
+VDBGPU_API int vdbgpu_collection_search_grouped(vdbgpu_collection* c, const float* queries,
+                                                uint64_t nq, uint32_t k,
+                                                const vdbgpu_search_params* params,
+                                                const char* const* filters, uint32_t nfilters,
+                                                const int32_t* query_filter, uint64_t* out_ids,
+                                                float* out_dist, vdbgpu_hit* out_hits);
+
+/* Collection::Search with explain for one query: JSON array with one object per local disk
+ * segment {"id", "strategy", "matches", "live_rows", "distance_computations", "results"}
+ * (SegmentExplain, include/vdb/collection.h:45-58). Returns VDBGPU_RESOURCE_EXHAUSTED when cap
+ * is too small. */
+VDBGPU_API int vdbgpu_collection_explain(vdbgpu_collection* c, const float* query, uint32_t k,
+                                         const vdbgpu_search_params* params,
+                                         const char* filter_json, char* out_json, size_t cap);
+
+/* SegmentColumns::Evaluate (src/meta/columns.cc:185-250) of a filter on one segment, minus its
+ * deleted rows (planner.cc:64-65): out_words receives (rows + 31) / 32 words (bit r of word
+ * r / 32, host or device), matches (nullable) the number of rows. */
+VDBGPU_API int vdbgpu_collection_filter_bitmap(vdbgpu_collection* c, const char* filter_json,
+                                               uint32_t segment_id, uint32_t* out_words,
+                                               uint64_t* matches);
+
+/* The merge of CollectionImpl::Search over lists of hits that are each already merged
+ * (ascending (dist, part, row), one hit per id): lists = nlists x nq x k records (host or
+ * device), e.g. the per-GPU results of a sharded collection gathered over NCCL. Writes the
+ * first k distinct ids per query. out_hits nullable. */
+VDBGPU_API int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
+                                 uint64_t nq, uint32_t k, uint64_t* out_ids, float* out_dist,
+                                 vdbgpu_hit* out_hits);
+
+/* FilterExpr::Parse (src/meta/filter_parser.cc) against a schema (JSON, schema.cc:246-270),
+ * without a GPU: VDBGPU_OK with the parsed filter's description (FilterExpr::ToString) in out,
+ * or the reference's status code with its message in out. */
+VDBGPU_API int vdbgpu_filter_describe(const char* schema_json, const char* filter_json, char* out,
+                                      size_t cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -203,70 +203,112 @@ class RefIndex:
             pass
 
 
+STRATEGIES = {"auto": 0, "prefilter": 1, "exact": 1, "graph": 2, "postfilter": 3}
+
+
+def _engine_lib(lib_path: str = REF_ENGINE_LIB):
+    if not os.path.exists(lib_path):
+        raise ImportError(f"{lib_path} is missing (build with `make -C oracle engine`)")
+    l = ctypes.CDLL(lib_path)
+    c64, c32, ci = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int
+    sig = {
+        "ref_coll_last_error": (ctypes.c_char_p, []),
+        "ref_coll_create": (_P, [ctypes.c_char_p, ctypes.c_char_p, ci]),
+        "ref_coll_free": (None, [_P]),
+        "ref_coll_bulk_load": (ci, [_P, _P, _P, c64, _P, _P, c32]),
+        "ref_coll_bulk_load_json": (ci, [_P, _P, _P, c64, ctypes.c_char_p]),
+        "ref_coll_search_batch": (ci, [_P, _P, c64, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, _P, _P]),
+        "ref_coll_explain": (ci, [_P, _P, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, ctypes.c_char_p,
+                                  ctypes.c_size_t]),
+        "ref_segment_filter_bitmap": (ci, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _P, c64]),
+        "ref_filter_parse": (ci, [ctypes.c_char_p, ctypes.c_char_p]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(l, name)
+        f.restype = res
+        f.argtypes = args
+    return l
+
+
+def ref_filter_parse(schema: list, filter_json: str, lib_path: str = REF_ENGINE_LIB):
+    """FilterExpr::Parse of the reference: (0, canonical text) or (status code, message)."""
+    import json
+    l = _engine_lib(lib_path)
+    rc = l.ref_filter_parse(json.dumps(schema).encode(), filter_json.encode())
+    return rc, l.ref_coll_last_error().decode()
+
+
+def ref_segment_bitmap(segment_dir: str, schema: list, filter_json: str, rows: int,
+                       lib_path: str = REF_ENGINE_LIB) -> np.ndarray:
+    """The reference's filter bitmap over one segment's meta.bin (32 rows per uint32 word)."""
+    import json
+    l = _engine_lib(lib_path)
+    out = np.zeros((rows + 31) // 32, np.uint32)
+    rc = l.ref_segment_filter_bitmap(segment_dir.encode(), json.dumps(schema).encode(),
+                                     filter_json.encode(), _ptr(out), rows)
+    if rc != 0:
+        raise RuntimeError(l.ref_coll_last_error().decode())
+    return out
+
+
 class RefCollection:
     """The reference's Collection (oracle/_ref/libvdbref_engine.so): bulk-loaded on-disk segments
-    with year / tags metadata, filtered batched search through its planner and merge."""
+    with metadata, filtered batched search through its planner and merge."""
 
     def __init__(self, path: str, dim: int, metric: str = "cosine", index: Optional[dict] = None,
-                 threads: int = 0, lib_path: str = REF_ENGINE_LIB):
+                 schema: Optional[list] = None, threads: int = 0, lib_path: str = REF_ENGINE_LIB):
         import json
-        if not os.path.exists(lib_path):
-            raise ImportError(f"{lib_path} is missing (build with `make -C oracle engine`)")
-        l = ctypes.CDLL(lib_path)
-        sig = {
-            "ref_coll_last_error": (ctypes.c_char_p, []),
-            "ref_coll_create": (_P, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int]),
-            "ref_coll_free": (None, [_P]),
-            "ref_coll_bulk_load": (ctypes.c_int, [_P, _P, _P, ctypes.c_uint64, _P, _P, ctypes.c_uint32]),
-            "ref_coll_search_batch": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64,
-                                                     ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
-                                                     _P, _P]),
-            "ref_coll_explain": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int,
-                                                ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
-        }
-        for name, (res, args) in sig.items():
-            f = getattr(l, name)
-            f.restype = res
-            f.argtypes = args
-        self.l = l
+        self.l = _engine_lib(lib_path)
         self.dim = dim
         self.path = path
+        self.schema = schema if schema is not None else [{"name": "year", "type": "int64"},
+                                                          {"name": "tags", "type": "keyword_list"}]
         opts = {"dim": dim, "metric": metric, "sync": "none",
                 "index": index or {"type": "hnsw", "M": 16, "ef_construction": 200},
-                "schema": [{"name": "year", "type": "int64"}, {"name": "tags", "type": "keyword_list"}]}
-        self.h = l.ref_coll_create(path.encode(), json.dumps(opts).encode(), threads)
+                "schema": self.schema}
+        self.h = self.l.ref_coll_create(path.encode(), json.dumps(opts).encode(), threads)
         if not self.h:
-            raise RuntimeError(l.ref_coll_last_error().decode())
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
 
-    def bulk_load(self, ids: np.ndarray, vectors: np.ndarray, years=None, tags=None):
+    def bulk_load(self, ids: np.ndarray, vectors: np.ndarray, years=None, tags=None, metadata=None):
+        """One on-disk segment. Metadata either as (years int64, tags uint32 word ids with
+        UINT32_MAX = unused, stored as keywords "w<id>") or as a list of dicts."""
+        import json
         v = np.ascontiguousarray(vectors[:, :self.dim], dtype=np.float32)
         ids = np.ascontiguousarray(ids, dtype=np.uint64)
-        mt = 0 if tags is None else tags.shape[1]
-        rc = self.l.ref_coll_bulk_load(self.h, _ptr(ids), _ptr(v), ids.size,
-                                       _ptr(None if years is None else np.ascontiguousarray(years, np.int64)),
-                                       _ptr(None if tags is None else np.ascontiguousarray(tags, np.uint32)), mt)
+        if metadata is not None:
+            rc = self.l.ref_coll_bulk_load_json(self.h, _ptr(ids), _ptr(v), ids.size,
+                                                json.dumps(metadata).encode())
+        else:
+            mt = 0 if tags is None else tags.shape[1]
+            rc = self.l.ref_coll_bulk_load(self.h, _ptr(ids), _ptr(v), ids.size,
+                                           _ptr(None if years is None else np.ascontiguousarray(years, np.int64)),
+                                           _ptr(None if tags is None else np.ascontiguousarray(tags, np.uint32)), mt)
         if rc != 0:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
 
-    def search(self, q: np.ndarray, k=10, ef=64, nprobe=16, rerank=-1, strategy=0, filter=None):
-        import json
+    def search(self, q: np.ndarray, k=10, ef=64, nprobe=16, rerank=-1, strategy="auto", filter=None,
+               prefilter_threshold=10000, post_filter_alpha=10):
+        """Collection::SearchBatch: (ids uint64, distances float32), misses UINT64_MAX / +inf."""
         q = np.ascontiguousarray(q[:, :self.dim], dtype=np.float32)
         nq = q.shape[0]
         ids = np.empty((nq, k), np.uint64)
         d = np.empty((nq, k), np.float32)
-        fj = None if filter is None else json.dumps(filter).encode()
-        rc = self.l.ref_coll_search_batch(self.h, _ptr(q), nq, k, ef, nprobe, rerank, strategy, fj,
+        rc = self.l.ref_coll_search_batch(self.h, _ptr(q), nq, k, ef, nprobe, rerank, STRATEGIES[strategy],
+                                          prefilter_threshold, post_filter_alpha, _fj(filter),
                                           _ptr(ids), _ptr(d))
         if rc != 0:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
         return ids, d
 
-    def explain(self, q: np.ndarray, k=10, ef=64, strategy=0, filter=None):
+    def explain(self, q: np.ndarray, k=10, ef=64, nprobe=16, rerank=-1, strategy="auto", filter=None,
+                prefilter_threshold=10000, post_filter_alpha=10):
+        """Per-part explain of Collection::Search for one query (mutable part first)."""
         import json
         q = np.ascontiguousarray(q[:self.dim], dtype=np.float32)
         buf = ctypes.create_string_buffer(1 << 20)
-        fj = None if filter is None else json.dumps(filter).encode()
-        rc = self.l.ref_coll_explain(self.h, _ptr(q), k, ef, strategy, fj, buf, len(buf))
+        rc = self.l.ref_coll_explain(self.h, _ptr(q), k, ef, nprobe, rerank, STRATEGIES[strategy],
+                                     prefilter_threshold, post_filter_alpha, _fj(filter), buf, len(buf))
         if rc != 0:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
         return json.loads(buf.value.decode())
@@ -285,6 +327,28 @@ class RefCollection:
             self.close()
         except Exception:
             pass
+
+
+def _fj(filter) -> Optional[bytes]:
+    import json
+    if filter is None:
+        return None
+    return (filter if isinstance(filter, str) else json.dumps(filter)).encode()
+
+
+def merge_hits_py(cands, k):
+    """The merge of CollectionImpl::Search (src/engine/collection_impl.cc:1079-1108) for one
+    query: cands = iterable of (dist, part, row, id); sorted by (dist, part, row), the first hit
+    of every id, first k. Returns a list of (dist, part, row, id)."""
+    out, seen = [], set()
+    for c in sorted(cands, key=lambda t: (t[0], t[1], t[2])):
+        if c[3] in seen:
+            continue
+        seen.add(c[3])
+        out.append(c)
+        if len(out) >= k:
+            break
+    return out
 
 
 # ---------------------------------------------------------------------------------------- files

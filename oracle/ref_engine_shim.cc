@@ -15,6 +15,13 @@
 #include <vector>
 
 #include "engine/options_json.h"
+#include "meta/columns.h"
+#include "meta/filter.h"
+#include "meta/schema.h"
+#include "storage/env.h"
+#include "storage/file_format.h"
+#include "storage/segment.h"
+#include "util/coding.h"
 #include "vdb/collection.h"
 
 namespace {
@@ -90,15 +97,114 @@ int ref_coll_bulk_load(ref_coll* h, const uint64_t* ids, const float* vectors, u
   return 0;
 }
 
+// One segment with arbitrary metadata: meta_json is a JSON array of n objects (null = none),
+// converted by MetadataFromJson (src/meta/schema.cc:179) against the collection's schema.
+int ref_coll_bulk_load_json(ref_coll* h, const uint64_t* ids, const float* vectors, uint64_t n,
+                            const char* meta_json) {
+  std::vector<vdb::Metadata> md;
+  if (meta_json != nullptr) {
+    auto j = nlohmann::json::parse(meta_json, nullptr, false);
+    if (j.is_discarded() || !j.is_array() || j.size() != n) {
+      g_err = "metadata must be a JSON array with one entry per row";
+      return 3;
+    }
+    md.resize(n);
+    for (uint64_t i = 0; i < n; ++i) {
+      vdb::Status s = vdb::MetadataFromJson(j[i], h->c->options().schema, &md[i]);
+      if (!s.ok()) {
+        g_err = s.ToString();
+        return static_cast<int>(s.code());
+      }
+    }
+  }
+  vdb::Status s = h->c->BulkLoad(ids, vectors, n, meta_json != nullptr ? &md : nullptr);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  return 0;
+}
+
+// The filter bitmap of one segment: SegmentColumns::Build over the segment's meta.bin
+// (segment_reader.cc:75-95) then SegmentColumns::Evaluate (columns.cc:185-205). out receives
+// (rows + 31) / 32 words, bit r of word r / 32 set for every matching row.
+int ref_segment_filter_bitmap(const char* segment_dir, const char* schema_json,
+                              const char* filter_json, uint32_t* out, uint64_t rows) {
+  auto sj = nlohmann::json::parse(schema_json, nullptr, false);
+  vdb::Schema schema;
+  vdb::Status s = sj.is_discarded() ? vdb::Status::InvalidArgument("schema must be JSON")
+                                    : vdb::SchemaFromJson(sj, &schema);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  std::string storage;
+  std::string_view payload;
+  s = vdb::ReadBlobFile(vdb::Env::Default(), std::string(segment_dir) + "/meta.bin", vdb::kMetaMagic,
+                        &storage, &payload);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  vdb::ByteReader r(payload);
+  uint64_t n = 0;
+  std::string_view offs_bytes;
+  if (!r.GetU64(&n) || n != rows || !r.GetBytes((rows + 1) * sizeof(uint64_t), &offs_bytes)) {
+    g_err = "bad meta.bin";
+    return 9;
+  }
+  std::vector<uint64_t> offs(rows + 1);
+  std::memcpy(offs.data(), offs_bytes.data(), offs_bytes.size());
+  std::string_view bytes(r.position(), r.remaining());
+  vdb::SegmentColumns cols;
+  s = cols.Build(schema, rows, [&](size_t i) { return bytes.substr(offs[i], offs[i + 1] - offs[i]); });
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  auto f = vdb::FilterExpr::Parse(filter_json, schema);
+  if (!f.ok()) {
+    g_err = f.status().ToString();
+    return static_cast<int>(f.status().code());
+  }
+  roaring::Roaring bm = cols.Evaluate((*f)->root());
+  std::memset(out, 0, (rows + 31) / 32 * 4);
+  for (uint32_t row : bm) out[row >> 5] |= 1u << (row & 31);
+  return 0;
+}
+
+// FilterExpr::Parse alone (src/meta/filter_parser.cc): 0, or the status code with the message
+// in ref_coll_last_error().
+int ref_filter_parse(const char* schema_json, const char* filter_json) {
+  auto sj = nlohmann::json::parse(schema_json, nullptr, false);
+  vdb::Schema schema;
+  vdb::Status s = sj.is_discarded() ? vdb::Status::InvalidArgument("schema must be JSON")
+                                    : vdb::SchemaFromJson(sj, &schema);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  auto f = vdb::FilterExpr::Parse(filter_json, schema);
+  if (!f.ok()) {
+    g_err = f.status().message();
+    return static_cast<int>(f.status().code());
+  }
+  g_err = (*f)->ToString();
+  return 0;
+}
+
 // Collection::SearchBatch with an optional JSON filter. Misses: UINT64_MAX / +inf.
 int ref_coll_search_batch(ref_coll* h, const float* q, uint64_t nq, uint32_t k, uint64_t ef,
-                          uint64_t nprobe, int rerank, int strategy, const char* filter_json,
-                          uint64_t* out_ids, float* out_dist) {
+                          uint64_t nprobe, int rerank, int strategy, uint64_t prefilter_threshold,
+                          uint64_t post_filter_alpha, const char* filter_json, uint64_t* out_ids,
+                          float* out_dist) {
   vdb::SearchParams p;
   p.ef = ef;
   p.nprobe = nprobe;
   p.rerank = rerank;
   p.strategy = static_cast<vdb::FilterStrategy>(strategy);
+  p.prefilter_threshold = prefilter_threshold;
+  p.post_filter_alpha = post_filter_alpha;
   std::unique_ptr<vdb::Filter> f;
   if (filter_json != nullptr) {
     auto pf = h->c->ParseFilter(filter_json);
@@ -125,13 +231,18 @@ int ref_coll_search_batch(ref_coll* h, const float* q, uint64_t nq, uint32_t k, 
 
 // Collection::Search of one query with explain: per part (mutable first, then disk segments in
 // snapshot order) the strategy name, matches and distance computations, as JSON.
-int ref_coll_explain(ref_coll* h, const float* q, uint32_t k, uint64_t ef, int strategy,
-                     const char* filter_json, char* out, size_t cap) {
+int ref_coll_explain(ref_coll* h, const float* q, uint32_t k, uint64_t ef, uint64_t nprobe,
+                     int rerank, int strategy, uint64_t prefilter_threshold,
+                     uint64_t post_filter_alpha, const char* filter_json, char* out, size_t cap) {
   vdb::SearchRequest req;
   req.vector = q;
   req.k = k;
   req.params.ef = ef;
+  req.params.nprobe = nprobe;
+  req.params.rerank = rerank;
   req.params.strategy = static_cast<vdb::FilterStrategy>(strategy);
+  req.params.prefilter_threshold = prefilter_threshold;
+  req.params.post_filter_alpha = post_filter_alpha;
   std::unique_ptr<vdb::Filter> f;
   if (filter_json != nullptr) {
     auto pf = h->c->ParseFilter(filter_json);
@@ -151,7 +262,7 @@ int ref_coll_explain(ref_coll* h, const float* q, uint32_t k, uint64_t ef, int s
   }
   nlohmann::json j = nlohmann::json::array();
   for (const auto& e : ex.segments)
-    j.push_back({{"id", e.segment_id}, {"kind", e.kind}, {"strategy", e.strategy},
+    j.push_back({{"id", e.segment_id}, {"kind", e.kind}, {"strategy", e.strategy}, {"index", e.index},
                  {"matches", e.matches}, {"live_rows", e.live_rows}, {"ef", e.ef},
                  {"distance_computations", e.distance_computations}, {"results", e.results}});
   const std::string str = j.dump();

@@ -1,0 +1,183 @@
+"""Generates the collection fixtures (tests/golden/coll_*.npz) by running the reference's own
+engine layer: Collection::Create / BulkLoad / SearchBatch / Search with explain, and
+SegmentColumns::Evaluate for filter bitmaps (oracle/_ref/libvdbref_engine.so, built from the
+reference sources by oracle/Makefile).
+
+Each fixture holds a small collection directory exactly as the reference wrote it (CURRENT, the
+manifest, and per segment vectors.f32 / ids.u64 / meta.bin / index.<type>), the raw queries,
+the filters, and for every (case, filter) the reference's merged results, its per-segment
+explain of query 0, and the filter bitmap of every segment.
+
+Run from the repo root (needs the reference sources at build time):
+    python tests/golden/make_collection_golden.py
+"""
+import json
+import os
+import shutil
+import sys
+import tempfile
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "hnsw-vector-db_b200"))
+
+import oracle  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+SCHEMA = [{"name": "year", "type": "int64"}, {"name": "score", "type": "float64"},
+          {"name": "lang", "type": "keyword"}, {"name": "tags", "type": "keyword_list"},
+          {"name": "flag", "type": "bool"}]
+
+FILTERS = [
+    {"and": [{"field": "year", "gte": 2020}, {"field": "tags", "eq": "t0"}]},
+    {"and": [{"field": "year", "gte": 2020}, {"field": "tags", "eq": "t5"}]},
+    {"field": "tags", "in": ["t1", "t2", "t29"]},
+    {"not": {"field": "lang", "eq": "en"}},
+    {"field": "lang", "ne": "en"},
+    {"or": [{"field": "score", "lt": -1.5}, {"field": "score", "gte": 2.0}]},
+    {"and": [{"field": "flag", "eq": True}, {"field": "year", "exists": False}]},
+    {"field": "flag", "ne": True},
+    {"field": "score", "in": [0.5, -0.25, 1.0, 0.125]},
+    {"field": "tags", "eq": "nope"},
+    {"and": [{"field": "year", "lte": 2000}, {"not": {"field": "tags", "ne": "t0"}}]},
+    {"field": "tags", "exists": True},
+    {"field": "year", "eq": 2001},
+    {"field": "tags", "ne": "t0"},
+    {"or": [{"field": "lang", "in": ["de", "es"]}, {"field": "year", "gt": 2022}]},
+    {"not": {"or": [{"field": "flag", "exists": True}, {"field": "score", "lte": 0}]}},
+]
+
+# (strategy, prefilter_threshold, ef, nprobe, k)
+CASES = [
+    ("auto", 10000, 64, 16, 10),
+    ("auto", 100, 16, 2, 10),
+    ("graph", 10000, 32, 4, 10),
+    ("postfilter", 10000, 64, 16, 10),
+    ("prefilter", 10000, 64, 16, 7),
+]
+
+
+def metadata(rng, n, vocab=30):
+    langs = ["en", "fr", "de", "es"]
+    md = []
+    for _ in range(n):
+        m = {}
+        if rng.random() > 0.1:
+            m["year"] = int(rng.integers(1990, 2025))
+        if rng.random() > 0.15:
+            m["score"] = float(np.round(rng.normal(0, 2) * 8) / 8)  # repeated exact values
+        if rng.random() > 0.2:
+            m["lang"] = langs[int(rng.integers(0, 4))]
+        if rng.random() > 0.1:
+            nt = int(rng.integers(0, 5))  # 0 -> an empty list (present, no tags)
+            m["tags"] = ["t%d" % min(vocab - 1, int(rng.zipf(1.3)) - 1) for _ in range(nt)]
+        if rng.random() > 0.3:
+            m["flag"] = bool(rng.random() < 0.5)
+        md.append(m)
+    return md
+
+
+def rows_mixture(rng, n, dim, centres):
+    c = centres[rng.integers(0, centres.shape[0], n)]
+    return (c + 0.35 * rng.standard_normal((n, dim))).astype(np.float32)
+
+
+def pack_dir(path):
+    files = {}
+    for dp, _, fns in os.walk(path):
+        for fn in fns:
+            full = os.path.join(dp, fn)
+            rel = os.path.relpath(full, path)
+            if rel.startswith("wal"):
+                continue
+            with open(full, "rb") as f:
+                files["file:" + rel] = np.frombuffer(f.read(), dtype=np.uint8)
+    return files
+
+
+def make(name, dim, metric, index, sizes, seed, nq=24, filters=FILTERS, cases=CASES):
+    rng = np.random.default_rng(seed)
+    tmp = tempfile.mkdtemp()
+    path = os.path.join(tmp, "coll")
+    coll = oracle.RefCollection(path, dim, metric=metric, index=index, schema=SCHEMA, threads=4)
+    centres = rng.standard_normal((12, dim)).astype(np.float32)
+    next_id = 1000
+    for n in sizes:
+        rows = rows_mixture(rng, n, dim, centres)
+        ids = np.arange(next_id, next_id + n, dtype=np.uint64) * 3  # external ids, not row numbers
+        next_id += n
+        coll.bulk_load(ids, rows, metadata=metadata(rng, n))
+    q = rows_mixture(rng, nq, dim, centres)
+    out = {"queries": q, "dim": np.array(dim), "metric": np.array({"l2": 0, "ip": 1, "cosine": 2}[metric]),
+           "filters": np.array([json.dumps(f) for f in filters]), "schema": np.array(json.dumps(SCHEMA)),
+           "cases": np.array([json.dumps(c) for c in cases]), "sizes": np.array(sizes)}
+    for ci, (strategy, thr, ef, nprobe, k) in enumerate(cases):
+        for fi, f in enumerate(filters + [None]):
+            ids, d = coll.search(q, k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
+                                 prefilter_threshold=thr)
+            out[f"ids_{ci}_{fi}"] = ids
+            out[f"dist_{ci}_{fi}"] = d
+            ex = coll.explain(q[0], k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
+                              prefilter_threshold=thr)
+            disk = [e for e in ex if e["kind"] == "disk"]
+            out[f"explain_{ci}_{fi}"] = np.array(json.dumps(disk))
+    segdirs = coll.segment_dirs()
+    for fi, f in enumerate(filters):
+        for si, (sd, n) in enumerate(zip(segdirs, sizes)):
+            out[f"bitmap_{fi}_{si}"] = oracle.ref_segment_bitmap(sd, SCHEMA, json.dumps(f), n)
+    out["segment_ids"] = np.array([int(os.path.basename(s)[4:]) for s in segdirs])
+    coll.close()
+    out.update(pack_dir(path))
+    shutil.rmtree(tmp)
+    np.savez_compressed(os.path.join(OUT, name + ".npz"), **out)
+    print("wrote", name, os.path.getsize(os.path.join(OUT, name + ".npz")), "bytes")
+
+
+# Filter texts for the parser pin: valid ones of every operator and type, and every error path of
+# Parser::Node / Literal (src/meta/filter_parser.cc:51-138).
+PARSE_CASES = [json.dumps(f) for f in FILTERS] + [
+    'not json', '[]', '3', '{}', '{"and": []}', '{"and": {"field": "year"}}', '{"or": [1]}',
+    '{"and": [{"field": "year", "gte": 1}], "x": 1}', '{"not": {"field": "year", "gte": 1}, "y": 2}',
+    '{"field": "year"}', '{"field": 3, "eq": 1}', '{"field": "year", "eq": 1, "ne": 2}',
+    '{"field": "nope", "eq": 1}', '{"field": "year", "between": 1}', '{"field": "year", "eq": "x"}',
+    '{"field": "tags", "eq": 1}', '{"field": "flag", "eq": 1}', '{"field": "flag", "in": [true]}',
+    '{"field": "lang", "gt": "a"}', '{"field": "year", "in": []}', '{"field": "year", "in": 5}',
+    '{"field": "year", "exists": "yes"}', '{"field": "score", "eq": 1e400}',
+    '{"field": "year", "in": [' + ",".join(["1"] * 1025) + ']}',
+    '{"field": "score", "in": [1e-7, 123456789012345678, 0.1, -0.0, 5e-324, 1e16, 12345.678]}',
+    '{"field": "lang", "eq": "quote\\"d \\u00e9 \\n"}',
+    '{"field": "year", "eq": 18446744073709551615}', '{"field": "year", "eq": -9223372036854775808}',
+    '{"field":"year","gte":2020,"field":"lang"}',
+    '{"field": "year", "eq": 1} trailing',
+    "{" * 40 + "}" * 40,
+    '{"not": ' * 33 + '{"field": "year", "eq": 1}' + "}" * 33,
+    '{"not": ' * 32 + '{"field": "year", "eq": 1}' + "}" * 32,
+]
+
+
+def parse_golden():
+    codes, texts = [], []
+    for c in PARSE_CASES:
+        rc, t = oracle.ref_filter_parse(SCHEMA, c)
+        codes.append(rc)
+        texts.append(t)
+    np.savez_compressed(os.path.join(OUT, "filter_parse.npz"), cases=np.array(PARSE_CASES),
+                        codes=np.array(codes), texts=np.array(texts), schema=np.array(json.dumps(SCHEMA)))
+    print("wrote filter_parse", len(PARSE_CASES), "cases")
+
+
+def main():
+    oracle.build(ref=True)
+    parse_golden()
+    make("coll_hnsw", 48, "cosine", {"type": "hnsw", "M": 8, "ef_construction": 64}, [900, 1300, 700], seed=11)
+    make("coll_ivfpq", 32, "l2", {"type": "ivf_pq", "nlist": 16, "pq_m": 8}, [1000, 800], seed=12,
+         filters=FILTERS[:6] + [FILTERS[13]])
+    make("coll_flat", 20, "ip", {"type": "flat"}, [600, 500, 400], seed=13,
+         filters=FILTERS[:4] + [FILTERS[8], FILTERS[15]])
+
+
+if __name__ == "__main__":
+    main()

@@ -40,3 +40,18 @@ def assert_same_neighbors(ids_a, d_a, ids_b, d_b, rel=1e-4, exact_dist=True):
     if exact_dist:
         same = ids_a == ids_b
         np.testing.assert_array_equal(d_a[same], d_b[same])
+
+
+def extract_collection(g, dest):
+    """Writes the collection directory stored in a coll_* fixture (keys "file:<relpath>") under
+    dest and returns its path."""
+    import os
+    path = os.path.join(str(dest), "coll")
+    for key in g:
+        if not key.startswith("file:"):
+            continue
+        full = os.path.join(path, key[5:])
+        os.makedirs(os.path.dirname(full), exist_ok=True)
+        with open(full, "wb") as f:
+            f.write(np.asarray(g[key]).tobytes())
+    return path

@@ -1,0 +1,72 @@
+"""Host side of the collection read path, without a GPU: the filter parser against the
+reference's FilterExpr::Parse (golden texts, and the live reference engine when it is built),
+the collection fixtures' integrity, and the shard assignment of segments to ranks."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from helpers import golden
+
+
+def test_filter_parser_matches_reference_golden():
+    import vdb_b200
+    g = golden("filter_parse")
+    schema = str(g["schema"])
+    for case, code, text in zip(g["cases"], g["codes"], g["texts"]):
+        assert vdb_b200.filter_describe(schema, str(case)) == (int(code), str(text)), str(case)[:80]
+
+
+def test_filter_parser_matches_live_reference():
+    import oracle
+    import vdb_b200
+    if not os.path.exists(oracle.REF_ENGINE_LIB):
+        pytest.skip("the reference engine is not built here")
+    schema = [{"name": "a", "type": "int64"}, {"name": "b", "type": "keyword_list"},
+              {"name": "c", "type": "float64"}, {"name": "d", "type": "bool"}, {"name": "e", "type": "keyword"}]
+    rng = np.random.default_rng(5)
+    ops = ["eq", "ne", "in", "lt", "lte", "gt", "gte", "exists", "nope"]
+    fields = ["a", "b", "c", "d", "e", "zz"]
+    vals = [1, -2.5, "x", True, [1, 2], ["x", "y"], [], None, 1e300, "é"]
+
+    def leaf():
+        return {"field": fields[rng.integers(len(fields))], ops[rng.integers(len(ops))]: vals[rng.integers(len(vals))]}
+
+    def node(d):
+        r = rng.random()
+        if d > 3 or r < 0.4:
+            return leaf()
+        if r < 0.6:
+            return {"not": node(d + 1)}
+        return {["and", "or"][rng.integers(2)]: [node(d + 1) for _ in range(rng.integers(1, 4))]}
+
+    for _ in range(400):
+        text = json.dumps(node(0))
+        assert vdb_b200.filter_describe(schema, text) == oracle.ref_filter_parse(schema, text), text
+
+
+@pytest.mark.parametrize("name", ["coll_hnsw", "coll_ivfpq", "coll_flat"])
+def test_collection_fixture_is_the_reference_layout(name, tmp_path):
+    """The stored directory is what Collection::Open reads: CURRENT names the manifest, every
+    manifest segment has its four files."""
+    from helpers import extract_collection
+    g = golden(name)
+    path = extract_collection(g, tmp_path)
+    cur = open(os.path.join(path, "CURRENT")).read().strip()
+    assert cur.startswith("MANIFEST-") and os.path.exists(os.path.join(path, cur))
+    for sid in g["segment_ids"]:
+        d = os.path.join(path, "segments", "seg-%06d" % int(sid))
+        names = set(os.listdir(d))
+        assert {"vectors.f32", "ids.u64", "meta.bin"} <= names
+        assert any(n.startswith("index.") for n in names)
+
+
+def test_shard_assignment_round_robin():
+    """Segment ordinal i goes to rank i % world (the sharding of the collection read path)."""
+    from vdb_b200 import sharded
+    for world in (1, 2, 3, 8):
+        owners = [sharded.owner(i, world) for i in range(64)]
+        for r in range(world):
+            mine = [i for i, o in enumerate(owners) if o == r]
+            assert mine == list(range(r, 64, world))
