@@ -25,6 +25,7 @@ enum DeviceError : int {
   kDevOverflow = 6,        // a bounded on-chip structure overflowed
   kDevBadIndex = 7,        // an index read from a graph/list was out of range
   kDevStepLimit = 8,       // a graph walk exceeded its expansion cap
+  kDevCandOverflow = 9,    // a graph walk's candidate array overflowed (retry with a larger one)
 };
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s of wall-clock per wait

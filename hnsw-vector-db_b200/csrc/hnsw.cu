@@ -232,7 +232,7 @@ template <bool kSq8>
 __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const HnswArgs a) {
   extern __shared__ __align__(16) uint8_t hsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = blockIdx.x * kHnswWarps + warp;
+  const int q = blockIdx.x * (blockDim.x >> 5) + warp;
   if (q >= a.nq) return;
   const int pd = a.pd;
   const size_t per_warp = HnswWarpSmemBytes(pd, a.hash_bits, a.ef, a.cand_cap);
@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
               if (nres >= ef && neighbor_dist(s.cand[ncand - 1]) > lower) {
                 --ncand;
               } else {
-                if (lane == 0) set_error(a.status, kDevOverflow);
+                if (lane == 0) set_error(a.status, kDevCandOverflow);
                 bad = true;
                 break;
               }
@@ -446,19 +446,20 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
 }  // namespace
 
 cudaError_t LaunchHnswSearch(const HnswArgs& a, cudaStream_t stream) {
-  const size_t smem = kHnswWarps * HnswWarpSmemBytes(a.pd, a.hash_bits, a.ef, a.cand_cap);
-  const int blocks = (a.nq + kHnswWarps - 1) / kHnswWarps;
+  const int warps = a.warps >= 1 && a.warps <= kHnswWarps ? a.warps : kHnswWarps;
+  const size_t smem = warps * HnswWarpSmemBytes(a.pd, a.hash_bits, a.ef, a.cand_cap);
+  const int blocks = (a.nq + warps - 1) / warps;
   cudaError_t e;
   if (a.codes != nullptr) {
     e = cudaFuncSetAttribute(hnsw_search_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    hnsw_search_kernel<true><<<blocks, kHnswWarps * 32, smem, stream>>>(a);
+    hnsw_search_kernel<true><<<blocks, warps * 32, smem, stream>>>(a);
   } else {
     e = cudaFuncSetAttribute(hnsw_search_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    hnsw_search_kernel<false><<<blocks, kHnswWarps * 32, smem, stream>>>(a);
+    hnsw_search_kernel<false><<<blocks, warps * 32, smem, stream>>>(a);
   }
   return cudaGetLastError();
 }

@@ -32,6 +32,7 @@ struct HnswArgs {
   const uint32_t* allow;   // allowed-row bitset (32 per word) or null
   int hash_bits;           // visited hash: 1 << hash_bits slots per warp
   int cand_cap;            // candidate array capacity per warp
+  int warps;               // queries (warps) per block, 1..4
   int step_limit;          // bounded walk: expansions per query
   float* out_dist;
   uint32_t* out_row;

@@ -115,19 +115,30 @@ class HnswGpuIndex final : public GpuIndex {
     a.entry = g_.entry;
     a.n = n_;
     a.allow = b.allow;
-    a.cand_cap = static_cast<int>(2 * ef + 64);
     a.step_limit = 1 << 22;
     a.out_dist = b.out_dist;
     a.out_row = b.out_row;
     a.out_dc = b.dist_comps;
     a.status = ctx.status_word();
-    // Visited hash sized for the walk; on overflow the batch reruns with a table twice as large.
+    // Visited hash and candidate array sized for an unfiltered walk. A walk that overflows one
+    // (a filtered walk keeps every reached node as a candidate until it holds ef allowed rows,
+    // as the reference's unbounded heap does) reruns the batch with that structure doubled,
+    // and with fewer queries per block once four no longer fit in shared memory.
     int bits = std::max(11, Log2Ceil(32 * ef));
+    int cap = static_cast<int>(2 * ef + 64);
     for (;;) {
       a.hash_bits = bits;
-      const size_t smem = 4 * HnswWarpSmemBytes(a.pd, bits, a.ef, a.cand_cap);
-      if (smem > 227 * 1024)
-        return Status(Status::kResourceExhausted, "HNSW search state does not fit in shared memory");
+      a.cand_cap = cap;
+      a.warps = 0;
+      for (int w = 4; w >= 1; w /= 2)
+        if (static_cast<size_t>(w) * HnswWarpSmemBytes(a.pd, bits, a.ef, cap) <= 227 * 1024) {
+          a.warps = w;
+          break;
+        }
+      if (a.warps == 0)
+        return Status(Status::kNotSupported,
+                      "the graph walk's state exceeds the GPU's shared memory (a very selective filter "
+                      "reaches too much of the graph); use the prefilter strategy");
       ctx.Mark(0);
       ctx.Mark(1);
       VDBGPU_CUDA(LaunchHnswSearch(a, ctx.stream()));
@@ -135,8 +146,15 @@ class HnswGpuIndex final : public GpuIndex {
       ctx.Mark(3);
       Status s = ctx.Sync("hnsw search");
       if (s.ok()) return s;
-      if (s.message().find("code 6") == std::string::npos || bits >= 16) return s;
-      ++bits;  // visited table overflow (kDevOverflow): retry larger
+      const bool hash_full = s.message().find("code 6") != std::string::npos;
+      const bool cand_full = s.message().find("code 9") != std::string::npos;
+      if (hash_full && bits < 16) {
+        ++bits;
+      } else if (cand_full && cap < (1 << 16)) {
+        cap *= 2;
+      } else {
+        return s;
+      }
     }
   }
 

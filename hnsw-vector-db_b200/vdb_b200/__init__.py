@@ -314,7 +314,10 @@ class Index:
 
     def free(self):
         if getattr(self, "_h", None):
-            lib().vdbgpu_index_free(self._h)
+            # A context closed first (garbage collection can finalise a cycle in any order) took
+            # its device memory with it; the handle is then dropped, not freed.
+            if getattr(self.ctx, "_h", None):
+                lib().vdbgpu_index_free(self._h)
             self._h = None
 
     def __del__(self):
@@ -493,7 +496,8 @@ class Collection:
 
     def free(self):
         if getattr(self, "_h", None):
-            lib().vdbgpu_collection_free(self._h)
+            if getattr(self.ctx, "_h", None):
+                lib().vdbgpu_collection_free(self._h)
             self._h = None
 
     def __del__(self):

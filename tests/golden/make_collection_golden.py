@@ -50,14 +50,17 @@ FILTERS = [
     {"not": {"or": [{"field": "flag", "exists": True}, {"field": "score", "lte": 0}]}},
 ]
 
-# (strategy, prefilter_threshold, ef, nprobe, k)
+# (strategy, prefilter_threshold, ef, nprobe, k, post_filter_alpha)
 CASES = [
-    ("auto", 10000, 64, 16, 10),
-    ("auto", 100, 16, 2, 10),
-    ("graph", 10000, 32, 4, 10),
-    ("postfilter", 10000, 64, 16, 10),
-    ("prefilter", 10000, 64, 16, 7),
+    ("auto", 10000, 64, 16, 10, 10),
+    ("auto", 100, 16, 2, 10, 10),
+    ("graph", 10000, 32, 4, 10, 10),
+    ("postfilter", 10000, 64, 16, 10, 10),
+    ("prefilter", 10000, 64, 16, 7, 10),
 ]
+# IVF-PQ re-ranks max(10 k, 100) candidates (RerankDepth, src/index/quant/ivf_pq.cc:16-19); the
+# GPU path keeps at most 256, so its post-filter case searches k * 2.
+CASES_IVF = CASES[:3] + [("postfilter", 10000, 64, 16, 10, 2)] + CASES[4:]
 
 
 def metadata(rng, n, vocab=30):
@@ -114,14 +117,14 @@ def make(name, dim, metric, index, sizes, seed, nq=24, filters=FILTERS, cases=CA
     out = {"queries": q, "dim": np.array(dim), "metric": np.array({"l2": 0, "ip": 1, "cosine": 2}[metric]),
            "filters": np.array([json.dumps(f) for f in filters]), "schema": np.array(json.dumps(SCHEMA)),
            "cases": np.array([json.dumps(c) for c in cases]), "sizes": np.array(sizes)}
-    for ci, (strategy, thr, ef, nprobe, k) in enumerate(cases):
+    for ci, (strategy, thr, ef, nprobe, k, alpha) in enumerate(cases):
         for fi, f in enumerate(filters + [None]):
             ids, d = coll.search(q, k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
-                                 prefilter_threshold=thr)
+                                 prefilter_threshold=thr, post_filter_alpha=alpha)
             out[f"ids_{ci}_{fi}"] = ids
             out[f"dist_{ci}_{fi}"] = d
             ex = coll.explain(q[0], k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
-                              prefilter_threshold=thr)
+                              prefilter_threshold=thr, post_filter_alpha=alpha)
             disk = [e for e in ex if e["kind"] == "disk"]
             out[f"explain_{ci}_{fi}"] = np.array(json.dumps(disk))
     segdirs = coll.segment_dirs()
@@ -174,7 +177,7 @@ def main():
     parse_golden()
     make("coll_hnsw", 48, "cosine", {"type": "hnsw", "M": 8, "ef_construction": 64}, [900, 1300, 700], seed=11)
     make("coll_ivfpq", 32, "l2", {"type": "ivf_pq", "nlist": 16, "pq_m": 8}, [1000, 800], seed=12,
-         filters=FILTERS[:6] + [FILTERS[13]])
+         filters=FILTERS[:6] + [FILTERS[13]], cases=CASES_IVF)
     make("coll_flat", 20, "ip", {"type": "flat"}, [600, 500, 400], seed=13,
          filters=FILTERS[:4] + [FILTERS[8], FILTERS[15]])
 

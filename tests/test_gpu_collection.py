@@ -27,8 +27,8 @@ def colls(tmp_path_factory):
 
 
 def _case(g, ci):
-    strategy, thr, ef, nprobe, k = json.loads(str(g["cases"][ci]))
-    return dict(strategy=strategy, prefilter_threshold=thr, ef=ef, nprobe=nprobe, k=k)
+    strategy, thr, ef, nprobe, k, alpha = json.loads(str(g["cases"][ci]))
+    return dict(strategy=strategy, prefilter_threshold=thr, ef=ef, nprobe=nprobe, k=k, post_filter_alpha=alpha)
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -50,13 +50,17 @@ def test_search_matches_reference(colls, name):
     g, c, _ = cs[name]
     q = g["queries"]
     filters = [str(f) for f in g["filters"]] + [None]
+    bad = []
     for ci in range(len(g["cases"])):
         kw = _case(g, ci)
         for fi, f in enumerate(filters):
             ids, d = c.search(q, filter=f, **kw)
             wi, wd = g[f"ids_{ci}_{fi}"], g[f"dist_{ci}_{fi}"]
-            assert np.array_equal(ids, wi), (name, ci, f)
-            assert np.array_equal(d, wd), (name, ci, f)
+            rows = np.where(~(np.all(ids == wi, axis=1) & np.all(d == wd, axis=1)))[0]
+            if rows.size:
+                r = int(rows[0])
+                bad.append((ci, fi, rows.size, ids[r].tolist(), wi[r].tolist(), d[r].tolist(), wd[r].tolist()))
+    assert not bad, (name, len(bad), bad[:4])
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -64,6 +68,7 @@ def test_explain_matches_reference(colls, name):
     _, cs = colls
     g, c, _ = cs[name]
     filters = [str(f) for f in g["filters"]] + [None]
+    bad = []
     for ci in range(len(g["cases"])):
         kw = _case(g, ci)
         for fi, f in enumerate(filters):
@@ -72,7 +77,9 @@ def test_explain_matches_reference(colls, name):
             assert len(got) == len(want)
             for a, b in zip(got, want):
                 for key in ("id", "strategy", "matches", "live_rows", "distance_computations", "results"):
-                    assert a[key] == b[key], (name, ci, f, key, a, b)
+                    if a[key] != b[key]:
+                        bad.append((ci, fi, key, a[key], b[key]))
+    assert not bad, (name, len(bad), bad[:12])
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -112,6 +119,17 @@ def test_shards_merge_to_the_whole(colls):
                 ids, d = vdb_b200.merge_hits(ctx, lists, k)
                 assert np.array_equal(ids, g[f"ids_{ci}_{fi}"]), (world, ci, f)
                 assert np.array_equal(d, g[f"dist_{ci}_{fi}"]), (world, ci, f)
+
+
+def test_ivfpq_deep_rerank_is_refused(colls):
+    """IVF-PQ re-ranks max(10 k, 100) candidates; the GPU path keeps at most 256, so a post-filter
+    search of k * 10 = 100 (depth 1000) is refused rather than answered differently."""
+    import vdb_b200
+    _, cs = colls
+    g, c, _ = cs["coll_ivfpq"]
+    with pytest.raises(vdb_b200.VdbError) as e:
+        c.search(g["queries"][:2], k=10, strategy="postfilter", post_filter_alpha=10, filter=str(g["filters"][0]))
+    assert e.value.code == vdb_b200.NOT_SUPPORTED
 
 
 def test_errors_match_reference(colls):
