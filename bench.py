@@ -33,8 +33,19 @@ WORKLOAD = ("config 1: SQ8 cosine exhaustive scan + fp32 re-rank of the top 100,
             "1M x 128 rows, 10k-query batches, k=10")
 
 
+C4_SEGMENTS, C4_SEG_ROWS, C4_EF = 64, 1_562_500, 64
+C4_WORKLOAD = ("config 4: sharded filtered multi-segment search, {segs} segments x {rows} rows x 128 "
+               "cosine (year int64 U[1990,2024], 1-5 Zipf(1.1) tags of 1000 words), HNSW M=16 per "
+               "segment built on the GPU, filter year>=2020 AND tags contains a Zipf(1.1) tag per query "
+               "(queries grouped by tag, one filter per group), auto planner, 10k-query batches, k=10, "
+               "ef=64, per-GPU top-k merged after an NCCL all-gather")
+
+
 def parse():
     p = argparse.ArgumentParser()
+    p.add_argument("--workload", default="c1", choices=["c1", "c4"])
+    p.add_argument("--segments", type=int, default=C4_SEGMENTS)
+    p.add_argument("--seg-rows", type=int, default=C4_SEG_ROWS)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
@@ -310,8 +321,252 @@ def traffic_per_launch():
     return None
 
 
+# ------------------------------------------------------------------------------------- config 4
+
+C4_OPTIONS = {"dim": DIM, "metric": "cosine", "index": {"type": "hnsw", "M": 16, "ef_construction": 200},
+              "schema": [{"name": "year", "type": "int64"}, {"name": "tags", "type": "keyword_list"}]}
+
+
+def c4_segment(s, seg_rows):
+    """Segment s of config 4: rows (normalised mixture), external ids, year / tags metadata."""
+    from vdb_b200 import synth
+    rows = synth.mixture(seg_rows, DIM, 100, centres="uniform", lo=0.0, hi=100.0, sigma=10.0, normalize=True,
+                         seed=4, stream=10 + s)
+    ids = np.arange(s * seg_rows, (s + 1) * seg_rows, dtype=np.uint64)
+    years, tags = synth.metadata(seg_rows, seed=1000 + s)
+    return rows, ids, years, tags
+
+
+def c4_queries(nq):
+    """Queries of config 4 and their filters: one filter per distinct Zipf-drawn tag."""
+    from vdb_b200 import synth
+    qs = synth.mixture(nq, DIM, 100, centres="uniform", lo=0.0, hi=100.0, sigma=10.0, normalize=True, seed=4,
+                       stream=9)
+    qtags = synth.zipf_tags(nq, seed=5)
+    distinct = sorted(set(qtags.tolist()))
+    pos = {t: i for i, t in enumerate(distinct)}
+    filters = [json.dumps({"and": [{"field": "year", "gte": 2020}, {"field": "tags", "eq": f"w{t}"}]})
+               for t in distinct]
+    qf = np.array([pos[t] for t in qtags.tolist()], dtype=np.int32)
+    return qs, filters, qf
+
+
+def run_c4_ours(args):
+    import datetime
+    import torch
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                             device_id=torch.device("cuda", local))
+    import vdb_b200
+    from vdb_b200 import sharded, synth
+    ctx = vdb_b200.Context(local)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    coll = vdb_b200.Collection.create(ctx, C4_OPTIONS)
+    t_setup = time.time()
+    build_s = 0.0
+    for s in range(args.segments):
+        if sharded.owner(s, world) != rank:
+            continue
+        rows, ids, years, tags = c4_segment(s, args.seg_rows)
+        rows_dev = torch.from_numpy(rows).cuda()
+        t = time.time()
+        graph = vdb_b200.build_hnsw(ctx, "cosine", rows_dev, DIM, M=16, seed=42 + s)
+        build_s += time.time() - t
+        coll.add_segment(s, s, rows_dev, ids, synth.meta_payload(years, tags), graph)
+        del rows_dev, graph
+    setup_s = time.time() - t_setup
+    qs, filters, qf = c4_queries(args.batch)
+    nq = qs.shape[0]
+    q_dev = torch.from_numpy(qs).cuda()
+    hits = torch.empty(nq * K * 24, dtype=torch.uint8, device="cuda")
+    ids_dev = torch.empty((nq, K), dtype=torch.int64, device="cuda")
+    d_dev = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+
+    def step(queries, out_ids, out_d, qfilt=qf, strategy="auto", hit_buf=hits):
+        n = int(queries.shape[0])
+        if world == 1:
+            coll.search_grouped(queries, filters, qfilt, k=K, ef=C4_EF, strategy=strategy, out=(out_ids, out_d))
+            return
+        coll.search_grouped(queries, filters, qfilt, k=K, ef=C4_EF, strategy=strategy, out=False, hits=hit_buf)
+        gathered = sharded.gather_hits(hit_buf)
+        if rank == 0:
+            vdb_b200.merge_hits(ctx, gathered.view(world, n, K * 24), K, out=(out_ids, out_d))
+
+    for _ in range(max(3, args.warmup)):
+        step(q_dev, ids_dev, d_dev)
+    coll.stats(enable=True)
+    step(q_dev, ids_dev, d_dev)
+    st = coll.stats(enable=False)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(q_dev, ids_dev, d_dev)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    t = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    # e2e: host queries and host results through the same calls.
+    q_host = torch.from_numpy(qs).pin_memory()
+    ids_host = torch.empty((nq, K), dtype=torch.int64).pin_memory()
+    d_host = torch.empty((nq, K), dtype=torch.float32).pin_memory()
+    step(q_host, ids_host, d_host)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_steps = max(2, args.steps // 2)
+    for _ in range(e2e_steps):
+        step(q_host, ids_host, d_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    # Recall@10 against exact filtered search (the prefilter strategy forced on every segment) on
+    # a query sample.
+    ns = min(nq, 1000)
+    sel = np.arange(0, nq, max(1, nq // ns))[:ns]
+    qs_s = torch.from_numpy(np.ascontiguousarray(qs[sel])).cuda()
+    qf_s = np.ascontiguousarray(qf[sel])
+    hb = torch.empty(len(sel) * K * 24, dtype=torch.uint8, device="cuda")
+    a_ids = torch.empty((len(sel), K), dtype=torch.int64, device="cuda")
+    a_d = torch.empty((len(sel), K), dtype=torch.float32, device="cuda")
+    e_ids = torch.empty((len(sel), K), dtype=torch.int64, device="cuda")
+    e_d = torch.empty((len(sel), K), dtype=torch.float32, device="cuda")
+    step(qs_s, a_ids, a_d, qf_s, "auto", hb)
+    step(qs_s, e_ids, e_d, qf_s, "prefilter", hb)
+    recall = None
+    if rank == 0:
+        ai, ei = a_ids.cpu().numpy(), e_ids.cpu().numpy()
+        recall = float(np.mean([len(set(x[x >= 0].tolist()) & set(y[y >= 0].tolist())) / max(1, int((y >= 0).sum()))
+                                for x, y in zip(ai, ei)]))
+    # Work per step summed over ranks (rows gathered exactly or by graph walks, bitmap words).
+    w = torch.tensor([st["exact_rows"], st["index_distance_computations"], st["bitmap_words"],
+                      st["prefilter_pairs"], st["graph_pairs"], st["empty_pairs"]], dtype=torch.float64,
+                     device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(w, op=torch.distributed.ReduceOp.SUM)
+    w = w.cpu().numpy()
+    if rank == 0:
+        _, _, hbm, src = peaks()
+        pd = 128
+        row_bytes = (w[0] + w[1]) * pd * 4
+        bitmap_bytes = w[2] * 4 * 3  # two leaf words read, one result word written
+        achieved = (row_bytes + bitmap_bytes) / (ms / 1000.0) / 1e9 / world
+        total_rows = args.segments * args.seg_rows
+        result = {
+            "metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": C4_WORKLOAD.format(segs=args.segments, rows=args.seg_rows),
+                       "rows": total_rows, "segments": args.segments, "dim": DIM, "batch": nq, "k": K,
+                       "ef": C4_EF, "distinct_filters": len(filters),
+                       "parallelism": f"segments sharded over {world} GPUs" if world > 1 else "single GPU",
+                       "l2": f"inputs larger than L2: {total_rows * pd * 4 / 1e9:.1f} GB of fp32 rows"},
+            "roofline": {"bound": "hbm", "kernel": "whole step (exact-over-bitmap rows, graph walks, bitmaps)",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_kind": f"{src} copy bandwidth", "traffic": None,
+                         "algorithmic": f"per step: {w[0]:.3e} rows scored exactly + {w[1]:.3e} graph "
+                                        f"distance computations (x {pd * 4} B) + {w[2]:.3e} bitmap words "
+                                        "(x 12 B), per GPU"},
+            "plan_per_step": {"prefilter_pairs": w[3], "graph_pairs": w[4], "empty_pairs": w[5]},
+            "recall_at_10_vs_exact_filtered": recall,
+            "e2e": {"value": nq / (float(te.item()) / 1000.0), "unit": "queries/s",
+                    "h2d_bytes_per_step": nq * DIM * 4, "d2h_bytes_per_step": nq * K * 12},
+            "gpu_launches": None,
+            "clocks": clk,
+            "setup_s": {"total": setup_s, "hnsw_build_rank0": build_s},
+        }
+        print(json.dumps(result), flush=True)
+    coll.free()
+    ctx.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def c4_reference_sample(args, ref_segments, seconds):
+    """The reference's Collection (oracle/_ref/libvdbref_engine.so, its own code): BulkLoad of
+    `ref_segments` full-size config-4 segments (it builds its HNSW graphs itself), then
+    SearchBatch per filter group over a query sample of about `seconds` of CPU work. Returns
+    (queries per second over those segments, queries timed, build seconds)."""
+    import shutil
+    import oracle
+    tmp = tempfile.mkdtemp(prefix="vdb_c4_ref_")
+    try:
+        coll = oracle.RefCollection(os.path.join(tmp, "c"), DIM, metric="cosine", index=C4_OPTIONS["index"],
+                                    schema=C4_OPTIONS["schema"], threads=os.cpu_count())
+        t = time.time()
+        for s in range(ref_segments):
+            rows, ids, years, tags = c4_segment(s, args.seg_rows)
+            coll.bulk_load(ids, rows, years, tags)
+        build = time.time() - t
+        qs, filters, qf = c4_queries(args.batch)
+        order = np.argsort(qf, kind="stable")
+
+        def run(qidx):
+            groups = {}
+            for i in qidx:
+                groups.setdefault(int(qf[i]), []).append(i)
+            t0 = time.perf_counter()
+            for f, members in groups.items():
+                coll.search(qs[members], k=K, ef=C4_EF, filter=filters[f])
+            return time.perf_counter() - t0
+
+        probe = order[:: max(1, len(order) // 64)][:64]
+        per_q = max(run(probe) / len(probe), 1e-6)
+        n = int(min(len(order), max(64, seconds / per_q)))
+        sample = order[:: max(1, len(order) // n)][:n]
+        secs = run(sample)
+        coll.close()
+        return len(sample) / secs, len(sample), build
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
+def run_c4_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    ref_segments = 1
+    qps_seg, nq_timed, build = c4_reference_sample(args, ref_segments, args.cpu_seconds)
+    qps = qps_seg * ref_segments / args.segments  # every query searches every segment
+    out = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": args.gpus,
+        "steps": 1, "warmup": 1, "ms_per_step": 1000.0 * args.batch / qps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": C4_WORKLOAD.format(segs=args.segments, rows=args.seg_rows),
+                   "rows": args.segments * args.seg_rows, "segments": args.segments, "batch": args.batch,
+                   "k": K, "ef": C4_EF},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",
+                         "sample": f"{nq_timed} queries (grouped by tag, one SearchBatch per filter) over "
+                                   f"{ref_segments} full segment of {args.seg_rows} rows built by the reference "
+                                   f"in {build:.0f} s; QPS scaled by {ref_segments}/{args.segments} segments "
+                                   f"({cpu_model()})"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "c4":
+        if args.impl == "reference":
+            return run_c4_reference(args)
+        return run_c4_ours(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

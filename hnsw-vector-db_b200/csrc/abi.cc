@@ -3,6 +3,7 @@
 #include "../../include/vdbgpu.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -495,6 +496,14 @@ int vdbgpu_collection_search(vdbgpu_collection* c, const float* queries, uint64_
                                           nullptr, out_ids, out_dist, nullptr);
 }
 
+int vdbgpu_collection_stats(vdbgpu_collection* c, int enable, uint64_t* out, int cap) {
+  if (c == nullptr) return 0;
+  if (enable >= 0) c->c->set_stats(enable != 0);
+  const int n = std::min(cap, vdbgpu::GpuCollection::kStats);
+  for (int i = 0; out != nullptr && i < n; ++i) out[i] = c->c->stats()[i];
+  return out != nullptr ? n : 0;
+}
+
 int vdbgpu_collection_explain(vdbgpu_collection* c, const float* query, uint32_t k,
                               const vdbgpu_search_params* params, const char* filter_json, char* out_json,
                               size_t cap) {
@@ -595,6 +604,30 @@ int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
   s = cx.Sync("merge hits");
   return s.ok() ? VDBGPU_OK : Fail(ctx, s);
 }
+
+int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows, uint64_t nrows, uint32_t dim,
+                      uint32_t padded_dim, uint32_t M, uint32_t candidates, uint64_t seed, void** out_file,
+                      size_t* out_bytes) {
+  if (ctx == nullptr || out_file == nullptr || out_bytes == nullptr || (nrows > 0 && rows == nullptr))
+    return VDBGPU_INVALID_ARGUMENT;
+  *out_file = nullptr;
+  *out_bytes = 0;
+  if (metric < 0 || metric > 2 || dim == 0 || dim > padded_dim || padded_dim % 16 != 0)
+    return Fail(ctx, Status(Status::kInvalidArgument, "bad geometry or metric"));
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  std::string file;
+  Status s = vdbgpu::BuildHnswFile(*ctx->c, metric, rows, nrows, dim, padded_dim, M, candidates, seed, &file);
+  if (!s.ok()) return Fail(ctx, s);
+  void* p = std::malloc(file.size());
+  if (p == nullptr) return Fail(ctx, Status(Status::kResourceExhausted, "host allocation"));
+  std::memcpy(p, file.data(), file.size());
+  *out_file = p;
+  *out_bytes = file.size();
+  return VDBGPU_OK;
+}
+
+void vdbgpu_buffer_free(void* p) { std::free(p); }
 
 int vdbgpu_filter_describe(const char* schema_json, const char* filter_json, char* out, size_t cap) {
   if (schema_json == nullptr || filter_json == nullptr) return VDBGPU_INVALID_ARGUMENT;

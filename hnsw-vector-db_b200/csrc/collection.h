@@ -100,6 +100,14 @@ class GpuCollection {
   // A filter leaf as the GPU evaluates it (collection_host.cc).
   struct LeafSpec;
 
+  // Work of the last Search: [0] queries, [1] rows scored exactly (prefilter and fallback, per
+  // query), [2] distance computations of index searches (only while stats are enabled), [3]
+  // prefilter pairs, [4] filtered-index pairs, [5] post-filter pairs, [6] empty pairs, [7] filter
+  // bitmap words evaluated, [8] (query, segment) index searches.
+  static constexpr int kStats = 9;
+  void set_stats(bool on) { stats_on_ = on; }
+  const uint64_t* stats() const { return stats_; }
+
   const CollectionOptions& options() const { return opt_; }
   uint32_t segments_total() const { return total_segments_; }
   size_t segments_local() const { return segs_.size(); }
@@ -119,6 +127,8 @@ class GpuCollection {
 
   CollectionOptions opt_;
   uint32_t total_segments_ = 0;
+  bool stats_on_ = false;
+  uint64_t stats_[kStats] = {};
   std::vector<std::unique_ptr<GpuSegment>> segs_;
   // Per-batch device scratch (grow-only).
   DeviceBuffer q_raw_, perm_, prepared_, qstatus_, keys_, dc_, short_, leafbits_, pairbits_,

@@ -623,6 +623,8 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
   if (r.k == 0 || r.k > kMaxK) return Status(Status::kInvalidArgument, "k must be in 1..10000");
   if (r.k > kMaxGpuK) return Status(Status::kNotSupported, "k above 240 is not supported on the GPU");
   if (r.nq == 0) return Status::OK();
+  for (auto& v : stats_) v = 0;
+  stats_[0] = r.nq;
   const uint32_t pd = opt_.pd, dim = opt_.dim;
   Batch b;
   b.r = &r;
@@ -697,6 +699,14 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
   b.strat.assign(S * (b.F + 1), "");
   b.matches.assign(S * (b.F + 1), 0);
   VDBGPU_RETURN_IF_ERROR(SearchGroups(ctx, b));
+  if (stats_on_ && S > 0) {
+    std::vector<uint64_t> dc(S * b.nq);
+    VDBGPU_CUDA(cudaMemcpyAsync(dc.data(), b.dc, dc.size() * 8, cudaMemcpyDeviceToHost, st));
+    VDBGPU_RETURN_IF_ERROR(ctx.Sync("stats"));
+    uint64_t tot = 0;
+    for (uint64_t v : dc) tot += v;
+    stats_[2] = tot >= stats_[1] ? tot - stats_[1] : 0;
+  }
 
   // Merge the per-segment lists (collection_impl.cc:1079-1108).
   std::vector<uint32_t> part_no(S);
@@ -789,6 +799,7 @@ Status GpuCollection::RunIndex(Context& ctx, Batch& b, size_t s, uint32_t g, uin
                                const uint32_t* allow, const uint32_t* keep, uint32_t need, int* short_flags) {
   const uint64_t q0 = b.goff[g], nqg = b.goff[g + 1] - q0;
   if (nqg == 0) return Status::OK();
+  stats_[8] += nqg;
   if (kk > 256) return Status(Status::kNotSupported, "post-filter depth above 256 is not supported on the GPU");
   GpuSegment& seg = *segs_[s];
   VDBGPU_RETURN_IF_ERROR(tmp_dist_.ensure(nqg * kk * 4));
@@ -861,6 +872,7 @@ Status GpuCollection::Bitmaps(Context& ctx, Batch& b, const std::vector<uint32_t
   const uint64_t nchunks_w = (max_words + kProgChunkWords - 1) / kProgChunkWords;
   std::vector<int> slot;
   const int nslots = CountSlots(b.leaves, &slot);
+  for (size_t si = 0; si < cs; ++si) stats_[7] += fq.size() * segs_[s0 + si]->words;
   VDBGPU_RETURN_IF_ERROR(leafbits_.ensure(std::max<uint64_t>(1, nslots * cs * max_words) * 4));
   VDBGPU_RETURN_IF_ERROR(pairbits_.ensure(std::max<uint64_t>(1, fq.size() * cs * max_words) * 4));
   VDBGPU_RETURN_IF_ERROR(counts_.ensure(std::max<uint64_t>(1, fq.size() * cs * nchunks_w) * 4));
@@ -1081,6 +1093,8 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
               p.nprobe, static_cast<uint64_t>(std::ceil(static_cast<double>(p.nprobe) / sc)));
         }
         plan[pi] = pl;
+        ++stats_[pl == kEmpty ? 6 : pl == kPre ? 3 : pl == kGraph ? 4 : 5];
+        if (pl == kPre) stats_[1] += m * (b.goff[fq[fi] + 1] - b.goff[fq[fi]]);
         const size_t gi = (s0 + si) * G + fq[fi];
         b.matches[gi] = m;
         b.strat[gi] = pl == kEmpty ? "empty" : pl == kPre ? "prefilter_exact" : pl == kGraph ? "filtered_index" : "post_filter";
@@ -1167,9 +1181,10 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
       for (size_t pi : graph) {
         const size_t fi = pi / cs, s = s0 + pi % cs;
         const uint32_t f = fq[fi];
-        bool any = false;
-        for (uint64_t q = b.goff[f]; q < b.goff[f + 1] && !any; ++q) any = sh[s * b.nq + q] != 0;
-        if (any) fb.push_back(pi);
+        uint64_t nshort = 0;
+        for (uint64_t q = b.goff[f]; q < b.goff[f + 1]; ++q) nshort += sh[s * b.nq + q] != 0 ? 1 : 0;
+        if (nshort > 0) fb.push_back(pi);
+        stats_[1] += nshort * matches[pi];
       }
       VDBGPU_RETURN_IF_ERROR(run_exact(fb, true));
     }

@@ -228,6 +228,158 @@ __device__ __forceinline__ void insert_sorted(uint64_t* arr, int b, int n, uint6
   __syncwarp();
 }
 
+// ------------------------------------------------------------------ pooled candidates
+//
+// Large walks (a filtered walk keeps every reached node as a candidate until it holds ef allowed
+// rows) keep the kPoolFront smallest candidates sorted in shared memory and the rest unsorted in a
+// per-query pool in global memory, with every pool key above every front key (pmin = the pool's
+// smallest key). The front's head is then the least candidate overall: the pop order of the
+// reference's heap. The visited set is a per-query bitmap in global memory.
+
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t w = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    v = w < v ? w : v;
+  }
+  return v;
+}
+
+// Merges one candidate key per lane (where want) into the candidates. Returns false when the pool
+// is full.
+__device__ bool pool_merge(uint64_t key, bool want, uint64_t* front, int& chead, int& ncand, uint64_t* pool,
+                           int& npool, int pool_cap, uint64_t& pmin) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  const bool to_pool = want && key >= pmin;
+  const bool to_front = want && key < pmin;
+  const uint32_t mp = __ballot_sync(0xFFFFFFFFu, to_pool);
+  const int np = __popc(mp);
+  if (npool + np > pool_cap) return false;
+  if (to_pool) pool[npool + __popc(mp & lt)] = key;
+  npool += np;
+  const uint32_t mf = __ballot_sync(0xFFFFFFFFu, to_front);
+  if (mf == 0) return true;
+  uint64_t x[4];
+#pragma unroll
+  for (int e = 0; e < 3; ++e) {
+    const int i = e * 32 + lane;
+    x[e] = i < ncand ? front[chead + i] : ~0ull;
+  }
+  x[3] = to_front ? key : ~0ull;
+  __syncwarp();
+  warp_sort<4>(x);
+  const int total = ncand + __popc(mf);
+  const int keep = total < kPoolFront ? total : kPoolFront;
+  const int nover = total - keep;
+  if (npool + nover > pool_cap) return false;
+  uint64_t over_min = ~0ull;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int i = e * 32 + lane;
+    if (i < keep) {
+      front[i] = x[e];
+    } else if (i < total) {
+      pool[npool + (i - keep)] = x[e];
+      over_min = x[e] < over_min ? x[e] : over_min;
+    }
+  }
+  if (nover > 0) pmin = warp_min_u64(over_min);  // overflow keys lie below the old pmin
+  npool += nover;
+  chead = 0;
+  ncand = keep;
+  __syncwarp();
+  return true;
+}
+
+// Refills the empty front with the kPoolRefill smallest live pool keys (live: not prunable,
+// i.e. nres < ef or dist <= lower): the r-th smallest by a radix select over the 64-bit keys (4
+// bits per pass), then one pass that moves keys <= it to the front (sorted afterwards) and
+// compacts the rest.
+__device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* pool, int& npool, uint64_t& pmin,
+                            uint32_t* hist, bool prune, float lower) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  auto live = [&](uint64_t k) { return !prune || !(neighbor_dist(k) > lower); };
+  int nlive = 0;
+  for (int i = lane; i < npool; i += 32) nlive += live(pool[i]) ? 1 : 0;
+  nlive = __reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(nlive));
+  const int r = nlive < kPoolRefill ? nlive : kPoolRefill;
+  uint64_t thr = ~0ull;
+  if (r > 0 && r < nlive) {
+    uint64_t prefix = 0, pmask = 0;
+    int need = r;
+    for (int shift = 60; shift >= 0; shift -= 4) {
+      if (lane < 16) hist[lane] = 0;
+      __syncwarp();
+      for (int i = lane; i < npool; i += 32) {
+        const uint64_t k = pool[i];
+        if (live(k) && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 15ull], 1u);
+      }
+      __syncwarp();
+      const int c = lane < 16 ? static_cast<int>(hist[lane]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const uint32_t hit = __ballot_sync(0xFFFFFFFFu, lane < 16 && incl >= need);
+      if (hit == 0) {  // cannot happen for a consistent pool; select everything that fits
+        prefix = ~0ull;
+        break;
+      }
+      const int d = __ffs(hit) - 1;
+      const int before = __shfl_sync(0xFFFFFFFFu, incl - c, d);
+      prefix |= static_cast<uint64_t>(d) << shift;
+      pmask |= 15ull << shift;
+      need -= before;
+      __syncwarp();
+    }
+    thr = prefix;  // keys are unique, so exactly r live keys are <= thr
+  }
+  int nsel = 0, nkeep = 0;
+  uint64_t kmin = ~0ull;
+  for (int base = 0; base < npool; base += 32) {
+    const int i = base + lane;
+    const uint64_t k = i < npool ? pool[i] : ~0ull;
+    const bool lv = i < npool && live(k);
+    const bool sel = lv && k <= thr;
+    const bool kp = lv && !sel;
+    const uint32_t ms = __ballot_sync(0xFFFFFFFFu, sel);
+    const uint32_t mk = __ballot_sync(0xFFFFFFFFu, kp);
+    __syncwarp();
+    if (sel && nsel + __popc(ms & lt) < 128) front[nsel + __popc(ms & lt)] = k;
+    if (kp) {
+      pool[nkeep + __popc(mk & lt)] = k;  // nkeep <= base: never ahead of unread entries
+      kmin = k < kmin ? k : kmin;
+    }
+    nsel += __popc(ms);
+    nkeep += __popc(mk);
+    __syncwarp();
+  }
+  kmin = warp_min_u64(kmin);
+  nsel = nsel < 128 ? nsel : 128;
+  npool = nkeep;
+  pmin = nkeep > 0 ? kmin : ~0ull;
+  uint64_t x[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int i = e * 32 + lane;
+    x[e] = i < nsel ? front[i] : ~0ull;
+  }
+  __syncwarp();
+  warp_sort<4>(x);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int i = e * 32 + lane;
+    if (i < nsel) front[i] = x[e];
+  }
+  __syncwarp();
+  chead = 0;
+  ncand = nsel;
+}
+
 template <bool kSq8>
 __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const HnswArgs a) {
   extern __shared__ __align__(16) uint8_t hsm[];
@@ -240,12 +392,13 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
   WarpSmem s;
   s.q = reinterpret_cast<float*>(base);
   s.hash = reinterpret_cast<uint32_t*>(base + static_cast<size_t>(pd) * 4);
-  s.res = reinterpret_cast<uint64_t*>(s.hash + (1u << a.hash_bits));
+  const uint32_t hash_slots = a.hash_bits < 1 ? 2u : (1u << a.hash_bits);  // even: keeps res 8-aligned
+  s.res = reinterpret_cast<uint64_t*>(s.hash + hash_slots);
   s.cand = s.res + a.ef;
   s.nb_id = reinterpret_cast<uint32_t*>(s.cand + a.cand_cap);
   s.nb_d = reinterpret_cast<float*>(s.nb_id + 32);
   for (int i = lane; i < pd; i += 32) s.q[i] = a.queries[static_cast<size_t>(q) * pd + i];
-  for (int i = lane; i < (1 << a.hash_bits); i += 32) s.hash[i] = kEmpty;
+  for (int i = lane; i < static_cast<int>(hash_slots); i += 32) s.hash[i] = kEmpty;
   __syncwarp();
   const bool l2 = a.metric == 0;
   const uint64_t n = a.n;
@@ -296,96 +449,191 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
     const int ef = a.ef;
     const bool filtered = a.allow != nullptr;
     auto allowed = [&](uint32_t id) { return !filtered || ((a.allow[id >> 5] >> (id & 31)) & 1u); };
-    bool full = false;
-    if (lane == 0) visit(s.hash, a.hash_bits, cur, &full);
-    float lower = INFINITY;
-    int chead = 0, ncand = 0;
-    if (allowed(cur)) {
-      if (lane == 0) s.res[0] = pack_neighbor(curd, cur);
-      nres = 1;
-      lower = curd;
-    }
-    if (lane == 0) s.cand[0] = pack_neighbor(curd, cur);
-    ncand = 1;
-    __syncwarp();
-    int steps = 0;
-    while (ncand > 0 && !bad) {
-      const uint64_t c = s.cand[chead];
-      const float cd = neighbor_dist(c);
-      if (cd > lower && (!filtered || nres >= ef)) break;
-      ++chead;
-      --ncand;
-      if (++steps > a.step_limit) {
-        if (lane == 0) set_error(a.status, kDevStepLimit);
-        bad = true;
-        break;
+    if (a.pooled) {
+      // Pooled walk: visited bits and overflow candidates in global memory (see pool_merge).
+      uint32_t* vis = a.visited + static_cast<uint64_t>(q) * a.vwords;
+      uint64_t* pool = a.pool + static_cast<uint64_t>(q) * a.pool_cap;
+      uint32_t* hist = reinterpret_cast<uint32_t*>(s.cand + 128);
+      int npool = 0;
+      uint64_t pmin = ~0ull;
+      if (lane == 0) atomicOr(&vis[cur >> 5], 1u << (cur & 31));
+      float lower = INFINITY;
+      int chead = 0, ncand = 0;
+      if (allowed(cur)) {
+        if (lane == 0) s.res[0] = pack_neighbor(curd, cur);
+        nres = 1;
+        lower = curd;
       }
-      const uint32_t cid = neighbor_id(c);
-      const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
-      const uint32_t cnt = ll[0];
-      uint32_t e = 0;
-      bool fresh = false;
-      if (lane < static_cast<int>(cnt)) {
-        e = ll[1 + lane];
-        if (e >= n) {
-          bad = true;
-        } else {
-          fresh = visit(s.hash, a.hash_bits, e, &full);
-        }
-      }
-      if (__any_sync(0xFFFFFFFFu, bad || full)) {
-        if (lane == 0) set_error(a.status, full ? kDevOverflow : kDevBadIndex);
-        bad = true;
-        break;
-      }
-      const uint32_t fm = __ballot_sync(0xFFFFFFFFu, fresh);
-      const int nf = __popc(fm);
-      if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
+      if (lane == 0) s.cand[0] = pack_neighbor(curd, cur);
+      ncand = 1;
       __syncwarp();
-      dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
-      dc += static_cast<uint64_t>(nf);
-      // Heap updates in list order (the fresh neighbours keep their list order).
-      for (int i = 0; i < nf; ++i) {
-        const uint32_t id = s.nb_id[i];
-        const float de = s.nb_d[i];
-        if (nres < ef || de < lower) {
-          const uint64_t key = pack_neighbor(de, id);
-          if (chead + ncand >= a.cand_cap) {
-            // Compact to the front; if still full, drop the farthest candidate when it can never
-            // be expanded again (results full and it lies beyond the current worst result).
-            for (int k0 = 0; k0 < ncand; k0 += 32) {
-              const int k = k0 + lane;
-              uint64_t v = 0;
-              if (k < ncand) v = s.cand[chead + k];
-              __syncwarp();
-              if (k < ncand) s.cand[k] = v;
-              __syncwarp();
-            }
-            chead = 0;
-            if (ncand >= a.cand_cap) {
-              if (nres >= ef && neighbor_dist(s.cand[ncand - 1]) > lower) {
-                --ncand;
-              } else {
-                if (lane == 0) set_error(a.status, kDevCandOverflow);
-                bad = true;
-                break;
-              }
-            }
+      int steps = 0;
+      while (!bad) {
+        if (ncand == 0) {
+          if (npool == 0) break;
+          // Candidates beyond a full result set's worst can never be expanded (lower only falls).
+          pool_refill(s.cand, chead, ncand, pool, npool, pmin, hist, nres >= ef, lower);
+          if (ncand == 0) break;
+        }
+        const uint64_t c = s.cand[chead];
+        const float cd = neighbor_dist(c);
+        if (cd > lower && (!filtered || nres >= ef)) break;
+        ++chead;
+        --ncand;
+        if (++steps > a.step_limit) {
+          if (lane == 0) set_error(a.status, kDevStepLimit);
+          bad = true;
+          break;
+        }
+        const uint32_t cid = neighbor_id(c);
+        const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
+        const uint32_t cnt = ll[0];
+        uint32_t e = 0;
+        bool fresh = false;
+        if (lane < static_cast<int>(cnt)) {
+          e = ll[1 + lane];
+          if (e >= n) {
+            bad = true;
+          } else {
+            const uint32_t bit = 1u << (e & 31);
+            fresh = (atomicOr(&vis[e >> 5], bit) & bit) == 0u;
           }
-          insert_sorted(s.cand, chead, ncand, key);
-          ++ncand;
-          if (allowed(id)) {
-            if (nres < ef) {
-              insert_sorted(s.res, 0, nres, key);
-              ++nres;
-            } else {
-              // Push then evict the greatest: only changes anything when key is below the max.
-              if (key < s.res[ef - 1]) {
+        }
+        if (__any_sync(0xFFFFFFFFu, bad)) {
+          if (lane == 0) set_error(a.status, kDevBadIndex);
+          bad = true;
+          break;
+        }
+        const uint32_t fm = __ballot_sync(0xFFFFFFFFu, fresh);
+        const int nf = __popc(fm);
+        if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
+        __syncwarp();
+        dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
+        dc += static_cast<uint64_t>(nf);
+        // Result updates in list order decide which neighbours become candidates; the candidates
+        // themselves are merged afterwards (their order of insertion does not matter).
+        uint64_t mykey = ~0ull;
+        bool mywant = false;
+        for (int i = 0; i < nf; ++i) {
+          const uint32_t id = s.nb_id[i];
+          const float de = s.nb_d[i];
+          if (nres < ef || de < lower) {
+            const uint64_t key = pack_neighbor(de, id);
+            if (lane == i) {
+              mykey = key;
+              mywant = true;
+            }
+            if (allowed(id)) {
+              if (nres < ef) {
+                insert_sorted(s.res, 0, nres, key);
+                ++nres;
+              } else if (key < s.res[ef - 1]) {
                 __syncwarp();
                 insert_sorted(s.res, 0, ef - 1, key);
               }
+              lower = neighbor_dist(s.res[nres - 1]);
             }
-            lower = neighbor_dist(s.res[nres - 1]);
+          }
+        }
+        if (!pool_merge(mykey, mywant, s.cand, chead, ncand, pool, npool, a.pool_cap, pmin)) {
+          if (lane == 0) set_error(a.status, kDevCandOverflow);
+          bad = true;
+          break;
+        }
+      }
+    } else {
+      bool full = false;
+      if (lane == 0) visit(s.hash, a.hash_bits, cur, &full);
+      float lower = INFINITY;
+      int chead = 0, ncand = 0;
+      if (allowed(cur)) {
+        if (lane == 0) s.res[0] = pack_neighbor(curd, cur);
+        nres = 1;
+        lower = curd;
+      }
+      if (lane == 0) s.cand[0] = pack_neighbor(curd, cur);
+      ncand = 1;
+      __syncwarp();
+      int steps = 0;
+      while (ncand > 0 && !bad) {
+        const uint64_t c = s.cand[chead];
+        const float cd = neighbor_dist(c);
+        if (cd > lower && (!filtered || nres >= ef)) break;
+        ++chead;
+        --ncand;
+        if (++steps > a.step_limit) {
+          if (lane == 0) set_error(a.status, kDevStepLimit);
+          bad = true;
+          break;
+        }
+        const uint32_t cid = neighbor_id(c);
+        const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
+        const uint32_t cnt = ll[0];
+        uint32_t e = 0;
+        bool fresh = false;
+        if (lane < static_cast<int>(cnt)) {
+          e = ll[1 + lane];
+          if (e >= n) {
+            bad = true;
+          } else {
+            fresh = visit(s.hash, a.hash_bits, e, &full);
+          }
+        }
+        const bool any_full = __any_sync(0xFFFFFFFFu, full);
+        if (__any_sync(0xFFFFFFFFu, bad || full)) {
+          if (lane == 0) set_error(a.status, any_full ? kDevOverflow : kDevBadIndex);
+          bad = true;
+          break;
+        }
+        const uint32_t fm = __ballot_sync(0xFFFFFFFFu, fresh);
+        const int nf = __popc(fm);
+        if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
+        __syncwarp();
+        dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
+        dc += static_cast<uint64_t>(nf);
+        // Heap updates in list order (the fresh neighbours keep their list order).
+        for (int i = 0; i < nf; ++i) {
+          const uint32_t id = s.nb_id[i];
+          const float de = s.nb_d[i];
+          if (nres < ef || de < lower) {
+            const uint64_t key = pack_neighbor(de, id);
+            if (chead + ncand >= a.cand_cap) {
+              // Compact to the front; if still full, drop the farthest candidate when it can never
+              // be expanded again (results full and it lies beyond the current worst result).
+              for (int k0 = 0; k0 < ncand; k0 += 32) {
+                const int k = k0 + lane;
+                uint64_t v = 0;
+                if (k < ncand) v = s.cand[chead + k];
+                __syncwarp();
+                if (k < ncand) s.cand[k] = v;
+                __syncwarp();
+              }
+              chead = 0;
+              if (ncand >= a.cand_cap) {
+                if (nres >= ef && neighbor_dist(s.cand[ncand - 1]) > lower) {
+                  --ncand;
+                } else {
+                  if (lane == 0) set_error(a.status, kDevCandOverflow);
+                  bad = true;
+                  break;
+                }
+              }
+            }
+            insert_sorted(s.cand, chead, ncand, key);
+            ++ncand;
+            if (allowed(id)) {
+              if (nres < ef) {
+                insert_sorted(s.res, 0, nres, key);
+                ++nres;
+              } else {
+                // Push then evict the greatest: only changes anything when key is below the max.
+                if (key < s.res[ef - 1]) {
+                  __syncwarp();
+                  insert_sorted(s.res, 0, ef - 1, key);
+                }
+              }
+              lower = neighbor_dist(s.res[nres - 1]);
+            }
           }
         }
       }

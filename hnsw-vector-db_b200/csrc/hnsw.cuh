@@ -33,6 +33,12 @@ struct HnswArgs {
   int hash_bits;           // visited hash: 1 << hash_bits slots per warp
   int cand_cap;            // candidate array capacity per warp
   int warps;               // queries (warps) per block, 1..4
+  // Pooled mode (large walks, e.g. filtered): visited bits and overflow candidates in global memory.
+  int pooled;
+  uint32_t* visited;       // nq x vwords bitmaps, zeroed before the launch
+  uint64_t vwords;
+  uint64_t* pool;          // nq x pool_cap candidate keys
+  int pool_cap;
   int step_limit;          // bounded walk: expansions per query
   float* out_dist;
   uint32_t* out_row;
@@ -40,9 +46,16 @@ struct HnswArgs {
   int* status;
 };
 
+// Pooled mode: sorted candidates kept in shared memory (the rest wait in the global pool).
+constexpr int kPoolFront = 96;
+constexpr int kPoolRefill = 64;
+constexpr int kPoolFrontSlots = 128 + 8;  // 128 sort slots + a 16-counter histogram
+
 // Shared memory of one query's warp: query, visited hash, results, candidates, neighbour scratch.
 __host__ __device__ inline size_t HnswWarpSmemBytes(int pd, int hash_bits, int ef, int cand_cap) {
-  const size_t b = static_cast<size_t>(pd) * 4 + (static_cast<size_t>(1) << hash_bits) * 4 +
+  // The hash holds at least 2 slots so the 8-byte arrays after it stay 8-byte aligned.
+  const size_t slots = hash_bits < 1 ? 2 : (static_cast<size_t>(1) << hash_bits);
+  const size_t b = static_cast<size_t>(pd) * 4 + slots * 4 +
                    static_cast<size_t>(ef) * 8 + static_cast<size_t>(cand_cap) * 8 + 32 * 4 + 32 * 4;
   return (b + 15) / 16 * 16;
 }

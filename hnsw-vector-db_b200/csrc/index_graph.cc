@@ -120,25 +120,38 @@ class HnswGpuIndex final : public GpuIndex {
     a.out_row = b.out_row;
     a.out_dc = b.dist_comps;
     a.status = ctx.status_word();
-    // Visited hash and candidate array sized for an unfiltered walk. A walk that overflows one
-    // (a filtered walk keeps every reached node as a candidate until it holds ef allowed rows,
-    // as the reference's unbounded heap does) reruns the batch with that structure doubled,
-    // and with fewer queries per block once four no longer fit in shared memory.
+    // Unfiltered walks keep their state in shared memory: a visited hash and a candidate array
+    // sized for the walk; one that overflows reruns the batch with that structure doubled (and
+    // fewer queries per block once four no longer fit). Filtered walks keep every reached node
+    // as a candidate until they hold ef allowed rows (the reference's unbounded heap), so they
+    // run pooled: visited bits and candidates beyond a sorted front in global memory, the pool
+    // growing fourfold on overflow.
+    const bool pooled = b.allow != nullptr;
     int bits = std::max(11, Log2Ceil(32 * ef));
     int cap = static_cast<int>(2 * ef + 64);
+    int pool_cap = static_cast<int>(std::max<uint64_t>(4096, 32 * ef));
     for (;;) {
-      a.hash_bits = bits;
-      a.cand_cap = cap;
+      a.pooled = pooled ? 1 : 0;
+      a.hash_bits = pooled ? 1 : bits;  // pooled walks mark visits in global memory
+      a.cand_cap = pooled ? kPoolFrontSlots : cap;
+      if (pooled) {
+        a.vwords = (n_ + 31) / 32;
+        VDBGPU_RETURN_IF_ERROR(visited_.ensure(std::max<uint64_t>(1, b.nq * a.vwords) * 4));
+        VDBGPU_RETURN_IF_ERROR(pool_.ensure(std::max<uint64_t>(1, b.nq) * pool_cap * 8));
+        VDBGPU_CUDA(cudaMemsetAsync(visited_.get(), 0, b.nq * a.vwords * 4, ctx.stream()));
+        a.visited = visited_.as<uint32_t>();
+        a.pool = pool_.as<uint64_t>();
+        a.pool_cap = pool_cap;
+      }
       a.warps = 0;
       for (int w = 4; w >= 1; w /= 2)
-        if (static_cast<size_t>(w) * HnswWarpSmemBytes(a.pd, bits, a.ef, cap) <= 227 * 1024) {
+        if (static_cast<size_t>(w) * HnswWarpSmemBytes(a.pd, a.hash_bits, a.ef, a.cand_cap) <= 227 * 1024) {
           a.warps = w;
           break;
         }
       if (a.warps == 0)
         return Status(Status::kNotSupported,
-                      "the graph walk's state exceeds the GPU's shared memory (a very selective filter "
-                      "reaches too much of the graph); use the prefilter strategy");
+                      "the graph walk's state exceeds the GPU's shared memory; use a smaller ef");
       ctx.Mark(0);
       ctx.Mark(1);
       VDBGPU_CUDA(LaunchHnswSearch(a, ctx.stream()));
@@ -148,9 +161,11 @@ class HnswGpuIndex final : public GpuIndex {
       if (s.ok()) return s;
       const bool hash_full = s.message().find("code 6") != std::string::npos;
       const bool cand_full = s.message().find("code 9") != std::string::npos;
-      if (hash_full && bits < 16) {
+      if (pooled && cand_full && pool_cap < (1 << 24)) {
+        pool_cap *= 4;
+      } else if (!pooled && hash_full && bits < 16) {
         ++bits;
-      } else if (cand_full && cap < (1 << 16)) {
+      } else if (!pooled && cand_full && cap < (1 << 16)) {
         cap *= 2;
       } else {
         return s;
@@ -163,6 +178,7 @@ class HnswGpuIndex final : public GpuIndex {
   uint64_t n_ = 0;
   HnswGraphData g_;
   DeviceBuffer rows_, codes_, vmin_, scale_, links0_, upper_, upper_off_, level_;
+  DeviceBuffer visited_, pool_;  // pooled walks' scratch (grow-only)
 };
 
 }  // namespace

@@ -235,6 +235,11 @@ Status LoadGraphOrListIndex(Context& ctx, int type, std::string_view body, int m
                             const float* rows, uint64_t n, uint32_t dim, uint32_t pd,
                             std::unique_ptr<GpuIndex>* out);
 
+// An HNSW graph over rows (host or device, n x pd) built on the GPU, as a complete index file in
+// the reference's index.hnsw format (hnsw_build.cc).
+Status BuildHnswFile(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim, uint32_t pd, uint32_t M,
+                     uint32_t kcand, uint64_t seed, std::string* file);
+
 // Shared by flat and SQ8-flat search: a tensor-core pre-rank of every row followed by the exact
 // finalize. Declared here so the HNSW/IVF indexes can reuse it for exact fallbacks.
 struct ScanOperands {

@@ -17,6 +17,7 @@
 #include <cstring>
 #include <random>
 #include <thread>
+#include <string>
 #include <vector>
 
 namespace {
@@ -142,6 +143,62 @@ void synth_zipf(uint64_t n, uint32_t vocab, double zipf_s, uint64_t seed, uint32
     auto w = static_cast<uint32_t>(std::lower_bound(cdf.begin(), cdf.end(), u(rng)) - cdf.begin());
     out[i] = w >= vocab ? vocab - 1 : w;
   }
+}
+
+// The payload of a segment's meta.bin (SegmentWriter, src/storage/segment_writer.cc:103-120) for
+// the schema [year int64, tags keyword_list]: u64 rows, u64 offsets[rows + 1], then every row as
+// EncodeMetaRow writes it (src/meta/schema.cc:97-124) with the tags as keywords "w<id>" in drawn
+// order (unused slots = UINT32_MAX skipped). Returns the payload size; writes only when it fits
+// in cap (out may be null to size it).
+uint64_t synth_meta_payload(uint64_t n, const int64_t* years, const uint32_t* tags, uint32_t max_tags,
+                            uint8_t* out, uint64_t cap) {
+  auto row_bytes = [&](uint64_t i) {
+    uint64_t b = 2 + (2 + 1 + 8) + (2 + 1 + 4);
+    for (uint32_t j = 0; j < max_tags; ++j) {
+      const uint32_t w = tags[i * max_tags + j];
+      if (w == UINT32_MAX) continue;
+      b += 4 + 1 + std::to_string(w).size();
+    }
+    return b;
+  };
+  uint64_t total = 8 + (n + 1) * 8;
+  for (uint64_t i = 0; i < n; ++i) total += row_bytes(i);
+  if (out == nullptr || cap < total) return total;
+  auto put = [](uint8_t*& p, const void* v, size_t k) {
+    std::memcpy(p, v, k);
+    p += k;
+  };
+  uint8_t* p = out;
+  put(p, &n, 8);
+  uint8_t* offs = p;
+  p += (n + 1) * 8;
+  uint8_t* base = p;
+  for (uint64_t i = 0; i < n; ++i) {
+    const uint64_t o = static_cast<uint64_t>(p - base);
+    std::memcpy(offs + i * 8, &o, 8);
+    const uint16_t count = 2, f0 = 0, f1 = 1;
+    const uint8_t t_int = 0, t_list = 3;
+    put(p, &count, 2);
+    put(p, &f0, 2);
+    put(p, &t_int, 1);
+    put(p, &years[i], 8);
+    put(p, &f1, 2);
+    put(p, &t_list, 1);
+    uint32_t nt = 0;
+    for (uint32_t j = 0; j < max_tags; ++j) nt += tags[i * max_tags + j] != UINT32_MAX ? 1u : 0u;
+    put(p, &nt, 4);
+    for (uint32_t j = 0; j < max_tags; ++j) {
+      const uint32_t w = tags[i * max_tags + j];
+      if (w == UINT32_MAX) continue;
+      const std::string s = "w" + std::to_string(w);
+      const uint32_t len = static_cast<uint32_t>(s.size());
+      put(p, &len, 4);
+      put(p, s.data(), s.size());
+    }
+  }
+  const uint64_t o = static_cast<uint64_t>(p - base);
+  std::memcpy(offs + n * 8, &o, 8);
+  return total;
 }
 
 }  // extern "C"

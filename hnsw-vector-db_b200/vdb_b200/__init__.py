@@ -104,12 +104,17 @@ _SIGNATURES = {
                                                         ctypes.POINTER(SearchParams),
                                                         ctypes.POINTER(ctypes.c_char_p), ctypes.c_uint32,
                                                         _P, _P, _P, _P]),
+    "vdbgpu_collection_stats": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int]),
     "vdbgpu_collection_explain": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.POINTER(SearchParams),
                                                  ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
     "vdbgpu_collection_filter_bitmap": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_uint32, _P,
                                                        ctypes.POINTER(ctypes.c_uint64)]),
     "vdbgpu_merge_hits": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
                                          _P, _P, _P]),
+    "vdbgpu_hnsw_build": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
+                                         ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, ctypes.POINTER(_P),
+                                         ctypes.POINTER(ctypes.c_size_t)]),
+    "vdbgpu_buffer_free": (None, [_P]),
     "vdbgpu_filter_describe": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                               ctypes.c_size_t]),
 }
@@ -486,6 +491,15 @@ class Collection:
                                                        _filter_text(filter), buf, len(buf)))
         return json.loads(buf.value.decode())
 
+    STAT_NAMES = ("queries", "exact_rows", "index_distance_computations", "prefilter_pairs",
+                  "graph_pairs", "postfilter_pairs", "empty_pairs", "bitmap_words", "index_searches")
+
+    def stats(self, enable: Optional[bool] = None) -> dict:
+        """Work counters of the last search (index distance computations only while enabled)."""
+        out = np.zeros(len(self.STAT_NAMES), np.uint64)
+        n = lib().vdbgpu_collection_stats(self._h, -1 if enable is None else int(bool(enable)), _ptr(out), out.size)
+        return {k: int(v) for k, v in zip(self.STAT_NAMES[:n], out[:n])}
+
     def filter_bitmap(self, filter, segment_id: int, rows: int) -> Tuple[np.ndarray, int]:
         """The rows of one segment a filter selects: (uint32 words, bit r of word r//32; count)."""
         words = np.zeros((rows + 31) // 32, np.uint32)
@@ -524,6 +538,21 @@ def merge_hits(ctx: Context, lists, k: int, out=None, hits=None):
         ids, dists = out
     ctx.check(lib().vdbgpu_merge_hits(ctx._h, _ptr(lists), nl, nq, int(k), _ptr(ids), _ptr(dists), _ptr(hits)))
     return ids, dists
+
+
+def build_hnsw(ctx: Context, metric, rows, dim: int, M: int = 16, candidates: int = 0, seed: int = 42) -> bytes:
+    """An HNSW index file (the reference's index.hnsw format) built on the GPU over rows
+    (n, padded_dim) float32, numpy or a CUDA tensor."""
+    m = METRICS[metric] if isinstance(metric, str) else int(metric)
+    n, pd = int(rows.shape[0]), int(rows.shape[1])
+    p = _P()
+    nb = ctypes.c_size_t(0)
+    ctx.check(lib().vdbgpu_hnsw_build(ctx._h, m, _ptr(rows), n, int(dim), pd, int(M), int(candidates), int(seed),
+                                      ctypes.byref(p), ctypes.byref(nb)))
+    try:
+        return ctypes.string_at(p, nb.value)
+    finally:
+        lib().vdbgpu_buffer_free(p)
 
 
 def filter_describe(schema, filter) -> Tuple[int, str]:

@@ -28,6 +28,9 @@ def _l():
         l.synth_metadata.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32,
                                      ctypes.c_uint32, ctypes.c_double, ctypes.c_uint64, ctypes.c_void_p,
                                      ctypes.c_void_p, ctypes.c_int]
+        l.synth_meta_payload.restype = ctypes.c_uint64
+        l.synth_meta_payload.argtypes = [ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                                         ctypes.c_void_p, ctypes.c_uint64]
         l.synth_zipf.restype = None
         l.synth_zipf.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_double, ctypes.c_uint64,
                                  ctypes.c_void_p]
@@ -78,6 +81,17 @@ def metadata(n, seed=4, year_lo=1990, year_hi=2024, max_tags=5, vocab=1000, zipf
     _l().synth_metadata(n, year_lo, year_hi, max_tags, vocab, zipf_s, seed, years.ctypes.data,
                         tags.ctypes.data, threads)
     return years, tags
+
+
+def meta_payload(years, tags) -> bytes:
+    """meta.bin's payload for the schema [year int64, tags keyword_list] (tags as "w<id>")."""
+    years = np.ascontiguousarray(years, dtype=np.int64)
+    tags = np.ascontiguousarray(tags, dtype=np.uint32)
+    n, mt = tags.shape
+    size = _l().synth_meta_payload(n, years.ctypes.data, tags.ctypes.data, mt, None, 0)
+    out = np.empty(size, dtype=np.uint8)
+    _l().synth_meta_payload(n, years.ctypes.data, tags.ctypes.data, mt, out.ctypes.data, size)
+    return out.tobytes()
 
 
 def zipf_tags(n, vocab=1000, zipf_s=1.1, seed=5):

@@ -263,6 +263,14 @@ VDBGPU_API int vdbgpu_collection_search_grouped(vdbgpu_collection* c, const floa
                                                 const int32_t* query_filter, uint64_t* out_ids,
                                                 float* out_dist, vdbgpu_hit* out_hits);
 
+/* Work counters of the collection's last search (the batch form of SearchExplain's
+ * distance_computations): out[0] queries, [1] rows scored exactly (prefilter and exact
+ * fallback, summed over queries), [2] distance computations of index searches (counted only
+ * while enabled), [3] prefilter (filter, segment) pairs, [4] filtered-index pairs, [5] post-filter
+ * pairs, [6] empty pairs, [7] filter bitmap words evaluated, [8] (query, segment) index searches.
+ * enable: 1 / 0 turns the index-search count on / off, -1 leaves it. Returns the count written. */
+VDBGPU_API int vdbgpu_collection_stats(vdbgpu_collection* c, int enable, uint64_t* out, int cap);
+
 /* Collection::Search with explain for one query: JSON array with one object per local disk
  * segment {"id", "strategy", "matches", "live_rows", "distance_computations", "results"}
  * (SegmentExplain, include/vdb/collection.h:45-58). Returns VDBGPU_RESOURCE_EXHAUSTED when cap
@@ -285,6 +293,22 @@ VDBGPU_API int vdbgpu_collection_filter_bitmap(vdbgpu_collection* c, const char*
 VDBGPU_API int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
                                  uint64_t nq, uint32_t k, uint64_t* out_ids, float* out_dist,
                                  vdbgpu_hit* out_hits);
+
+/* Index::build for HNSW (HnswIndex, src/index/hnsw/hnsw_index.h:12-41) on the GPU: a graph over
+ * nrows rows (nrows x padded_dim floats, host or device; cosine rows already normalised) with
+ * M links per upper layer and 2M on layer 0, returned as a complete index file in the
+ * reference's format (HnswIndex::save, hnsw_index.cc:36-41), readable by vdbgpu_index_load,
+ * vdbgpu_collection_add_segment and the reference's LoadIndex. Nodes are linked by
+ * HnswGraph's neighbour heuristic (hnsw_graph.h:569-616) applied to every node's `candidates`
+ * exact nearest neighbours (0 = 4M, at most 127) instead of the reference's one-at-a-time
+ * insertion, so the graph is not the reference's. Levels follow level_for (hnsw_graph.h:
+ * 470-474) with `seed`. *out_file is malloc'd; release it with vdbgpu_buffer_free. */
+VDBGPU_API int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows, uint64_t nrows,
+                                 uint32_t dim, uint32_t padded_dim, uint32_t M, uint32_t candidates,
+                                 uint64_t seed, void** out_file, size_t* out_bytes);
+
+/* Releases a buffer returned by the library (vdbgpu_hnsw_build). */
+VDBGPU_API void vdbgpu_buffer_free(void* p);
 
 /* FilterExpr::Parse (src/meta/filter_parser.cc) against a schema (JSON, schema.cc:246-270),
  * without a GPU: VDBGPU_OK with the parsed filter's description (FilterExpr::ToString) in out,

@@ -392,6 +392,14 @@ class HnswFile:
     upper: np.ndarray
     upper_off: np.ndarray
 
+    def links(self, node: int, layer: int) -> list:
+        """The link list of node on layer (hnsw_graph.h links_at)."""
+        if layer == 0:
+            b = node * (1 + 2 * self.M)
+            return self.links0[b + 1:b + 1 + int(self.links0[b])].tolist()
+        b = int(self.upper_off[node]) + (layer - 1) * (1 + self.M)
+        return self.upper[b + 1:b + 1 + int(self.upper[b])].tolist()
+
 
 def _parse_graph(r: _R) -> HnswFile:
     """HnswGraph::serialize layout (src/index/hnsw/hnsw_graph.h:387-401)."""
