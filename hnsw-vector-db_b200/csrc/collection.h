@@ -131,6 +131,7 @@ class GpuCollection {
   uint64_t stats_[kStats] = {};
   std::vector<std::unique_ptr<GpuSegment>> segs_;
   // Per-batch device scratch (grow-only).
+  MultiScratch multi_;
   DeviceBuffer q_raw_, perm_, prepared_, qstatus_, keys_, dc_, short_, leafbits_, pairbits_,
       counts_, matches_, rowlists_, tmp_dist_, tmp_row_, tasks_, merged_, out_ids_, out_dist_;
 };

@@ -9,6 +9,7 @@
 #include <sstream>
 
 #include "formats.h"
+#include "hnsw.cuh"
 
 namespace vdbgpu {
 
@@ -1165,8 +1166,44 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
       else if (plan[pi] == kPost) post.push_back(pi);
     }
     VDBGPU_RETURN_IF_ERROR(run_exact(pre, false));
-    // ---- filtered index search (planner.cc:88-105).
-    for (size_t pi : graph) {
+    // ---- filtered index search (planner.cc:88-105). HNSW segments: every (pair, query) walk of
+    // the chunk in batched launches; other index types: one index search per pair.
+    bool batched = false;
+    if (!graph.empty()) {
+      std::vector<const GpuIndex*> idx(cs);
+      bool hnsw = true;
+      for (size_t si = 0; si < cs; ++si) {
+        idx[si] = segs_[s0 + si]->index.get();
+        const int t = idx[si]->type();
+        hnsw = hnsw && (t == kIndexHnsw || t == kIndexHnswSq8);
+      }
+      if (hnsw) {
+        std::vector<HnswItem> items;
+        for (size_t pi : graph) {
+          const size_t fi = pi / cs, si = pi % cs;
+          const uint32_t f = fq[fi];
+          const uint32_t need = p.strategy == 0 ? static_cast<uint32_t>(std::min<uint64_t>(b.k, matches[pi])) : 0u;
+          for (uint64_t q = b.goff[f]; q < b.goff[f + 1]; ++q) {
+            HnswItem it{};
+            it.seg = static_cast<uint32_t>(si);
+            it.query = static_cast<uint32_t>(q);
+            it.allow = pair_ptr(fi, si);
+            it.slot = (s0 + si) * b.nq + q;
+            it.need = need;
+            items.push_back(it);
+          }
+        }
+        Status st = HnswSearchMulti(ctx, idx, items.data(), items.size(), b.prepared, b.k, p, b.keys, b.dc, b.shortf,
+                                    &multi_);
+        if (st.ok()) {
+          batched = true;
+          stats_[8] += items.size();
+        } else if (st.code() != Status::kNotSupported) {
+          return st;
+        }
+      }
+    }
+    for (size_t pi : batched ? std::vector<size_t>() : graph) {
       const size_t fi = pi / cs, si = pi % cs, s = s0 + si;
       const uint32_t f = fq[fi];
       const uint32_t need = p.strategy == 0 ? static_cast<uint32_t>(std::min<uint64_t>(b.k, matches[pi])) : 0u;

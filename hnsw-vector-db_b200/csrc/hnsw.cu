@@ -381,11 +381,35 @@ __device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* p
 }
 
 template <bool kSq8>
-__global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const HnswArgs a) {
+__global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const HnswArgs a0) {
   extern __shared__ __align__(16) uint8_t hsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (q >= a.nq) return;
+  if (q >= a0.nq) return;
+  // The walk's graph: the launch's index, or in multi-segment mode this warp's item's segment.
+  HnswArgs a = a0;
+  const float* qsrc = a0.queries + static_cast<size_t>(q) * a0.pd;
+  uint64_t slot = static_cast<uint64_t>(q);
+  uint32_t need = 0;
+  if (a0.segs != nullptr) {
+    const HnswItem it = a0.items[q];
+    const HnswSegment sg = a0.segs[it.seg];
+    a.rows = sg.rows;
+    a.codes = sg.codes;
+    a.vmin = sg.vmin;
+    a.scale = sg.scale;
+    a.links0 = sg.links0;
+    a.upper = sg.upper;
+    a.upper_off = sg.upper_off;
+    a.level = sg.level;
+    a.n = sg.n;
+    a.entry = sg.entry;
+    a.max_level = sg.max_level;
+    a.allow = it.allow;
+    qsrc = a0.queries + static_cast<size_t>(it.query) * a0.pd;
+    slot = it.slot;
+    need = it.need;
+  }
   const int pd = a.pd;
   const size_t per_warp = HnswWarpSmemBytes(pd, a.hash_bits, a.ef, a.cand_cap);
   uint8_t* base = hsm + warp * per_warp;
@@ -397,7 +421,7 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
   s.cand = s.res + a.ef;
   s.nb_id = reinterpret_cast<uint32_t*>(s.cand + a.cand_cap);
   s.nb_d = reinterpret_cast<float*>(s.nb_id + 32);
-  for (int i = lane; i < pd; i += 32) s.q[i] = a.queries[static_cast<size_t>(q) * pd + i];
+  for (int i = lane; i < pd; i += 32) s.q[i] = qsrc[i];
   for (int i = lane; i < static_cast<int>(hash_slots); i += 32) s.hash[i] = kEmpty;
   __syncwarp();
   const bool l2 = a.metric == 0;
@@ -678,6 +702,15 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
     }
   }
   const int kout = a.k;
+  if (a0.segs != nullptr) {
+    for (int i = lane; i < kout; i += 32)
+      a0.out_keys[slot * kout + i] = (!bad && i < nout) ? s.res[i] : ~0ull;
+    if (lane == 0) {
+      if (a0.out_dc != nullptr) a0.out_dc[slot] = dc;
+      if (a0.out_short != nullptr) a0.out_short[slot] = (!bad && static_cast<uint32_t>(nout) < need) ? 1 : 0;
+    }
+    return;
+  }
   for (int i = lane; i < kout; i += 32) {
     const size_t o = static_cast<size_t>(q) * kout + i;
     if (!bad && i < nout) {

@@ -7,6 +7,32 @@
 
 namespace vdbgpu {
 
+// One segment's graph, for walks over several segments in one launch.
+struct HnswSegment {
+  const float* rows;
+  const uint8_t* codes;
+  const float* vmin;
+  const float* scale;
+  const uint32_t* links0;
+  const uint32_t* upper;
+  const uint64_t* upper_off;
+  const uint8_t* level;
+  uint64_t n;
+  uint32_t entry;
+  int max_level;
+};
+
+// One walk of a multi-segment launch: segment, query row, allowed rows, and the output slot
+// (keys at slot * k, distance computations and the short flag at slot).
+struct HnswItem {
+  uint32_t seg;
+  uint32_t query;
+  const uint32_t* allow;
+  uint64_t slot;
+  uint32_t need;  // fewer results than this sets the short flag (the exact fallback)
+  uint32_t pad;
+};
+
 struct HnswArgs {
   int nq, pd;
   int k;           // results written per query
@@ -39,6 +65,12 @@ struct HnswArgs {
   uint64_t vwords;
   uint64_t* pool;          // nq x pool_cap candidate keys
   int pool_cap;
+  // Multi-segment mode (segs non-null): warp i walks items[i] over segs[items[i].seg] and writes
+  // packed (dist, row) keys to out_keys, its count to out_dc and the short flag to out_short.
+  const HnswSegment* segs;
+  const HnswItem* items;
+  uint64_t* out_keys;
+  int* out_short;
   int step_limit;          // bounded walk: expansions per query
   float* out_dist;
   uint32_t* out_row;

@@ -173,6 +173,23 @@ class HnswGpuIndex final : public GpuIndex {
     }
   }
 
+  bool sq8() const { return sq8_; }
+  uint32_t graph_m() const { return g_.M; }
+  // The device arrays a multi-segment walk reads.
+  void Describe(HnswSegment* d) const {
+    d->rows = rows_.as<float>();
+    d->codes = sq8_ ? codes_.as<uint8_t>() : nullptr;
+    d->vmin = sq8_ ? vmin_.as<float>() : nullptr;
+    d->scale = sq8_ ? scale_.as<float>() : nullptr;
+    d->links0 = links0_.as<uint32_t>();
+    d->upper = upper_.as<uint32_t>();
+    d->upper_off = upper_off_.as<uint64_t>();
+    d->level = level_.as<uint8_t>();
+    d->n = n_;
+    d->entry = g_.entry;
+    d->max_level = g_.size > 0 ? g_.max_level : -1;
+  }
+
  private:
   bool sq8_;
   uint64_t n_ = 0;
@@ -182,6 +199,90 @@ class HnswGpuIndex final : public GpuIndex {
 };
 
 }  // namespace
+
+Status HnswSearchMulti(Context& ctx, const std::vector<const GpuIndex*>& indexes, const HnswItem* items,
+                       size_t nitems, const float* queries, uint32_t k, const SearchParams& p, uint64_t* out_keys,
+                       uint64_t* out_dc, int* out_short, MultiScratch* sc) {
+  if (nitems == 0) return Status::OK();
+  std::vector<HnswSegment> segs(indexes.size());
+  const HnswGpuIndex* first = nullptr;
+  uint64_t max_n = 1;
+  for (size_t i = 0; i < indexes.size(); ++i) {
+    const auto* h = dynamic_cast<const HnswGpuIndex*>(indexes[i]);
+    if (h == nullptr) return Status(Status::kNotSupported, "not an HNSW index");
+    if (first == nullptr) first = h;
+    if (h->sq8() != first->sq8() || h->graph_m() != first->graph_m() || h->pd != first->pd || h->metric != first->metric)
+      return Status(Status::kNotSupported, "segments with different graph parameters");
+    h->Describe(&segs[i]);
+    max_n = std::max<uint64_t>(max_n, segs[i].n);
+  }
+  // Search parameters exactly as HnswGpuIndex::Search derives them.
+  const uint64_t pef = p.ef;
+  uint64_t depth = 0, kg = k, ef = std::max<uint64_t>(pef, k);
+  if (first->sq8()) {
+    depth = p.rerank < 0 ? std::max<uint64_t>(pef, k) : static_cast<uint64_t>(p.rerank);
+    ef = std::max({pef, static_cast<uint64_t>(k), depth});
+    kg = depth == 0 ? k : std::max<uint64_t>(depth, k);
+    ef = std::max(ef, kg);
+  }
+  if (ef > 4096) return Status(Status::kNotSupported, "ef above 4096 is not supported on the GPU");
+  VDBGPU_RETURN_IF_ERROR(sc->segs.ensure(segs.size() * sizeof(HnswSegment)));
+  VDBGPU_CUDA(cudaMemcpyAsync(sc->segs.get(), segs.data(), segs.size() * sizeof(HnswSegment), cudaMemcpyHostToDevice,
+                              ctx.stream()));
+  HnswArgs a{};
+  a.pd = static_cast<int>(first->pd);
+  a.k = static_cast<int>(k);
+  a.k_graph = static_cast<int>(kg);
+  a.ef = static_cast<int>(ef);
+  a.depth = static_cast<int>(depth);
+  a.metric = first->metric;
+  a.order = ctx.order();
+  a.queries = queries;
+  a.M0 = 2 * first->graph_m();
+  a.M = first->graph_m();
+  a.step_limit = 1 << 22;
+  a.status = ctx.status_word();
+  a.pooled = 1;
+  a.hash_bits = 1;
+  a.cand_cap = kPoolFrontSlots;
+  a.vwords = (max_n + 31) / 32;
+  a.segs = sc->segs.as<HnswSegment>();
+  a.out_keys = out_keys;
+  a.out_dc = out_dc;
+  a.out_short = out_short;
+  a.codes = first->sq8() ? segs[0].codes : nullptr;  // selects the SQ8 kernel
+  a.warps = 4;
+  // Walks per launch: their visited bitmaps and candidate pools within ~4 GiB.
+  int pool_cap = static_cast<int>(std::max<uint64_t>(8192, 64 * ef));
+  size_t done = 0;
+  while (done < nitems) {
+    const uint64_t per = a.vwords * 4 + static_cast<uint64_t>(pool_cap) * 8;
+    const size_t chunk = static_cast<size_t>(std::max<uint64_t>(
+        1, std::min<uint64_t>(nitems - done, (4ull << 30) / per)));
+    VDBGPU_RETURN_IF_ERROR(sc->items.ensure(chunk * sizeof(HnswItem)));
+    VDBGPU_RETURN_IF_ERROR(sc->visited.ensure(chunk * a.vwords * 4));
+    VDBGPU_RETURN_IF_ERROR(sc->pool.ensure(chunk * static_cast<uint64_t>(pool_cap) * 8));
+    VDBGPU_CUDA(cudaMemcpyAsync(sc->items.get(), items + done, chunk * sizeof(HnswItem), cudaMemcpyHostToDevice,
+                                ctx.stream()));
+    VDBGPU_CUDA(cudaMemsetAsync(sc->visited.get(), 0, chunk * a.vwords * 4, ctx.stream()));
+    a.nq = static_cast<int>(chunk);
+    a.items = sc->items.as<HnswItem>();
+    a.visited = sc->visited.as<uint32_t>();
+    a.pool = sc->pool.as<uint64_t>();
+    a.pool_cap = pool_cap;
+    VDBGPU_CUDA(LaunchHnswSearch(a, ctx.stream()));
+    Status s = ctx.Sync("hnsw multi-segment search");
+    if (!s.ok()) {
+      if (s.message().find("code 9") != std::string::npos && pool_cap < (1 << 22)) {
+        pool_cap *= 4;  // a walk's candidate pool overflowed: rerun this chunk with larger pools
+        continue;
+      }
+      return s;
+    }
+    done += chunk;
+  }
+  return Status::OK();
+}
 
 Status LoadGraphOrListIndex(Context& ctx, int type, std::string_view body, int metric,
                             const float* rows, uint64_t n, uint32_t dim, uint32_t pd,

@@ -235,6 +235,17 @@ Status LoadGraphOrListIndex(Context& ctx, int type, std::string_view body, int m
                             const float* rows, uint64_t n, uint32_t dim, uint32_t pd,
                             std::unique_ptr<GpuIndex>* out);
 
+// Filtered walks of many (segment, query) pairs over HNSW / HNSW-SQ8 segments of one collection in
+// batched launches (index_graph.cc). items: host array; outputs at each item's slot (keys at
+// slot * k). NotSupported when an index is not HNSW or the segments' graph parameters differ.
+struct HnswItem;
+struct MultiScratch {
+  DeviceBuffer segs, items, visited, pool;
+};
+Status HnswSearchMulti(Context& ctx, const std::vector<const GpuIndex*>& indexes, const HnswItem* items,
+                       size_t nitems, const float* queries, uint32_t k, const SearchParams& p, uint64_t* out_keys,
+                       uint64_t* out_dc, int* out_short, MultiScratch* scratch);
+
 // An HNSW graph over rows (host or device, n x pd) built on the GPU, as a complete index file in
 // the reference's index.hnsw format (hnsw_build.cc).
 Status BuildHnswFile(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim, uint32_t pd, uint32_t M,
