@@ -487,6 +487,7 @@ def run_c4_ours(args):
             "gpu_launches": None,
             "clocks": clk,
             "setup_s": {"total": setup_s, "hnsw_build_rank0": build_s},
+            "phase_ms_rank0": {k[3:]: st[k] / 1000.0 for k in ("us_bitmaps_plan", "us_exact", "us_index", "us_other")},
         }
         print(json.dumps(result), flush=True)
     coll.free()

@@ -103,8 +103,9 @@ class GpuCollection {
   // Work of the last Search: [0] queries, [1] rows scored exactly (prefilter and fallback, per
   // query), [2] distance computations of index searches (only while stats are enabled), [3]
   // prefilter pairs, [4] filtered-index pairs, [5] post-filter pairs, [6] empty pairs, [7] filter
-  // bitmap words evaluated, [8] (query, segment) index searches.
-  static constexpr int kStats = 9;
+  // bitmap words evaluated, [8] (query, segment) index searches; [9..12] host wall microseconds of
+  // filter bitmaps + planning, exact search over bitmaps, index searches, and the rest.
+  static constexpr int kStats = 13;
   void set_stats(bool on) { stats_on_ = on; }
   const uint64_t* stats() const { return stats_; }
 

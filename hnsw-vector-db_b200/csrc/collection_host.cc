@@ -1,6 +1,7 @@
 #include "collection.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -14,6 +15,12 @@
 namespace vdbgpu {
 
 namespace {
+
+uint64_t NowUs() {
+  return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::microseconds>(
+                                   std::chrono::steady_clock::now().time_since_epoch())
+                                   .count());
+}
 
 constexpr size_t kSegmentHeaderSize = 4096;  // src/storage/segment.h:33
 constexpr size_t kBlobHeaderSize = 24;       // src/storage/file_format.h:13
@@ -626,6 +633,7 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
   if (r.nq == 0) return Status::OK();
   for (auto& v : stats_) v = 0;
   stats_[0] = r.nq;
+  const uint64_t t_search = NowUs();
   const uint32_t pd = opt_.pd, dim = opt_.dim;
   Batch b;
   b.r = &r;
@@ -790,7 +798,11 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
       }
     }
   }
-  return ctx.Sync("collection search");
+  Status done = ctx.Sync("collection search");
+  const uint64_t total = NowUs() - t_search;
+  const uint64_t parts = stats_[9] + stats_[10] + stats_[11];
+  stats_[12] = total > parts ? total - parts : 0;
+  return done;
 }
 
 // Searches the index of segment s for the queries of group g with kk results per query, then
@@ -850,13 +862,13 @@ static int CountSlots(const std::vector<GpuCollection::LeafSpec>& leaves, std::v
   return n;
 }
 
-// Segments per chunk: the leaf and pair bitmaps of one chunk within ~2 GiB of scratch.
+// Segments per chunk: the leaf and pair bitmaps of one chunk within ~12 GiB of scratch.
 size_t GpuCollection::SegmentsPerChunk(const Batch& b, size_t nfilters) const {
   std::vector<int> slot;
   const int nslots = CountSlots(b.leaves, &slot);
   const uint64_t per_seg = (static_cast<uint64_t>(nslots) + nfilters) * MaxWords() * 4;
   return static_cast<size_t>(std::max<uint64_t>(
-      1, std::min<uint64_t>(segs_.size(), (2ull << 30) / std::max<uint64_t>(per_seg, 1))));
+      1, std::min<uint64_t>(segs_.size(), (12ull << 30) / std::max<uint64_t>(per_seg, 1))));
 }
 
 uint32_t* GpuCollection::PairBits(size_t fi, size_t si, size_t cs) const {
@@ -1063,6 +1075,7 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
   for (size_t s0 = 0; s0 < S; s0 += chunk) {
     const size_t s1 = std::min(S, s0 + chunk), cs = s1 - s0;
     std::vector<uint64_t> matches;
+    uint64_t t0 = NowUs();
     VDBGPU_RETURN_IF_ERROR(Bitmaps(ctx, b, fq, s0, cs, &matches));
     auto pair_ptr = [&](size_t fi, size_t si) -> uint32_t* { return PairBits(fi, si, cs); };
 
@@ -1165,7 +1178,11 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
       else if (plan[pi] == kGraph) graph.push_back(pi);
       else if (plan[pi] == kPost) post.push_back(pi);
     }
+    stats_[9] += NowUs() - t0;
+    t0 = NowUs();
     VDBGPU_RETURN_IF_ERROR(run_exact(pre, false));
+    stats_[10] += NowUs() - t0;
+    t0 = NowUs();
     // ---- filtered index search (planner.cc:88-105). HNSW segments: every (pair, query) walk of
     // the chunk in batched launches; other index types: one index search per pair.
     bool batched = false;
@@ -1210,6 +1227,8 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
       VDBGPU_RETURN_IF_ERROR(RunIndex(ctx, b, s, f, b.k, pparams[pi], pair_ptr(fi, si), nullptr, need,
                                       b.shortf + s * b.nq + b.goff[f]));
     }
+    stats_[11] += NowUs() - t0;
+    t0 = NowUs();
     if (!graph.empty() && p.strategy == 0) {
       std::vector<int> sh(S * b.nq);
       VDBGPU_CUDA(cudaMemcpyAsync(sh.data(), b.shortf, sh.size() * 4, cudaMemcpyDeviceToHost, st));
@@ -1225,6 +1244,7 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
       }
       VDBGPU_RETURN_IF_ERROR(run_exact(fb, true));
     }
+    stats_[10] += NowUs() - t0;
     // ---- post-filter (planner.cc:106-123).
     for (size_t pi : post) {
       const size_t fi = pi / cs, si = pi % cs, s = s0 + si;

@@ -188,10 +188,61 @@ __device__ __forceinline__ float group_dist(const HnswArgs& a, const float* q_s,
   return l2 ? r : -r;
 }
 
+// pd == 128, AVX-512 order, float rows: group_dist's arithmetic with all loads of 8 rows issued
+// before any of it (two rows per quarter-warp per pass), so a pass costs one memory round trip.
+__device__ __forceinline__ void dists_of_128(const HnswArgs& a, const float* q_s, const uint32_t* ids, float* d,
+                                             int n, bool l2) {
+  const int lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
+  for (int i = 0; i < n; i += 8) {
+    float x[2][16];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int my = i + 4 * h + g;
+      const float* xp = a.rows + static_cast<size_t>(ids[my < n ? my : i]) * 128;
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) x[h][4 * t + c] = __ldg(&xp[32 * t + 8 * c + j]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float a0 = 0.f, a0b = 0.f, a1 = 0.f, a1b = 0.f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int e = 32 * t + j;
+        if (l2) {
+          const float d0 = __fsub_rn(q_s[e], x[h][4 * t]), d1 = __fsub_rn(q_s[e + 8], x[h][4 * t + 1]);
+          const float d2 = __fsub_rn(q_s[e + 16], x[h][4 * t + 2]), d3 = __fsub_rn(q_s[e + 24], x[h][4 * t + 3]);
+          a0 = __fmaf_rn(d0, d0, a0);
+          a0b = __fmaf_rn(d1, d1, a0b);
+          a1 = __fmaf_rn(d2, d2, a1);
+          a1b = __fmaf_rn(d3, d3, a1b);
+        } else {
+          a0 = __fmaf_rn(q_s[e], x[h][4 * t], a0);
+          a0b = __fmaf_rn(q_s[e + 8], x[h][4 * t + 1], a0b);
+          a1 = __fmaf_rn(q_s[e + 16], x[h][4 * t + 2], a1);
+          a1b = __fmaf_rn(q_s[e + 24], x[h][4 * t + 3], a1b);
+        }
+      }
+      float t3 = __fadd_rn(__fadd_rn(a0b, a1b), __fadd_rn(a0, a1));
+      t3 = __fadd_rn(t3, __shfl_xor_sync(0xFFFFFFFFu, t3, 4));
+      t3 = __fadd_rn(t3, __shfl_xor_sync(0xFFFFFFFFu, t3, 2));
+      t3 = __fadd_rn(t3, __shfl_xor_sync(0xFFFFFFFFu, t3, 1));
+      const int my = i + 4 * h + g;
+      if (j == 0 && my < n) d[my] = l2 ? t3 : -t3;
+    }
+  }
+  __syncwarp();
+}
+
 // Distances of ids[0..n) (n <= 32) into d[0..n), four rows per pass.
 template <bool kSq8>
 __device__ void dists_of(const HnswArgs& a, const float* q_s, const uint32_t* ids, float* d, int n,
                          bool l2) {
+  if (!kSq8 && a.pd == 128 && a.order == kOrderAvx512) {
+    dists_of_128(a, q_s, ids, d, n, l2);
+    return;
+  }
   const int lane = threadIdx.x & 31, g = lane >> 3;
   for (int i = 0; i < n; i += 4) {
     const int my = i + g;
@@ -247,6 +298,24 @@ __device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
 
 // Merges one candidate key per lane (where want) into the candidates. Returns false when the pool
 // is full.
+// Removes the dead slots (~0: moved to the front or pruned) from the pool.
+__device__ void pool_compact(uint64_t* pool, int& npool) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  int nkeep = 0;
+  for (int base = 0; base < npool; base += 32) {
+    const int i = base + lane;
+    const uint64_t k = i < npool ? pool[i] : ~0ull;
+    const bool kp = k != ~0ull;
+    const uint32_t mk = __ballot_sync(0xFFFFFFFFu, kp);
+    __syncwarp();
+    if (kp) pool[nkeep + __popc(mk & lt)] = k;  // nkeep <= base: never ahead of unread entries
+    nkeep += __popc(mk);
+    __syncwarp();
+  }
+  npool = nkeep;
+}
+
 __device__ bool pool_merge(uint64_t key, bool want, uint64_t* front, int& chead, int& ncand, uint64_t* pool,
                            int& npool, int pool_cap, uint64_t& pmin) {
   const int lane = threadIdx.x & 31;
@@ -255,7 +324,8 @@ __device__ bool pool_merge(uint64_t key, bool want, uint64_t* front, int& chead,
   const bool to_front = want && key < pmin;
   const uint32_t mp = __ballot_sync(0xFFFFFFFFu, to_pool);
   const int np = __popc(mp);
-  if (npool + np > pool_cap) return false;
+  if (npool + np + 32 > pool_cap) pool_compact(pool, npool);
+  if (npool + np + 32 > pool_cap) return false;
   if (to_pool) pool[npool + __popc(mp & lt)] = key;
   npool += np;
   const uint32_t mf = __ballot_sync(0xFFFFFFFFu, to_front);
@@ -271,8 +341,7 @@ __device__ bool pool_merge(uint64_t key, bool want, uint64_t* front, int& chead,
   warp_sort<4>(x);
   const int total = ncand + __popc(mf);
   const int keep = total < kPoolFront ? total : kPoolFront;
-  const int nover = total - keep;
-  if (npool + nover > pool_cap) return false;
+  const int nover = total - keep;  // <= 32: room was reserved above
   uint64_t over_min = ~0ull;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -292,76 +361,130 @@ __device__ bool pool_merge(uint64_t key, bool want, uint64_t* front, int& chead,
   return true;
 }
 
-// Refills the empty front with the kPoolRefill smallest live pool keys (live: not prunable,
-// i.e. nres < ef or dist <= lower): the r-th smallest by a radix select over the 64-bit keys (4
-// bits per pass), then one pass that moves keys <= it to the front (sorted afterwards) and
-// compacts the rest.
+// Refills the empty front with every live pool key at or below a threshold (live: not dead and
+// not prunable, i.e. nres < ef or dist <= lower). Any threshold keeps every front key below every
+// pool key; the threshold is picked so the keys fit in the front: pass 1 finds the live minimum,
+// pass 2 counts live keys under eight thresholds min + delta * 4^j, pass 3 moves the keys under
+// the largest one that fits (their pool slots become dead, ~0) and finds the new pool minimum.
+// delta adapts from refill to refill. When even the smallest threshold holds more keys than fit
+// (many equal distances), an exact radix select over the 64-bit keys picks kPoolRefill keys.
 __device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* pool, int& npool, uint64_t& pmin,
-                            uint32_t* hist, bool prune, float lower) {
+                            uint32_t* hist, bool prune, float lower, float& delta) {
   const int lane = threadIdx.x & 31;
   const uint32_t lt = (1u << lane) - 1u;
-  auto live = [&](uint64_t k) { return !prune || !(neighbor_dist(k) > lower); };
+  auto live = [&](uint64_t k) { return k != ~0ull && (!prune || !(neighbor_dist(k) > lower)); };
+  uint64_t m = ~0ull;
   int nlive = 0;
-  for (int i = lane; i < npool; i += 32) nlive += live(pool[i]) ? 1 : 0;
-  nlive = __reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(nlive));
-  const int r = nlive < kPoolRefill ? nlive : kPoolRefill;
-  uint64_t thr = ~0ull;
-  if (r > 0 && r < nlive) {
-    uint64_t prefix = 0, pmask = 0;
-    int need = r;
-    for (int shift = 60; shift >= 0; shift -= 4) {
-      if (lane < 16) hist[lane] = 0;
-      __syncwarp();
+  for (int i = lane; i < npool; i += 32) {
+    const uint64_t k = pool[i];
+    if (live(k)) {
+      ++nlive;
+      m = k < m ? k : m;
+    }
+  }
+  m = warp_min_u64(m);
+  nlive = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(nlive)));
+  chead = 0;
+  ncand = 0;
+  if (nlive == 0) {
+    npool = 0;
+    pmin = ~0ull;
+    return;
+  }
+  uint64_t thr = ~0ull;  // move live keys <= thr
+  if (nlive > kPoolFront) {
+    const float base = neighbor_dist(m);
+    bool found = false;
+    for (int attempt = 0; attempt < 4 && !found; ++attempt) {
+      int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int i = lane; i < npool; i += 32) {
         const uint64_t k = pool[i];
-        if (live(k) && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 15ull], 1u);
-      }
-      __syncwarp();
-      const int c = lane < 16 ? static_cast<int>(hist[lane]) : 0;
-      int incl = c;
+        if (!live(k)) continue;
+        const float d = neighbor_dist(k);
+        float t = base + delta;
 #pragma unroll
-      for (int o = 1; o < 16; o <<= 1) {
-        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += v;
+        for (int j = 0; j < 8; ++j, t = base + (t - base) * 4.f) c[j] += d <= t ? 1 : 0;
       }
-      const uint32_t hit = __ballot_sync(0xFFFFFFFFu, lane < 16 && incl >= need);
-      if (hit == 0) {  // cannot happen for a consistent pool; select everything that fits
-        prefix = ~0ull;
-        break;
+      int best = -1;
+      float t = base + delta;
+#pragma unroll
+      for (int j = 0; j < 8; ++j, t = base + (t - base) * 4.f) {
+        const int cj = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c[j])));
+        if (cj <= kPoolFront) {
+          best = j;
+          thr = (static_cast<uint64_t>(float_key(t)) << 32) | 0xFFFFFFFFull;
+        }
+        if (j == 0 && cj > kPoolFront) break;
       }
-      const int d = __ffs(hit) - 1;
-      const int before = __shfl_sync(0xFFFFFFFFu, incl - c, d);
-      prefix |= static_cast<uint64_t>(d) << shift;
-      pmask |= 15ull << shift;
-      need -= before;
-      __syncwarp();
+      if (best >= 0) {
+        found = true;
+        if (best == 7) delta *= 16.f;  // thresholds too tight: widen next time
+        if (best < 3) delta *= 0.25f;
+      } else {
+        delta *= 1.0f / 64.f;  // even the smallest threshold holds too many keys
+      }
     }
-    thr = prefix;  // keys are unique, so exactly r live keys are <= thr
+    if (!found) {
+      // Exact: the kPoolRefill-th smallest live key by a 4-bit radix select.
+      uint64_t prefix = 0, pmask = 0;
+      int need = kPoolRefill;
+      for (int shift = 60; shift >= 0; shift -= 4) {
+        if (lane < 16) hist[lane] = 0;
+        __syncwarp();
+        for (int i = lane; i < npool; i += 32) {
+          const uint64_t k = pool[i];
+          if (live(k) && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 15ull], 1u);
+        }
+        __syncwarp();
+        const int cc = lane < 16 ? static_cast<int>(hist[lane]) : 0;
+        int incl = cc;
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) {
+          const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const uint32_t hit = __ballot_sync(0xFFFFFFFFu, lane < 16 && incl >= need);
+        if (hit == 0) {  // cannot happen for a consistent pool
+          prefix = m;
+          break;
+        }
+        const int d = __ffs(hit) - 1;
+        const int before = __shfl_sync(0xFFFFFFFFu, incl - cc, d);
+        prefix |= static_cast<uint64_t>(d) << shift;
+        pmask |= 15ull << shift;
+        need -= before;
+        __syncwarp();
+      }
+      thr = prefix;  // keys are unique: exactly kPoolRefill live keys are <= thr
+    }
   }
-  int nsel = 0, nkeep = 0;
+  int nsel = 0;
   uint64_t kmin = ~0ull;
+  bool any_left = false;
   for (int base = 0; base < npool; base += 32) {
     const int i = base + lane;
     const uint64_t k = i < npool ? pool[i] : ~0ull;
     const bool lv = i < npool && live(k);
     const bool sel = lv && k <= thr;
-    const bool kp = lv && !sel;
     const uint32_t ms = __ballot_sync(0xFFFFFFFFu, sel);
-    const uint32_t mk = __ballot_sync(0xFFFFFFFFu, kp);
-    __syncwarp();
-    if (sel && nsel + __popc(ms & lt) < 128) front[nsel + __popc(ms & lt)] = k;
-    if (kp) {
-      pool[nkeep + __popc(mk & lt)] = k;  // nkeep <= base: never ahead of unread entries
+    if (sel) {
+      const int at = nsel + __popc(ms & lt);
+      if (at < 128) front[at] = k;
+    }
+    if (i < npool && !lv && k != ~0ull) pool[i] = ~0ull;  // pruned: dead
+    if (sel) pool[i] = ~0ull;                              // moved to the front
+    if (lv && !sel) {
       kmin = k < kmin ? k : kmin;
+      any_left = true;
     }
     nsel += __popc(ms);
-    nkeep += __popc(mk);
-    __syncwarp();
   }
+  __syncwarp();
   kmin = warp_min_u64(kmin);
-  nsel = nsel < 128 ? nsel : 128;
-  npool = nkeep;
-  pmin = nkeep > 0 ? kmin : ~0ull;
+  any_left = __any_sync(0xFFFFFFFFu, any_left);
+  if (!any_left) npool = 0;  // every slot is dead
+  pmin = any_left ? kmin : ~0ull;
+  nsel = nsel < kPoolFront ? nsel : kPoolFront;
   uint64_t x[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -376,12 +499,11 @@ __device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* p
     if (i < nsel) front[i] = x[e];
   }
   __syncwarp();
-  chead = 0;
   ncand = nsel;
 }
 
 template <bool kSq8>
-__global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const HnswArgs a0) {
+__global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const HnswArgs a0) {
   extern __shared__ __align__(16) uint8_t hsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -480,6 +602,8 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
       uint32_t* hist = reinterpret_cast<uint32_t*>(s.cand + 128);
       int npool = 0;
       uint64_t pmin = ~0ull;
+      float delta = fmaxf(fabsf(curd), 1e-3f) * 1e-3f;  // refill threshold step (adapts)
+      unsigned long long c_exp = 0, c_ref = 0, c_scan = 0, c_merge = 0, c_ins = 0;
       if (lane == 0) atomicOr(&vis[cur >> 5], 1u << (cur & 31));
       float lower = INFINITY;
       int chead = 0, ncand = 0;
@@ -496,7 +620,9 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
         if (ncand == 0) {
           if (npool == 0) break;
           // Candidates beyond a full result set's worst can never be expanded (lower only falls).
-          pool_refill(s.cand, chead, ncand, pool, npool, pmin, hist, nres >= ef, lower);
+          ++c_ref;
+          c_scan += static_cast<unsigned long long>(npool);
+          pool_refill(s.cand, chead, ncand, pool, npool, pmin, hist, nres >= ef, lower, delta);
           if (ncand == 0) break;
         }
         const uint64_t c = s.cand[chead];
@@ -504,6 +630,7 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
         if (cd > lower && (!filtered || nres >= ef)) break;
         ++chead;
         --ncand;
+        ++c_exp;
         if (++steps > a.step_limit) {
           if (lane == 0) set_error(a.status, kDevStepLimit);
           bad = true;
@@ -511,16 +638,19 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
         }
         const uint32_t cid = neighbor_id(c);
         const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
+        // The list's count and its slots load together (a block always holds M0 slots).
         const uint32_t cnt = ll[0];
+        const uint32_t e_raw = lane < static_cast<int>(a.M0) ? ll[1 + lane] : 0u;
         uint32_t e = 0;
-        bool fresh = false;
+        bool fresh = false, al = false;
         if (lane < static_cast<int>(cnt)) {
-          e = ll[1 + lane];
+          e = e_raw;
           if (e >= n) {
             bad = true;
           } else {
             const uint32_t bit = 1u << (e & 31);
             fresh = (atomicOr(&vis[e >> 5], bit) & bit) == 0u;
+            al = allowed(e);  // the filter bit loads beside the visited mark
           }
         }
         if (__any_sync(0xFFFFFFFFu, bad)) {
@@ -532,6 +662,10 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
         const int nf = __popc(fm);
         if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
         __syncwarp();
+        // The filter bits in the compacted (list) order of the fresh neighbours.
+        const int src = lane < nf ? static_cast<int>(__fns(fm, 0, lane + 1)) : 0;
+        const int al_c = __shfl_sync(0xFFFFFFFFu, al ? 1 : 0, src);
+        const uint32_t amask = __ballot_sync(0xFFFFFFFFu, lane < nf && al_c != 0);
         dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
         dc += static_cast<uint64_t>(nf);
         // Result updates in list order decide which neighbours become candidates; the candidates
@@ -547,7 +681,8 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
               mykey = key;
               mywant = true;
             }
-            if (allowed(id)) {
+            if ((amask >> i) & 1u) {
+              ++c_ins;
               if (nres < ef) {
                 insert_sorted(s.res, 0, nres, key);
                 ++nres;
@@ -559,11 +694,21 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
             }
           }
         }
+        c_merge += __any_sync(0xFFFFFFFFu, mywant && mykey < pmin) ? 1 : 0;
         if (!pool_merge(mykey, mywant, s.cand, chead, ncand, pool, npool, a.pool_cap, pmin)) {
           if (lane == 0) set_error(a.status, kDevCandOverflow);
           bad = true;
           break;
         }
+      }
+      if (lane == 0 && a0.counters != nullptr) {
+        atomicAdd(&a0.counters[0], 1ull);
+        atomicAdd(&a0.counters[1], c_exp);
+        atomicAdd(&a0.counters[2], c_ref);
+        atomicAdd(&a0.counters[3], c_scan);
+        atomicAdd(&a0.counters[4], c_merge);
+        atomicAdd(&a0.counters[5], c_ins);
+        atomicMax(&a0.counters[6], c_exp);
       }
     } else {
       bool full = false;
@@ -613,6 +758,8 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
         const int nf = __popc(fm);
         if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
         __syncwarp();
+        // The filter bits of all fresh neighbours at once (one load per lane, not one per step).
+        const uint32_t amask = __ballot_sync(0xFFFFFFFFu, lane < nf && allowed(s.nb_id[lane]));
         dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
         dc += static_cast<uint64_t>(nf);
         // Heap updates in list order (the fresh neighbours keep their list order).
@@ -645,7 +792,7 @@ __global__ void __launch_bounds__(kHnswWarps * 32) hnsw_search_kernel(const Hnsw
             }
             insert_sorted(s.cand, chead, ncand, key);
             ++ncand;
-            if (allowed(id)) {
+            if ((amask >> i) & 1u) {
               if (nres < ef) {
                 insert_sorted(s.res, 0, nres, key);
                 ++nres;

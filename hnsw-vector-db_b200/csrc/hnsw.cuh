@@ -71,6 +71,9 @@ struct HnswArgs {
   const HnswItem* items;
   uint64_t* out_keys;
   int* out_short;
+  // Work counters (null = off): [0] walks, [1] expansions, [2] front refills, [3] pool slots scanned
+  // by refills, [4] merges into the front, [5] result inserts, [6] most expansions of one walk.
+  unsigned long long* counters;
   int step_limit;          // bounded walk: expansions per query
   float* out_dist;
   uint32_t* out_row;

@@ -48,7 +48,7 @@ void Put(std::string* s, T v) {
 
 Status BuildHnswFile(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim, uint32_t pd, uint32_t M,
                      uint32_t kcand, uint64_t seed, std::string* file) {
-  if (M < 2 || M > 64) return Status(Status::kInvalidArgument, "M must be in 2..64 for the GPU builder");
+  if (M < 2 || M > 16) return Status(Status::kInvalidArgument, "M must be in 2..16 for the GPU builder");
   if (n >= (uint64_t{1} << 32) - 1) return Status(Status::kInvalidArgument, "too many rows");
   const uint32_t M0 = 2 * M;
   if (kcand == 0) kcand = std::min<uint32_t>(2 * M0, 127);

@@ -64,6 +64,9 @@ class HnswGpuIndex final : public GpuIndex {
         VDBGPU_CUDA(cudaMemcpyAsync(codes_.get(), codes.data(), n * pd, cudaMemcpyHostToDevice, ctx.stream()));
     }
     VDBGPU_RETURN_IF_ERROR(ParseHnswGraph(r, n, &g_));
+    // The walk gives every link of a list its own lane: at most 32 links on layer 0 (M0 = 2M).
+    if (g_.M > 16)
+      return Status(Status::kNotSupported, "HNSW graphs with M above 16 are not supported on the GPU");
     VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.links0, &links0_));
     VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.upper, &upper_));
     VDBGPU_RETURN_IF_ERROR(Upload(ctx, g_.upper_off, &upper_off_));
@@ -251,14 +254,19 @@ Status HnswSearchMulti(Context& ctx, const std::vector<const GpuIndex*>& indexes
   a.out_dc = out_dc;
   a.out_short = out_short;
   a.codes = first->sq8() ? segs[0].codes : nullptr;  // selects the SQ8 kernel
+  a.counters = ctx.timing() ? ctx.counters() : nullptr;
+  if (a.counters != nullptr)
+    VDBGPU_CUDA(cudaMemsetAsync(a.counters, 0, 8 * sizeof(unsigned long long), ctx.stream()));
   a.warps = 4;
-  // Walks per launch: their visited bitmaps and candidate pools within ~4 GiB.
-  int pool_cap = static_cast<int>(std::max<uint64_t>(8192, 64 * ef));
+  // Walks per launch: their visited bitmaps and candidate pools within ~16 GiB.
+  // Filtered walks at a few percent selectivity reach ~10^4 candidates: size the pools for that so
+  // a launch rarely reruns.
+  int pool_cap = static_cast<int>(std::max<uint64_t>(32768, 64 * ef));
   size_t done = 0;
   while (done < nitems) {
     const uint64_t per = a.vwords * 4 + static_cast<uint64_t>(pool_cap) * 8;
     const size_t chunk = static_cast<size_t>(std::max<uint64_t>(
-        1, std::min<uint64_t>(nitems - done, (4ull << 30) / per)));
+        1, std::min<uint64_t>(nitems - done, (16ull << 30) / per)));
     VDBGPU_RETURN_IF_ERROR(sc->items.ensure(chunk * sizeof(HnswItem)));
     VDBGPU_RETURN_IF_ERROR(sc->visited.ensure(chunk * a.vwords * 4));
     VDBGPU_RETURN_IF_ERROR(sc->pool.ensure(chunk * static_cast<uint64_t>(pool_cap) * 8));

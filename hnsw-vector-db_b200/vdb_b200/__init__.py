@@ -492,7 +492,8 @@ class Collection:
         return json.loads(buf.value.decode())
 
     STAT_NAMES = ("queries", "exact_rows", "index_distance_computations", "prefilter_pairs",
-                  "graph_pairs", "postfilter_pairs", "empty_pairs", "bitmap_words", "index_searches")
+                  "graph_pairs", "postfilter_pairs", "empty_pairs", "bitmap_words", "index_searches",
+                  "us_bitmaps_plan", "us_exact", "us_index", "us_other")
 
     def stats(self, enable: Optional[bool] = None) -> dict:
         """Work counters of the last search (index distance computations only while enabled)."""

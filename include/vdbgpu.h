@@ -267,8 +267,9 @@ VDBGPU_API int vdbgpu_collection_search_grouped(vdbgpu_collection* c, const floa
  * distance_computations): out[0] queries, [1] rows scored exactly (prefilter and exact
  * fallback, summed over queries), [2] distance computations of index searches (counted only
  * while enabled), [3] prefilter (filter, segment) pairs, [4] filtered-index pairs, [5] post-filter
- * pairs, [6] empty pairs, [7] filter bitmap words evaluated, [8] (query, segment) index searches.
- * enable: 1 / 0 turns the index-search count on / off, -1 leaves it. Returns the count written. */
+ * pairs, [6] empty pairs, [7] filter bitmap words evaluated, [8] (query, segment) index searches,
+ * [9..12] host wall microseconds of the filter bitmaps and planning, the exact searches over
+ * bitmaps, the index searches, and the rest of the call. enable: 1 / 0 turns the index-search count on / off, -1 leaves it. Returns the count written. */
 VDBGPU_API int vdbgpu_collection_stats(vdbgpu_collection* c, int enable, uint64_t* out, int cap);
 
 /* Collection::Search with explain for one query: JSON array with one object per local disk
