@@ -529,8 +529,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeArgs
     if (!dup) {
       if (lane == 0) {
         kept[nkept] = rec.id;
-        const uint64_t oi = q * k + nkept;
-        if (a.out_records != nullptr) a.out_records[oi] = rec;
+        if (a.out_records != nullptr) a.out_records[outq * k + nkept] = rec;
         if (a.out_ids != nullptr) {
           a.out_ids[outq * k + nkept] = rec.id;
           a.out_dist[outq * k + nkept] = rec.dist;
@@ -548,7 +547,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeArgs
       m.row = UINT32_MAX;
       m.pad = 0;
       m.id = ~0ull;
-      a.out_records[q * k + i] = m;
+      a.out_records[outq * k + i] = m;
     }
     if (a.out_ids != nullptr) {
       a.out_ids[outq * k + i] = ~0ull;

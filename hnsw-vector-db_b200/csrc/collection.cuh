@@ -130,7 +130,7 @@ struct MergeArgs {
   const uint32_t* part_no;
   const uint64_t* const* ids;
   const HitRecord* records;
-  HitRecord* out_records;   // nq x k or null
+  HitRecord* out_records;   // nq x k (row perm[q]) or null
   uint64_t* out_ids;        // nq x k (row perm[q]) or null
   float* out_dist;
   const uint32_t* perm;     // sorted query -> caller's query, or null

@@ -107,6 +107,8 @@ def test_shards_merge_to_the_whole(colls):
     ctx, cs = colls
     g, c, path = cs["coll_hnsw"]
     q = g["queries"]
+    nf = len(g["filters"])
+    qf = np.random.default_rng(7).integers(-1, nf, size=q.shape[0]).astype(np.int32)
     for world in (2, 3):
         shards = [vdb_b200.Collection.open(ctx, path, shard=r, nshards=world) for r in range(world)]
         for ci in (0, 1, 3):
@@ -119,6 +121,16 @@ def test_shards_merge_to_the_whole(colls):
                 ids, d = vdb_b200.merge_hits(ctx, lists, k)
                 assert np.array_equal(ids, g[f"ids_{ci}_{fi}"]), (world, ci, f)
                 assert np.array_equal(d, g[f"dist_{ci}_{fi}"]), (world, ci, f)
+            # Several filters in one batch (queries grouped, so the hit records must come back in
+            # the caller's query order).
+            lists = np.empty((world, q.shape[0], k), dtype=vdb_b200.HIT_DTYPE)
+            for r, s in enumerate(shards):
+                s.search_grouped(q, [str(x) for x in g["filters"]], qf, hits=lists[r], **kw)
+            ids, d = vdb_b200.merge_hits(ctx, lists, k)
+            for i in range(q.shape[0]):
+                fi = nf if qf[i] < 0 else int(qf[i])
+                assert np.array_equal(ids[i], g[f"ids_{ci}_{fi}"][i]), (world, ci, i)
+                assert np.array_equal(d[i], g[f"dist_{ci}_{fi}"][i]), (world, ci, i)
 
 
 def test_ivfpq_deep_rerank_is_refused(colls):
