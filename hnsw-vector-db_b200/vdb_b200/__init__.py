@@ -191,7 +191,10 @@ class Context:
         self.check(lib().vdbgpu_synchronize(self._h))
 
     def set_stream(self, stream_handle: int = 0):
-        """Launch on a caller's CUDA stream (e.g. torch.cuda.current_stream().cuda_stream)."""
+        """Launch on a caller's CUDA stream (e.g. torch.cuda.current_stream().cuda_stream). A handle
+        of 0 (which is also torch's default stream) selects the context's own non-blocking stream:
+        every call still returns only when its work is done, but it is not ordered after other
+        work on the default stream, so finish such work (synchronize) before passing its output."""
         self.check(lib().vdbgpu_set_stream(self._h, stream_handle or None))
 
     def set_timing(self, on: bool = True):

@@ -34,6 +34,10 @@ def gather_hits(local, group=None):
     flat = local.contiguous().view(-1)
     out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
     dist.all_gather_into_tensor(out, flat, group=group)
+    if out.is_cuda:
+        # The collective is ordered on torch's stream only; the library launches on its own
+        # stream, so the gathered records must be complete before this returns.
+        torch.cuda.current_stream(out.device).synchronize()
     return out.view(world, flat.numel())
 
 
@@ -62,7 +66,6 @@ class ShardedCollection:
         hits = torch.empty(nq * k * HIT_BYTES, dtype=torch.uint8, device=dev)
         self.local.search_grouped(queries, list(filters), query_filter, k=k, out=False, hits=hits, **params)
         gathered = gather_hits(hits, self.group)
-        torch.cuda.current_stream(dev).synchronize()
         if not on_all_ranks and self.rank != 0:
             return None
         ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
