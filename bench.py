@@ -43,7 +43,7 @@ C4_WORKLOAD = ("config 4: sharded filtered multi-segment search, {segs} segments
 
 def parse():
     p = argparse.ArgumentParser()
-    p.add_argument("--workload", default="c1", choices=["c1", "c4"])
+    p.add_argument("--workload", default="c1", choices=["c0", "c1", "c3", "c4"])
     p.add_argument("--segments", type=int, default=C4_SEGMENTS)
     p.add_argument("--seg-rows", type=int, default=C4_SEG_ROWS)
     p.add_argument("--gpus", type=int, default=1)
@@ -562,8 +562,143 @@ def run_c4_reference(args):
     return 0
 
 
+# ---------------------------------------------------------------------------- configs 0 and 3
+
+C0_WORKLOAD = ("config 0: exact flat L2 search, 100,000 x 128 integer rows (100-centre mixture, "
+               "U[0,100] centres, sigma 10, clipped to [0,255] and rounded), 1,000-query batches, k=10")
+C3_WORKLOAD = ("config 3: HNSW batched search, 1,000,000 x 128 integer rows (config-0 mixture), L2, graph "
+               "M=16 built on the GPU (reference index.hnsw format), ef={ef}, 10,000-query batches, k=10")
+
+
+def _timed(step, steps, warmup, stream, local):
+    import torch
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, clocks.stop()
+
+
+def _recall(ids, gt):
+    return float(np.mean([len(set(a.tolist()) & set(b.tolist())) / gt.shape[1] for a, b in zip(ids, gt)]))
+
+
+def run_c0_c3(args):
+    """Configs 0 and 3 on one GPU (single-segment configs: replicas only, so one line per GPU)."""
+    import torch
+    import oracle
+    import vdb_b200
+    from vdb_b200 import synth
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    ctx = vdb_b200.Context(local)
+    stream = torch.cuda.current_stream()
+    sustained, burst, hbm, src = peaks()
+    ref = oracle.Ref()
+    if args.workload == "c0":
+        base, qs = synth.flat_int(100_000, 1_000, seed=0)
+        idx = vdb_b200.Index.create(ctx, "flat", "l2", base, DIM)
+        q_dev = torch.from_numpy(qs).cuda()
+        ids_dev = torch.empty((qs.shape[0], K), dtype=torch.int32, device="cuda")
+        d_dev = torch.empty((qs.shape[0], K), dtype=torch.float32, device="cuda")
+        ctx.set_timing(True)
+        scan = []
+
+        def step():
+            idx.search(q_dev, k=K, out=(ids_dev, d_dev))
+            scan.append(ctx.stage_times()[1])
+        ms, clk = _timed(step, max(args.steps, 50), args.warmup, stream, local)
+        nq = qs.shape[0]
+        flops = 2.0 * nq * base.shape[0] * DIM
+        scan_s = float(np.median(scan)) / 1000.0
+        ref_ids, _ = ref.flat_search_batch(oracle.L2, base, DIM, qs[:200], K, threads=0)
+        t0 = time.perf_counter()
+        ref_ids, _ = ref.flat_search_batch(oracle.L2, base, DIM, qs, K, threads=0)
+        cpu_s = time.perf_counter() - t0
+        gpu_ids = ids_dev.cpu().numpy().view(np.uint32)
+        out = {"metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": 1, "steps": max(args.steps, 50),
+               "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "f16 tensor-core pre-rank (exact for these integer rows), f32 re-rank",
+               "data": "synthetic", "config": {"workload": C0_WORKLOAD, "rows": base.shape[0], "batch": nq, "k": K,
+                                              "l2": "inputs smaller than L2 (51 MB rows): repeated batches"},
+               "roofline": {"bound": "tensor", "kernel": "scan_mma_kernel", "achieved": flops / scan_s / 1e12,
+                            "peak": burst, "unit": "TFLOP/s", "frac": flops / scan_s / 1e12 / burst,
+                            "peak_kind": f"{src} bf16 dense, burst", "traffic": None},
+               "identical_ids_vs_reference": float(np.mean(np.all(gpu_ids == ref_ids, axis=1))),
+               "cpu_baseline": {"value": nq / cpu_s, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",
+                                "sample": f"all {nq} queries (FlatSearchBatch, {cpu_model()}, kernel set {ref.kernel_set()})"},
+               "clocks": clk}
+        print(json.dumps(out), flush=True)
+        return 0
+    # config 3
+    base, qs = synth.flat_int(1_000_000, args.batch, seed=0)
+    b_dev = torch.from_numpy(base).cuda()
+    t = time.time()
+    graph = vdb_b200.build_hnsw(ctx, "l2", b_dev, DIM, M=16, seed=42)
+    build_s = time.time() - t
+    idx = vdb_b200.Index.load(ctx, graph, "l2", base, DIM)
+    flat = vdb_b200.Index.create(ctx, "flat", "l2", b_dev, DIM)
+    q_dev = torch.from_numpy(qs).cuda()
+    nq = qs.shape[0]
+    gt_ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    gt_d = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    flat.search(q_dev, k=K, out=(gt_ids, gt_d))
+    gt = gt_ids.cpu().numpy().view(np.uint32)
+    rref = ref.load_index(graph, oracle.L2, base, DIM)
+    for ef in (64, 128, 256):
+        ids_dev = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+        d_dev = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+
+        def step():
+            idx.search(q_dev, k=K, ef=ef, out=(ids_dev, d_dev))
+        ms, clk = _timed(step, args.steps, args.warmup, stream, local)
+        _, _, dc = idx.search(qs, k=K, ef=ef, stats=True)
+        gpu_ids = ids_dev.cpu().numpy().view(np.uint32)
+        bytes_per_q = float(dc.mean()) * (DIM * 4 + 4 * 33)
+        achieved = bytes_per_q * nq / (ms / 1000.0) / 1e9
+        # The reference's own HnswIndex over the same graph file, all host threads, every query.
+        sample = qs
+        rref.search(sample[:100], k=K, ef=ef)
+        t0 = time.perf_counter()
+        r_ids, _, _ = rref.search(sample, k=K, ef=ef)
+        cpu_s = time.perf_counter() - t0
+        out = {"metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+               "config": {"workload": C3_WORKLOAD.format(ef=ef), "rows": base.shape[0], "batch": nq, "k": K, "ef": ef,
+                          "l2": "inputs larger than L2: 512 MB rows + 132 MB graph"},
+               "roofline": {"bound": "hbm", "kernel": "hnsw_search_kernel", "achieved": achieved, "peak": hbm,
+                            "unit": "GB/s", "frac": achieved / hbm, "peak_kind": f"{src} copy bandwidth",
+                            "traffic": None,
+                            "algorithmic": f"dc x (pd x 4 + 132) B per query, dc = {dc.mean():.0f} (mean)"},
+               "recall_at_10_vs_exact": _recall(gpu_ids, gt),
+               "identical_ids_vs_reference_same_graph": float(np.mean(np.all(gpu_ids[: len(sample)] == r_ids, axis=1))),
+               "differing_queries": np.nonzero(~np.all(gpu_ids[: len(sample)] == r_ids, axis=1))[0][:8].tolist(),
+               "cpu_baseline": {"value": len(sample) / cpu_s, "unit": "queries/s", "cores": os.cpu_count(),
+                                "kind": "reference",
+                                "sample": f"{len(sample)} queries, the reference's HnswIndex on the same index.hnsw "
+                                          f"({cpu_model()}, kernel set {ref.kernel_set()})"},
+               "graph_build_s_gpu": build_s, "clocks": clk}
+        print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload in ("c0", "c3"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "configs 0 and 3 time the reference inside "
+                                                                  "the same run (cpu_baseline)"}))
+            return 0
+        return run_c0_c3(args)
     if args.workload == "c4":
         if args.impl == "reference":
             return run_c4_reference(args)

@@ -3,6 +3,7 @@
 //   HnswSq8Index  (hnsw_index.h:63-96, file body hnsw_index.cc:104-129)
 //   PqFlatIndex / IvfPqIndex (src/index/quant/ivf_pq.h) in index_ivfpq.cc
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -129,7 +130,12 @@ class HnswGpuIndex final : public GpuIndex {
     // as a candidate until they hold ef allowed rows (the reference's unbounded heap), so they
     // run pooled: visited bits and candidates beyond a sorted front in global memory, the pool
     // growing fourfold on overflow.
-    const bool pooled = b.allow != nullptr;
+    // Walks run pooled by default (measured faster at every ef: the sorted shared-memory arrays
+    // cost O(ef) per insert). VDB_HNSW_POOLED_EF=<n> keeps unfiltered walks with ef <= n in shared
+    // memory (read on every call).
+    const char* pe = std::getenv("VDB_HNSW_POOLED_EF");
+    const uint64_t pooled_ef = pe != nullptr ? std::strtoull(pe, nullptr, 10) : 0ull;
+    const bool pooled = b.allow != nullptr || ef > pooled_ef;
     int bits = std::max(11, Log2Ceil(32 * ef));
     int cap = static_cast<int>(2 * ef + 64);
     int pool_cap = static_cast<int>(std::max<uint64_t>(4096, 32 * ef));
@@ -137,15 +143,6 @@ class HnswGpuIndex final : public GpuIndex {
       a.pooled = pooled ? 1 : 0;
       a.hash_bits = pooled ? 1 : bits;  // pooled walks mark visits in global memory
       a.cand_cap = pooled ? kPoolFrontSlots : cap;
-      if (pooled) {
-        a.vwords = (n_ + 31) / 32;
-        VDBGPU_RETURN_IF_ERROR(visited_.ensure(std::max<uint64_t>(1, b.nq * a.vwords) * 4));
-        VDBGPU_RETURN_IF_ERROR(pool_.ensure(std::max<uint64_t>(1, b.nq) * pool_cap * 8));
-        VDBGPU_CUDA(cudaMemsetAsync(visited_.get(), 0, b.nq * a.vwords * 4, ctx.stream()));
-        a.visited = visited_.as<uint32_t>();
-        a.pool = pool_.as<uint64_t>();
-        a.pool_cap = pool_cap;
-      }
       a.warps = 0;
       for (int w = 4; w >= 1; w /= 2)
         if (static_cast<size_t>(w) * HnswWarpSmemBytes(a.pd, a.hash_bits, a.ef, a.cand_cap) <= 227 * 1024) {
@@ -157,7 +154,30 @@ class HnswGpuIndex final : public GpuIndex {
                       "the graph walk's state exceeds the GPU's shared memory; use a smaller ef");
       ctx.Mark(0);
       ctx.Mark(1);
-      VDBGPU_CUDA(LaunchHnswSearch(a, ctx.stream()));
+      if (pooled) {
+        // Queries per launch: their visited bitmaps and candidate pools within ~8 GiB.
+        a.vwords = (n_ + 31) / 32;
+        const uint64_t per = a.vwords * 4 + static_cast<uint64_t>(pool_cap) * 8;
+        const uint64_t chunk = std::max<uint64_t>(1, std::min<uint64_t>(b.nq, (8ull << 30) / per));
+        VDBGPU_RETURN_IF_ERROR(visited_.ensure(chunk * a.vwords * 4));
+        VDBGPU_RETURN_IF_ERROR(pool_.ensure(chunk * static_cast<uint64_t>(pool_cap) * 8));
+        a.visited = visited_.as<uint32_t>();
+        a.pool = pool_.as<uint64_t>();
+        a.pool_cap = pool_cap;
+        for (uint64_t q0 = 0; q0 < b.nq; q0 += chunk) {
+          const uint64_t nqc = std::min(chunk, b.nq - q0);
+          VDBGPU_CUDA(cudaMemsetAsync(visited_.get(), 0, nqc * a.vwords * 4, ctx.stream()));
+          HnswArgs ac = a;
+          ac.nq = static_cast<int>(nqc);
+          ac.queries = b.queries + q0 * pd;
+          ac.out_dist = b.out_dist + q0 * k;
+          ac.out_row = b.out_row + q0 * k;
+          ac.out_dc = b.dist_comps != nullptr ? b.dist_comps + q0 : nullptr;
+          VDBGPU_CUDA(LaunchHnswSearch(ac, ctx.stream()));
+        }
+      } else {
+        VDBGPU_CUDA(LaunchHnswSearch(a, ctx.stream()));
+      }
       ctx.Mark(2);
       ctx.Mark(3);
       Status s = ctx.Sync("hnsw search");

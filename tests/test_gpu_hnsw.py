@@ -10,6 +10,18 @@ from helpers import golden, inputs
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["pooled", "shared_memory"], autouse=True)
+def walk_mode(request, monkeypatch):
+    """Every test runs with both walk state layouts: pooled (the default: visited bits and
+    candidates beyond a sorted front in global memory) and the shared-memory arrays kept for
+    unfiltered walks when VDB_HNSW_POOLED_EF is large."""
+    if request.param == "shared_memory":
+        monkeypatch.setenv("VDB_HNSW_POOLED_EF", "1000000")
+    else:
+        monkeypatch.delenv("VDB_HNSW_POOLED_EF", raising=False)
+    return request.param
+
+
 def test_hnsw_matches_reference_exactly(ctx):
     import vdb_b200
     g = golden("hnsw")
