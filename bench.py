@@ -204,7 +204,9 @@ def run_ours(args):
     q_dev = torch.from_numpy(qs).cuda()
     ids_dev = torch.empty((nq, K), dtype=torch.int32, device="cuda")
     d_dev = torch.empty((nq, K), dtype=torch.float32, device="cuda")
-    launches_per_step = 3  # prep_queries, scan_mma, finalize
+    # prep_queries, scan_mma over the row sample, scan_seed, scan_mma, finalize (a seeded scan);
+    # queries rescanned unseeded add gather, prep, scan, finalize and scatter launches.
+    launches_per_step = 5
 
     def step():
         idx.search(q_dev, k=K, rerank=DEPTH, out=(ids_dev, d_dev))
@@ -215,7 +217,7 @@ def run_ours(args):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks = Clocks(local)
-    scan_ms, stage, counters = [], np.zeros(3), np.zeros(4)
+    scan_ms, stage, counters, resc_steps = [], np.zeros(3), np.zeros(7), 0
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
@@ -223,7 +225,9 @@ def run_ours(args):
         st = ctx.stage_times()
         scan_ms.append(st[1])
         stage += np.array(st[:3])
-        counters += np.array(ctx.stage_counters()[:4], dtype=np.float64)
+        c = np.array(ctx.stage_counters()[:7], dtype=np.float64)
+        counters += c
+        resc_steps += int(c[4] > 0)
     ev1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -284,10 +288,13 @@ def run_ours(args):
             "scan_counters_per_step": {"chunks": counters[0] / args.steps,
                                        "chunks_with_candidates": counters[1] / args.steps,
                                        "candidates_per_query": counters[2] / args.steps / nq,
-                                       "compactions_per_query": counters[3] / args.steps / nq},
+                                       "compactions_per_query": counters[3] / args.steps / nq,
+                                       "seeded": bool(counters[5] > 0),
+                                       "seed_keep": counters[6] / max(counters[5], 1),
+                                       "rescanned_queries": counters[4] / args.steps},
             "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": nq * DIM * 4,
                     "d2h_bytes_per_step": nq * K * 8},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": launches_per_step * args.steps + 5 * resc_steps,
             "clocks": clk,
         }
         if world == 1:

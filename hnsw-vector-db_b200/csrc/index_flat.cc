@@ -1,11 +1,23 @@
 // Exact flat search (FlatIndex, src/index/flat_index.h:24-44) and the exhaustive SQ8 scan with
 // an fp32 re-rank on the GPU. Both run the same pipeline (ScanSearch):
 //   prep_queries -> tensor-core scan with fused top-C (scan_mma.cu) -> exact finalize (select.cu)
+//
+// Seeded scans. On large batches over large operands (at least 1e9 query-row pairs, 64k rows) the
+// pipeline first scans a strided sample of the rows (every s-th row, s = 16 by default;
+// VDB_SCAN_SAMPLE sets s, 0 turns seeding off) keeping m candidates per query, and takes the m-th smallest sample
+// key as the query's starting bound for the full scan, with m chosen so that about 2.25 C rows of
+// the whole operand are expected below it. Every slice of the full scan then starts from that
+// bound instead of from nothing, so few 32 x 32 chunks hold a candidate and the lists stay short.
+// The bound is only an estimate: finalize checks that at least C keys lie below the query's final
+// bound, which makes the C best exactly the C best of the whole operand (every row below the
+// bound was kept), and the rare query with fewer is rescanned without a seed.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
+#include "hnsw_build.cuh"
 #include "kernels.cuh"
 #include "runtime.h"
 #include "scan_mma.cuh"
@@ -42,6 +54,26 @@ void ChooseUnits(uint64_t qtiles, uint64_t ntiles, int sms, int* upq, int* tiles
   }
 }
 
+constexpr uint64_t kSampleMinRows = 65536;
+constexpr double kSeedMinWork = 1e9;  // queries x rows below which scans are not seeded
+
+uint32_t SampleStride() {
+  const char* v = std::getenv("VDB_SCAN_SAMPLE");
+  if (v == nullptr || *v == 0) return 16;
+  const long s = std::strtol(v, nullptr, 10);
+  return s < 0 ? 0u : static_cast<uint32_t>(std::min<long>(s, 1024));
+}
+
+// Sample candidates per query: the m-th smallest of every s-th row sits near rank m * s of the
+// whole operand; m * s ~ 2.25 C, at least 24 keys so the estimate's spread stays within the
+// margin. VDB_SCAN_SEED_KEEP sets m directly.
+int SeedKeep(int cpre, uint32_t stride) {
+  if (const char* v = std::getenv("VDB_SCAN_SEED_KEEP"); v != nullptr && *v != 0)
+    return std::max(1, std::min(static_cast<int>(std::strtol(v, nullptr, 10)), kScanCap - 64));
+  const int m = static_cast<int>(std::ceil(2.25 * cpre / stride));
+  return std::max(24, m);
+}
+
 // Copies n x pd floats from host or device memory to a new device buffer.
 Status UploadRows(Context& ctx, const float* rows, uint64_t n, uint32_t pd, DeviceBuffer* out) {
   VDBGPU_RETURN_IF_ERROR(out->alloc(std::max<uint64_t>(1, n * pd) * sizeof(float)));
@@ -57,7 +89,7 @@ class FlatGpuIndex final : public GpuIndex {
   uint64_t rows() const override { return n_; }
   const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
-    return rows_.size() + operand_.size() + norms_.size();
+    return rows_.size() + operand_.size() + norms_.size() + sample_rowterm_.size();
   }
 
   Status Build(Context& ctx, const float* rows, uint64_t n) {
@@ -94,6 +126,7 @@ class FlatGpuIndex final : public GpuIndex {
     op_.rows_f32 = rows_.as<float>();
     VDBGPU_RETURN_IF_ERROR(
         ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, op_.ab_format));
+    VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, &sample_rowterm_));
     return ctx.Sync("flat index build");
   }
 
@@ -121,7 +154,7 @@ class FlatGpuIndex final : public GpuIndex {
 
  private:
   uint64_t n_ = 0;
-  DeviceBuffer rows_, operand_, norms_;
+  DeviceBuffer rows_, operand_, norms_, sample_rowterm_;
   ScanOperands op_;
 };
 
@@ -132,7 +165,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
   const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + codes_.size() + operand_.size() + rowterm_.size() + vmin_.size() +
-           scale_.size();
+           scale_.size() + sample_rowterm_.size();
   }
 
   // Sq8Quantizer::train + encode (src/index/quant/sq8.cc:9-37) on the GPU, or loads a trained
@@ -199,6 +232,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
     op_.vmin = vmin_.as<float>();
     op_.scale = scale_.as<float>();
     VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, 0));
+    VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, &sample_rowterm_));
     return ctx.Sync("sq8 index build");
   }
 
@@ -252,14 +286,40 @@ class Sq8FlatGpuIndex final : public GpuIndex {
   }
 
   uint64_t n_ = 0;
-  DeviceBuffer rows_, codes_, operand_, rowterm_, vmin_, scale_;
+  DeviceBuffer rows_, codes_, operand_, rowterm_, vmin_, scale_, sample_rowterm_;
   ScanOperands op_;
 };
 
 }  // namespace
 
-Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
-                  const SearchBatch& b, int cpre, int depth) {
+Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer* rowterm_s) {
+  op->sample_stride = 0;
+  op->sample_rows = 0;
+  op->sample_rowterm = nullptr;
+  const uint32_t s = SampleStride();
+  if (s < 2 || op->rows < kSampleMinRows) return Status::OK();
+  const uint64_t ns = (op->rows + s - 1) / s;
+  if (op->rowterm != nullptr) {
+    const uint64_t nspad = RoundUp(ns, kScanBN);
+    VDBGPU_RETURN_IF_ERROR(rowterm_s->alloc(nspad * sizeof(float)));
+    VDBGPU_CUDA(cudaMemsetAsync(rowterm_s->get(), 0, nspad * sizeof(float), ctx.stream()));
+    VDBGPU_CUDA(cudaMemcpy2DAsync(rowterm_s->get(), sizeof(float), op->rowterm, s * sizeof(float),
+                                  sizeof(float), ns, cudaMemcpyDeviceToDevice, ctx.stream()));
+    op->sample_rowterm = rowterm_s->as<float>();
+  }
+  VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op->sample_map, op->b_operand, ns, op->kpad, kScanBN,
+                                              op->ab_format, static_cast<uint64_t>(op->kpad) * 2 * s));
+  op->sample_stride = s;
+  op->sample_rows = ns;
+  return Status::OK();
+}
+
+namespace {
+
+// One scan (plus its seed) and finalize over b; seeded scans rescan the queries finalize
+// returns (fewer than cpre keys below their bound) without a seed.
+Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
+                      const SearchBatch& b, int cpre, int depth, bool top) {
   if (b.nq == 0) return Status::OK();
   if (op.rows == 0) {
     // Nothing to scan: every slot is a miss.
@@ -280,7 +340,7 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsQTau, nq * sizeof(uint32_t), &qtau));
   VDBGPU_CUDA(cudaMemsetAsync(qtau, 0xFF, nq * sizeof(uint32_t), ctx.stream()));
 
-  ctx.Mark(0);
+  if (top) ctx.Mark(0);
   PrepArgs pa{};
   pa.nq = static_cast<int>(nq);
   pa.nq_pad = static_cast<int>(nq_pad);
@@ -306,9 +366,22 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   const uint64_t nunits = qtiles * static_cast<uint64_t>(upq);
   // One candidate list per (unit, epilogue warpgroup, query).
   const uint64_t wgs = static_cast<uint64_t>(ctx.scan_wgs());
-  VDBGPU_RETURN_IF_ERROR(
-      ctx.workspace(kWsCand, nunits * wgs * kScanBM * kScanCap * sizeof(uint2), &cand));
-  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, nunits * wgs * kScanBM * sizeof(int), &cnt));
+
+  // Seed: a scan of the row sample keeping m per query, then the m-th key per query.
+  // Small batches gain less than the sample pass and the count read-back cost.
+  const bool seeded = top && b.allow == nullptr && op.sample_stride >= 2 &&
+                      static_cast<double>(nq) * static_cast<double>(op.rows) >= kSeedMinWork &&
+                      op.sample_rows >= static_cast<uint64_t>(SeedKeep(cpre, op.sample_stride));
+  int upq_s = 1, tpu_s = 1, m = 0;
+  uint64_t nunits_s = 0;
+  if (seeded) {
+    m = SeedKeep(cpre, op.sample_stride);
+    ChooseUnits(qtiles, (op.sample_rows + kScanBN - 1) / kScanBN, ctx.sm_count(), &upq_s, &tpu_s);
+    nunits_s = qtiles * static_cast<uint64_t>(upq_s);
+  }
+  const uint64_t lists = std::max(nunits, nunits_s) * wgs * kScanBM;
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCand, lists * kScanCap * sizeof(uint2), &cand));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, lists * sizeof(int), &cnt));
 
   ScanArgs sa{};
   sa.nq = static_cast<int>(nq);
@@ -324,17 +397,38 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   sa.rowterm = op.rowterm;
   sa.allow = b.allow;
   sa.wgs = static_cast<int>(wgs);
-  sa.counters = ctx.timing() ? ctx.counters() : nullptr;
+  sa.counters = (top && ctx.timing()) ? ctx.counters() : nullptr;
   if (sa.counters != nullptr)
     VDBGPU_CUDA(cudaMemsetAsync(sa.counters, 0, 8 * sizeof(unsigned long long), ctx.stream()));
   sa.cand = static_cast<uint2*>(cand);
   sa.cand_count = static_cast<int*>(cnt);
   sa.qtau = static_cast<uint32_t*>(qtau);
   sa.status = ctx.status_word();
+  if (top) ctx.Mark(1);
+  if (seeded) {
+    ScanArgs ss = sa;
+    ss.nrows = static_cast<int>(op.sample_rows);
+    ss.keep = m;
+    ss.units_per_qtile = upq_s;
+    ss.rows_per_unit = tpu_s * kScanBN;
+    ss.nunits = static_cast<int>(nunits_s);
+    ss.rowterm = op.sample_rowterm;
+    ss.counters = nullptr;
+    const int grid_s = static_cast<int>(std::min<uint64_t>(nunits_s, static_cast<uint64_t>(ctx.sm_count())));
+    VDBGPU_CUDA(LaunchScan(amap, op.sample_map, ss, grid_s, ctx.stream()));
+    SeedArgs sd{};
+    sd.nq = static_cast<int>(nq);
+    sd.m = m;
+    sd.units_per_qtile = upq_s;
+    sd.wgs = static_cast<int>(wgs);
+    sd.cand = static_cast<const uint2*>(cand);
+    sd.cand_count = static_cast<const int*>(cnt);
+    sd.qtau_out = static_cast<uint32_t*>(qtau);
+    VDBGPU_CUDA(LaunchScanSeed(sd, ctx.stream()));
+  }
   const int grid = static_cast<int>(std::min<uint64_t>(nunits, static_cast<uint64_t>(ctx.sm_count())));
-  ctx.Mark(1);
   VDBGPU_CUDA(LaunchScan(amap, op.b_map, sa, grid, ctx.stream()));
-  ctx.Mark(2);
+  if (top) ctx.Mark(2);
 
   FinalizeArgs fa{};
   fa.nq = static_cast<int>(nq);
@@ -356,9 +450,52 @@ Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
   fa.scale = op.scale;
   fa.out_dist = b.out_dist;
   fa.out_row = b.out_row;
+  uint32_t* fb = nullptr;  // [0] count, [1..] queries to rescan
+  if (seeded) {
+    void* p;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsFallback, (nq + 1) * sizeof(uint32_t), &p));
+    fb = static_cast<uint32_t*>(p);
+    VDBGPU_CUDA(cudaMemsetAsync(fb, 0, sizeof(uint32_t), ctx.stream()));
+    fa.fb_count = reinterpret_cast<int*>(fb);
+    fa.fb_list = fb + 1;
+  }
   VDBGPU_CUDA(LaunchFinalize(fa, ctx.stream()));
-  ctx.Mark(3);
+  if (top) ctx.Mark(3);
+  if (!seeded) return Status::OK();
+
+  uint32_t nfb = 0;
+  VDBGPU_CUDA(cudaMemcpyAsync(&nfb, fb, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx.stream()));
+  VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+  if (sa.counters != nullptr) {
+    const unsigned long long extra[3] = {nfb, 1ull, static_cast<unsigned long long>(m)};
+    VDBGPU_CUDA(cudaMemcpyAsync(sa.counters + 4, extra, sizeof(extra), cudaMemcpyHostToDevice, ctx.stream()));
+    VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+  }
+  if (nfb == 0) return Status::OK();
+  if (nfb > nq) return Status(Status::kInternal, "seeded scan: fallback count out of range");
+  void *fq, *fd, *fr;
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsFbQueries, static_cast<uint64_t>(nfb) * pd * sizeof(float), &fq));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsFbDist, static_cast<uint64_t>(nfb) * b.k * sizeof(float), &fd));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsFbRow, static_cast<uint64_t>(nfb) * b.k * sizeof(uint32_t), &fr));
+  VDBGPU_CUDA(LaunchGatherRows(b.queries, fb + 1, nfb, static_cast<int>(pd), static_cast<float*>(fq),
+                               ctx.stream()));
+  SearchBatch sub = b;
+  sub.queries = static_cast<const float*>(fq);
+  sub.nq = nfb;
+  sub.out_dist = static_cast<float*>(fd);
+  sub.out_row = static_cast<uint32_t*>(fr);
+  sub.dist_comps = nullptr;
+  VDBGPU_RETURN_IF_ERROR(ScanSearchImpl(ctx, op, metric, pd, sub, cpre, depth, false));
+  VDBGPU_CUDA(LaunchScatterResults(static_cast<const float*>(fd), static_cast<const uint32_t*>(fr), fb + 1,
+                                   nfb, static_cast<int>(b.k), b.out_dist, b.out_row, ctx.stream()));
   return Status::OK();
+}
+
+}  // namespace
+
+Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
+                  const SearchBatch& b, int cpre, int depth) {
+  return ScanSearchImpl(ctx, op, metric, pd, b, cpre, depth, true);
 }
 
 Status CreateFlatIndex(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim,

@@ -28,8 +28,31 @@ struct FinalizeArgs {
   const float* scale;
   float* out_dist;
   uint32_t* out_row;
+  // Seeded scans: a query whose lists hold fewer than cpre keys below its final bound is
+  // appended to fb_list (the seed was too tight; its result must come from an unseeded scan).
+  uint32_t* fb_list;
+  int* fb_count;
 };
 cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream);
+
+// Seed of a scan's per-query bound: the m-th smallest key (ordered) among the candidate lists
+// a scan of a row sample left for the query (units_per_qtile x wgs lists of the FinalizeArgs
+// layout), written to qtau_out[q]; 0xFFFFFFFF when the lists hold fewer than m keys.
+struct SeedArgs {
+  int nq;
+  int m;
+  int units_per_qtile;
+  int wgs;
+  const uint2* cand;
+  const int* cand_count;
+  uint32_t* qtau_out;
+};
+cudaError_t LaunchScanSeed(const SeedArgs& a, cudaStream_t stream);
+
+// out_dist / out_row rows list[i] (k each) = src rows i, i < n.
+cudaError_t LaunchScatterResults(const float* src_dist, const uint32_t* src_row, const uint32_t* list,
+                                 uint32_t n, int k, float* out_dist, uint32_t* out_row,
+                                 cudaStream_t stream);
 
 enum PrepKind : int { kPrepFlat = 0, kPrepSq8Ip = 1, kPrepSq8L2 = 2 };
 

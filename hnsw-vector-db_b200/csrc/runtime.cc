@@ -152,10 +152,10 @@ Status Context::workspace(int slot, size_t bytes, void** out) {
 }
 
 Status Context::EncodeOperandMap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t kpad,
-                                 uint32_t box_rows, int ab_format) const {
+                                 uint32_t box_rows, int ab_format, uint64_t row_pitch_bytes) const {
   auto fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(encode_fn_);
   cuuint64_t dims[2] = {kpad, rows};
-  cuuint64_t strides[1] = {kpad * 2};
+  cuuint64_t strides[1] = {row_pitch_bytes != 0 ? row_pitch_bytes : kpad * 2};
   cuuint32_t box[2] = {64, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, ab_format == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,

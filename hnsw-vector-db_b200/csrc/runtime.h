@@ -120,8 +120,9 @@ class Context {
   Status workspace(int slot, size_t bytes, void** out);
 
   // 2-D K-major fp16/bf16 tensor map with a {64, box_rows} box and 128-byte swizzle.
+  // row_pitch_bytes 0 = kpad * 2 (contiguous rows); a larger pitch maps every n-th row.
   Status EncodeOperandMap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t kpad,
-                          uint32_t box_rows, int ab_format) const;
+                          uint32_t box_rows, int ab_format, uint64_t row_pitch_bytes = 0) const;
 
   // Reads and clears the device status word after the stream is synchronised.
   Status CheckDeviceStatus(const char* what);
@@ -164,6 +165,10 @@ enum WorkspaceSlot : int {
   kWsScratch1,
   kWsScratch2,
   kWsScratch3,
+  kWsFallback,
+  kWsFbQueries,
+  kWsFbDist,
+  kWsFbRow,
 };
 
 enum IndexKind : int {
@@ -267,7 +272,16 @@ struct ScanOperands {
   const float* vmin = nullptr;
   const float* scale = nullptr;
   CUtensorMap b_map;
+  // Seeding sample (index_flat.cc): every sample_stride-th operand row through sample_map, with
+  // its row terms in sample_rowterm when keys have one. sample_stride 0 = no sample.
+  uint32_t sample_stride = 0;
+  uint64_t sample_rows = 0;
+  const float* sample_rowterm = nullptr;
+  CUtensorMap sample_map;
 };
+// Attaches the seeding sample to `op` (after b_map / rowterm are set). rowterm_s receives the
+// sampled row terms. Small operands (and VDB_SCAN_SAMPLE=0) get none.
+Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer* rowterm_s);
 Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
                   const SearchBatch& b, int cpre, int depth);
 

@@ -269,6 +269,12 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       const float qs = valid_q ? a.qscale[q] : -1.f;
       const float qs_inv = 1.f / qs;
       float tau = valid_q ? INFINITY : -INFINITY;
+      // A bound present before the unit starts (a seeded estimate, or the C-th key another
+      // slice of this query published) applies from the first row on.
+      if (valid_q) {
+        const uint32_t g0 = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
+        if (g0 != 0xFFFFFFFFu) tau = key_float(g0);
+      }
       float tau_acc = tau * qs_inv;
       int count = 0;
       const size_t slot = (static_cast<size_t>(unit) * kWgs + wg) * kScanBM + row_in_tile;

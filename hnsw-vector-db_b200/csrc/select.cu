@@ -133,6 +133,12 @@ __global__ void __launch_bounds__(kFinWarps * 32)
     }
   }
   __syncwarp();
+  // With a seeded bound, fewer than cpre keys below it means some of the query's C best may
+  // lie above the seed: the query is rescanned without one.
+  if (a.fb_count != nullptr && nsurv < a.cpre) {
+    if (lane == 0) a.fb_list[atomicAdd(a.fb_count, 1)] = static_cast<uint32_t>(q);
+    return;
+  }
   int ncand;
   if (nsurv <= kMaxSurvivors) {
     sort_small(surv, nsurv);
@@ -241,6 +247,46 @@ __global__ void __launch_bounds__(kFinWarps * 32)
       a.out_row[o] = UINT32_MAX;
     }
   }
+}
+
+// ------------------------------------------------------------------ seeded scans
+
+// One warp per query: the m-th smallest ordered key over the query's lists, by a bitwise search
+// from the top bit (the largest v with fewer than m keys below it). Fewer than m keys in all
+// leaves every bit set: no bound.
+__global__ void __launch_bounds__(128) scan_seed_kernel(const SeedArgs a) {
+  const int q = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= a.nq) return;
+  const size_t qtiles = (static_cast<size_t>(a.nq) + kScanBM - 1) / kScanBM;
+  const int qtile = q / kScanBM, row_in_tile = q % kScanBM;
+  const int lists = a.units_per_qtile * a.wgs;
+  uint32_t ans = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = ans | (1u << bit);
+    int c = 0;
+    for (int p = 0; p < lists; ++p) {
+      const size_t unit = static_cast<size_t>(p / a.wgs) * qtiles + qtile;
+      const size_t slot = (unit * a.wgs + (p % a.wgs)) * kScanBM + row_in_tile;
+      const int n = a.cand_count[slot];
+      const uint2* b = a.cand + slot * kScanCap;
+      for (int e = lane; e < n; e += 32) c += float_key(__uint_as_float(b[e].x)) < cand ? 1 : 0;
+    }
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    if (c < a.m) ans = cand;
+  }
+  if (lane == 0) a.qtau_out[q] = ans;
+}
+
+__global__ void scatter_results_kernel(const float* src_dist, const uint32_t* src_row,
+                                       const uint32_t* list, uint32_t n, int k, float* out_dist,
+                                       uint32_t* out_row) {
+  const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<uint64_t>(n) * k) return;
+  const uint64_t r = i / k, j = i % k;
+  const uint64_t o = static_cast<uint64_t>(list[r]) * k + j;
+  out_dist[o] = src_dist[i];
+  out_row[o] = src_row[i];
 }
 
 // ------------------------------------------------------------------ operand preparation
@@ -401,6 +447,23 @@ cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const int blocks = (a.nq + kFinWarps - 1) / kFinWarps;
   finalize_kernel<<<blocks, kFinWarps * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchScanSeed(const SeedArgs& a, cudaStream_t stream) {
+  if (a.nq <= 0) return cudaSuccess;
+  const int blocks = (a.nq + 3) / 4;
+  scan_seed_kernel<<<blocks, 128, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchScatterResults(const float* src_dist, const uint32_t* src_row, const uint32_t* list,
+                                 uint32_t n, int k, float* out_dist, uint32_t* out_row,
+                                 cudaStream_t stream) {
+  const uint64_t total = static_cast<uint64_t>(n) * k;
+  if (total == 0) return cudaSuccess;
+  scatter_results_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      src_dist, src_row, list, n, k, out_dist, out_row);
   return cudaGetLastError();
 }
 

@@ -112,3 +112,64 @@ def test_sq8_scan_full_size_config1(ctx):
     oi, od = orc.sq8_scan_search(2, base, codes, vmin, scale, qs[sample], k=10, depth=100)
     assert_same_neighbors(ids[sample], d[sample], oi, od)
     assert np.all(np.diff(d, axis=1) >= 0)
+
+
+@pytest.mark.parametrize("keep", [None, 1, 6])
+def test_seeded_scan_is_exact(ctx, monkeypatch, keep):
+    """Batches of at least 1e9 (query, row) pairs over operands of 64k rows and more start every
+    query's bound from a strided row sample. The
+    seed is an estimate: queries left with fewer than C keys below it are rescanned unseeded.
+    keep = 1 makes most queries fall back (about s - 1 rows of the operand lie below the minimum of
+    a sample of every s-th row), keep = 6 some of them; results stay identical to the unseeded scan and to the
+    oracle, ties included (integer rows)."""
+    import vdb_b200
+    from vdb_b200 import synth
+    base, qs = synth.flat_int(120_000, 8400, dim=128, seed=11)
+    idx = vdb_b200.Index.create(ctx, "flat", "l2", base, 128)
+    if keep is not None:
+        monkeypatch.setenv("VDB_SCAN_SEED_KEEP", str(keep))
+    ctx.set_timing(True)
+    ids, d = idx.search(qs, k=10)
+    c = ctx.stage_counters()
+    ctx.set_timing(False)
+    assert c[5] == 1, "the scan was not seeded"
+    if keep == 1:
+        assert 0.5 * len(qs) < c[4] <= len(qs)
+    elif keep == 6:
+        assert 0 < c[4] < len(qs)
+    orc = oracle.Oracle()
+    sample = np.arange(0, len(qs), 280)
+    oi, od = orc.flat_search(0, base, qs[sample], 10)
+    np.testing.assert_array_equal(ids[sample], oi)
+    np.testing.assert_array_equal(d[sample], od)
+    monkeypatch.setenv("VDB_SCAN_SAMPLE", "0")
+    plain = vdb_b200.Index.create(ctx, "flat", "l2", base, 128)
+    pi, pd_ = plain.search(qs, k=10)
+    np.testing.assert_array_equal(ids, pi)
+    np.testing.assert_array_equal(d, pd_)
+    plain.free()
+    idx.free()
+
+
+def test_seeded_sq8_scan_with_fallbacks(ctx, monkeypatch):
+    """The seeded SQ8 scan (cosine, C = 128) with part of the batch rescanned: same ids and
+    distances as the unseeded scan."""
+    import vdb_b200
+    from vdb_b200 import synth
+    base, qs = synth.sq8_cosine(200_000, 5000, dim=128, seed=12)
+    idx = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
+    monkeypatch.setenv("VDB_SCAN_SEED_KEEP", "15")
+    ctx.set_timing(True)
+    ids, d = idx.search(qs, k=10, rerank=100)
+    c = ctx.stage_counters()
+    ctx.set_timing(False)
+    assert c[5] == 1 and 0 < c[4] < len(qs)
+    monkeypatch.delenv("VDB_SCAN_SEED_KEEP")
+    ids2, d2 = idx.search(qs, k=10, rerank=100)
+    monkeypatch.setenv("VDB_SCAN_SAMPLE", "0")
+    plain = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
+    pi, pd_ = plain.search(qs, k=10, rerank=100)
+    for a, b in ((ids, pi), (d, pd_), (ids2, pi), (d2, pd_)):
+        np.testing.assert_array_equal(a, b)
+    plain.free()
+    idx.free()
