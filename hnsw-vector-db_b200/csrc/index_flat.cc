@@ -364,14 +364,15 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   int upq = 1, tpu = 1;
   ChooseUnits(qtiles, ntiles, ctx.sm_count(), &upq, &tpu);
   const uint64_t nunits = qtiles * static_cast<uint64_t>(upq);
-  // One candidate list per (unit, epilogue warpgroup, query).
-  const uint64_t wgs = static_cast<uint64_t>(ctx.scan_wgs());
-
   // Seed: a scan of the row sample keeping m per query, then the m-th key per query.
   // Small batches gain less than the sample pass and the count read-back cost.
   const bool seeded = top && b.allow == nullptr && op.sample_stride >= 2 &&
                       static_cast<double>(nq) * static_cast<double>(op.rows) >= kSeedMinWork &&
                       op.sample_rows >= static_cast<uint64_t>(SeedKeep(cpre, op.sample_stride));
+  // One candidate list per (unit, epilogue warpgroup, query). Two warpgroups split each tile's
+  // columns and halve the time an accumulator waits for its epilogue, but double the lists: a
+  // win once seeding keeps the lists short.
+  const uint64_t wgs = static_cast<uint64_t>(ctx.scan_wgs() > 0 ? ctx.scan_wgs() : (seeded ? 2 : 1));
   int upq_s = 1, tpu_s = 1, m = 0;
   uint64_t nunits_s = 0;
   if (seeded) {
@@ -390,6 +391,8 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   sa.mode = op.rowterm != nullptr ? kKeyRowTerm : kKeyScaled;
   sa.ab_format = op.ab_format;
   sa.keep = cpre;
+  sa.stages = ScanMaxStagesFor(sa.kblocks);
+  if (ctx.scan_stages() > 0) sa.stages = std::min(sa.stages, ctx.scan_stages());
   sa.units_per_qtile = upq;
   sa.rows_per_unit = tpu * kScanBN;
   sa.nunits = static_cast<int>(nunits);
@@ -409,6 +412,8 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
     ScanArgs ss = sa;
     ss.nrows = static_cast<int>(op.sample_rows);
     ss.keep = m;
+    // The sample's lists compact early: cheap 128-slot compactions tighten its bounds sooner.
+    ss.compact_at = m < 64 ? 96 : 0;
     ss.units_per_qtile = upq_s;
     ss.rows_per_unit = tpu_s * kScanBN;
     ss.nunits = static_cast<int>(nunits_s);

@@ -87,8 +87,10 @@ Status Context::Open(int device, std::unique_ptr<Context>* out) {
   if (q != cudaDriverEntryPointSuccess || c->encode_fn_ == nullptr)
     return Status(Status::kUnavailable, "cuTensorMapEncodeTiled is not available");
   c->order_ = DetectKernelOrder();
-  if (const char* w = std::getenv("VDB_SCAN_WARPGROUPS"); w != nullptr && std::strcmp(w, "2") == 0)
-    c->scan_wgs_ = 2;
+  if (const char* w = std::getenv("VDB_SCAN_WARPGROUPS"); w != nullptr && *w != 0)
+    c->scan_wgs_ = std::strcmp(w, "2") == 0 ? 2 : 1;
+  if (const char* v = std::getenv("VDB_SCAN_STAGES"); v != nullptr && *v != 0)
+    c->scan_stages_ = std::max(0, static_cast<int>(std::strtol(v, nullptr, 10)));
   *out = std::move(c);
   return Status::OK();
 }

@@ -110,8 +110,11 @@ class Context {
   // only while timing is enabled.
   unsigned long long* counters() const { return counters_.as<unsigned long long>(); }
   int Counters(unsigned long long* out, int cap);
-  // Epilogue warpgroups of the scan (VDB_SCAN_WARPGROUPS, default 1).
+  // Epilogue warpgroups of the scan (VDB_SCAN_WARPGROUPS=1 or 2; 0 = per scan: 2 for seeded
+  // scans, whose lists stay short, else 1).
   int scan_wgs() const { return scan_wgs_; }
+  // B stages of the scan (VDB_SCAN_STAGES; 0 = as many as fit).
+  int scan_stages() const { return scan_stages_; }
   int sm_count() const { return sm_count_; }
   int order() const { return order_; }
   int* status_word() const { return status_.as<int>(); }
@@ -140,7 +143,8 @@ class Context {
   bool timing_ = false;
   cudaEvent_t marks_[kMaxMarks] = {};
   DeviceBuffer counters_;
-  int scan_wgs_ = 1;
+  int scan_wgs_ = 0;
+  int scan_stages_ = 0;
   int sm_count_ = 0;
   int order_ = 1;
   DeviceBuffer status_;

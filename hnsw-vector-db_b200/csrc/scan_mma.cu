@@ -10,9 +10,10 @@
 //               k-blocks (256 rows x 64 fp16) through a 4-stage mbarrier ring.
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one thread issues
 //               tcgen05.mma (M=128, N=256, K=16) into alternating accumulators.
-//   warps 2..5  epilogue: each thread owns one query (one TMEM lane) and reads its 256 columns in
-//               chunks of 32 (tcgen05.ld). A chunk whose best key does not beat the thread's
-//               threshold costs one min per value; otherwise qualifying (key, row) pairs are
+//   warps 2..   epilogue: each thread owns one query (one TMEM lane) and reads its 256 columns in
+//               chunks of 32 (tcgen05.ld), keeping each chunk's best score (one min per value);
+//               one vote per chunk finds the chunks where some query of the warp beats its
+//               threshold, and only those are read again and their qualifying (key, row) pairs
 //               appended to the query's candidate buffer in global memory. A full buffer is
 //               compacted by the whole warp to its C best (by key, then row) and the C-th key
 //               becomes the new threshold, also published to every unit of the same query.
@@ -32,8 +33,8 @@ constexpr uint32_t kBBytesPerStage = kScanBN * 128;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
 
 struct __align__(8) ScanBarriers {
-  uint64_t full[kScanStages];
-  uint64_t empty[kScanStages];
+  uint64_t full[kScanMaxStages];
+  uint64_t empty[kScanMaxStages];
   uint64_t a_full;
   uint64_t a_empty;
   uint64_t acc_full[2];
@@ -55,11 +56,11 @@ __device__ __forceinline__ void unit_rows(const ScanArgs& a, int unit, int* qtil
   *r1 = e < a.nrows ? e : a.nrows;
 }
 
-// Warp-cooperative compaction of lane `src`'s candidate buffer (n entries, in row order) to
-// its `keep` best by (key, row). Returns the keep-th key (ordered) to every lane.
+// Warp-cooperative compaction of lane `src`'s candidate buffer (n <= 32 kT entries, in row order)
+// to its `keep` best by (key, row). Returns the keep-th key (ordered) to every lane.
+template <int kT>
 __device__ uint32_t compact_buffer(uint2* buf, int n, int keep) {
   const int lane = threadIdx.x & 31;
-  constexpr int kT = kScanCap / 32;
   uint32_t keys[kT];
   uint2 ent[kT];
 #pragma unroll
@@ -111,14 +112,15 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + a.kblocks * kABytesPerKB;
+  const int nstages = a.stages > 0 ? a.stages : kScanStages;
   ScanBarriers* bars =
-      reinterpret_cast<ScanBarriers*>(smem_b + kScanStages * kBBytesPerStage);
+      reinterpret_cast<ScanBarriers*>(smem_b + nstages * kBBytesPerStage);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kScanStages; ++s) {
+    for (int s = 0; s < nstages; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
@@ -126,9 +128,8 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
     mbar_init(&bars->a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
-      // Two epilogue warpgroups: warpgroup b drains accumulator b alone (128 threads). One
-      // warpgroup drains both.
-      mbar_init(&bars->acc_empty[b], 128);
+      // Every epilogue thread drains its share of every tile.
+      mbar_init(&bars->acc_empty[b], 128 * kWgs);
     }
     mbar_init(&bars->mma_done, 1);
     fence_barrier_init();
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
                         kb * kScanBK, row0);
             issued |= 1u << stage;
             last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-            if (++stage == kScanStages) {
+            if (++stage == nstages) {
               stage = 0;
               phase ^= 1u;
             }
@@ -190,7 +191,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       }
       // Every copy this thread issued lands before the CTA may exit (bounded): the last load
       // into each stage completes the phase recorded for it.
-      for (int s = 0; s < kScanStages; ++s)
+      for (int s = 0; s < nstages; ++s)
         if ((issued >> s) & 1u)
           mbar_wait(&bars->full[s], (last_parity >> s) & 1u, nullptr, 0);
       if (a_issued) mbar_wait(&bars->a_full, a_parity, nullptr, 0);
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
                        idesc, (kb | kk) != 0 ? 1u : 0u);
             }
             umma_commit(&bars->empty[stage]);
-            if (++stage == kScanStages) {
+            if (++stage == nstages) {
               stage = 0;
               phase ^= 1u;
             }
@@ -250,14 +251,18 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue
-    // Two warpgroups; warpgroup w takes the tiles that land in accumulator w (every other tile
-    // of the CTA's sequence), keeping its own threshold and candidate list per query.
+    // kWgs warpgroups split every tile's columns (warpgroup w takes chunks [w kChunks,
+    // (w + 1) kChunks)), so an accumulator is free again after 1 / kWgs of a tile's epilogue
+    // latency; each warpgroup keeps its own threshold and candidate list per query.
     const int wg = kWgs == 1 ? 0 : (warp - 2) >> 2;
+    constexpr int kChunks = kScanBN / 32 / kWgs;
+    const int col0 = wg * kChunks * 32;
     unsigned long long n_chunks = 0, n_trig = 0, n_ins = 0, n_comp = 0;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    uint32_t acc_phase = 0;
-    uint32_t tcount = 0;  // tiles of this CTA so far (both warpgroups count all of them)
+    uint32_t tcount = 0;  // tiles of this CTA so far
+    // A list holding more than compact_at entries is compacted to `keep` (at most 32 land per chunk).
+    const int compact_at = a.compact_at > 0 ? a.compact_at : kScanCap - 32;
     bool ok = true;
     for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
       int qtile, r0, r1;
@@ -292,7 +297,9 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
                                      kScanCap;
           ++n_comp;
           __syncwarp();
-          const uint32_t kth = compact_buffer(sbuf, n, a.keep);
+          // Short lists (the sample pass compacts at 96 + 32) take the 4-slot variant.
+          const uint32_t kth = n <= 128 ? compact_buffer<4>(sbuf, n, a.keep)
+                                        : compact_buffer<kScanCap / 32>(sbuf, n, a.keep);
           if (lane == src) {
             count = a.keep;
             tau = fminf(tau, key_float(kth));
@@ -303,19 +310,17 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
         }
       };
 
-      // One chunk of 32 accumulator columns starting at row c0. Scores: raw accumulators
-      // (larger is closer, scaled-key mode) or keys (smaller is closer, row-term mode); masked
-      // columns get the worst score. A max/min tree over the 32 scores is the fast path's
-      // filter; when some lane of the warp has a hit, the warp descends the tree with votes and
-      // each lane appends only its qualifying columns, in column order.
-      auto process = [&](uint32_t (&v)[32], int c0) {
+      // Scores of one chunk of 32 accumulator columns starting at row c0, in place: raw
+      // accumulators (larger is closer, scaled-key mode) or keys (smaller is closer, row-term
+      // mode); masked columns get the worst score.
+      constexpr bool kMin = kMode == kKeyRowTerm;
+      auto better = [](float x, float y) { return kMin ? fminf(x, y) : fmaxf(x, y); };
+      auto scores = [&](uint32_t (&v)[32], int c0) {
         uint32_t allow_bits = 0xFFFFFFFFu;
         if (a.allow != nullptr) allow_bits = __ldg(&a.allow[c0 >> 5]);
         const int nvalid = r1 - c0;
         const bool full = nvalid >= 32 && allow_bits == 0xFFFFFFFFu;
-        constexpr bool kMin = kMode == kKeyRowTerm;
         const float worst = kMin ? INFINITY : -INFINITY;
-        const float bound = kMin ? tau : tau_acc;
         if constexpr (kMode == kKeyRowTerm) {
           const float4* rt4 = reinterpret_cast<const float4*>(a.rowterm + c0);
 #pragma unroll
@@ -332,69 +337,103 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
           for (int j = 0; j < 32; ++j)
             if (j >= nvalid || !((allow_bits >> j) & 1u)) v[j] = __float_as_uint(worst);
         }
-        auto better = [&](float x, float y) { return kMin ? fminf(x, y) : fmaxf(x, y); };
+      };
+      auto best32 = [&](const uint32_t (&v)[32]) {
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = better(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+#pragma unroll
+        for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] = better(t[2 * i], t[2 * i + 1]);
+        return t[0];
+      };
+      // Appends the chunk's qualifying columns in column order, descending by groups of 8
+      // (hits are sparse: most groups of a chunk with a hit cost one vote).
+      auto extract = [&](const uint32_t (&v)[32], int c0) {
+        const float bound = kMin ? tau : tau_acc;
         auto passes = [&](float x) { return kMin ? (x < bound) : (x > bound); };
-        float t1[16], t2[8], t3[4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) t1[i] = better(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        for (int g = 0; g < 4; ++g) {
+          float m = __uint_as_float(v[8 * g]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) t2[i] = better(t1[2 * i], t1[2 * i + 1]);
+          for (int j = 8 * g + 1; j < 8 * g + 8; ++j) m = better(m, __uint_as_float(v[j]));
+          if (!__any_sync(0xFFFFFFFFu, passes(m))) continue;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) t3[i] = better(t2[2 * i], t2[2 * i + 1]);
-        ++n_chunks;
-        if (!__any_sync(0xFFFFFFFFu, passes(better(better(t3[0], t3[1]), better(t3[2], t3[3]))))) return;
-        ++n_trig;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sc = __uint_as_float(v[j]);
-          if (passes(sc)) {
-            const float key = kMin ? sc : qs * sc;
-            buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c0 + j));
-            ++count;
-            ++n_ins;
+          for (int j = 8 * g; j < 8 * g + 8; ++j) {
+            const float sc = __uint_as_float(v[j]);
+            if (passes(sc)) {
+              const float key = kMin ? sc : qs * sc;
+              buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c0 + j));
+              ++count;
+              ++n_ins;
+            }
           }
         }
-        compact_lanes(kScanCap - 32);
+        compact_lanes(compact_at);
       };
 
+      // Per tile: pass 1 reads the 8 chunks back to back and keeps each chunk's best score
+      // (no branches); one vote per chunk marks the chunks where some query of the warp has a
+      // hit; pass 2 reloads only those chunks from TMEM (the accumulator stays put until
+      // acc_empty) and appends their hits.
       for (int row0 = r0; row0 < r1; row0 += kScanBN, ++tcount) {
         const int accb = static_cast<int>(tcount & 1u);
-        if (kWgs == 2 && accb != wg) continue;
-        // The shared threshold is read now and applied after the first chunk (hides latency).
+        // The shared threshold is read now and applied after pass 1 (hides latency).
         uint32_t g = 0xFFFFFFFFu;
         if (valid_q) g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
-        if (!mbar_wait(&bars->acc_full[accb], kWgs == 2 ? acc_phase : (tcount >> 1) & 1u, a.status,
-                       kDevTimeoutAcc)) {
+        if (!mbar_wait(&bars->acc_full[accb], (tcount >> 1) & 1u, a.status, kDevTimeoutAcc)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                static_cast<uint32_t>(accb * kScanBN);
+                                static_cast<uint32_t>(accb * kScanBN + col0);
+        const int c_base = row0 + col0;
         uint32_t va[32], vb[32];
+        float cbest[kChunks];
         __syncwarp();
         tmem_ld_32x32b_x32(t_addr, va);
         tmem_ld_wait_regs(va);
-#pragma unroll 1
-        for (int ch = 0; ch < kScanBN / 32; ch += 2) {
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ch += 2) {
           __syncwarp();
-          tmem_ld_32x32b_x32(t_addr + (ch + 1) * 32, vb);  // in flight while va is processed
-          process(va, row0 + ch * 32);
-          if (ch == 0 && g != 0xFFFFFFFFu) {
-            tau = fminf(tau, key_float(g));
-            tau_acc = tau * qs_inv;
-          }
+          tmem_ld_32x32b_x32(t_addr + (ch + 1) * 32, vb);  // in flight while va is scored
+          scores(va, c_base + ch * 32);
+          cbest[ch] = best32(va);
           tmem_ld_wait_regs(vb);
-          if (ch + 2 < kScanBN / 32) {
+          if (ch + 2 < kChunks) {
             __syncwarp();
             tmem_ld_32x32b_x32(t_addr + (ch + 2) * 32, va);
           }
-          process(vb, row0 + (ch + 1) * 32);
+          scores(vb, c_base + (ch + 1) * 32);
+          cbest[ch + 1] = best32(vb);
+          if (ch + 2 < kChunks) tmem_ld_wait_regs(va);
+        }
+        if (g != 0xFFFFFFFFu) {
+          tau = fminf(tau, key_float(g));
+          tau_acc = tau * qs_inv;
+        }
+        uint32_t hits = 0;
+        {
+          const float bound = kMin ? tau : tau_acc;
+#pragma unroll
+          for (int ch = 0; ch < kChunks; ++ch)
+            if (__any_sync(0xFFFFFFFFu, kMin ? (cbest[ch] < bound) : (cbest[ch] > bound))) hits |= 1u << ch;
+        }
+        n_chunks += kChunks;
+        n_trig += __popc(hits);
+        while (hits != 0u) {
+          const int ch = __ffs(hits) - 1;
+          hits &= hits - 1u;
+          __syncwarp();
+          tmem_ld_32x32b_x32(t_addr + ch * 32, va);
           tmem_ld_wait_regs(va);
+          scores(va, c_base + ch * 32);
+          extract(va, c_base + ch * 32);
         }
         tc_fence_before();
         mbar_arrive(&bars->acc_empty[accb]);
-        acc_phase ^= 1u;
       }
       // Leave at most `keep` entries per query and publish this unit's keep-th key.
       if (ok) compact_lanes(a.keep);
@@ -424,15 +463,23 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
 
 }  // namespace
 
-size_t ScanSmemBytes(int kblocks) {
+size_t ScanSmemBytes(int kblocks, int stages) {
   return 1024 + static_cast<size_t>(kblocks) * kABytesPerKB +
-         static_cast<size_t>(kScanStages) * kBBytesPerStage + sizeof(ScanBarriers);
+         static_cast<size_t>(stages > 0 ? stages : kScanStages) * kBBytesPerStage + sizeof(ScanBarriers);
+}
+
+int ScanMaxStagesFor(int kblocks) {
+  int s = kScanMaxStages;
+  while (s > 1 && ScanSmemBytes(kblocks, s) > 227u * 1024u) --s;
+  return s;
 }
 
 template <int kMode, int kWgs>
 cudaError_t LaunchScanT(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
                         int grid, cudaStream_t stream) {
-  const size_t smem = ScanSmemBytes(a.kblocks);
+  if (a.stages < 0 || a.stages > kScanMaxStages) return cudaErrorInvalidValue;
+  const size_t smem = ScanSmemBytes(a.kblocks, a.stages);
+  if (smem > 227u * 1024u) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(scan_mma_kernel<kMode, kWgs>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));

@@ -10,7 +10,8 @@ namespace vdbgpu {
 constexpr int kScanBM = 128;      // queries per tile: TMEM lanes, M of the MMA
 constexpr int kScanBN = 256;      // rows per tile: TMEM columns of one accumulator, N of the MMA
 constexpr int kScanBK = 64;       // fp16 elements per k-block (one 128-byte swizzle atom)
-constexpr int kScanStages = 4;    // B k-block stages in flight
+constexpr int kScanStages = 4;    // B k-block stages in flight unless ScanArgs::stages says otherwise
+constexpr int kScanMaxStages = 6;
 constexpr int kScanMaxKB = 4;     // padded dims up to 256
 #ifndef VDBGPU_SCAN_CAP
 #define VDBGPU_SCAN_CAP 512
@@ -32,6 +33,8 @@ struct ScanArgs {
   int mode;             // ScanKeyMode
   int ab_format;        // 0 = fp16, 1 = bf16 (both operands)
   int keep;             // candidates kept per compaction (C), < kScanCap - 32
+  int compact_at;       // list length that triggers a compaction, <= kScanCap - 32 (0 = that)
+  int stages;           // B k-block stages in flight, 1..kScanMaxStages (0 = kScanStages)
   int units_per_qtile;  // row slices per 128-query tile
   int rows_per_unit;    // multiple of kScanBN
   int nunits;           // qtiles * units_per_qtile
@@ -51,6 +54,9 @@ struct ScanArgs {
 cudaError_t LaunchScan(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
                        int grid, cudaStream_t stream);
 
-size_t ScanSmemBytes(int kblocks);
+// Dynamic shared memory of a scan with `stages` B stages (0 = kScanStages).
+size_t ScanSmemBytes(int kblocks, int stages = 0);
+// The most B stages (<= kScanMaxStages) that fit next to the query tile in 227 KB.
+int ScanMaxStagesFor(int kblocks);
 
 }  // namespace vdbgpu
