@@ -4,13 +4,15 @@
 //
 // Seeded scans. On large batches over large operands (at least 1e9 query-row pairs, 64k rows) the
 // pipeline first scans a strided sample of the rows (every s-th row, s = 16 by default;
-// VDB_SCAN_SAMPLE sets s, 0 turns seeding off) keeping m candidates per query, and takes the m-th smallest sample
-// key as the query's starting bound for the full scan, with m chosen so that about 2.25 C rows of
-// the whole operand are expected below it. Every slice of the full scan then starts from that
-// bound instead of from nothing, so few 32 x 32 chunks hold a candidate and the lists stay short.
-// The bound is only an estimate: finalize checks that at least C keys lie below the query's final
-// bound, which makes the C best exactly the C best of the whole operand (every row below the
-// bound was kept), and the rare query with fewer is rescanned without a seed.
+// VDB_SCAN_SAMPLE sets s, 0 turns seeding off) keeping m candidates per query, and takes the m-th
+// smallest sample key as the query's starting bound for the full scan, with m chosen so that about
+// 2.25 C rows of the whole operand are expected below it. Every slice of the full scan then starts
+// from that bound instead of from nothing, so few 32 x 32 chunks hold a candidate and the lists
+// stay short. The sample scan can itself be seeded the same way from a 16 times coarser sample
+// (VDB_SCAN_SAMPLE_LEVELS=2; a query whose coarse seed leaves fewer than m sample keys gets no
+// seed). The bound is only an estimate: finalize checks that at least C keys lie below the
+// query's final bound, which makes the C best exactly the C best of the whole operand (every row
+// below the bound was kept), and the rare query with fewer is rescanned without a seed.
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -56,6 +58,8 @@ void ChooseUnits(uint64_t qtiles, uint64_t ntiles, int sms, int* upq, int* tiles
 
 constexpr uint64_t kSampleMinRows = 65536;
 constexpr double kSeedMinWork = 1e9;  // queries x rows below which scans are not seeded
+constexpr uint64_t kSampleRatio = 16;     // stride of sample level 1 / stride of level 0
+constexpr uint64_t kSample2MinRows = 1024;
 
 uint32_t SampleStride() {
   const char* v = std::getenv("VDB_SCAN_SAMPLE");
@@ -89,7 +93,7 @@ class FlatGpuIndex final : public GpuIndex {
   uint64_t rows() const override { return n_; }
   const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
-    return rows_.size() + operand_.size() + norms_.size() + sample_rowterm_.size();
+    return rows_.size() + operand_.size() + norms_.size() + sample_rowterm_[0].size() + sample_rowterm_[1].size();
   }
 
   Status Build(Context& ctx, const float* rows, uint64_t n) {
@@ -126,7 +130,7 @@ class FlatGpuIndex final : public GpuIndex {
     op_.rows_f32 = rows_.as<float>();
     VDBGPU_RETURN_IF_ERROR(
         ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, op_.ab_format));
-    VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, &sample_rowterm_));
+    VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, sample_rowterm_));
     return ctx.Sync("flat index build");
   }
 
@@ -154,7 +158,8 @@ class FlatGpuIndex final : public GpuIndex {
 
  private:
   uint64_t n_ = 0;
-  DeviceBuffer rows_, operand_, norms_, sample_rowterm_;
+  DeviceBuffer rows_, operand_, norms_;
+  DeviceBuffer sample_rowterm_[2];
   ScanOperands op_;
 };
 
@@ -165,7 +170,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
   const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + codes_.size() + operand_.size() + rowterm_.size() + vmin_.size() +
-           scale_.size() + sample_rowterm_.size();
+           scale_.size() + sample_rowterm_[0].size() + sample_rowterm_[1].size();
   }
 
   // Sq8Quantizer::train + encode (src/index/quant/sq8.cc:9-37) on the GPU, or loads a trained
@@ -232,7 +237,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
     op_.vmin = vmin_.as<float>();
     op_.scale = scale_.as<float>();
     VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, 0));
-    VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, &sample_rowterm_));
+    VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, sample_rowterm_));
     return ctx.Sync("sq8 index build");
   }
 
@@ -286,31 +291,40 @@ class Sq8FlatGpuIndex final : public GpuIndex {
   }
 
   uint64_t n_ = 0;
-  DeviceBuffer rows_, codes_, operand_, rowterm_, vmin_, scale_, sample_rowterm_;
+  DeviceBuffer rows_, codes_, operand_, rowterm_, vmin_, scale_;
+  DeviceBuffer sample_rowterm_[2];
   ScanOperands op_;
 };
 
 }  // namespace
 
-Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer* rowterm_s) {
-  op->sample_stride = 0;
-  op->sample_rows = 0;
-  op->sample_rowterm = nullptr;
-  const uint32_t s = SampleStride();
-  if (s < 2 || op->rows < kSampleMinRows) return Status::OK();
-  const uint64_t ns = (op->rows + s - 1) / s;
-  if (op->rowterm != nullptr) {
-    const uint64_t nspad = RoundUp(ns, kScanBN);
-    VDBGPU_RETURN_IF_ERROR(rowterm_s->alloc(nspad * sizeof(float)));
-    VDBGPU_CUDA(cudaMemsetAsync(rowterm_s->get(), 0, nspad * sizeof(float), ctx.stream()));
-    VDBGPU_CUDA(cudaMemcpy2DAsync(rowterm_s->get(), sizeof(float), op->rowterm, s * sizeof(float),
-                                  sizeof(float), ns, cudaMemcpyDeviceToDevice, ctx.stream()));
-    op->sample_rowterm = rowterm_s->as<float>();
+Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer (&rowterm_s)[2]) {
+  op->nsamples = 0;
+  const uint32_t s0 = SampleStride();
+  if (s0 < 2 || op->rows < kSampleMinRows) return Status::OK();
+  // VDB_SCAN_SAMPLE_LEVELS=2 adds the coarser level (measured on config 1: no faster than one).
+  int max_levels = 1;
+  if (const char* v = std::getenv("VDB_SCAN_SAMPLE_LEVELS"); v != nullptr && *v == '2') max_levels = 2;
+  for (int lv = 0; lv < max_levels; ++lv) {
+    const uint64_t s = lv == 0 ? s0 : static_cast<uint64_t>(s0) * kSampleRatio;
+    const uint64_t ns = (op->rows + s - 1) / s;
+    if (lv == 1 && ns < kSample2MinRows) break;
+    ScanOperands::Sample& smp = op->samples[lv];
+    smp.rowterm = nullptr;
+    if (op->rowterm != nullptr) {
+      const uint64_t nspad = RoundUp(ns, kScanBN);
+      VDBGPU_RETURN_IF_ERROR(rowterm_s[lv].alloc(nspad * sizeof(float)));
+      VDBGPU_CUDA(cudaMemsetAsync(rowterm_s[lv].get(), 0, nspad * sizeof(float), ctx.stream()));
+      VDBGPU_CUDA(cudaMemcpy2DAsync(rowterm_s[lv].get(), sizeof(float), op->rowterm, s * sizeof(float),
+                                    sizeof(float), ns, cudaMemcpyDeviceToDevice, ctx.stream()));
+      smp.rowterm = rowterm_s[lv].as<float>();
+    }
+    VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&smp.map, op->b_operand, ns, op->kpad, kScanBN,
+                                                op->ab_format, static_cast<uint64_t>(op->kpad) * 2 * s));
+    smp.stride = static_cast<uint32_t>(s);
+    smp.rows = ns;
+    op->nsamples = lv + 1;
   }
-  VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op->sample_map, op->b_operand, ns, op->kpad, kScanBN,
-                                              op->ab_format, static_cast<uint64_t>(op->kpad) * 2 * s));
-  op->sample_stride = s;
-  op->sample_rows = ns;
   return Status::OK();
 }
 
@@ -366,19 +380,23 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   const uint64_t nunits = qtiles * static_cast<uint64_t>(upq);
   // Seed: a scan of the row sample keeping m per query, then the m-th key per query.
   // Small batches gain less than the sample pass and the count read-back cost.
-  const bool seeded = top && b.allow == nullptr && op.sample_stride >= 2 &&
+  const bool seeded = top && b.allow == nullptr && op.nsamples > 0 &&
                       static_cast<double>(nq) * static_cast<double>(op.rows) >= kSeedMinWork &&
-                      op.sample_rows >= static_cast<uint64_t>(SeedKeep(cpre, op.sample_stride));
+                      op.samples[0].rows >= static_cast<uint64_t>(SeedKeep(cpre, op.samples[0].stride));
   // One candidate list per (unit, epilogue warpgroup, query). Two warpgroups split each tile's
   // columns and halve the time an accumulator waits for its epilogue, but double the lists: a
   // win once seeding keeps the lists short.
   const uint64_t wgs = static_cast<uint64_t>(ctx.scan_wgs() > 0 ? ctx.scan_wgs() : (seeded ? 2 : 1));
-  int upq_s = 1, tpu_s = 1, m = 0;
+  // Sample levels, coarsest first: each starts from the bound the previous one seeded.
+  const int levels = seeded ? (op.nsamples > 1 && op.samples[1].rows >= 4u * static_cast<uint64_t>(
+                                                       SeedKeep(cpre, op.samples[0].stride)) ? 2 : 1)
+                            : 0;
+  int upq_s[2] = {1, 1}, tpu_s[2] = {1, 1}, m = 0;
   uint64_t nunits_s = 0;
-  if (seeded) {
-    m = SeedKeep(cpre, op.sample_stride);
-    ChooseUnits(qtiles, (op.sample_rows + kScanBN - 1) / kScanBN, ctx.sm_count(), &upq_s, &tpu_s);
-    nunits_s = qtiles * static_cast<uint64_t>(upq_s);
+  if (seeded) m = SeedKeep(cpre, op.samples[0].stride);
+  for (int lv = 0; lv < levels; ++lv) {
+    ChooseUnits(qtiles, (op.samples[lv].rows + kScanBN - 1) / kScanBN, ctx.sm_count(), &upq_s[lv], &tpu_s[lv]);
+    nunits_s = std::max(nunits_s, qtiles * static_cast<uint64_t>(upq_s[lv]));
   }
   const uint64_t lists = std::max(nunits, nunits_s) * wgs * kScanBM;
   VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCand, lists * kScanCap * sizeof(uint2), &cand));
@@ -408,23 +426,25 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   sa.qtau = static_cast<uint32_t*>(qtau);
   sa.status = ctx.status_word();
   if (top) ctx.Mark(1);
-  if (seeded) {
+  for (int lv = levels - 1; lv >= 0; --lv) {
+    const ScanOperands::Sample& smp = op.samples[lv];
+    const uint64_t nu = qtiles * static_cast<uint64_t>(upq_s[lv]);
     ScanArgs ss = sa;
-    ss.nrows = static_cast<int>(op.sample_rows);
+    ss.nrows = static_cast<int>(smp.rows);
     ss.keep = m;
     // The sample's lists compact early: cheap 128-slot compactions tighten its bounds sooner.
     ss.compact_at = m < 64 ? 96 : 0;
-    ss.units_per_qtile = upq_s;
-    ss.rows_per_unit = tpu_s * kScanBN;
-    ss.nunits = static_cast<int>(nunits_s);
-    ss.rowterm = op.sample_rowterm;
+    ss.units_per_qtile = upq_s[lv];
+    ss.rows_per_unit = tpu_s[lv] * kScanBN;
+    ss.nunits = static_cast<int>(nu);
+    ss.rowterm = smp.rowterm;
     ss.counters = nullptr;
-    const int grid_s = static_cast<int>(std::min<uint64_t>(nunits_s, static_cast<uint64_t>(ctx.sm_count())));
-    VDBGPU_CUDA(LaunchScan(amap, op.sample_map, ss, grid_s, ctx.stream()));
+    const int grid_s = static_cast<int>(std::min<uint64_t>(nu, static_cast<uint64_t>(ctx.sm_count())));
+    VDBGPU_CUDA(LaunchScan(amap, smp.map, ss, grid_s, ctx.stream()));
     SeedArgs sd{};
     sd.nq = static_cast<int>(nq);
     sd.m = m;
-    sd.units_per_qtile = upq_s;
+    sd.units_per_qtile = upq_s[lv];
     sd.wgs = static_cast<int>(wgs);
     sd.cand = static_cast<const uint2*>(cand);
     sd.cand_count = static_cast<const int*>(cnt);

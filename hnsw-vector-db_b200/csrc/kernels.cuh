@@ -37,7 +37,8 @@ cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream);
 
 // Seed of a scan's per-query bound: the m-th smallest key (ordered) among the candidate lists
 // a scan of a row sample left for the query (units_per_qtile x wgs lists of the FinalizeArgs
-// layout), written to qtau_out[q]; 0xFFFFFFFF when the lists hold fewer than m keys.
+// layout), written to qtau_out[q], which holds that sample scan's own bound on entry;
+// 0xFFFFFFFF when fewer than m keys lie below that bound.
 struct SeedArgs {
   int nq;
   int m;

@@ -276,16 +276,21 @@ struct ScanOperands {
   const float* vmin = nullptr;
   const float* scale = nullptr;
   CUtensorMap b_map;
-  // Seeding sample (index_flat.cc): every sample_stride-th operand row through sample_map, with
-  // its row terms in sample_rowterm when keys have one. sample_stride 0 = no sample.
-  uint32_t sample_stride = 0;
-  uint64_t sample_rows = 0;
-  const float* sample_rowterm = nullptr;
-  CUtensorMap sample_map;
+  // Seeding samples (index_flat.cc): level i maps every stride-th operand row through `map`, with
+  // its row terms in `rowterm` when keys have one; level 1, when present, samples level 0's
+  // stride 16 times more coarsely. nsamples 0 = no seeding.
+  struct Sample {
+    uint32_t stride = 0;
+    uint64_t rows = 0;
+    const float* rowterm = nullptr;
+    CUtensorMap map;
+  };
+  Sample samples[2];
+  int nsamples = 0;
 };
-// Attaches the seeding sample to `op` (after b_map / rowterm are set). rowterm_s receives the
-// sampled row terms. Small operands (and VDB_SCAN_SAMPLE=0) get none.
-Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer* rowterm_s);
+// Attaches the seeding samples to `op` (after b_map / rowterm are set). rowterm_s[0..1] receive
+// the sampled row terms. Small operands (and VDB_SCAN_SAMPLE=0) get none.
+Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer (&rowterm_s)[2]);
 Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
                   const SearchBatch& b, int cpre, int depth);
 

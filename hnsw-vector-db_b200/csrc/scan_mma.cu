@@ -373,10 +373,11 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
         compact_lanes(compact_at);
       };
 
-      // Per tile: pass 1 reads the 8 chunks back to back and keeps each chunk's best score
+      // Per tile: pass 1 reads the warp's chunks back to back and keeps each chunk's best score
       // (no branches); one vote per chunk marks the chunks where some query of the warp has a
       // hit; pass 2 reloads only those chunks from TMEM (the accumulator stays put until
-      // acc_empty) and appends their hits.
+      // acc_empty) and appends their hits. (Keeping a warp's 4 chunks of a two-warpgroup tile in
+      // registers instead spills at the 168 registers such a CTA allows, and is slower.)
       for (int row0 = r0; row0 < r1; row0 += kScanBN, ++tcount) {
         const int accb = static_cast<int>(tcount & 1u);
         // The shared threshold is read now and applied after pass 1 (hides latency).
@@ -390,47 +391,51 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
         const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                 static_cast<uint32_t>(accb * kScanBN + col0);
         const int c_base = row0 + col0;
-        uint32_t va[32], vb[32];
-        float cbest[kChunks];
-        __syncwarp();
-        tmem_ld_32x32b_x32(t_addr, va);
-        tmem_ld_wait_regs(va);
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ch += 2) {
-          __syncwarp();
-          tmem_ld_32x32b_x32(t_addr + (ch + 1) * 32, vb);  // in flight while va is scored
-          scores(va, c_base + ch * 32);
-          cbest[ch] = best32(va);
-          tmem_ld_wait_regs(vb);
-          if (ch + 2 < kChunks) {
-            __syncwarp();
-            tmem_ld_32x32b_x32(t_addr + (ch + 2) * 32, va);
+        auto vote = [&](const float (&cbest)[kChunks]) {
+          if (g != 0xFFFFFFFFu) {
+            tau = fminf(tau, key_float(g));
+            tau_acc = tau * qs_inv;
           }
-          scores(vb, c_base + (ch + 1) * 32);
-          cbest[ch + 1] = best32(vb);
-          if (ch + 2 < kChunks) tmem_ld_wait_regs(va);
-        }
-        if (g != 0xFFFFFFFFu) {
-          tau = fminf(tau, key_float(g));
-          tau_acc = tau * qs_inv;
-        }
-        uint32_t hits = 0;
-        {
           const float bound = kMin ? tau : tau_acc;
+          uint32_t hits = 0;
 #pragma unroll
           for (int ch = 0; ch < kChunks; ++ch)
             if (__any_sync(0xFFFFFFFFu, kMin ? (cbest[ch] < bound) : (cbest[ch] > bound))) hits |= 1u << ch;
-        }
-        n_chunks += kChunks;
-        n_trig += __popc(hits);
-        while (hits != 0u) {
-          const int ch = __ffs(hits) - 1;
-          hits &= hits - 1u;
+          n_chunks += kChunks;
+          n_trig += __popc(hits);
+          return hits;
+        };
+        {
+          uint32_t va[32], vb[32];
+          float cbest[kChunks];
           __syncwarp();
-          tmem_ld_32x32b_x32(t_addr + ch * 32, va);
+          tmem_ld_32x32b_x32(t_addr, va);
           tmem_ld_wait_regs(va);
-          scores(va, c_base + ch * 32);
-          extract(va, c_base + ch * 32);
+#pragma unroll
+          for (int ch = 0; ch < kChunks; ch += 2) {
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_addr + (ch + 1) * 32, vb);  // in flight while va is scored
+            scores(va, c_base + ch * 32);
+            cbest[ch] = best32(va);
+            tmem_ld_wait_regs(vb);
+            if (ch + 2 < kChunks) {
+              __syncwarp();
+              tmem_ld_32x32b_x32(t_addr + (ch + 2) * 32, va);
+            }
+            scores(vb, c_base + (ch + 1) * 32);
+            cbest[ch + 1] = best32(vb);
+            if (ch + 2 < kChunks) tmem_ld_wait_regs(va);
+          }
+          uint32_t hits = vote(cbest);
+          while (hits != 0u) {
+            const int ch = __ffs(hits) - 1;
+            hits &= hits - 1u;
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_addr + ch * 32, va);
+            tmem_ld_wait_regs(va);
+            scores(va, c_base + ch * 32);
+            extract(va, c_base + ch * 32);
+          }
         }
         tc_fence_before();
         mbar_arrive(&bars->acc_empty[accb]);

@@ -251,29 +251,68 @@ __global__ void __launch_bounds__(kFinWarps * 32)
 
 // ------------------------------------------------------------------ seeded scans
 
-// One warp per query: the m-th smallest ordered key over the query's lists, by a bitwise search
-// from the top bit (the largest v with fewer than m keys below it). Fewer than m keys in all
-// leaves every bit set: no bound.
-__global__ void __launch_bounds__(128) scan_seed_kernel(const SeedArgs a) {
-  const int q = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
+// One warp per query: the m-th smallest ordered key over the query's lists. Keys at or above the
+// bound the pass itself left in qtau_out[q] cannot be among the m smallest (a slice that compacted
+// kept m keys below it; without compactions every list holds all keys below it), so only keys
+// below it are gathered, once, into shared memory, and searched bit by bit from the top (the
+// largest v with fewer than m keys below it). Fewer than m keys below the bound: no estimate.
+constexpr int kSeedWarps = 4;
+constexpr int kSeedCap = 1024;
+
+__global__ void __launch_bounds__(kSeedWarps * 32) scan_seed_kernel(const SeedArgs a) {
+  __shared__ uint32_t keys_s[kSeedWarps][kSeedCap];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = static_cast<int>(blockIdx.x) * kSeedWarps + warp;
   if (q >= a.nq) return;
   const size_t qtiles = (static_cast<size_t>(a.nq) + kScanBM - 1) / kScanBM;
   const int qtile = q / kScanBM, row_in_tile = q % kScanBM;
   const int lists = a.units_per_qtile * a.wgs;
-  uint32_t ans = 0;
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = ans | (1u << bit);
-    int c = 0;
-    for (int p = 0; p < lists; ++p) {
-      const size_t unit = static_cast<size_t>(p / a.wgs) * qtiles + qtile;
-      const size_t slot = (unit * a.wgs + (p % a.wgs)) * kScanBM + row_in_tile;
-      const int n = a.cand_count[slot];
-      const uint2* b = a.cand + slot * kScanCap;
-      for (int e = lane; e < n; e += 32) c += float_key(__uint_as_float(b[e].x)) < cand ? 1 : 0;
+  const uint32_t thr = a.qtau_out[q];
+  const uint32_t lt = (1u << lane) - 1u;
+  uint32_t* ks = keys_s[warp];
+  auto list_of = [&](int p, int* n) {
+    const size_t unit = static_cast<size_t>(p / a.wgs) * qtiles + qtile;
+    const size_t slot = (unit * a.wgs + (p % a.wgs)) * kScanBM + row_in_tile;
+    *n = a.cand_count[slot];
+    return a.cand + slot * kScanCap;
+  };
+  int n = 0;
+  for (int p = 0; p < lists; ++p) {
+    int cnt;
+    const uint2* b = list_of(p, &cnt);
+    for (int e0 = 0; e0 < cnt; e0 += 32) {
+      const int e = e0 + lane;
+      uint32_t key = 0xFFFFFFFFu;
+      if (e < cnt) key = float_key(__uint_as_float(b[e].x));
+      const bool pass = e < cnt && key < thr;
+      const uint32_t mk = __ballot_sync(0xFFFFFFFFu, pass);
+      const int pos = n + __popc(mk & lt);
+      if (pass && pos < kSeedCap) ks[pos] = key;
+      n += __popc(mk);
     }
-    c = __reduce_add_sync(0xFFFFFFFFu, c);
-    if (c < a.m) ans = cand;
+  }
+  __syncwarp();
+  uint32_t ans = 0xFFFFFFFFu;
+  if (n >= a.m) {
+    ans = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = ans | (1u << bit);
+      int c = 0;
+      if (n <= kSeedCap) {
+        for (int i = lane; i < n; i += 32) c += ks[i] < cand ? 1 : 0;
+      } else {  // rare: too many keys below the bound for shared memory
+        for (int p = 0; p < lists; ++p) {
+          int cnt;
+          const uint2* b = list_of(p, &cnt);
+          for (int e = lane; e < cnt; e += 32) {
+            const uint32_t key = float_key(__uint_as_float(b[e].x));
+            c += (key < thr && key < cand) ? 1 : 0;
+          }
+        }
+      }
+      c = __reduce_add_sync(0xFFFFFFFFu, c);
+      if (c < a.m) ans = cand;
+    }
   }
   if (lane == 0) a.qtau_out[q] = ans;
 }
@@ -452,8 +491,8 @@ cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream) {
 
 cudaError_t LaunchScanSeed(const SeedArgs& a, cudaStream_t stream) {
   if (a.nq <= 0) return cudaSuccess;
-  const int blocks = (a.nq + 3) / 4;
-  scan_seed_kernel<<<blocks, 128, 0, stream>>>(a);
+  const int blocks = (a.nq + kSeedWarps - 1) / kSeedWarps;
+  scan_seed_kernel<<<blocks, kSeedWarps * 32, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

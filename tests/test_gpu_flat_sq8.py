@@ -151,12 +151,14 @@ def test_seeded_scan_is_exact(ctx, monkeypatch, keep):
     idx.free()
 
 
-def test_seeded_sq8_scan_with_fallbacks(ctx, monkeypatch):
-    """The seeded SQ8 scan (cosine, C = 128) with part of the batch rescanned: same ids and
-    distances as the unseeded scan."""
+@pytest.mark.parametrize("levels", ["1", "2"])
+def test_seeded_sq8_scan_with_fallbacks(ctx, monkeypatch, levels):
+    """The seeded SQ8 scan (cosine, C = 128; 300k rows, one or two sample levels) with part of
+    the batch rescanned: same ids and distances as the unseeded scan."""
     import vdb_b200
     from vdb_b200 import synth
-    base, qs = synth.sq8_cosine(200_000, 5000, dim=128, seed=12)
+    monkeypatch.setenv("VDB_SCAN_SAMPLE_LEVELS", levels)
+    base, qs = synth.sq8_cosine(300_000, 3400, dim=128, seed=12)
     idx = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
     monkeypatch.setenv("VDB_SCAN_SEED_KEEP", "15")
     ctx.set_timing(True)
