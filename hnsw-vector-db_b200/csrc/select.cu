@@ -40,14 +40,38 @@ __device__ void sort_into_smem(uint64_t* s, int n) {
   __syncwarp();
 }
 
-// Sorts s[0..n) (n <= 1024) ascending in place, padding to the sort size with kNoNeighbor.
+// Sorts s[0..n) (n <= 256) ascending in place, padding to the sort size with kNoNeighbor.
 __device__ void sort_small(uint64_t* s, int n) {
   if (n <= 32) sort_into_smem<1>(s, n);
   else if (n <= 64) sort_into_smem<2>(s, n);
   else if (n <= 128) sort_into_smem<4>(s, n);
-  else if (n <= 256) sort_into_smem<8>(s, n);
-  else if (n <= 512) sort_into_smem<16>(s, n);
-  else sort_into_smem<32>(s, n);
+  else sort_into_smem<8>(s, n);
+}
+
+// Keeps the c smallest of the n distinct packed keys s[0..n) (c < n <= kMaxSurvivors) in
+// s[0..c), unordered: the c-th smallest by a bitwise search from the top bit, then a stable
+// in-place compaction of the keys at or below it.
+__device__ void keep_smallest(uint64_t* s, int n, int c) {
+  const int lane = threadIdx.x & 31;
+  uint64_t ans = 0;
+  for (int bit = 63; bit >= 0; --bit) {
+    const uint64_t cand = ans | (1ull << bit);
+    int cnt = 0;
+    for (int i = lane; i < n; i += 32) cnt += s[i] < cand ? 1 : 0;
+    cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+    if (cnt < c) ans = cand;
+  }
+  const uint32_t lt = (1u << lane) - 1u;
+  int w = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const uint64_t x = i < n ? s[i] : kNoNeighbor;
+    const bool keep = i < n && x <= ans;
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
+    if (keep) s[w + __popc(m & lt)] = x;  // every read of this round precedes the ballot
+    w += __popc(m);
+  }
+  __syncwarp();
 }
 
 // Candidate slot of (query tile, list, query row). A query has `wgs` lists per row slice (one
@@ -111,25 +135,43 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   const uint32_t thr = a.qtau[q];  // keep key < thr (ordered); 0xFFFFFFFF keeps all
   const uint32_t lt = (1u << lane) - 1u;
 
-  // 1. Gather the entries that can still be among the C best.
+  // 1. Gather the entries that can still be among the C best. All list counts come in one
+  // load (lane p: list p of each group of 32); the first 32 entries of four lists at a time are
+  // loaded before any of them is filed, so the loads overlap.
   int nsurv = 0;
-  for (int p = 0; p < a.wgs * a.units_per_qtile; ++p) {
-    const size_t slot = unit_slot(a, qtile, p, row_in_tile);
-    const int n = a.cand_count[slot];
-    const uint2* b = a.cand + slot * kScanCap;
-    for (int e0 = 0; e0 < n; e0 += 32) {
-      const int e = e0 + lane;
-      uint2 v = make_uint2(0, 0);
-      bool pass = false;
-      if (e < n) {
-        v = b[e];
-        pass = float_key(__uint_as_float(v.x)) < thr;
+  const int lists = a.wgs * a.units_per_qtile;
+  auto file = [&](uint2 v, bool valid) {
+    const bool pass = valid && float_key(__uint_as_float(v.x)) < thr;
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
+    const int pos = nsurv + __popc(m & lt);
+    if (pass && pos < kMaxSurvivors)
+      surv[pos] = (static_cast<uint64_t>(float_key(__uint_as_float(v.x))) << 32) | v.y;
+    nsurv += __popc(m);
+  };
+  for (int p0 = 0; p0 < lists; p0 += 32) {
+    const int np = lists - p0 < 32 ? lists - p0 : 32;
+    const int my_cnt = lane < np ? a.cand_count[unit_slot(a, qtile, p0 + lane, row_in_tile)] : 0;
+    for (int j0 = 0; j0 < np; j0 += 4) {
+      uint2 v[4];
+      int n[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        n[u] = j0 + u < np ? __shfl_sync(0xFFFFFFFFu, my_cnt, j0 + u) : 0;
+        v[u] = make_uint2(0, 0);
+        if (lane < n[u]) v[u] = a.cand[unit_slot(a, qtile, p0 + j0 + u, row_in_tile) * kScanCap + lane];
       }
-      const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
-      const int pos = nsurv + __popc(m & lt);
-      if (pass && pos < kMaxSurvivors)
-        surv[pos] = (static_cast<uint64_t>(float_key(__uint_as_float(v.x))) << 32) | v.y;
-      nsurv += __popc(m);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (n[u] == 0) continue;
+        file(v[u], lane < n[u]);
+        if (n[u] > 32) {
+          const uint2* b = a.cand + unit_slot(a, qtile, p0 + j0 + u, row_in_tile) * kScanCap;
+          for (int e0 = 32; e0 < n[u]; e0 += 32) {
+            const int e = e0 + lane;
+            file(e < n[u] ? b[e] : make_uint2(0, 0), e < n[u]);
+          }
+        }
+      }
     }
   }
   __syncwarp();
@@ -141,8 +183,9 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   }
   int ncand;
   if (nsurv <= kMaxSurvivors) {
-    sort_small(surv, nsurv);
     ncand = nsurv < a.cpre ? nsurv : a.cpre;
+    if (nsurv > a.cpre) keep_smallest(surv, nsurv, a.cpre);
+    sort_small(surv, ncand);
   } else {
     // Rare: select the cpre-th key over all entries, then gather exactly those <= it.
     const uint64_t kth = global_kth(a, qtile, row_in_tile, thr, a.cpre);
