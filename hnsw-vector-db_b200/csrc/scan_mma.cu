@@ -406,26 +406,23 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
           return hits;
         };
         {
-          uint32_t va[32], vb[32];
+          // Pass 1 reads two chunks per tcgen05.ld (64 columns): half the TMEM round trips of
+          // single-chunk loads, in the same registers as two of them.
+          uint32_t v2[64];
           float cbest[kChunks];
-          __syncwarp();
-          tmem_ld_32x32b_x32(t_addr, va);
-          tmem_ld_wait_regs(va);
 #pragma unroll
           for (int ch = 0; ch < kChunks; ch += 2) {
             __syncwarp();
-            tmem_ld_32x32b_x32(t_addr + (ch + 1) * 32, vb);  // in flight while va is scored
+            tmem_ld_32x32b_x64(t_addr + ch * 32, v2);
+            tmem_ld_wait_regs(v2);
+            uint32_t (&va)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v2[0]);
+            uint32_t (&vb)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v2[32]);
             scores(va, c_base + ch * 32);
             cbest[ch] = best32(va);
-            tmem_ld_wait_regs(vb);
-            if (ch + 2 < kChunks) {
-              __syncwarp();
-              tmem_ld_32x32b_x32(t_addr + (ch + 2) * 32, va);
-            }
             scores(vb, c_base + (ch + 1) * 32);
             cbest[ch + 1] = best32(vb);
-            if (ch + 2 < kChunks) tmem_ld_wait_regs(va);
           }
+          uint32_t (&va)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v2[0]);
           uint32_t hits = vote(cbest);
           while (hits != 0u) {
             const int ch = __ffs(hits) - 1;
