@@ -425,7 +425,6 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   sa.cand_count = static_cast<int*>(cnt);
   sa.qtau = static_cast<uint32_t*>(qtau);
   sa.status = ctx.status_word();
-  if (top) ctx.Mark(1);
   for (int lv = levels - 1; lv >= 0; --lv) {
     const ScanOperands::Sample& smp = op.samples[lv];
     const uint64_t nu = qtiles * static_cast<uint64_t>(upq_s[lv]);
@@ -451,6 +450,9 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
     sd.qtau_out = static_cast<uint32_t*>(qtau);
     VDBGPU_CUDA(LaunchScanSeed(sd, ctx.stream()));
   }
+  // Stage marks: [0, 1) query preparation and the seeding sample scan, [1, 2) the scan, [2, 3)
+  // finalize.
+  if (top) ctx.Mark(1);
   const int grid = static_cast<int>(std::min<uint64_t>(nunits, static_cast<uint64_t>(ctx.sm_count())));
   VDBGPU_CUDA(LaunchScan(amap, op.b_map, sa, grid, ctx.stream()));
   if (top) ctx.Mark(2);

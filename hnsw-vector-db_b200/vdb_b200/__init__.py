@@ -201,7 +201,8 @@ class Context:
         self.check(lib().vdbgpu_set_timing(self._h, 1 if on else 0))
 
     def stage_times(self):
-        """Device ms of the last search: [prep, scan/walk, select+re-rank]."""
+        """Device ms of the last search: [prep (+ a seeded scan's sample pass), scan/walk,
+        select+re-rank]."""
         buf = (ctypes.c_float * 8)()
         n = lib().vdbgpu_stage_times(self._h, buf, 8)
         return [buf[i] for i in range(n)]

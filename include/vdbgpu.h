@@ -105,8 +105,9 @@ VDBGPU_API int vdbgpu_set_stream(vdbgpu_ctx* ctx, void* stream);
 VDBGPU_API int vdbgpu_set_timing(vdbgpu_ctx* ctx, int enable);
 
 /* Device milliseconds of the last search's stages (CUDA events on the launching stream):
- * out[0] = query preparation, out[1] = the dominant scan or walk kernel, out[2] = selection and
- * re-rank. Returns the number of stages written (0 when timing is off). */
+ * out[0] = query preparation (plus, for a seeded flat / SQ8 scan, the scan of the row sample
+ * and the seed), out[1] = the dominant scan or walk kernel, out[2] = selection and re-rank.
+ * Returns the number of stages written (0 when timing is off). */
 VDBGPU_API int vdbgpu_stage_times(vdbgpu_ctx* ctx, float* out, int cap);
 
 /* Work counters of the last search's dominant kernel, collected while timing is on. For the
