@@ -627,6 +627,29 @@ int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows, uint64_t n
   return VDBGPU_OK;
 }
 
+int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, uint64_t nrows, uint32_t dim,
+                       uint32_t padded_dim, uint32_t nlist, uint32_t pq_m, uint32_t max_train_ppc,
+                       uint64_t seed, void** out_file, size_t* out_bytes) {
+  if (ctx == nullptr || out_file == nullptr || out_bytes == nullptr || (nrows > 0 && rows == nullptr))
+    return VDBGPU_INVALID_ARGUMENT;
+  *out_file = nullptr;
+  *out_bytes = 0;
+  if (dim == 0 || dim > padded_dim || padded_dim % 16 != 0 || nrows > 0xFFFFFFFFull)
+    return Fail(ctx, Status(Status::kInvalidArgument, "bad geometry"));
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  std::string file;
+  Status s = vdbgpu::BuildIvfPqFile(*ctx->c, type, rows, nrows, dim, padded_dim, nlist, pq_m, max_train_ppc,
+                                    seed, &file);
+  if (!s.ok()) return Fail(ctx, s);
+  void* p = std::malloc(file.size());
+  if (p == nullptr) return Fail(ctx, Status(Status::kResourceExhausted, "host allocation"));
+  std::memcpy(p, file.data(), file.size());
+  *out_file = p;
+  *out_bytes = file.size();
+  return VDBGPU_OK;
+}
+
 void vdbgpu_buffer_free(void* p) { std::free(p); }
 
 int vdbgpu_filter_describe(const char* schema_json, const char* filter_json, char* out, size_t cap) {

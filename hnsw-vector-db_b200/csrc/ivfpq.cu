@@ -28,37 +28,6 @@ constexpr int kIvfWarps = 4;
 constexpr int kIvfCap = 512;  // candidates per warp buffer
 constexpr uint64_t kNone = ~0ull;
 
-__device__ __forceinline__ float dot_any(const float* a, const float* b, int d) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  int i = 0;
-  for (; i + 4 <= d; i += 4) {
-    s0 = __fadd_rn(s0, __fmul_rn(a[i], b[i]));
-    s1 = __fadd_rn(s1, __fmul_rn(a[i + 1], b[i + 1]));
-    s2 = __fadd_rn(s2, __fmul_rn(a[i + 2], b[i + 2]));
-    s3 = __fadd_rn(s3, __fmul_rn(a[i + 3], b[i + 3]));
-  }
-  for (; i < d; ++i) s0 = __fadd_rn(s0, __fmul_rn(a[i], b[i]));
-  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-}
-
-__device__ __forceinline__ float l2_any(const float* a, const float* b, int d) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  int i = 0;
-  for (; i + 4 <= d; i += 4) {
-    const float t0 = __fsub_rn(a[i], b[i]), t1 = __fsub_rn(a[i + 1], b[i + 1]);
-    const float t2 = __fsub_rn(a[i + 2], b[i + 2]), t3 = __fsub_rn(a[i + 3], b[i + 3]);
-    s0 = __fadd_rn(s0, __fmul_rn(t0, t0));
-    s1 = __fadd_rn(s1, __fmul_rn(t1, t1));
-    s2 = __fadd_rn(s2, __fmul_rn(t2, t2));
-    s3 = __fadd_rn(s3, __fmul_rn(t3, t3));
-  }
-  for (; i < d; ++i) {
-    const float t = __fsub_rn(a[i], b[i]);
-    s0 = __fadd_rn(s0, __fmul_rn(t, t));
-  }
-  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-}
-
 // ProductQuantizer::adc over one code (m bytes), four partial sums.
 __device__ __forceinline__ float adc(const float* table, const uint8_t* __restrict__ code, int m) {
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;

@@ -257,6 +257,10 @@ Status HnswSearchMulti(Context& ctx, const std::vector<const GpuIndex*>& indexes
 
 // An HNSW graph over rows (host or device, n x pd) built on the GPU, as a complete index file in
 // the reference's index.hnsw format (hnsw_build.cc).
+// IvfPqIndex / PqFlatIndex build + save on the GPU (ivfpq_build_host.cc): type kIndexIvfPq or
+// kIndexPqFlat; the reference's index file for the same rows and options.
+Status BuildIvfPqFile(Context& ctx, int type, const float* rows, uint64_t n, uint32_t dim, uint32_t pd,
+                      uint32_t nlist, uint32_t pq_m, uint32_t max_train_ppc, uint64_t seed, std::string* file);
 Status BuildHnswFile(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim, uint32_t pd, uint32_t M,
                      uint32_t kcand, uint64_t seed, std::string* file);
 

@@ -51,6 +51,40 @@ __device__ __forceinline__ void warp_sort(uint64_t (&x)[E]) {
 // Kernel-set summation orders of the reference (src/distance/cpu_features.cc:36-60).
 enum SumOrder : int { kOrderScalar = 0, kOrderAvx512 = 1, kOrderAvx2 = 2 };
 
+// DotAny / L2SqAny (src/distance/scalar.cc:43-73): four partial sums over any length, combined as
+// (s0 + s1) + (s2 + s3), without FMA.
+__device__ __forceinline__ float dot_any(const float* a, const float* b, int d) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= d; i += 4) {
+    s0 = __fadd_rn(s0, __fmul_rn(a[i], b[i]));
+    s1 = __fadd_rn(s1, __fmul_rn(a[i + 1], b[i + 1]));
+    s2 = __fadd_rn(s2, __fmul_rn(a[i + 2], b[i + 2]));
+    s3 = __fadd_rn(s3, __fmul_rn(a[i + 3], b[i + 3]));
+  }
+  for (; i < d; ++i) s0 = __fadd_rn(s0, __fmul_rn(a[i], b[i]));
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+__device__ __forceinline__ float l2_any(const float* a, const float* b, int d) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= d; i += 4) {
+    const float t0 = __fsub_rn(a[i], b[i]), t1 = __fsub_rn(a[i + 1], b[i + 1]);
+    const float t2 = __fsub_rn(a[i + 2], b[i + 2]), t3 = __fsub_rn(a[i + 3], b[i + 3]);
+    s0 = __fadd_rn(s0, __fmul_rn(t0, t0));
+    s1 = __fadd_rn(s1, __fmul_rn(t1, t1));
+    s2 = __fadd_rn(s2, __fmul_rn(t2, t2));
+    s3 = __fadd_rn(s3, __fmul_rn(t3, t3));
+  }
+  for (; i < d; ++i) {
+    const float t = __fsub_rn(a[i], b[i]);
+    s0 = __fadd_rn(s0, __fmul_rn(t, t));
+  }
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+
 // Exact fp32 distance between the warp's query and one row, summed in the order of the
 // reference kernel set (all lanes receive the result). q_s and x point to pd floats; q_s may be
 // shared memory. l2 selects squared L2, otherwise minus the dot product.

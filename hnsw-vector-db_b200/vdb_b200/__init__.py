@@ -114,6 +114,9 @@ _SIGNATURES = {
     "vdbgpu_hnsw_build": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                          ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, ctypes.POINTER(_P),
                                          ctypes.POINTER(ctypes.c_size_t)]),
+    "vdbgpu_ivfpq_build": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
+                                          ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64,
+                                          ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t)]),
     "vdbgpu_buffer_free": (None, [_P]),
     "vdbgpu_filter_describe": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                               ctypes.c_size_t]),
@@ -554,6 +557,24 @@ def build_hnsw(ctx: Context, metric, rows, dim: int, M: int = 16, candidates: in
     nb = ctypes.c_size_t(0)
     ctx.check(lib().vdbgpu_hnsw_build(ctx._h, m, _ptr(rows), n, int(dim), pd, int(M), int(candidates), int(seed),
                                       ctypes.byref(p), ctypes.byref(nb)))
+    try:
+        return ctypes.string_at(p, nb.value)
+    finally:
+        lib().vdbgpu_buffer_free(p)
+
+
+def build_ivfpq(ctx: Context, rows, dim: int, type="ivf_pq", nlist: int = 1024, pq_m: int = 16,
+                max_train_points_per_centroid: int = 256, seed: int = 42) -> bytes:
+    """The reference's IVF-PQ (or PQ-flat, type "pq_flat") index file for rows (n, padded_dim)
+    float32, numpy or a CUDA tensor, built on the GPU with the reference's seeded k-means replayed
+    exactly (IndexOptions nlist, pq_m, max_train_points_per_centroid, seed)."""
+    t = INDEX_TYPES[type] if isinstance(type, str) else int(type)
+    n, pd = int(rows.shape[0]), int(rows.shape[1])
+    p = _P()
+    nb = ctypes.c_size_t(0)
+    ctx.check(lib().vdbgpu_ivfpq_build(ctx._h, t, _ptr(rows), n, int(dim), pd, int(nlist), int(pq_m),
+                                       int(max_train_points_per_centroid), int(seed), ctypes.byref(p),
+                                       ctypes.byref(nb)))
     try:
         return ctypes.string_at(p, nb.value)
     finally:

@@ -309,7 +309,19 @@ VDBGPU_API int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows,
                                  uint32_t dim, uint32_t padded_dim, uint32_t M, uint32_t candidates,
                                  uint64_t seed, void** out_file, size_t* out_bytes);
 
-/* Releases a buffer returned by the library (vdbgpu_hnsw_build). */
+/* Index::build + save for IVF-PQ (type VDBGPU_INDEX_IVF_PQ) and PQ-flat (VDBGPU_INDEX_PQ_FLAT) on
+ * the GPU (IvfPqIndex::build, src/index/quant/ivf_pq.cc:106-150; PqFlatIndex::build, :45-58):
+ * the reference's seeded k-means (kmeans.cc:55-174) replayed exactly (host RNG and sums, GPU
+ * nearest-centroid searches in the reference kernel set's summation order), so the returned
+ * file is the reference's own index file, byte for byte, for the same rows (nrows x padded_dim
+ * floats, host or device), nlist, pq_m, max_train_points_per_centroid and seed. Padded
+ * dimensions up to 256. *out_file is malloc'd; release it with vdbgpu_buffer_free. */
+VDBGPU_API int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, uint64_t nrows,
+                                  uint32_t dim, uint32_t padded_dim, uint32_t nlist, uint32_t pq_m,
+                                  uint32_t max_train_ppc, uint64_t seed, void** out_file,
+                                  size_t* out_bytes);
+
+/* Releases a buffer returned by the library (vdbgpu_hnsw_build, vdbgpu_ivfpq_build). */
 VDBGPU_API void vdbgpu_buffer_free(void* p);
 
 /* FilterExpr::Parse (src/meta/filter_parser.cc) against a schema (JSON, schema.cc:246-270),
