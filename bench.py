@@ -43,7 +43,7 @@ C4_WORKLOAD = ("config 4: sharded filtered multi-segment search, {segs} segments
 
 def parse():
     p = argparse.ArgumentParser()
-    p.add_argument("--workload", default="c1", choices=["c0", "c1", "c3", "c4"])
+    p.add_argument("--workload", default="c1", choices=["c0", "c1", "c2", "c3", "c4"])
     p.add_argument("--segments", type=int, default=C4_SEGMENTS)
     p.add_argument("--seg-rows", type=int, default=C4_SEG_ROWS)
     p.add_argument("--gpus", type=int, default=1)
@@ -700,8 +700,121 @@ def run_c0_c3(args):
     return 0
 
 
+# -------------------------------------------------------------------------------------- config 2
+
+C2_ROWS, C2_DIM, C2_NLIST, C2_M, C2_PPC, C2_NPROBE = 10_000_000, 96, 4096, 48, 122, 32
+C2_WORKLOAD = ("config 2: IVF-PQ L2 search, 10,000,000 x 96 rows (1,000-component mixture, centres U[-1,1]^96, "
+               "sigma 0.15), nlist 4096, PQ M=48 x 8 bits, trained by the reference's seeded k-means on a "
+               "499,712-row sample (122 points per centroid), replayed on the GPU (the reference's index file, "
+               "byte for byte), nprobe 32, re-rank 100, 10,000-query batches, k=10")
+
+
+def run_c2(args):
+    """Config 2 on one GPU (one segment: replicas only). The index is built by the GPU builder; the
+    reference loads the same file and is timed on the host cores over a query sample."""
+    import torch
+    import oracle
+    import vdb_b200
+    from vdb_b200 import synth
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    ctx = vdb_b200.Context(local)
+    stream = torch.cuda.current_stream()
+    sustained, burst, hbm, src = peaks()
+    nq = args.batch
+    rows = synth.mixture(C2_ROWS, C2_DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=0)
+    qs = synth.mixture(nq, C2_DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=1)
+    t = time.time()
+    data = vdb_b200.build_ivfpq(ctx, rows, C2_DIM, nlist=C2_NLIST, pq_m=C2_M,
+                                max_train_points_per_centroid=C2_PPC, seed=42)
+    build_s = time.time() - t
+    b_dev = torch.from_numpy(rows).cuda()
+    idx = vdb_b200.Index.load(ctx, data, "l2", b_dev, C2_DIM)
+    q_dev = torch.from_numpy(qs).cuda()
+    ids_dev = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    d_dev = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+
+    def step():
+        idx.search(q_dev, k=K, nprobe=C2_NPROBE, out=(ids_dev, d_dev))
+    ms, clk = _timed(step, args.steps, args.warmup, stream, local)
+    gpu_ids = ids_dev.cpu().numpy().view(np.uint32).copy()
+    # End to end through the C ABI from pinned host buffers.
+    q_host = torch.from_numpy(qs).pin_memory()
+    ids_host = torch.empty((nq, K), dtype=torch.int32).pin_memory()
+    d_host = torch.empty((nq, K), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        idx.search(q_host, k=K, nprobe=C2_NPROBE, out=(ids_host, d_host))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(e2e_steps):
+        idx.search(q_host, k=K, nprobe=C2_NPROBE, out=(ids_host, d_host))
+    torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    _, _, dc = idx.search(qs[:1000], k=K, nprobe=C2_NPROBE, stats=True)
+    # Algorithmic bytes per query: the codes and ids of the probed lists, one 1 KB table per
+    # subquantizer per list, and the re-ranked rows.
+    scanned = float(dc.mean()) - C2_NLIST - DEPTH
+    bytes_per_q = scanned * (C2_M + 4) + C2_NPROBE * C2_M * 1024 + DEPTH * C2_DIM * 4
+    achieved = bytes_per_q * nq / (ms / 1000.0) / 1e9
+    # Exact ground truth on the GPU (flat index over the same rows).
+    flat = vdb_b200.Index.create(ctx, "flat", "l2", b_dev, C2_DIM)
+    gt_ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    gt_d = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    flat.search(q_dev, k=K, out=(gt_ids, gt_d))
+    gt = gt_ids.cpu().numpy().view(np.uint32)
+    flat.free()
+    # The reference's own IvfPqIndex on the same file, all host threads, a bounded query sample.
+    ref = oracle.Ref()
+    rref = ref.load_index(data, oracle.L2, rows, C2_DIM, pq_m=C2_M)
+    rref.search(qs[:50], k=K, nprobe=C2_NPROBE)
+    t0 = time.perf_counter()
+    sample = 0
+    r_ids = []
+    while sample < nq and time.perf_counter() - t0 < args.cpu_seconds:
+        r, _, _ = rref.search(qs[sample:sample + 500], k=K, nprobe=C2_NPROBE)
+        r_ids.append(r)
+        sample += r.shape[0]
+    cpu_s = time.perf_counter() - t0
+    r_ids = np.concatenate(r_ids)
+    out = {"metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32 ADC tables, f32 re-rank", "data": "synthetic",
+           "config": {"workload": C2_WORKLOAD, "rows": C2_ROWS, "dim": C2_DIM, "batch": nq, "k": K,
+                      "nlist": C2_NLIST, "pq_m": C2_M, "nprobe": C2_NPROBE, "rerank": DEPTH,
+                      "l2": "inputs larger than L2: 520 MB of codes and ids + 3.8 GB rows"},
+           "roofline": {"bound": "hbm", "kernel": "ivfpq_kernel", "achieved": achieved, "peak": hbm,
+                        "unit": "GB/s", "frac": achieved / hbm, "peak_kind": f"{src} copy bandwidth",
+                        "traffic": None,
+                        "algorithmic": f"scanned x (m + 4) + nprobe x m x 1 KB + 100 x pd x 4 B per query, "
+                                       f"scanned = {scanned:.0f} codes (mean), over the whole step "
+                                       f"(coarse probe included)"},
+           "e2e": {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": nq * C2_DIM * 4,
+                   "d2h_bytes_per_step": nq * K * 8},
+           # per step: the coarse probe (a flat search over the 4096 centroids: prep, scan, finalize)
+           # and the list scan with its re-rank
+           "gpu_launches": 4 * args.steps,
+           "recall_at_10_vs_exact": _recall(gpu_ids, gt),
+           "identical_ids_vs_reference_same_index": float(np.mean(np.all(gpu_ids[:sample] == r_ids, axis=1))),
+           "cpu_baseline": {"value": sample / cpu_s, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",
+                            "sample": f"{sample} queries, the reference's IvfPqIndex on the same index file "
+                                      f"({cpu_model()}, kernel set {ref.kernel_set()})"},
+           "index_build_s_gpu": build_s, "index_bytes": len(data), "clocks": clk}
+    print(json.dumps(out), flush=True)
+    idx.free()
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "c2":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 2 times the reference inside the same "
+                                                                  "run (cpu_baseline)"}))
+            return 0
+        return run_c2(args)
     if args.workload in ("c0", "c3"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "configs 0 and 3 time the reference inside "

@@ -53,6 +53,27 @@ __device__ __forceinline__ float adc(const float* table, const uint8_t* __restri
   return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
 }
 
+// ProductQuantizer::adc over a code held in registers (m = 16 nv bytes), the same four partial
+// sums as adc.
+__device__ __forceinline__ float adc_regs(const float* table, const uint4 (&v)[4], int nv) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    if (t < nv) {
+      const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = (t * 4 + u) * 4;
+        s0 = __fadd_rn(s0, table[(j + 0) * 256 + (w[u] & 0xFFu)]);
+        s1 = __fadd_rn(s1, table[(j + 1) * 256 + ((w[u] >> 8) & 0xFFu)]);
+        s2 = __fadd_rn(s2, table[(j + 2) * 256 + ((w[u] >> 16) & 0xFFu)]);
+        s3 = __fadd_rn(s3, table[(j + 3) * 256 + (w[u] >> 24)]);
+      }
+    }
+  }
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
 // Keeps the `keep` smallest packed keys of buf[0..n) (n <= kIvfCap), sorted, at the front.
 __device__ int warp_keep_best(uint64_t* buf, int n, int keep) {
   const int lane = threadIdx.x & 31;
@@ -111,6 +132,8 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
   uint64_t dc = 0;
   const uint32_t lt = (1u << lane) - 1u;
   const int nprobe = a.mode == kPqFlat ? 1 : a.nprobe;
+  const int nv = m >> 4;
+  const bool vec_codes = (m & 15) == 0 && nv >= 1 && nv <= 4 && (reinterpret_cast<uintptr_t>(a.codes) & 15u) == 0;
   for (int pi = 0; pi < nprobe; ++pi) {
     uint32_t l = 0;
     float offset = 0.f;
@@ -146,17 +169,9 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
     const uint64_t e0 = a.mode == kPqFlat ? a.n : a.list_off[l + 1];
     dc += e0 - b0;
     uint64_t cur_bound = bound;
-    for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += kIvfWarps * 32) {
-      const uint64_t i = base + lane;
-      uint64_t key = kNone;
-      if (i < e0) {
-        const uint32_t id = a.mode == kPqFlat ? static_cast<uint32_t>(i) : __ldg(&a.ids[i]);
-        const bool ok = a.allow == nullptr || ((__ldg(&a.allow[id >> 5]) >> (id & 31)) & 1u);
-        if (ok) {
-          const float d = __fadd_rn(offset, adc(table, a.codes + i * m, m));
-          key = pack_neighbor(d, id);
-        }
-      }
+    // Appends a key below the bound to this warp's buffer; a full buffer is cut to its R best,
+    // whose R-th key becomes the warp's bound (and the shared inclusive bound).
+    auto file = [&](uint64_t key) {
       const bool pass = key < cur_bound;
       const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
       if (pm != 0u) {
@@ -171,6 +186,51 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
             if (lane == 0) atomicMin(reinterpret_cast<unsigned long long*>(&tau_shared), tau + 1);
           }
         }
+      }
+    };
+    const uint64_t span = static_cast<uint64_t>(kIvfWarps) * 32;
+    if (vec_codes) {
+      // Codes of 16 nv bytes in 16-byte loads, two groups of 32 rows per warp in flight.
+      for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += 2 * span) {
+        uint4 v[2][4];
+        uint32_t id[2];
+        bool in[2];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const uint64_t i = base + g * span + lane;
+          in[g] = i < e0;
+          id[g] = 0;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[g][t] = make_uint4(0u, 0u, 0u, 0u);
+          if (in[g]) {
+            id[g] = a.mode == kPqFlat ? static_cast<uint32_t>(i) : __ldg(&a.ids[i]);
+            const uint4* cp = reinterpret_cast<const uint4*>(a.codes + i * m);
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              if (t < nv) v[g][t] = __ldg(&cp[t]);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          uint64_t key = kNone;
+          if (in[g] && (a.allow == nullptr || ((__ldg(&a.allow[id[g] >> 5]) >> (id[g] & 31)) & 1u)))
+            key = pack_neighbor(__fadd_rn(offset, adc_regs(table, v[g], nv)), id[g]);
+          file(key);
+        }
+      }
+    } else {
+      for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += span) {
+        const uint64_t i = base + lane;
+        uint64_t key = kNone;
+        if (i < e0) {
+          const uint32_t id = a.mode == kPqFlat ? static_cast<uint32_t>(i) : __ldg(&a.ids[i]);
+          const bool ok = a.allow == nullptr || ((__ldg(&a.allow[id >> 5]) >> (id & 31)) & 1u);
+          if (ok) {
+            const float d = __fadd_rn(offset, adc(table, a.codes + i * m, m));
+            key = pack_neighbor(d, id);
+          }
+        }
+        file(key);
       }
     }
     __syncthreads();  // table is rebuilt for the next list
