@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--rows", type=int, default=N_ROWS)
     p.add_argument("--batch", type=int, default=NQ)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--c2-rows", type=int, default=10_000_000,
+                   help="config 2 rows (smaller only for profiling captures)")
     return p.parse_args()
 
 
@@ -724,7 +726,8 @@ def run_c2(args):
     stream = torch.cuda.current_stream()
     sustained, burst, hbm, src = peaks()
     nq = args.batch
-    rows = synth.mixture(C2_ROWS, C2_DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=0)
+    n_rows = args.c2_rows
+    rows = synth.mixture(n_rows, C2_DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=0)
     qs = synth.mixture(nq, C2_DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=1)
     t = time.time()
     data = vdb_b200.build_ivfpq(ctx, rows, C2_DIM, nlist=C2_NLIST, pq_m=C2_M,
@@ -782,7 +785,8 @@ def run_c2(args):
     out = {"metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32 ADC tables, f32 re-rank", "data": "synthetic",
-           "config": {"workload": C2_WORKLOAD, "rows": C2_ROWS, "dim": C2_DIM, "batch": nq, "k": K,
+           "config": {"workload": C2_WORKLOAD if n_rows == C2_ROWS else f"config 2 shape at {n_rows} rows",
+                      "rows": n_rows, "dim": C2_DIM, "batch": nq, "k": K,
                       "nlist": C2_NLIST, "pq_m": C2_M, "nprobe": C2_NPROBE, "rerank": DEPTH,
                       "l2": "inputs larger than L2: 520 MB of codes and ids + 3.8 GB rows"},
            "roofline": {"bound": "hbm", "kernel": "ivfpq_kernel", "achieved": achieved, "peak": hbm,

@@ -150,6 +150,9 @@ class IvfPqGpuIndex final : public GpuIndex {
     }
     if (IvfPqSmemBytes(a.pd, a.m, a.mode) > 227 * 1024)
       return Status(Status::kNotSupported, "PQ tables do not fit in shared memory");
+    void* cand;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsScratch2, IvfPqCandBytes(a.nq, a.k, a.depth), &cand));
+    a.cand = static_cast<uint64_t*>(cand);
     ctx.Mark(2);
     VDBGPU_CUDA(LaunchIvfPq(a, ctx.stream()));
     ctx.Mark(3);

@@ -1,4 +1,4 @@
-// IVF-PQ and PQ-flat ADC scan with re-rank (sm_100a): one CTA of four warps per query.
+// IVF-PQ and PQ-flat ADC scan with re-rank (sm_100a): one CTA per query.
 //
 // Follows IvfPqIndex::search (src/index/quant/ivf_pq.cc:169-222) and PqFlatIndex::search
 // (:59-76) float operation for float:
@@ -11,7 +11,8 @@
 //   * ADC: four partial sums over the m sub-quantisers (ProductQuantizer::adc, pq.h:36-47), then
 //     offset + adc;
 //   * TopK(R) by (dist, id) over all probed rows, then Rerank on fp32 rows (index.cc:89-95).
-// The four warps share the query's tables in shared memory and split each list's rows; each warp
+// The CTA's warps (eight, or four for re-rank depths above 128) share the query's tables in shared
+// memory and split each list's rows; each warp
 // keeps its own candidate buffer and threshold (exact: a warp's threshold is the R-th best of
 // the entries it has seen, and the tighter of the warps' thresholds is shared as an inclusive
 // bound), and the buffers are merged at the end.
@@ -24,8 +25,7 @@
 namespace vdbgpu {
 namespace {
 
-constexpr int kIvfWarps = 4;
-constexpr int kIvfCap = 512;  // candidates per warp buffer
+constexpr int kIvfCap = 512;  // candidates per warp buffer (global memory)
 constexpr uint64_t kNone = ~0ull;
 
 // ProductQuantizer::adc over one code (m bytes), four partial sums.
@@ -91,6 +91,7 @@ __device__ int warp_keep_best(uint64_t* buf, int n, int keep) {
   return n < keep ? n : keep;
 }
 
+template <int kIvfWarps>
 __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a) {
   extern __shared__ __align__(16) uint8_t ism[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -100,7 +101,9 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
   float* r_s = q_s + pd;                                      // pd (residual)
   float* table = r_s + pd;                                    // ts
   float* qtab = table + ts;                                   // ts (precomputed L2 only)
-  uint64_t* bufs = reinterpret_cast<uint64_t*>(qtab + (a.mode == kIvfPrecomputed ? ts : 0));
+  // Candidate buffers live in global memory (inserts are rare), so a CTA's shared memory is just
+  // the query's tables and two CTAs of eight warps fit on an SM.
+  uint64_t* bufs = a.cand + static_cast<size_t>(q) * kIvfWarps * kIvfCap;
   uint64_t* buf = bufs + warp * kIvfCap;
   __shared__ uint64_t tau_shared;
   __shared__ float offset_s;
@@ -147,7 +150,14 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
     if (a.mode == kIvfPrecomputed) {
       offset = a.probe_dist[static_cast<size_t>(q) * a.nprobe + pi];
       const float* t2 = a.term2 + static_cast<size_t>(l) * ts;
-      for (int i = threadIdx.x; i < ts; i += blockDim.x) table[i] = __fadd_rn(__ldg(&t2[i]), qtab[i]);
+      // 16-byte steps: ts = 256 m floats, and term2 / table / qtab start on 16-byte boundaries.
+      const float4* t24 = reinterpret_cast<const float4*>(t2);
+      const float4* qt4 = reinterpret_cast<const float4*>(qtab);
+      float4* tb4 = reinterpret_cast<float4*>(table);
+      for (int i = threadIdx.x; i < (ts >> 2); i += blockDim.x) {
+        const float4 x = __ldg(&t24[i]), y = qt4[i];
+        tb4[i] = make_float4(__fadd_rn(x.x, y.x), __fadd_rn(x.y, y.y), __fadd_rn(x.z, y.z), __fadd_rn(x.w, y.w));
+      }
     } else if (a.mode == kIvfResidual) {
       const float* c = a.coarse + static_cast<size_t>(l) * pd;
       for (int j = threadIdx.x; j < a.dim; j += blockDim.x) r_s[j] = __fsub_rn(q_s[j], c[j]);
@@ -241,7 +251,7 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
   __syncthreads();
   if (warp == 0) {
     // Gather the candidates of all warps into warp 0's buffer region after its own R entries
-    // (bufs has kIvfWarps * kIvfCap slots; R <= 256 so the total fits in 1024 <= kIvfWarps * kIvfCap).
+    // (kIvfWarps * R <= 1024 keys, the size of the sort below; IvfPqWarps picks the warps).
     uint64_t* all = bufs;  // reuse: compact all warps' lists to the front
     int total = count_s[0];
     for (int w = 1; w < kIvfWarps; ++w) {
@@ -346,16 +356,33 @@ __global__ void term2_kernel(const float* __restrict__ coarse, uint32_t nlist, i
 
 size_t IvfPqSmemBytes(int pd, int m, int mode) {
   const size_t ts = static_cast<size_t>(m) * 256;
-  return (2 * static_cast<size_t>(pd) + ts + (mode == kIvfPrecomputed ? ts : 0)) * 4 +
-         static_cast<size_t>(kIvfWarps) * kIvfCap * 8;
+  return (2 * static_cast<size_t>(pd) + ts + (mode == kIvfPrecomputed ? ts : 0)) * 4;
+}
+
+int IvfPqWarps(int k, int depth) {
+  // The final merge sorts every warp's R best at once (at most 1024 keys).
+  const int r = depth > k ? depth : k;
+  return 8 * r <= 1024 ? 8 : 4;
+}
+
+size_t IvfPqCandBytes(int nq, int k, int depth) {
+  return static_cast<size_t>(nq) * IvfPqWarps(k, depth) * kIvfCap * sizeof(uint64_t);
 }
 
 cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream) {
   const size_t smem = IvfPqSmemBytes(a.pd, a.m, a.mode);
-  cudaError_t e = cudaFuncSetAttribute(ivfpq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  ivfpq_kernel<<<a.nq, kIvfWarps * 32, smem, stream>>>(a);
+  if (a.cand == nullptr) return cudaErrorInvalidValue;
+  if (IvfPqWarps(a.k, a.depth) == 8) {
+    cudaError_t e = cudaFuncSetAttribute(ivfpq_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    ivfpq_kernel<8><<<a.nq, 8 * 32, smem, stream>>>(a);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(ivfpq_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    ivfpq_kernel<4><<<a.nq, 4 * 32, smem, stream>>>(a);
+  }
   return cudaGetLastError();
 }
 

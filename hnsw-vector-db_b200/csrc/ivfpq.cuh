@@ -34,10 +34,12 @@ struct IvfPqArgs {
   float* out_dist;
   uint32_t* out_row;
   uint64_t* out_dc;
+  uint64_t* cand;             // IvfPqCandBytes(nq, k, depth) of candidate buffers
   int* status;
 };
 
 size_t IvfPqSmemBytes(int pd, int m, int mode);
+size_t IvfPqCandBytes(int nq, int k, int depth);
 cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream);
 cudaError_t LaunchTerm2(const float* coarse, uint32_t nlist, int pd, const float* centroids, int m,
                         int ds, float* term2, cudaStream_t stream);
