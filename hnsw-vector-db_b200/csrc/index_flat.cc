@@ -4,7 +4,8 @@
 //
 // Seeded scans. On large batches over large operands (at least 1e9 query-row pairs, 64k rows) the
 // pipeline first scans a strided sample of the rows (every s-th row, s = 16 by default;
-// VDB_SCAN_SAMPLE sets s, 0 turns seeding off) keeping m candidates per query, and takes the m-th
+// VDB_SCAN_SAMPLE sets s, 0 turns seeding off), where each 32-row chunk offers only its best key,
+// keeping m candidates per query, and takes the m-th
 // smallest sample key as the query's starting bound for the full scan, with m chosen so that about
 // 2.25 C rows of the whole operand are expected below it. Every slice of the full scan then starts
 // from that bound instead of from nothing, so few 32 x 32 chunks hold a candidate and the lists
@@ -438,6 +439,7 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
     ss.nunits = static_cast<int>(nu);
     ss.rowterm = smp.rowterm;
     ss.counters = nullptr;
+    ss.chunk_best = 1;
     const int grid_s = static_cast<int>(std::min<uint64_t>(nu, static_cast<uint64_t>(ctx.sm_count())));
     VDBGPU_CUDA(LaunchScan(amap, smp.map, ss, grid_s, ctx.stream()));
     SeedArgs sd{};

@@ -7,7 +7,7 @@
 //
 // One persistent CTA per SM walks "units": a 128-query tile against a contiguous slice of rows.
 //   warp 0      TMA producer: loads the query tile once per unit (resident), then streams row
-//               k-blocks (256 rows x 64 fp16) through a 4-stage mbarrier ring.
+//               k-blocks (256 rows x 64 fp16) through an mbarrier ring of up to 6 stages.
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one thread issues
 //               tcgen05.mma (M=128, N=256, K=16) into alternating accumulators.
 //   warps 2..   epilogue: each thread owns one query (one TMEM lane) and reads its 256 columns in
@@ -17,6 +17,7 @@
 //               appended to the query's candidate buffer in global memory. A full buffer is
 //               compacted by the whole warp to its C best (by key, then row) and the C-th key
 //               becomes the new threshold, also published to every unit of the same query.
+// A seeding sample scan (chunk_best) appends only each chunk's best key instead.
 // Rows inside one unit arrive in increasing order, so a strict "key < threshold" test keeps
 // ties exactly as the reference's (dist, id) order does. Thresholds from other units are
 // applied as "key <= their C-th key", which can never drop a member of the global top C.
@@ -424,6 +425,24 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
           }
           uint32_t (&va)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v2[0]);
           uint32_t hits = vote(cbest);
+          if (a.chunk_best) {
+            // A seeding sample scan needs an estimate of the keep-th key only: each chunk's best
+            // key (a real row's) stands for the chunk, and nothing is read again.
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch) {
+              if ((hits >> ch) & 1u) {
+                const float sc = cbest[ch];
+                if (kMin ? (sc < tau) : (sc > tau_acc)) {
+                  const float key = kMin ? sc : qs * sc;
+                  buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c_base + ch * 32));
+                  ++count;
+                  ++n_ins;
+                }
+                compact_lanes(compact_at);
+              }
+            }
+            hits = 0u;
+          }
           while (hits != 0u) {
             const int ch = __ffs(hits) - 1;
             hits &= hits - 1u;
