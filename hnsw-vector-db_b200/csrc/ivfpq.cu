@@ -12,7 +12,8 @@
 //     offset + adc;
 //   * TopK(R) by (dist, id) over all probed rows, then Rerank on fp32 rows (index.cc:89-95).
 // The CTA's warps (eight, or four for re-rank depths above 128) share the query's tables in shared
-// memory and split each list's rows; each warp
+// memory and split each list's rows (codes of 16-byte multiples in software-pipelined 16-byte
+// loads); each warp
 // keeps its own candidate buffer and threshold (exact: a warp's threshold is the R-th best of
 // the entries it has seen, and the tighter of the warps' thresholds is shared as an inclusive
 // bound), and the buffers are merged at the end.
@@ -147,6 +148,28 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
         break;
       }
     }
+    const uint64_t b0 = a.mode == kPqFlat ? 0 : a.list_off[l];
+    const uint64_t e0 = a.mode == kPqFlat ? a.n : a.list_off[l + 1];
+    // Row i's id and code (16 nv bytes in 16-byte loads); rows past the list end read nothing.
+    auto load_row = [&](uint64_t i, uint4 (&v)[4], uint32_t& id, bool& in) {
+      in = i < e0;
+      id = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[t] = make_uint4(0u, 0u, 0u, 0u);
+      if (in) {
+        id = a.mode == kPqFlat ? static_cast<uint32_t>(i) : __ldg(&a.ids[i]);
+        const uint4* cp = reinterpret_cast<const uint4*>(a.codes + i * m);
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (t < nv) v[t] = __ldg(&cp[t]);
+      }
+    };
+    // The warp's first rows of the list are requested before the table is built, so their
+    // latency overlaps the build.
+    uint4 nxt_v[4];
+    uint32_t nxt_id = 0;
+    bool nxt_in = false;
+    if (vec_codes) load_row(b0 + static_cast<uint64_t>(warp) * 32 + lane, nxt_v, nxt_id, nxt_in);
     if (a.mode == kIvfPrecomputed) {
       offset = a.probe_dist[static_cast<size_t>(q) * a.nprobe + pi];
       const float* t2 = a.term2 + static_cast<size_t>(l) * ts;
@@ -175,8 +198,6 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
     // The tighter shared bound (another warp's R-th best, inclusive) also prunes this warp.
     const uint64_t tb = tau_shared;
     const uint64_t bound = tb < tau ? tb : tau;
-    const uint64_t b0 = a.mode == kPqFlat ? 0 : a.list_off[l];
-    const uint64_t e0 = a.mode == kPqFlat ? a.n : a.list_off[l + 1];
     dc += e0 - b0;
     uint64_t cur_bound = bound;
     // Appends a key below the bound to this warp's buffer; a full buffer is cut to its R best,
@@ -200,33 +221,19 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
     };
     const uint64_t span = static_cast<uint64_t>(kIvfWarps) * 32;
     if (vec_codes) {
-      // Codes of 16 nv bytes in 16-byte loads, two groups of 32 rows per warp in flight.
-      for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += 2 * span) {
-        uint4 v[2][4];
-        uint32_t id[2];
-        bool in[2];
+      // Software-pipelined: the warp's next 32 rows are requested before the current ones are
+      // scored.
+      for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += span) {
+        uint4 v[4];
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const uint64_t i = base + g * span + lane;
-          in[g] = i < e0;
-          id[g] = 0;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) v[g][t] = make_uint4(0u, 0u, 0u, 0u);
-          if (in[g]) {
-            id[g] = a.mode == kPqFlat ? static_cast<uint32_t>(i) : __ldg(&a.ids[i]);
-            const uint4* cp = reinterpret_cast<const uint4*>(a.codes + i * m);
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-              if (t < nv) v[g][t] = __ldg(&cp[t]);
-          }
-        }
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          uint64_t key = kNone;
-          if (in[g] && (a.allow == nullptr || ((__ldg(&a.allow[id[g] >> 5]) >> (id[g] & 31)) & 1u)))
-            key = pack_neighbor(__fadd_rn(offset, adc_regs(table, v[g], nv)), id[g]);
-          file(key);
-        }
+        for (int t = 0; t < 4; ++t) v[t] = nxt_v[t];
+        const uint32_t id = nxt_id;
+        const bool in = nxt_in;
+        load_row(base + span + lane, nxt_v, nxt_id, nxt_in);
+        uint64_t key = kNone;
+        if (in && (a.allow == nullptr || ((__ldg(&a.allow[id >> 5]) >> (id & 31)) & 1u)))
+          key = pack_neighbor(__fadd_rn(offset, adc_regs(table, v, nv)), id);
+        file(key);
       }
     } else {
       for (uint64_t base = b0 + static_cast<uint64_t>(warp) * 32; base < e0; base += span) {
