@@ -84,29 +84,87 @@ __device__ __forceinline__ size_t unit_slot(const FinalizeArgs& a, int qtile, in
   return (unit * a.wgs + (p % a.wgs)) * kScanBM + row_in_tile;
 }
 
-// The c-th smallest packed key (1-based) among entries passing `thr`, by bitwise search over
-// every entry of the query's buffers. Used only when more than kMaxSurvivors entries pass.
-__device__ uint64_t global_kth(const FinalizeArgs& a, int qtile, int row_in_tile, uint32_t thr,
-                               int c) {
-  uint64_t ans = 0;
-  for (int bit = 63; bit >= 0; --bit) {
-    const uint64_t cand = ans | (1ull << bit);
-    int cnt = 0;
-    for (int p = 0; p < a.wgs * a.units_per_qtile; ++p) {
+// The c-th smallest packed key (1-based) among the query's entries below `thr`, in four passes
+// over its lists: a radix select on the pre-rank key (8-bit digits, a per-warp histogram of the
+// keys that still match) finds the c-th key K and its rank r among the entries whose key is K;
+// only when r leaves some of those out does a 32-pass search on their rows follow. Reached when a query's lists hold more than
+// kMaxSurvivors entries below its bound (unseeded scans of few queries over many row slices).
+__device__ uint64_t global_kth_radix(const FinalizeArgs& a, int qtile, int row_in_tile, uint32_t thr, int c,
+                                     uint32_t* hist) {
+  const int lane = threadIdx.x & 31;
+  const int lists = a.wgs * a.units_per_qtile;
+  uint32_t prefix = 0, mask = 0, at_k = 0;
+  int r = c;  // rank (1-based) of the c-th key among the keys that match the prefix
+  for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll
+    for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0;
+    __syncwarp();
+    for (int p = 0; p < lists; ++p) {
       const size_t slot = unit_slot(a, qtile, p, row_in_tile);
       const int n = a.cand_count[slot];
-      const uint2* b = a.cand + slot * kScanCap;
-      for (int e = threadIdx.x & 31; e < n; e += 32) {
-        const uint2 v = b[e];
-        const uint32_t key = float_key(__uint_as_float(v.x));
-        const uint64_t pk = (static_cast<uint64_t>(key) << 32) | v.y;
-        cnt += (key < thr && pk < cand) ? 1 : 0;
+      const uint2* bp = a.cand + slot * kScanCap;
+      for (int e = lane; e < n; e += 32) {
+        const uint32_t key = float_key(__uint_as_float(bp[e].x));
+        if (key < thr && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+    }
+    __syncwarp();
+    uint32_t h[8], tot = 0;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      h[b] = hist[lane * 8 + b];
+      tot += h[b];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const uint32_t excl = incl - tot;
+    const uint32_t owner =
+        __ballot_sync(0xFFFFFFFFu, excl < static_cast<uint32_t>(r) && static_cast<uint32_t>(r) <= incl);
+    const int src = __ffs(owner) - 1;
+    uint32_t digit = 0, before = 0, cnt = 0;
+    if (lane == src) {
+      uint32_t run = excl;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        if (cnt == 0 && static_cast<uint32_t>(r) <= run + h[b]) {
+          digit = static_cast<uint32_t>(lane * 8 + b);
+          before = run;
+          cnt = h[b];
+        }
+        run += h[b];
+      }
+    }
+    digit = __shfl_sync(0xFFFFFFFFu, digit, src);
+    before = __shfl_sync(0xFFFFFFFFu, before, src);
+    at_k = __shfl_sync(0xFFFFFFFFu, cnt, src);
+    r -= static_cast<int>(before);
+    prefix |= digit << shift;
+    mask |= 255u << shift;
+    __syncwarp();
+  }
+  if (static_cast<uint32_t>(r) == at_k) return (static_cast<uint64_t>(prefix) << 32) | 0xFFFFFFFFull;
+  // Ties on the key K: the r-th smallest row among the entries whose key is K.
+  uint32_t ans = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = ans | (1u << bit);
+    int cnt = 0;
+    for (int p = 0; p < lists; ++p) {
+      const size_t slot = unit_slot(a, qtile, p, row_in_tile);
+      const int n = a.cand_count[slot];
+      const uint2* bp = a.cand + slot * kScanCap;
+      for (int e = lane; e < n; e += 32) {
+        const uint2 v = bp[e];
+        cnt += (float_key(__uint_as_float(v.x)) == prefix && v.y < cand) ? 1 : 0;
       }
     }
     cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
-    if (cnt < c) ans = cand;
+    if (cnt < r) ans = cand;
   }
-  return ans;
+  return (static_cast<uint64_t>(prefix) << 32) | ans;
 }
 
 __global__ void __launch_bounds__(kFinWarps * 32)
@@ -121,6 +179,9 @@ __global__ void __launch_bounds__(kFinWarps * 32)
                    warp * (pd * sizeof(float) + kMaxSurvivors * sizeof(uint64_t));
   float* q_s = reinterpret_cast<float*>(wbase);
   uint64_t* surv = reinterpret_cast<uint64_t*>(wbase + pd * sizeof(float));
+  // The overflow path's histogram borrows the survivors' last 1 KB: that path selects before it
+  // writes survivors, and then writes at most cpre <= 256 of them.
+  uint32_t* hist = reinterpret_cast<uint32_t*>(surv + kMaxSurvivors - 128);
   if (a.codes != nullptr) {
     for (int i = threadIdx.x; i < pd; i += blockDim.x) {
       vmin_s[i] = a.vmin[i];
@@ -188,7 +249,7 @@ __global__ void __launch_bounds__(kFinWarps * 32)
     sort_small(surv, ncand);
   } else {
     // Rare: select the cpre-th key over all entries, then gather exactly those <= it.
-    const uint64_t kth = global_kth(a, qtile, row_in_tile, thr, a.cpre);
+    const uint64_t kth = global_kth_radix(a, qtile, row_in_tile, thr, a.cpre, hist);
     int w = 0;
     for (int p = 0; p < a.wgs * a.units_per_qtile; ++p) {
       const size_t slot = unit_slot(a, qtile, p, row_in_tile);

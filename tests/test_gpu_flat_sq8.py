@@ -175,3 +175,28 @@ def test_seeded_sq8_scan_with_fallbacks(ctx, monkeypatch, levels):
         np.testing.assert_array_equal(a, b)
     plain.free()
     idx.free()
+
+
+def test_small_batches_over_many_row_slices(ctx):
+    """A few queries over a large index spread over many row slices (unseeded), so a query's
+    candidate lists hold more entries than finalize keeps in shared memory and the C best are
+    selected over the lists in global memory, integer rows making ties on the pre-rank key at the
+    cut. Exact against the oracle (flat), against the reference's SQ8 arithmetic (SQ8)."""
+    import vdb_b200
+    from vdb_b200 import synth
+    base, qs = synth.flat_int(120_000, 40, dim=128, seed=13)
+    idx = vdb_b200.Index.create(ctx, "flat", "l2", base, 128)
+    orc = oracle.Oracle()
+    for nq in (1, 7, 40):
+        ids, d = idx.search(qs[:nq], k=10)
+        oi, od = orc.flat_search(0, base, qs[:nq], 10)
+        np.testing.assert_array_equal(ids, oi)
+        np.testing.assert_array_equal(d, od)
+    idx.free()
+    base, qs = synth.sq8_cosine(200_000, 20, dim=128, seed=14)
+    idx = vdb_b200.Index.create(ctx, "sq8_flat", "cosine", base, 128)
+    ids, d = idx.search(qs, k=10, rerank=100)
+    vmin, scale, codes = idx.sq8_export()
+    oi, od = orc.sq8_scan_search(2, base, codes, vmin, scale, qs, k=10, depth=100)
+    assert_same_neighbors(ids, d, oi, od)
+    idx.free()
