@@ -147,6 +147,12 @@ class IvfPqGpuIndex final : public GpuIndex {
       VDBGPU_RETURN_IF_ERROR(coarse_index_->Search(ctx, cb));
       a.probe_ids = static_cast<const uint32_t*>(pid);
       a.probe_dist = static_cast<const float*>(pdist);
+      void* ord;
+      VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsScratch3, (b.nq + nlist_ + 1) * sizeof(uint32_t), &ord));
+      uint32_t* counts = static_cast<uint32_t*>(ord) + b.nq;
+      VDBGPU_CUDA(LaunchProbeOrder(a.probe_ids, a.nq, a.nprobe, static_cast<uint32_t>(nlist_), counts,
+                                   static_cast<uint32_t*>(ord), ctx.stream()));
+      a.qorder = static_cast<const uint32_t*>(ord);
     }
     if (IvfPqSmemBytes(a.pd, a.m, a.mode) > 227 * 1024)
       return Status(Status::kNotSupported, "PQ tables do not fit in shared memory");

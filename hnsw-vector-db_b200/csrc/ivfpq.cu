@@ -96,7 +96,7 @@ template <int kIvfWarps>
 __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a) {
   extern __shared__ __align__(16) uint8_t ism[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = blockIdx.x;
+  const int q = a.qorder != nullptr ? static_cast<int>(a.qorder[blockIdx.x]) : static_cast<int>(blockIdx.x);
   const int m = a.m, ds = a.dsub, pd = a.pd, ts = m * 256;
   float* q_s = reinterpret_cast<float*>(ism);                 // pd
   float* r_s = q_s + pd;                                      // pd (residual)
@@ -359,6 +359,49 @@ __global__ void term2_kernel(const float* __restrict__ coarse, uint32_t nlist, i
   }
 }
 
+// Launch order of the list scan: the queries grouped by their nearest probed list (a counting
+// sort), so CTAs that run at the same time share lists and find their codes and term2 rows in L2.
+// Each query's result does not depend on when its CTA runs. Bucket nlist takes out-of-range ids
+// (the scan reports them).
+__global__ void probe_count_kernel(const uint32_t* probe_ids, int nq, int nprobe, uint32_t nlist,
+                                   uint32_t* counts) {
+  const int q = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (q >= nq) return;
+  const uint32_t l = probe_ids[static_cast<size_t>(q) * nprobe];
+  atomicAdd(&counts[l < nlist ? l : nlist], 1u);
+}
+
+// In-place exclusive scan of counts[0..n) by one block of 1024 threads (contiguous chunks).
+__global__ void __launch_bounds__(1024) probe_scan_kernel(uint32_t* counts, uint32_t n) {
+  __shared__ uint32_t part[1024];
+  const uint32_t per = (n + 1023) / 1024;
+  const uint32_t b = threadIdx.x * per, e = b + per < n ? b + per : n;
+  uint32_t sum = 0;
+  for (uint32_t i = b; i < e; ++i) sum += counts[i];
+  part[threadIdx.x] = sum;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const uint32_t v = threadIdx.x >= static_cast<unsigned>(o) ? part[threadIdx.x - o] : 0u;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  uint32_t run = part[threadIdx.x] - sum;
+  for (uint32_t i = b; i < e; ++i) {
+    const uint32_t c = counts[i];
+    counts[i] = run;
+    run += c;
+  }
+}
+
+__global__ void probe_place_kernel(const uint32_t* probe_ids, int nq, int nprobe, uint32_t nlist,
+                                   uint32_t* offsets, uint32_t* order) {
+  const int q = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (q >= nq) return;
+  const uint32_t l = probe_ids[static_cast<size_t>(q) * nprobe];
+  order[atomicAdd(&offsets[l < nlist ? l : nlist], 1u)] = static_cast<uint32_t>(q);
+}
+
 }  // namespace
 
 size_t IvfPqSmemBytes(int pd, int m, int mode) {
@@ -374,6 +417,18 @@ int IvfPqWarps(int k, int depth) {
 
 size_t IvfPqCandBytes(int nq, int k, int depth) {
   return static_cast<size_t>(nq) * IvfPqWarps(k, depth) * kIvfCap * sizeof(uint64_t);
+}
+
+cudaError_t LaunchProbeOrder(const uint32_t* probe_ids, int nq, int nprobe, uint32_t nlist, uint32_t* counts,
+                             uint32_t* order, cudaStream_t stream) {
+  if (nq <= 0) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(counts, 0, (static_cast<size_t>(nlist) + 1) * sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return e;
+  const int blocks = (nq + 255) / 256;
+  probe_count_kernel<<<blocks, 256, 0, stream>>>(probe_ids, nq, nprobe, nlist, counts);
+  probe_scan_kernel<<<1, 1024, 0, stream>>>(counts, nlist + 1);
+  probe_place_kernel<<<blocks, 256, 0, stream>>>(probe_ids, nq, nprobe, nlist, counts, order);
+  return cudaGetLastError();
 }
 
 cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream) {

@@ -35,11 +35,15 @@ struct IvfPqArgs {
   uint32_t* out_row;
   uint64_t* out_dc;
   uint64_t* cand;             // IvfPqCandBytes(nq, k, depth) of candidate buffers
+  const uint32_t* qorder;     // CTA b scans query qorder[b] (null: query b)
   int* status;
 };
 
 size_t IvfPqSmemBytes(int pd, int m, int mode);
 size_t IvfPqCandBytes(int nq, int k, int depth);
+// order[0..nq): the queries grouped by their first probed list; counts holds nlist + 1 words.
+cudaError_t LaunchProbeOrder(const uint32_t* probe_ids, int nq, int nprobe, uint32_t nlist, uint32_t* counts,
+                             uint32_t* order, cudaStream_t stream);
 cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream);
 cudaError_t LaunchTerm2(const float* coarse, uint32_t nlist, int pd, const float* centroids, int m,
                         int ds, float* term2, cudaStream_t stream);
