@@ -92,6 +92,23 @@ __device__ int warp_keep_best(uint64_t* buf, int n, int keep) {
   return n < keep ? n : keep;
 }
 
+// warp_keep_best for n <= 256 keys (an eight-per-lane sort).
+__device__ int keep_best_256(uint64_t* buf, int n, int keep) {
+  const int lane = threadIdx.x & 31;
+  uint64_t x[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int i = e * 32 + lane;
+    x[e] = i < n ? buf[i] : kNone;
+  }
+  warp_sort<8>(x);
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < 8; ++e) buf[e * 32 + lane] = x[e];
+  __syncwarp();
+  return n < keep ? n : keep;
+}
+
 template <int kIvfWarps>
 __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a) {
   extern __shared__ __align__(16) uint8_t ism[];
@@ -252,64 +269,56 @@ __global__ void __launch_bounds__(kIvfWarps * 32) ivfpq_kernel(const IvfPqArgs a
     }
     __syncthreads();  // table is rebuilt for the next list
   }
-  // Merge: every warp reduces to its R best, warp 0 merges the sorted lists.
+  // Merge: every warp reduces to its R best (sorted), then the lists merge pairwise in a tree
+  // into warp 0's buffer; all warps re-rank, warp 0 sorts and writes.
   count = warp_keep_best(buf, count, R);
   if (lane == 0) count_s[warp] = count;
   __syncthreads();
-  if (warp == 0) {
-    // Gather the candidates of all warps into warp 0's buffer region after its own R entries
-    // (kIvfWarps * R <= 1024 keys, the size of the sort below; IvfPqWarps picks the warps).
-    uint64_t* all = bufs;  // reuse: compact all warps' lists to the front
-    int total = count_s[0];
-    for (int w = 1; w < kIvfWarps; ++w) {
-      const int cw = count_s[w];
-      for (int i = lane; i < cw; i += 32) all[total + i] = bufs[w * kIvfCap + i];
-      total += cw;
+  for (int step = 1; step < kIvfWarps; step <<= 1) {
+    if ((warp & (2 * step - 1)) == 0) {
+      const int n0 = count_s[warp], n1 = count_s[warp + step];
+      const uint64_t* pb = bufs + static_cast<size_t>(warp + step) * kIvfCap;
+      for (int i = lane; i < n1; i += 32) buf[n0 + i] = pb[i];
       __syncwarp();
+      const int kept = n0 + n1 <= 256 ? keep_best_256(buf, n0 + n1, R) : warp_keep_best(buf, n0 + n1, R);
+      if (lane == 0) count_s[warp] = kept;
     }
-    // total <= 4 * R <= 1024
-    {
-      uint64_t x[32];
+    __syncthreads();
+  }
+  uint64_t* all = bufs;  // warp 0's buffer: the R best, sorted
+  const int ncand = count_s[0];
+  if (a.depth > 0) {
+    // Rerank the R best on fp32 rows (exact, reference kernel-set order), four rows per warp step.
+    for (int i = warp * 4; i < ncand; i += kIvfWarps * 4) {
+      uint32_t r[4];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int i = e * 32 + lane;
-        x[e] = i < total ? all[i] : kNone;
+      for (int c = 0; c < 4; ++c) r[c] = neighbor_id(all[i + c < ncand ? i + c : i]);
+      float d[4];
+      if (a.order == kOrderAvx512 && pd <= 8 * 32 + 16) {
+        warp_exact_dist4_avx512<8>(q_s, a.rows, r, ncand - i, pd, l2, d);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          d[c] = warp_exact_dist(q_s, a.rows + static_cast<size_t>(r[c]) * pd, pd, l2, a.order);
       }
-      warp_sort<32>(x);
       __syncwarp();
+      if (lane < 4 && i + lane < ncand) {
+        float dl = d[0];
+        uint32_t rl = r[0];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) all[e * 32 + lane] = x[e];
+        for (int c = 1; c < 4; ++c) {
+          dl = lane == c ? d[c] : dl;
+          rl = lane == c ? r[c] : rl;
+        }
+        all[i + lane] = pack_neighbor(dl, rl);
+      }
       __syncwarp();
     }
-    const int ncand = total < R ? total : R;
+    __syncthreads();
+  }
+  if (warp == 0) {
     int nout;
     if (a.depth > 0) {
-      // Rerank the R best on fp32 rows (exact, reference kernel-set order), keep k.
-      for (int i = 0; i < ncand; i += 4) {
-        uint32_t r[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) r[c] = neighbor_id(all[i + c < ncand ? i + c : i]);
-        float d[4];
-        if (a.order == kOrderAvx512 && pd <= 8 * 32 + 16) {
-          warp_exact_dist4_avx512<8>(q_s, a.rows, r, ncand - i, pd, l2, d);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            d[c] = warp_exact_dist(q_s, a.rows + static_cast<size_t>(r[c]) * pd, pd, l2, a.order);
-        }
-        __syncwarp();
-        if (lane < 4 && i + lane < ncand) {
-          float dl = d[0];
-          uint32_t rl = r[0];
-#pragma unroll
-          for (int c = 1; c < 4; ++c) {
-            dl = lane == c ? d[c] : dl;
-            rl = lane == c ? r[c] : rl;
-          }
-          all[i + lane] = pack_neighbor(dl, rl);
-        }
-        __syncwarp();
-      }
       {
         uint64_t x[8];
 #pragma unroll
