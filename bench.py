@@ -78,10 +78,17 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={device}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+        # nvidia-smi takes a moment to start: wait (bounded) for its first sample so that the
+        # samples cover the timed region that follows.
+        t0 = time.time()
+        while self.p is not None and time.time() - t0 < 3.0:
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.01)
 
     def stop(self):
         if self.p is None:
@@ -626,7 +633,7 @@ def run_c0_c3(args):
         def step():
             idx.search(q_dev, k=K, out=(ids_dev, d_dev))
             scan.append(ctx.stage_times()[1])
-        ms, clk = _timed(step, max(args.steps, 50), args.warmup, stream, local)
+        ms, clk = _timed(step, max(args.steps, 1000), args.warmup, stream, local)
         nq = qs.shape[0]
         flops = 2.0 * nq * base.shape[0] * DIM
         scan_s = float(np.median(scan)) / 1000.0
@@ -635,7 +642,7 @@ def run_c0_c3(args):
         ref_ids, _ = ref.flat_search_batch(oracle.L2, base, DIM, qs, K, threads=0)
         cpu_s = time.perf_counter() - t0
         gpu_ids = ids_dev.cpu().numpy().view(np.uint32)
-        out = {"metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": 1, "steps": max(args.steps, 50),
+        out = {"metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/s", "n_gpus": 1, "steps": max(args.steps, 1000),
                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                "vs_baseline": None, "dtype": "f16 tensor-core pre-rank (exact for these integer rows), f32 re-rank",
                "data": "synthetic", "config": {"workload": C0_WORKLOAD, "rows": base.shape[0], "batch": nq, "k": K,
