@@ -2,7 +2,7 @@
 // an fp32 re-rank on the GPU. Both run the same pipeline (ScanSearch):
 //   prep_queries -> tensor-core scan with fused top-C (scan_mma.cu) -> exact finalize (select.cu)
 //
-// Seeded scans. On large batches over large operands (at least 1e9 query-row pairs, 64k rows) the
+// Seeded scans. On batches of at least 5e7 query-row pairs over operands of 64k rows or more, the
 // pipeline first scans a strided sample of the rows (every s-th row, s = 16 by default;
 // VDB_SCAN_SAMPLE sets s, 0 turns seeding off), where each 32-row chunk offers only its best key,
 // keeping m candidates per query, and takes the m-th
@@ -58,7 +58,7 @@ void ChooseUnits(uint64_t qtiles, uint64_t ntiles, int sms, int* upq, int* tiles
 }
 
 constexpr uint64_t kSampleMinRows = 65536;
-constexpr double kSeedMinWork = 1e9;  // queries x rows below which scans are not seeded
+constexpr double kSeedMinWork = 5e7;  // queries x rows below which scans are not seeded
 constexpr uint64_t kSampleRatio = 16;     // stride of sample level 1 / stride of level 0
 constexpr uint64_t kSample2MinRows = 1024;
 

@@ -116,7 +116,7 @@ def test_sq8_scan_full_size_config1(ctx):
 
 @pytest.mark.parametrize("keep", [None, 1, 6])
 def test_seeded_scan_is_exact(ctx, monkeypatch, keep):
-    """Batches of at least 1e9 (query, row) pairs over operands of 64k rows and more start every
+    """Batches of at least 5e7 (query, row) pairs over operands of 64k rows and more start every
     query's bound from a strided row sample. The
     seed is an estimate: queries left with fewer than C keys below it are rescanned unseeded.
     keep = 1 makes most queries fall back (about s - 1 rows of the operand lie below the minimum of
