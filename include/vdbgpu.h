@@ -146,7 +146,9 @@ VDBGPU_API int vdbgpu_index_get_info(const vdbgpu_index* index, vdbgpu_index_inf
  * ties by row id. Missing slots are (+inf, UINT32_MAX). allow_bits (nullable) is a dense bitset
  * of allowed rows (bit r of word r/64), the RowFilter of src/index/index.h:23-27.
  * out_dist_comps (nullable, nq values) receives IndexSearchStats::distance_computations
- * (src/index/index.h:29-32). params may be NULL (defaults). */
+ * (src/index/index.h:29-32). params may be NULL (defaults). The call returns once the results
+ * are written: it synchronises the launching stream (also part-way through, for a large flat /
+ * SQ8 batch, to learn which queries its seeded scan must rescan). */
 VDBGPU_API int vdbgpu_index_search(vdbgpu_index* index, const float* queries, uint64_t nq, uint32_t k,
                         const vdbgpu_search_params* params, const uint64_t* allow_bits,
                         float* out_dist, uint32_t* out_row, uint64_t* out_dist_comps);
