@@ -104,11 +104,6 @@ const char* IndexFileName(int t) {
 
 uint32_t PaddedDim(uint32_t d) { return (d + 15) / 16 * 16; }  // include/vdb/types.h:30-32
 
-Status Cuda(cudaError_t e, const char* what) {
-  if (e == cudaSuccess) return Status::OK();
-  return Status(Status::kInternal, std::string(what) + ": " + cudaGetErrorString(e));
-}
-
 template <class T>
 Status UploadVec(Context& ctx, const std::vector<T>& v, DeviceBuffer* out) {
   VDBGPU_RETURN_IF_ERROR(out->alloc(std::max<size_t>(1, v.size()) * sizeof(T)));
