@@ -314,6 +314,8 @@ Status BuildIvfPqFile(Context& ctx, int type, const float* rows, uint64_t n, uin
                                                 ", m " + std::to_string(pq_m) + ")");
   if (pd > static_cast<uint32_t>(kAssignMaxDim))
     return Status(Status::kNotSupported, "the GPU builder supports padded dimensions up to 256");
+  if (dim / pq_m > 64)
+    return Status(Status::kNotSupported, "the GPU builder supports sub-vectors of up to 64 floats (dim / pq_m)");
   const size_t m = pq_m, dsub = dim / pq_m;
   // Host copy of the rows (the k-means sums, samples and residuals are host work).
   std::vector<float> host;

@@ -317,7 +317,8 @@ VDBGPU_API int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows,
  * nearest-centroid searches in the reference kernel set's summation order), so the returned
  * file is the reference's own index file, byte for byte, for the same rows (nrows x padded_dim
  * floats, host or device), nlist, pq_m, max_train_points_per_centroid and seed. Padded
- * dimensions up to 256. *out_file is malloc'd; release it with vdbgpu_buffer_free. */
+ * dimensions up to 256 and sub-vectors (dim / pq_m) up to 64 floats; larger requests return
+ * VDBGPU_NOT_SUPPORTED. *out_file is malloc'd; release it with vdbgpu_buffer_free. */
 VDBGPU_API int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, uint64_t nrows,
                                   uint32_t dim, uint32_t padded_dim, uint32_t nlist, uint32_t pq_m,
                                   uint32_t max_train_ppc, uint64_t seed, void** out_file,
