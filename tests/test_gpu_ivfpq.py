@@ -54,3 +54,22 @@ def test_ivfpq_filtered_and_cosine_against_oracle(ctx):
         np.testing.assert_array_equal(d, od)
     np.testing.assert_array_equal(dc, odc)
     assert np.all(ids[ids != np.uint32(0xFFFFFFFF)] % 2 == 1)
+
+
+@pytest.mark.parametrize("rerank", [120, 200])
+def test_ivfpq_deep_rerank_against_oracle(ctx, rerank):
+    """Re-rank depths above 100: 120 keeps the eight-warp scan (eight R-best lists merge within its
+    1024-key limit), 200 takes the four-warp variant whose pairwise merges sort 512 keys. Ids,
+    distances and distance computations against the oracle on the reference's index."""
+    import vdb_b200
+    g = golden("ivfpq")
+    base, qs = inputs("ivfpq", g)
+    f = oracle.parse_ivfpq(bytes(g["index_file"]))
+    orc = oracle.Oracle()
+    idx = vdb_b200.Index.load(ctx, bytes(g["index_file"]), "l2", base, 96)
+    ids, d, dc = idx.search(qs, k=10, nprobe=16, rerank=rerank, stats=True)
+    oi, od, odc = orc.ivfpq_search(f, 0, base, qs, k=10, nprobe=16, rerank=rerank)
+    np.testing.assert_array_equal(ids, oi)
+    np.testing.assert_array_equal(d, od)
+    np.testing.assert_array_equal(dc, odc)
+    idx.free()
