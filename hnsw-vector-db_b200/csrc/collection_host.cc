@@ -62,6 +62,89 @@ Status DecodeBlob(std::string_view file, std::string_view magic, std::string_vie
   return Status::OK();
 }
 
+// A delete file's payload (src/storage/segment_writer.cc:28-37 writes it with
+// roaring::Roaring::write(buf, true)): CRoaring's portable serialization. Layout:
+//   cookie u32: 12346 (no run containers), followed by the container count u32; or
+//               12347 | (count - 1) << 16, followed by a bitset of (count + 7) / 8 bytes that
+//               marks run containers;
+//   count × (key u16, cardinality - 1 u16), the high 16 bits of the values and their number;
+//   count × u32 byte offsets of the containers (absent with runs and count < 4);
+//   the containers: a run container is u16 n, then n × (start u16, length - 1 u16); otherwise
+//   cardinality > 4096 is a bitmap of 1024 u64 words, else an array of u16 values.
+// The set becomes the segment's delete bits, (rows + 31) / 32 words; like Segment::Open
+// (src/storage/segment_reader.cc:107-115) a value at or past rows is corruption.
+Status DecodeDeleteSet(std::string_view p, uint64_t rows, std::vector<uint32_t>* words) {
+  const Status bad(Status::kCorruption, "bad delete set");
+  size_t at = 0;
+  auto need = [&](size_t n) { return at <= p.size() && p.size() - at >= n; };
+  auto u16 = [&]() { const uint16_t x = GetAt<uint16_t>(p.data(), at); at += 2; return x; };
+  auto u32 = [&]() { const uint32_t x = GetAt<uint32_t>(p.data(), at); at += 4; return x; };
+  words->assign((rows + 31) / 32, 0u);
+  if (!need(4)) return bad;
+  const uint32_t cookie = u32();
+  uint32_t count = 0;
+  bool runs = false;
+  std::string_view runbits;
+  if ((cookie & 0xFFFFu) == 12347u) {
+    runs = true;
+    count = (cookie >> 16) + 1;
+    if (!need((count + 7) / 8)) return bad;
+    runbits = p.substr(at, (count + 7) / 8);
+    at += (count + 7) / 8;
+  } else if (cookie == 12346u) {
+    if (!need(4)) return bad;
+    count = u32();
+    if (count > 65536) return bad;
+  } else {
+    return bad;
+  }
+  if (!need(4 * static_cast<size_t>(count))) return bad;
+  std::vector<uint16_t> keys(count);
+  std::vector<uint32_t> cards(count);
+  for (uint32_t i = 0; i < count; ++i) {
+    keys[i] = u16();
+    cards[i] = static_cast<uint32_t>(u16()) + 1;
+    if (i > 0 && keys[i] <= keys[i - 1]) return bad;
+  }
+  if (!runs || count >= 4) {
+    if (!need(4 * static_cast<size_t>(count))) return bad;
+    at += 4 * static_cast<size_t>(count);
+  }
+  const Status range(Status::kCorruption, "delete set out of range");
+  auto set = [&](uint64_t v) {
+    if (v >= rows) return false;
+    (*words)[v / 32] |= 1u << (v % 32);
+    return true;
+  };
+  for (uint32_t i = 0; i < count; ++i) {
+    const uint64_t hi = static_cast<uint64_t>(keys[i]) << 16;
+    if (runs && (static_cast<uint8_t>(runbits[i / 8]) >> (i % 8) & 1u)) {
+      if (!need(2)) return bad;
+      const uint32_t n = u16();
+      if (!need(4 * static_cast<size_t>(n))) return bad;
+      for (uint32_t r = 0; r < n; ++r) {
+        const uint32_t start = u16(), len = u16();
+        if (start + len > 0xFFFFu) return bad;
+        if (hi + start + len >= rows) return range;
+        for (uint32_t x = start; x <= start + len; ++x) set(hi + x);
+      }
+    } else if (cards[i] > 4096) {
+      if (!need(8192)) return bad;
+      for (uint32_t w = 0; w < 1024; ++w) {
+        const uint64_t bits = GetAt<uint64_t>(p.data(), at + 8 * w);
+        for (uint64_t b = bits; b != 0; b &= b - 1)
+          if (!set(hi + 64 * w + static_cast<uint32_t>(__builtin_ctzll(b)))) return range;
+      }
+      at += 8192;
+    } else {
+      if (!need(2 * static_cast<size_t>(cards[i]))) return bad;
+      for (uint32_t k = 0; k < cards[i]; ++k)
+        if (!set(hi + u16())) return range;
+    }
+  }
+  return Status::OK();
+}
+
 bool OnDevice(const void* p) {
   if (p == nullptr) return false;
   cudaPointerAttributes a{};
@@ -190,10 +273,7 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
     const JsonValue* dfv = s.get("deletes_file");
     if (idv == nullptr || rv == nullptr || !idv->is_integer() || !rv->is_integer())
       return Status(Status::kCorruption, "bad manifest segment entry");
-    if (dfv != nullptr && dfv->is_string() && !dfv->s.empty())
-      return Status(Status::kNotSupported,
-                    "segment " + std::to_string(static_cast<uint64_t>(idv->number())) +
-                        " has a persisted delete set; pass deletes with vdbgpu_collection_set_deleted");
+    if (dfv != nullptr && !dfv->is_string()) return Status(Status::kCorruption, "bad manifest segment entry");
     const uint32_t id = static_cast<uint32_t>(idv->number());
     const uint64_t rows = static_cast<uint64_t>(rv->number());
     char name[32];
@@ -226,9 +306,25 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
     if (!st.ok()) return Status(Status::kCorruption, dir + "/meta.bin: " + st.message());
     std::vector<uint64_t> ids(rows);
     if (rows > 0) std::memcpy(ids.data(), ids_p.data(), rows * 8);
+    // The persisted delete set (segment_reader.cc:101-116): a "VDBDEL01" blob named by the
+    // manifest entry's deletes_file.
+    std::vector<uint32_t> del;
+    if (dfv != nullptr && !dfv->s.empty()) {
+      std::string delf;
+      VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/" + dfv->s, &delf));
+      std::string_view del_p;
+      st = DecodeBlob(delf, "VDBDEL01", &del_p);
+      if (!st.ok()) return Status(Status::kCorruption, dir + "/" + dfv->s + ": " + st.message());
+      st = DecodeDeleteSet(del_p, rows, &del);
+      if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
+    }
     st = c->AddSegment(ctx, id, static_cast<uint32_t>(i), reinterpret_cast<const float*>(h + kSegmentHeaderSize),
                        rows, ids.data(), meta_p, indexf);
     if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
+    if (!del.empty()) {
+      st = c->SetDeleted(ctx, id, del.data());
+      if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
+    }
   }
   *out = std::move(c);
   return Status::OK();

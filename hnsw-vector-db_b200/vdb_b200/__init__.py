@@ -21,7 +21,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_DIR = os.path.join(os.path.dirname(_HERE), "lib")
 LIB_PATH = os.environ.get("VDBGPU_LIB") or os.path.join(LIB_DIR, "libvdbgpu.so")
 
-OK, INVALID_ARGUMENT, NOT_FOUND = 0, 1, 2
+OK, INVALID_ARGUMENT, NOT_FOUND, IO_ERROR, CORRUPTION = 0, 1, 2, 4, 5
 RESOURCE_EXHAUSTED, UNAVAILABLE, NOT_SUPPORTED = 7, 8, 9
 STATUS_NAMES = {
     0: "OK", 1: "InvalidArgument", 2: "NotFound", 3: "AlreadyExists", 4: "IOError",

@@ -205,8 +205,9 @@ typedef struct vdbgpu_hit {
  * 95-150, Segment::Open, src/storage/segment_reader.cc:20-122): reads CURRENT, the manifest and
  * every segment directory (vectors.f32, ids.u64, meta.bin, index.<type>). With nshards > 1 only
  * the segments whose manifest position % nshards == shard are loaded (one shard per GPU).
- * Segments with a persisted delete set are refused (VDBGPU_NOT_SUPPORTED); pass deletes with
- * vdbgpu_collection_set_deleted. */
+ * A segment's persisted delete set (the manifest entry's deletes_file, a "VDBDEL01" blob holding a
+ * portable roaring bitmap) is loaded as its delete bits; a value at or past the segment's rows is
+ * VDBGPU_CORRUPTION, as Segment::Open. Later deletes go through vdbgpu_collection_set_deleted. */
 VDBGPU_API int vdbgpu_collection_open(vdbgpu_ctx* ctx, const char* path, uint32_t shard,
                                       uint32_t nshards, vdbgpu_collection** out);
 

@@ -217,6 +217,7 @@ def _engine_lib(lib_path: str = REF_ENGINE_LIB):
         "ref_coll_free": (None, [_P]),
         "ref_coll_bulk_load": (ci, [_P, _P, _P, c64, _P, _P, c32]),
         "ref_coll_bulk_load_json": (ci, [_P, _P, _P, c64, ctypes.c_char_p]),
+        "ref_coll_remove_flush": (ci, [_P, _P, c64, _P, _P, c64, _P]),
         "ref_coll_search_batch": (ci, [_P, _P, c64, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, _P, _P]),
         "ref_coll_explain": (ci, [_P, _P, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, ctypes.c_char_p,
                                   ctypes.c_size_t]),
@@ -286,6 +287,21 @@ class RefCollection:
                                            _ptr(None if tags is None else np.ascontiguousarray(tags, np.uint32)), mt)
         if rc != 0:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
+
+    def remove_flush(self, ids: np.ndarray, up_ids: np.ndarray, up_vectors: np.ndarray) -> int:
+        """Collection::RemoveBatch, UpsertBatch (up_ids / up_vectors, no metadata), then Flush: the
+        upserts become a new segment and the removed or superseded rows of disk segments are
+        written as delete files (deletes-<n>.roar) named in the new manifest. Returns how many of
+        ids were live."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint64)
+        up_ids = np.ascontiguousarray(up_ids, dtype=np.uint64)
+        v = np.ascontiguousarray(up_vectors[:, :self.dim], dtype=np.float32)
+        removed = np.zeros(1, dtype=np.uint64)
+        rc = self.l.ref_coll_remove_flush(self.h, _ptr(ids), ids.size, _ptr(up_ids), _ptr(v), up_ids.size,
+                                          _ptr(removed))
+        if rc != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+        return int(removed[0])
 
     def search(self, q: np.ndarray, k=10, ef=64, nprobe=16, rerank=-1, strategy="auto", filter=None,
                prefilter_threshold=10000, post_filter_alpha=10):

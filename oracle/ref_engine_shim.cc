@@ -194,6 +194,25 @@ int ref_filter_parse(const char* schema_json, const char* filter_json) {
 }
 
 // Collection::SearchBatch with an optional JSON filter. Misses: UINT64_MAX / +inf.
+// Collection::RemoveBatch then Collection::Flush: the deletes reach the disk segments' persisted
+// delete sets (deletes-<n>.roar, CollectionImpl::FlushFrozen).
+// RemoveBatch, then UpsertBatch of nup rows (an upsert of an id on disk deletes its old row), then
+// Flush. Flush persists the delete sets of disk segments only when the mutable segment holds rows
+// (CollectionImpl::FlushOnce, src/engine/collection_impl.cc:649-650), hence the upserts.
+int ref_coll_remove_flush(ref_coll* h, const uint64_t* ids, uint64_t n, const uint64_t* up_ids,
+                          const float* up_vectors, uint64_t nup, uint64_t* removed) {
+  size_t r = 0;
+  vdb::Status s = h->c->RemoveBatch(ids, n, &r);
+  if (s.ok() && nup > 0) s = h->c->UpsertBatch(up_ids, up_vectors, nup);
+  if (s.ok()) s = h->c->Flush();
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  if (removed != nullptr) *removed = r;
+  return 0;
+}
+
 int ref_coll_search_batch(ref_coll* h, const float* q, uint64_t nq, uint32_t k, uint64_t ef,
                           uint64_t nprobe, int rerank, int strategy, uint64_t prefilter_threshold,
                           uint64_t post_filter_alpha, const char* filter_json, uint64_t* out_ids,

@@ -172,8 +172,55 @@ def parse_golden():
     print("wrote filter_parse", len(PARSE_CASES), "cases")
 
 
+def make_deletes(name="coll_deletes", dim=4, seed=14, nq=32):
+    """A collection whose disk segments carry persisted delete sets (deletes-<n>.roar, written by
+    Collection::Flush after RemoveBatch and UpsertBatch). Segment A (200,000 rows) spans four
+    16-bit keys, and its set holds every container kind: scattered rows (array), two contiguous
+    ranges (run), every other row of a key (bitmap), and a superseded row. Segment B's set has no
+    run container (cookie 12346); segment C's is one run (cookie 12347 without offsets). Rows lie on
+    a 1/16 grid to keep the fixture small; half the queries sit next to deleted rows."""
+    rng = np.random.default_rng(seed)
+    tmp = tempfile.mkdtemp()
+    path = os.path.join(tmp, "coll")
+    coll = oracle.RefCollection(path, dim, metric="l2", index={"type": "flat"}, schema=[], threads=4)
+    sizes = [200000, 5000, 3000]
+    segs = []
+    next_id = 10
+    for n in sizes:
+        rows = (rng.integers(-64, 64, (n, dim)) / 16).astype(np.float32)
+        ids = np.arange(next_id, next_id + n, dtype=np.uint64) * 5
+        next_id += n
+        coll.bulk_load(ids, rows)
+        segs.append((ids, rows))
+    (ia, ra), (ib, _), (ic, _) = segs
+    rows_a = np.concatenate([np.sort(rng.choice(65536, 700, replace=False)),   # key 0: array
+                             np.arange(65536, 65600), np.arange(70000, 78000),  # key 1: two runs
+                             131072 + 2 * np.arange(4500),                      # key 2: bitmap
+                             np.arange(196608, 196700, 3)])                     # key 3: array
+    removed = np.concatenate([ia[rows_a], ib[rng.choice(5000, 40, replace=False)], ic[100:1100],
+                              np.array([7, 11], np.uint64)])                    # 7, 11: absent
+    up_ids = np.array([ia[199999], 3], np.uint64)  # supersedes A's last row; a new id
+    up_rows = (rng.integers(-64, 64, (2, dim)) / 16).astype(np.float32)
+    live = coll.remove_flush(removed, up_ids, up_rows)
+    near = ra[rng.choice(rows_a, nq // 2)] + rng.normal(0, 0.02, (nq // 2, dim)).astype(np.float32)
+    q = np.concatenate([near, rng.normal(0, 2, (nq - nq // 2, dim))]).astype(np.float32)
+    out = {"queries": q, "dim": np.array(dim), "sizes": np.array(sizes), "removed_live": np.array(live),
+           "deleted_rows_a": rows_a.astype(np.int64)}
+    for k in (10, 64):
+        ids, d = coll.search(q, k=k)
+        out[f"ids_{k}"], out[f"dist_{k}"] = ids, d
+    segdirs = coll.segment_dirs()
+    out["segment_ids"] = np.array([int(os.path.basename(s)[4:]) for s in segdirs])
+    coll.close()
+    out.update(pack_dir(path))
+    shutil.rmtree(tmp)
+    np.savez_compressed(os.path.join(OUT, name + ".npz"), **out)
+    print("wrote", name, os.path.getsize(os.path.join(OUT, name + ".npz")), "bytes")
+
+
 def main():
     oracle.build(ref=True)
+    make_deletes()
     parse_golden()
     make("coll_hnsw", 48, "cosine", {"type": "hnsw", "M": 8, "ef_construction": 64}, [900, 1300, 700], seed=11)
     make("coll_ivfpq", 32, "l2", {"type": "ivf_pq", "nlist": 16, "pq_m": 8}, [1000, 800], seed=12,

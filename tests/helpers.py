@@ -55,3 +55,64 @@ def extract_collection(g, dest):
         with open(full, "wb") as f:
             f.write(np.asarray(g[key]).tobytes())
     return path
+
+
+def crc32c(data: bytes) -> int:
+    """CRC-32C (Castagnoli, reflected polynomial 0x82F63B78), bitwise; small inputs only."""
+    crc = 0xFFFFFFFF
+    for b in data:
+        crc ^= b
+        for _ in range(8):
+            crc = (crc >> 1) ^ (0x82F63B78 & -(crc & 1))
+    return crc ^ 0xFFFFFFFF
+
+
+def blob(magic: bytes, payload: bytes) -> bytes:
+    """A reference blob file (src/storage/file_format.cc): magic 8, u32 version 1, u32 crc32c of
+    the payload, u64 payload length, the payload."""
+    return magic + np.array([1, crc32c(payload)], "<u4").tobytes() + np.array([len(payload)], "<u8").tobytes() + payload
+
+
+def decode_portable_roaring(p: bytes):
+    """CRoaring's portable serialization (RoaringFormatSpec) to (sorted values, per-container
+    kinds "array" / "bitmap" / "run", cookie, container count). Test-side reader for fixtures."""
+    at = 0
+
+    def take(fmt, n):
+        nonlocal at
+        v = np.frombuffer(p, fmt, n, at)
+        at += v.nbytes
+        return v
+
+    cookie = int(take("<u4", 1)[0])
+    if cookie & 0xFFFF == 12347:
+        count = (cookie >> 16) + 1
+        runbits = take("u1", (count + 7) // 8)
+        isrun = [bool(runbits[i // 8] >> (i % 8) & 1) for i in range(count)]
+    else:
+        assert cookie == 12346
+        count = int(take("<u4", 1)[0])
+        isrun = [False] * count
+    hdr = take("<u2", 2 * count).reshape(count, 2)
+    if not any(isrun) or count >= 4:
+        take("<u4", count)
+    vals, kinds = [], []
+    for i in range(count):
+        hi = int(hdr[i, 0]) << 16
+        card = int(hdr[i, 1]) + 1
+        if isrun[i]:
+            n = int(take("<u2", 1)[0])
+            r = take("<u2", 2 * n).reshape(n, 2).astype(np.int64)
+            for s, l in r:
+                vals.append(hi + np.arange(s, s + l + 1))
+            kinds.append("run")
+        elif card > 4096:
+            bits = np.unpackbits(take("u1", 8192), bitorder="little")
+            vals.append(hi + np.nonzero(bits)[0])
+            kinds.append("bitmap")
+        else:
+            vals.append(hi + take("<u2", card).astype(np.int64))
+            kinds.append("array")
+    assert at == len(p)
+    v = np.concatenate(vals) if vals else np.zeros(0, np.int64)
+    return v, kinds, cookie & 0xFFFF, count
