@@ -525,7 +525,8 @@ int vdbgpu_collection_explain(vdbgpu_collection* c, const float* query, uint32_t
   for (size_t i = 0; i < ex[0].size(); ++i) {
     const auto& e = ex[0][i];
     if (i > 0) j += ",";
-    j += "{\"id\":" + std::to_string(e.segment_id) + ",\"strategy\":\"" + e.strategy +
+    j += "{\"id\":" + std::to_string(e.segment_id) + ",\"kind\":\"" + (e.is_mutable ? "mutable" : "disk") +
+         "\",\"strategy\":\"" + e.strategy +
          "\",\"matches\":" + std::to_string(e.matches) + ",\"live_rows\":" + std::to_string(e.live_rows) +
          ",\"distance_computations\":" + std::to_string(e.dc) + ",\"results\":" + std::to_string(e.results) +
          "}";

@@ -43,7 +43,8 @@ struct GpuColumn {
 
 struct GpuSegment {
   uint32_t id = 0;
-  uint32_t ordinal = 0;  // position among the collection's disk segments (the merge's part order)
+  uint32_t ordinal = 0;  // the merge's part order: 0 the mutable segment, then disk segments
+  bool is_mutable = false;  // rebuilt from the log; always searched exhaustively
   uint64_t rows = 0, words = 0;
   uint64_t deleted = 0;
   std::unique_ptr<GpuIndex> index;
@@ -54,17 +55,20 @@ struct GpuSegment {
   std::vector<GpuColumn> cols;
 };
 
-// SegmentExplain (include/vdb/collection.h:45-58) of one disk segment for one query.
+// SegmentExplain (include/vdb/collection.h:45-58) of one segment for one query.
 struct PartExplain {
   uint32_t segment_id = 0;
+  bool is_mutable = false;
   std::string strategy;
   uint64_t live_rows = 0, matches = 0, dc = 0, results = 0;
 };
 
 class GpuCollection {
  public:
-  // Opens a collection directory written by the reference (CURRENT -> MANIFEST-<n> -> segments).
-  // With nshards > 1 only the segments whose ordinal % nshards == shard are loaded.
+  // Opens a collection directory written by the reference (CURRENT -> MANIFEST-<n> -> segments,
+  // their delete sets, then the logs replayed into the mutable segment). With nshards > 1 only
+  // the segments whose manifest position % nshards == shard are loaded; shard 0 holds the
+  // mutable segment.
   static Status Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
                      std::unique_ptr<GpuCollection>* out);
   // An empty collection with the reference's options JSON (engine/options_json.cc), to which

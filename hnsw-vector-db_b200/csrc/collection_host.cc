@@ -6,8 +6,12 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <map>
 #include <sstream>
+#include <unordered_map>
+
+#include <dirent.h>
 
 #include "formats.h"
 #include "hnsw.cuh"
@@ -240,96 +244,6 @@ Status GpuCollection::Create(std::string_view options_json, std::unique_ptr<GpuC
   return Status::OK();
 }
 
-Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
-                           std::unique_ptr<GpuCollection>* out) {
-  if (nshards == 0 || shard >= nshards) return Status(Status::kInvalidArgument, "bad shard");
-  // ReadCurrentManifest (src/storage/manifest.cc:116-127).
-  std::string current;
-  VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/CURRENT", &current));
-  while (!current.empty() && (current.back() == '\n' || current.back() == '\r' || current.back() == ' '))
-    current.pop_back();
-  if (current.rfind("MANIFEST-", 0) != 0) return Status(Status::kCorruption, "bad CURRENT file");
-  std::string mf;
-  VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/" + current, &mf));
-  std::string_view payload;
-  VDBGPU_RETURN_IF_ERROR(DecodeBlob(mf, "VDBMAN01", &payload));
-  JsonValue j;
-  if (!ParseJson(payload, &j) || !j.is_object()) return Status(Status::kCorruption, "manifest is not valid JSON");
-  const JsonValue* fv = j.get("format_version");
-  if (fv == nullptr || !fv->is_integer() || fv->number() != 1)
-    return Status(Status::kCorruption, "unknown manifest version");
-  const JsonValue* opts = j.get("options");
-  const JsonValue* segs = j.get("segments");
-  if (opts == nullptr || segs == nullptr || !segs->is_array()) return Status(Status::kCorruption, "bad manifest");
-  auto c = std::make_unique<GpuCollection>();
-  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, &c->opt_));
-  c->total_segments_ = static_cast<uint32_t>(segs->arr.size());
-  const uint32_t pd = c->opt_.pd;
-  for (size_t i = 0; i < segs->arr.size(); ++i) {
-    if (i % nshards != shard) continue;
-    const JsonValue& s = segs->arr[i];
-    const JsonValue* idv = s.get("id");
-    const JsonValue* rv = s.get("rows");
-    const JsonValue* dfv = s.get("deletes_file");
-    if (idv == nullptr || rv == nullptr || !idv->is_integer() || !rv->is_integer())
-      return Status(Status::kCorruption, "bad manifest segment entry");
-    if (dfv != nullptr && !dfv->is_string()) return Status(Status::kCorruption, "bad manifest segment entry");
-    const uint32_t id = static_cast<uint32_t>(idv->number());
-    const uint64_t rows = static_cast<uint64_t>(rv->number());
-    char name[32];
-    std::snprintf(name, sizeof(name), "seg-%06u", id);
-    const std::string dir = path + "/segments/" + name;
-    // vectors.f32 header checks of Segment::Open (segment_reader.cc:36-51).
-    std::string vec;
-    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/vectors.f32", &vec));
-    if (vec.size() < kSegmentHeaderSize) return Status(Status::kCorruption, dir + ": vectors.f32 shorter than its header");
-    const char* h = vec.data();
-    if (std::memcmp(h, "VDBSEG01", 8) != 0) return Status(Status::kCorruption, dir + ": bad magic");
-    if (GetAt<uint32_t>(h, kSegmentHeaderSize - 4) != Crc32c(h, kSegmentHeaderSize - 4))
-      return Status(Status::kCorruption, dir + ": header checksum mismatch");
-    const uint64_t hrows = GetAt<uint64_t>(h, 16);
-    const uint64_t data_len = GetAt<uint64_t>(h, 40);
-    if (GetAt<uint32_t>(h, 8) != 1 || GetAt<uint32_t>(h, 12) != static_cast<uint32_t>(c->opt_.metric) ||
-        hrows != rows || GetAt<uint32_t>(h, 24) != c->opt_.dim || GetAt<uint32_t>(h, 28) != pd ||
-        GetAt<uint64_t>(h, 32) != kSegmentHeaderSize || data_len != rows * pd * sizeof(float) ||
-        vec.size() < kSegmentHeaderSize + data_len)
-      return Status(Status::kCorruption, dir + ": header does not match the manifest");
-    std::string idsf, metaf, indexf;
-    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/ids.u64", &idsf));
-    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/meta.bin", &metaf));
-    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/" + IndexFileName(c->opt_.index_type), &indexf));
-    std::string_view ids_p, meta_p;
-    Status st = DecodeBlob(idsf, "VDBIDS01", &ids_p);
-    if (!st.ok()) return Status(Status::kCorruption, dir + "/ids.u64: " + st.message());
-    if (ids_p.size() != rows * 8) return Status(Status::kCorruption, dir + ": ids.u64 size mismatch");
-    st = DecodeBlob(metaf, "VDBMETA1", &meta_p);
-    if (!st.ok()) return Status(Status::kCorruption, dir + "/meta.bin: " + st.message());
-    std::vector<uint64_t> ids(rows);
-    if (rows > 0) std::memcpy(ids.data(), ids_p.data(), rows * 8);
-    // The persisted delete set (segment_reader.cc:101-116): a "VDBDEL01" blob named by the
-    // manifest entry's deletes_file.
-    std::vector<uint32_t> del;
-    if (dfv != nullptr && !dfv->s.empty()) {
-      std::string delf;
-      VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/" + dfv->s, &delf));
-      std::string_view del_p;
-      st = DecodeBlob(delf, "VDBDEL01", &del_p);
-      if (!st.ok()) return Status(Status::kCorruption, dir + "/" + dfv->s + ": " + st.message());
-      st = DecodeDeleteSet(del_p, rows, &del);
-      if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
-    }
-    st = c->AddSegment(ctx, id, static_cast<uint32_t>(i), reinterpret_cast<const float*>(h + kSegmentHeaderSize),
-                       rows, ids.data(), meta_p, indexf);
-    if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
-    if (!del.empty()) {
-      st = c->SetDeleted(ctx, id, del.data());
-      if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
-    }
-  }
-  *out = std::move(c);
-  return Status::OK();
-}
-
 namespace {
 
 // SegmentColumns::Build (src/meta/columns.cc:23-125) from meta.bin's payload: u64 rows,
@@ -347,6 +261,68 @@ struct RowValue {  // one decoded field of one row (the last occurrence wins, as
   bool b = false;
   std::vector<std::string> strs;
 };
+
+// One row of EncodeMetaRow (src/meta/schema.cc:97-124) into row (fields it does not hold keep
+// has = false; the last occurrence of a field wins, as DecodeMetaRow). False when malformed.
+bool DecodeMetaRowValues(const Schema& schema, std::string_view data, std::vector<RowValue>* rowp) {
+  std::vector<RowValue>& row = *rowp;
+  for (auto& v : row) v.has = false;
+  if (!data.empty()) {
+    Reader rr(data);
+    uint16_t count = 0;
+    if (!rr.u16(&count)) return false;
+    for (uint16_t k = 0; k < count; ++k) {
+      uint16_t fid = 0;
+      uint8_t type = 0;
+      if (!rr.u16(&fid) || !rr.u8(&type) || fid >= schema.size()) return false;
+      if (type != static_cast<uint8_t>(schema[fid].type)) return false;
+      RowValue& v = row[fid];
+      v.has = true;
+      v.strs.clear();
+      switch (static_cast<FieldType>(type)) {
+        case FieldType::Int64: {
+          int64_t x = 0;
+          if (!rr.i64(&x)) return false;
+          v.num = static_cast<double>(x);
+          break;
+        }
+        case FieldType::Float64: {
+          double x = 0;
+          if (!rr.f64(&x)) return false;
+          v.num = x;
+          break;
+        }
+        case FieldType::Keyword: {
+          uint32_t len = 0;
+          std::string_view sv;
+          if (!rr.u32(&len) || !rr.bytes(len, &sv)) return false;
+          v.strs.emplace_back(sv);
+          break;
+        }
+        case FieldType::KeywordList: {
+          uint32_t cnt = 0;
+          if (!rr.u32(&cnt) || cnt > rr.remaining() / 4) return false;
+          for (uint32_t e = 0; e < cnt; ++e) {
+            uint32_t len = 0;
+            std::string_view sv;
+            if (!rr.u32(&len) || !rr.bytes(len, &sv)) return false;
+            v.strs.emplace_back(sv);
+          }
+          break;
+        }
+        case FieldType::Bool: {
+          uint8_t b = 0;
+          if (!rr.u8(&b)) return false;
+          v.b = b != 0;
+          break;
+        }
+        default: return false;
+      }
+    }
+    if (rr.remaining() != 0) return false;
+  }
+  return true;
+}
 
 Status BuildColumns(const Schema& schema, uint64_t n, uint64_t words, std::string_view meta,
                     std::vector<HostColumn>* cols) {
@@ -374,63 +350,9 @@ Status BuildColumns(const Schema& schema, uint64_t n, uint64_t words, std::strin
     if (offs[i] > offs[i + 1] || offs[i + 1] > bytes.size()) return Status(Status::kCorruption, "bad meta.bin offsets");
   std::vector<RowValue> row(schema.size());
   for (uint64_t ri = 0; ri < n; ++ri) {
-    for (auto& v : row) v.has = false;
     const std::string_view data = bytes.substr(offs[ri], offs[ri + 1] - offs[ri]);
     const Status bad(Status::kCorruption, "bad metadata at row " + std::to_string(ri));
-    if (!data.empty()) {
-      Reader rr(data);
-      uint16_t count = 0;
-      if (!rr.u16(&count)) return bad;
-      for (uint16_t k = 0; k < count; ++k) {
-        uint16_t fid = 0;
-        uint8_t type = 0;
-        if (!rr.u16(&fid) || !rr.u8(&type) || fid >= schema.size()) return bad;
-        if (type != static_cast<uint8_t>(schema[fid].type)) return bad;
-        RowValue& v = row[fid];
-        v.has = true;
-        v.strs.clear();
-        switch (static_cast<FieldType>(type)) {
-          case FieldType::Int64: {
-            int64_t x = 0;
-            if (!rr.i64(&x)) return bad;
-            v.num = static_cast<double>(x);
-            break;
-          }
-          case FieldType::Float64: {
-            double x = 0;
-            if (!rr.f64(&x)) return bad;
-            v.num = x;
-            break;
-          }
-          case FieldType::Keyword: {
-            uint32_t len = 0;
-            std::string_view sv;
-            if (!rr.u32(&len) || !rr.bytes(len, &sv)) return bad;
-            v.strs.emplace_back(sv);
-            break;
-          }
-          case FieldType::KeywordList: {
-            uint32_t cnt = 0;
-            if (!rr.u32(&cnt) || cnt > rr.remaining() / 4) return bad;
-            for (uint32_t e = 0; e < cnt; ++e) {
-              uint32_t len = 0;
-              std::string_view sv;
-              if (!rr.u32(&len) || !rr.bytes(len, &sv)) return bad;
-              v.strs.emplace_back(sv);
-            }
-            break;
-          }
-          case FieldType::Bool: {
-            uint8_t b = 0;
-            if (!rr.u8(&b)) return bad;
-            v.b = b != 0;
-            break;
-          }
-          default: return bad;
-        }
-      }
-      if (rr.remaining() != 0) return bad;
-    }
+    if (!DecodeMetaRowValues(schema, data, &row)) return bad;
     const uint32_t r32 = static_cast<uint32_t>(ri);
     for (size_t f = 0; f < schema.size(); ++f) {
       const RowValue& v = row[f];
@@ -459,6 +381,373 @@ Status BuildColumns(const Schema& schema, uint64_t n, uint64_t words, std::strin
 }
 
 }  // namespace
+
+namespace {
+
+// ---- The log replay of Collection::Open (CollectionImpl::Recover step 5,
+// src/engine/collection_impl.cc:160-235; ApplyOp, :574-599).
+
+// Log files (src/storage/wal.h:27-37, src/storage/wal.cc): a 16-byte header ("VDBWAL01", u32
+// version 1, u32 0), then records [u32 crc32c][u32 payload length][u8 type: 1 upsert, 2 delete]
+// [u64 lsn][payload]; the crc covers everything after itself. Upsert payload: u64 id, u32 dim,
+// dim floats, u32 metadata length, the metadata row as EncodeMetaRow. Delete payload: u64 id.
+constexpr size_t kWalFileHeaderSize = 16, kWalRecordHeaderSize = 17;
+
+struct WalRecordView {
+  uint8_t type = 0;
+  uint64_t lsn = 0;
+  std::string_view payload;
+};
+
+bool TryParseWalRecord(std::string_view data, size_t pos, WalRecordView* rec, size_t* len) {
+  if (data.size() - pos < kWalRecordHeaderSize) return false;
+  const char* p = data.data() + pos;
+  const uint32_t plen = GetAt<uint32_t>(p, 4);
+  if (plen > data.size() - pos - kWalRecordHeaderSize) return false;
+  const uint8_t type = static_cast<uint8_t>(p[8]);
+  if (type != 1 && type != 2) return false;
+  if (Crc32c(p + 4, kWalRecordHeaderSize - 4 + plen) != GetAt<uint32_t>(p, 0)) return false;
+  rec->type = type;
+  rec->lsn = GetAt<uint64_t>(p, 9);
+  rec->payload = std::string_view(p + kWalRecordHeaderSize, plen);
+  *len = kWalRecordHeaderSize + plen;
+  return true;
+}
+
+// ParseWal (wal.cc): hands every valid record to cb in order. A bad record with no valid record at
+// any later offset is a torn tail (*torn); one followed by a valid record is corruption.
+Status ParseWalRecords(std::string_view data, const std::function<Status(const WalRecordView&)>& cb, bool* torn) {
+  *torn = false;
+  if (data.size() < kWalFileHeaderSize) {
+    *torn = !data.empty();
+    return Status::OK();
+  }
+  if (data.substr(0, 8) != "VDBWAL01" || GetAt<uint32_t>(data.data(), 8) != 1)
+    return Status(Status::kCorruption, "bad log file header");
+  size_t pos = kWalFileHeaderSize;
+  while (pos < data.size()) {
+    WalRecordView rec;
+    size_t len = 0;
+    if (TryParseWalRecord(data, pos, &rec, &len)) {
+      VDBGPU_RETURN_IF_ERROR(cb(rec));
+      pos += len;
+      continue;
+    }
+    for (size_t off = pos + 1; off + kWalRecordHeaderSize <= data.size(); ++off) {
+      WalRecordView later;
+      size_t later_len = 0;
+      if (TryParseWalRecord(data, off, &later, &later_len))
+        return Status(Status::kCorruption,
+                      "corrupt log record at offset " + std::to_string(pos) + " followed by valid records");
+    }
+    *torn = true;
+    break;
+  }
+  return Status::OK();
+}
+
+// "<prefix><digits><suffix>" -> the number (ParseWalFileName, ParseManifestFileName,
+// ParseSegmentDirName).
+bool ParseNumberedName(std::string_view name, std::string_view prefix, std::string_view suffix, uint64_t* num) {
+  if (name.size() <= prefix.size() + suffix.size() || name.substr(0, prefix.size()) != prefix ||
+      name.substr(name.size() - suffix.size()) != suffix)
+    return false;
+  uint64_t n = 0;
+  for (char ch : name.substr(prefix.size(), name.size() - prefix.size() - suffix.size())) {
+    if (ch < '0' || ch > '9') return false;
+    n = n * 10 + static_cast<uint64_t>(ch - '0');
+  }
+  *num = n;
+  return true;
+}
+
+std::vector<std::string> ListDir(const std::string& path) {
+  std::vector<std::string> names;
+  if (DIR* d = opendir(path.c_str())) {
+    while (const dirent* e = readdir(d)) {
+      const std::string n = e->d_name;
+      if (n != "." && n != "..") names.push_back(n);
+    }
+    closedir(d);
+  }
+  return names;
+}
+
+// One disk segment of the manifest, with its ids and delete bits once read.
+struct SegEntry {
+  uint32_t id = 0;
+  uint64_t rows = 0, lsn = 0;
+  std::string deletes_file, dir;
+  std::vector<uint64_t> ids;
+  std::vector<uint32_t> del;  // (rows + 31) / 32 words
+};
+
+Status LoadIdsAndDeletes(SegEntry* e) {
+  std::string idsf;
+  VDBGPU_RETURN_IF_ERROR(ReadFile(e->dir + "/ids.u64", &idsf));
+  std::string_view ids_p;
+  Status st = DecodeBlob(idsf, "VDBIDS01", &ids_p);
+  if (!st.ok()) return Status(Status::kCorruption, e->dir + "/ids.u64: " + st.message());
+  if (ids_p.size() != e->rows * 8) return Status(Status::kCorruption, e->dir + ": ids.u64 size mismatch");
+  e->ids.resize(e->rows);
+  if (e->rows > 0) std::memcpy(e->ids.data(), ids_p.data(), e->rows * 8);
+  e->del.assign((e->rows + 31) / 32, 0u);
+  // The persisted delete set (segment_reader.cc:101-116): a "VDBDEL01" blob named by the
+  // manifest entry's deletes_file.
+  if (!e->deletes_file.empty()) {
+    std::string delf;
+    VDBGPU_RETURN_IF_ERROR(ReadFile(e->dir + "/" + e->deletes_file, &delf));
+    std::string_view del_p;
+    st = DecodeBlob(delf, "VDBDEL01", &del_p);
+    if (!st.ok()) return Status(Status::kCorruption, e->dir + "/" + e->deletes_file + ": " + st.message());
+    st = DecodeDeleteSet(del_p, e->rows, &e->del);
+    if (!st.ok()) return Status(st.code(), e->dir + ": " + st.message());
+  }
+  return Status::OK();
+}
+
+// The mutable segment rebuilt from the logs (MutableSegment, src/engine/mutable_segment.h):
+// rows appended in log order, padded to pd floats, with their external ids, metadata rows and
+// delete bits.
+struct MutableRows {
+  uint64_t n = 0;
+  std::vector<float> rows;
+  std::vector<uint64_t> ids;
+  std::vector<std::string> meta;
+  std::vector<uint32_t> del;
+  // meta.bin's payload for these rows: u64 rows, u64 offsets[rows + 1], the rows.
+  std::string MetaPayload() const {
+    std::string out(8 * (n + 2), '\0');
+    std::memcpy(&out[0], &n, 8);
+    uint64_t off = 0;
+    for (uint64_t i = 0; i <= n; ++i) {
+      std::memcpy(&out[8 * (i + 1)], &off, 8);
+      if (i < n) off += meta[i].size();
+    }
+    for (const auto& m : meta) out += m;
+    return out;
+  }
+};
+
+constexpr uint64_t kMutableMaxRows = uint64_t{1} << 26;  // MutableSegment::kDefaultMaxRows
+
+// Replays the log records after flushed_lsn: the id map is rebuilt from the segments' live rows,
+// oldest segment first (Recover step 4), then each record is applied as ApplyOp does during
+// replay: a record older than the segment holding the id's current row leaves that row alone
+// (an upserted row is then appended deleted).
+Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, uint64_t flushed_lsn,
+                  const CollectionOptions& opt, std::vector<SegEntry>& segs, MutableRows* mut) {
+  struct Loc {
+    int64_t seg;  // index into segs, -1 = the mutable segment
+    uint32_t row;
+  };
+  std::unordered_map<uint64_t, Loc> ids;
+  std::vector<size_t> order(segs.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+  std::sort(order.begin(), order.end(), [&](size_t a, size_t b) {
+    return segs[a].lsn < segs[b].lsn || (segs[a].lsn == segs[b].lsn && segs[a].id < segs[b].id);
+  });
+  for (size_t i : order)
+    for (uint64_t r = 0; r < segs[i].rows; ++r)
+      if (!(segs[i].del[r / 32] >> (r % 32) & 1u)) ids[segs[i].ids[r]] = Loc{static_cast<int64_t>(i), static_cast<uint32_t>(r)};
+  auto mark = [&](const Loc& l) {
+    std::vector<uint32_t>& d = l.seg < 0 ? mut->del : segs[static_cast<size_t>(l.seg)].del;
+    d[l.row / 32] |= 1u << (l.row % 32);
+  };
+  const uint32_t pd = opt.pd;
+  std::vector<RowValue> row(opt.schema.size());
+  uint64_t expected = flushed_lsn + 1;
+  for (size_t li = 0; li < logs.size(); ++li) {
+    const std::string& path = logs[li].first;
+    bool torn = false;
+    Status ps = ParseWalRecords(logs[li].second, [&](const WalRecordView& rec) -> Status {
+      if (rec.lsn <= flushed_lsn) return Status::OK();
+      if (rec.lsn != expected)
+        return Status(Status::kCorruption, "log sequence gap: expected LSN " + std::to_string(expected) +
+                                               ", found " + std::to_string(rec.lsn));
+      ++expected;
+      Reader r(rec.payload);
+      uint64_t id = 0;
+      if (rec.type == 2) {
+        if (!r.u64(&id) || r.remaining() != 0)
+          return Status(Status::kCorruption, "bad delete record at LSN " + std::to_string(rec.lsn));
+      } else {
+        uint32_t dim = 0, mlen = 0;
+        std::string_view vec, meta;
+        if (!r.u64(&id) || !r.u32(&dim) || dim == 0 || !r.bytes(static_cast<size_t>(dim) * 4, &vec) ||
+            !r.u32(&mlen) || !r.bytes(mlen, &meta) || r.remaining() != 0 || dim != opt.dim)
+          return Status(Status::kCorruption, "bad upsert record at LSN " + std::to_string(rec.lsn));
+        if (!DecodeMetaRowValues(opt.schema, meta, &row))
+          return Status(Status::kCorruption, "bad metadata at LSN " + std::to_string(rec.lsn));
+        if (mut->n >= kMutableMaxRows) return Status(Status::kResourceExhausted, "mutable segment is full");
+        mut->rows.resize((mut->n + 1) * pd, 0.0f);
+        std::memcpy(mut->rows.data() + mut->n * pd, vec.data(), vec.size());
+        mut->ids.push_back(id);
+        mut->meta.emplace_back(meta);
+        if (mut->n % 32 == 0) mut->del.push_back(0u);
+      }
+      auto it = ids.find(id);
+      const bool old_is_newer =
+          it != ids.end() && it->second.seg >= 0 && segs[static_cast<size_t>(it->second.seg)].lsn >= rec.lsn;
+      if (it != ids.end() && !old_is_newer) mark(it->second);
+      if (rec.type == 2) {
+        if (it != ids.end() && !old_is_newer) ids.erase(it);
+        return Status::OK();
+      }
+      const Loc here{-1, static_cast<uint32_t>(mut->n)};
+      ++mut->n;
+      if (old_is_newer) {
+        mark(here);
+      } else {
+        ids[id] = here;
+      }
+      return Status::OK();
+    }, &torn);
+    if (!ps.ok()) return Status(ps.code(), path + ": " + ps.message());
+    // A torn tail is only acceptable at the end of the newest log (Open truncates it there; this
+    // loader reads the directory without changing it).
+    if (torn && li + 1 != logs.size())
+      return Status(Status::kCorruption, path + ": damaged record in a log that is not the newest");
+  }
+  return Status::OK();
+}
+
+}  // namespace
+
+Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
+                           std::unique_ptr<GpuCollection>* out) {
+  if (nshards == 0 || shard >= nshards) return Status(Status::kInvalidArgument, "bad shard");
+  // ReadCurrentManifest (src/storage/manifest.cc:116-127).
+  std::string current;
+  VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/CURRENT", &current));
+  while (!current.empty() && (current.back() == '\n' || current.back() == '\r' || current.back() == ' '))
+    current.pop_back();
+  if (current.rfind("MANIFEST-", 0) != 0) return Status(Status::kCorruption, "bad CURRENT file");
+  std::string mf;
+  VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/" + current, &mf));
+  std::string_view payload;
+  VDBGPU_RETURN_IF_ERROR(DecodeBlob(mf, "VDBMAN01", &payload));
+  JsonValue j;
+  if (!ParseJson(payload, &j) || !j.is_object()) return Status(Status::kCorruption, "manifest is not valid JSON");
+  const JsonValue* fv = j.get("format_version");
+  if (fv == nullptr || !fv->is_integer() || fv->number() != 1)
+    return Status(Status::kCorruption, "unknown manifest version");
+  const JsonValue* opts = j.get("options");
+  const JsonValue* segs = j.get("segments");
+  if (opts == nullptr || segs == nullptr || !segs->is_array()) return Status(Status::kCorruption, "bad manifest");
+  auto u64_of = [&](const char* key) -> uint64_t {
+    const JsonValue* v = j.get(key);
+    return v != nullptr && v->is_integer() ? static_cast<uint64_t>(v->number()) : 0;
+  };
+  const uint64_t flushed_lsn = u64_of("flushed_lsn"), wal_log_number = u64_of("wal_log_number");
+  uint64_t next = u64_of("next_file_number");
+  auto c = std::make_unique<GpuCollection>();
+  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, &c->opt_));
+  const uint32_t pd = c->opt_.pd;
+  std::vector<SegEntry> entries(segs->arr.size());
+  for (size_t i = 0; i < segs->arr.size(); ++i) {
+    const JsonValue& s = segs->arr[i];
+    const JsonValue* idv = s.get("id");
+    const JsonValue* rv = s.get("rows");
+    const JsonValue* lv = s.get("lsn");
+    const JsonValue* dfv = s.get("deletes_file");
+    if (idv == nullptr || rv == nullptr || !idv->is_integer() || !rv->is_integer() ||
+        (dfv != nullptr && !dfv->is_string()) || (lv != nullptr && !lv->is_integer()))
+      return Status(Status::kCorruption, "bad manifest segment entry");
+    SegEntry& e = entries[i];
+    e.id = static_cast<uint32_t>(idv->number());
+    e.rows = static_cast<uint64_t>(rv->number());
+    e.lsn = lv != nullptr ? static_cast<uint64_t>(lv->number()) : 0;
+    if (dfv != nullptr) e.deletes_file = dfv->s;
+    char name[32];
+    std::snprintf(name, sizeof(name), "seg-%06u", e.id);
+    e.dir = path + "/segments/" + name;
+  }
+  // The next file number (Recover steps 1, 2 and 5): past every manifest, segment directory and
+  // log; the mutable segment takes it.
+  uint64_t num = 0;
+  for (const auto& n : ListDir(path))
+    if (ParseNumberedName(n, "MANIFEST-", "", &num)) next = std::max(next, num + 1);
+  for (const auto& n : ListDir(path + "/segments"))
+    if (ParseNumberedName(n, "seg-", "", &num)) next = std::max(next, num + 1);
+  std::vector<std::pair<uint64_t, std::string>> lognames;
+  for (const auto& n : ListDir(path + "/wal")) {
+    if (!ParseNumberedName(n, "", ".log", &num)) continue;
+    next = std::max(next, num + 1);
+    if (num >= wal_log_number) lognames.emplace_back(num, path + "/wal/" + n);
+  }
+  std::sort(lognames.begin(), lognames.end());
+  std::vector<std::pair<std::string, std::string>> logs;
+  bool any_records = false;
+  for (const auto& [n, p] : lognames) {
+    std::string data;
+    VDBGPU_RETURN_IF_ERROR(ReadFile(p, &data));
+    any_records |= data.size() > kWalFileHeaderSize;
+    logs.emplace_back(p, std::move(data));
+  }
+  // Ids and delete sets: of this shard's segments, and of every segment when the logs hold
+  // records (an upsert or delete may name a row of any segment).
+  for (size_t i = 0; i < entries.size(); ++i)
+    if (any_records || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(LoadIdsAndDeletes(&entries[i]));
+  MutableRows mut;
+  if (any_records) VDBGPU_RETURN_IF_ERROR(ReplayLogs(logs, flushed_lsn, c->opt_, entries, &mut));
+
+  for (size_t i = 0; i < entries.size(); ++i) {
+    if (i % nshards != shard) continue;
+    const SegEntry& e = entries[i];
+    const std::string& dir = e.dir;
+    // vectors.f32 header checks of Segment::Open (segment_reader.cc:36-51).
+    std::string vec;
+    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/vectors.f32", &vec));
+    if (vec.size() < kSegmentHeaderSize) return Status(Status::kCorruption, dir + ": vectors.f32 shorter than its header");
+    const char* h = vec.data();
+    if (std::memcmp(h, "VDBSEG01", 8) != 0) return Status(Status::kCorruption, dir + ": bad magic");
+    if (GetAt<uint32_t>(h, kSegmentHeaderSize - 4) != Crc32c(h, kSegmentHeaderSize - 4))
+      return Status(Status::kCorruption, dir + ": header checksum mismatch");
+    const uint64_t hrows = GetAt<uint64_t>(h, 16);
+    const uint64_t data_len = GetAt<uint64_t>(h, 40);
+    if (GetAt<uint32_t>(h, 8) != 1 || GetAt<uint32_t>(h, 12) != static_cast<uint32_t>(c->opt_.metric) ||
+        hrows != e.rows || GetAt<uint32_t>(h, 24) != c->opt_.dim || GetAt<uint32_t>(h, 28) != pd ||
+        GetAt<uint64_t>(h, 32) != kSegmentHeaderSize || data_len != e.rows * pd * sizeof(float) ||
+        vec.size() < kSegmentHeaderSize + data_len)
+      return Status(Status::kCorruption, dir + ": header does not match the manifest");
+    std::string metaf, indexf;
+    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/meta.bin", &metaf));
+    VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/" + IndexFileName(c->opt_.index_type), &indexf));
+    std::string_view meta_p;
+    Status st = DecodeBlob(metaf, "VDBMETA1", &meta_p);
+    if (!st.ok()) return Status(Status::kCorruption, dir + "/meta.bin: " + st.message());
+    // Part 0 of the merge is the mutable segment (collection_impl.cc:1056-1059); disk segments
+    // follow in manifest order.
+    st = c->AddSegment(ctx, e.id, static_cast<uint32_t>(i + 1), reinterpret_cast<const float*>(h + kSegmentHeaderSize),
+                       e.rows, e.ids.data(), meta_p, indexf);
+    if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
+    bool any = false;
+    for (uint32_t w : e.del) any |= w != 0;
+    if (any) {
+      st = c->SetDeleted(ctx, e.id, e.del.data());
+      if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
+    }
+  }
+  // The mutable segment lives on shard 0 and is searched exhaustively (SearchMutable,
+  // planner.cc:131-149) through a flat index over its rows.
+  if (shard == 0 && mut.n > 0) {
+    std::string flat = "VDBFLAT1";
+    const uint32_t crc = Crc32c(flat.data(), flat.size());
+    flat.append(reinterpret_cast<const char*>(&crc), 4);
+    const std::string meta = mut.MetaPayload();
+    const uint32_t mid = static_cast<uint32_t>(next);
+    VDBGPU_RETURN_IF_ERROR(c->AddSegment(ctx, mid, 0, mut.rows.data(), mut.n, mut.ids.data(), meta, flat));
+    for (auto& s : c->segs_)
+      if (s->ordinal == 0) s->is_mutable = true;
+    bool any = false;
+    for (uint32_t w : mut.del) any |= w != 0;
+    if (any) VDBGPU_RETURN_IF_ERROR(c->SetDeleted(ctx, mid, mut.del.data()));
+  }
+  c->total_segments_ = static_cast<uint32_t>(entries.size() + (mut.n > 0 ? 1 : 0));
+  *out = std::move(c);
+  return Status::OK();
+}
 
 Status GpuCollection::AddSegment(Context& ctx, uint32_t id, uint32_t ordinal, const float* rows, uint64_t n,
                                  const uint64_t* ids, std::string_view meta, std::string_view index_file) {
@@ -878,11 +1167,12 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
       for (size_t s = 0; s < S; ++s) {
         PartExplain& e = (*r.explain)[q][s];
         e.segment_id = segs_[s]->id;
+        e.is_mutable = segs_[s]->is_mutable;
         e.live_rows = segs_[s]->rows - segs_[s]->deleted;
         e.strategy = b.strat[s * (b.F + 1) + gof[i]];
         e.matches = b.matches[s * (b.F + 1) + gof[i]];
         if (sh[s * b.nq + i] != 0 && e.strategy == "filtered_index") e.strategy = "filtered_index+exact_fallback";
-        e.dc = dc[s * b.nq + i];
+        e.dc = e.is_mutable ? e.matches : dc[s * b.nq + i];  // SearchMutable scores every match
         uint64_t res = 0;
         for (uint32_t j = 0; j < b.k; ++j) res += keys[(s * b.nq + i) * b.k + j] != ~0ull ? 1 : 0;
         e.results = res;
@@ -1150,7 +1440,7 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
   // ---- unfiltered queries: every segment's index (planner.cc:54-62).
   for (size_t s = 0; s < S && b.goff[b.F + 1] > b.goff[b.F]; ++s) {
     GpuSegment& seg = *segs_[s];
-    b.strat[s * G + b.F] = "index";
+    b.strat[s * G + b.F] = seg.is_mutable ? "scan" : "index";
     b.matches[s * G + b.F] = seg.rows - seg.deleted;
     VDBGPU_RETURN_IF_ERROR(RunIndex(ctx, b, s, b.F, b.k, p, seg.deleted > 0 ? seg.live.as<uint32_t>() : nullptr,
                                     nullptr, 0, nullptr));
@@ -1192,6 +1482,7 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
                       : 2;
         }
         int pl = m == 0 ? kEmpty : (strat == 1 ? kPre : (strat == 2 ? kGraph : kPost));
+        if (seg.is_mutable) pl = m == 0 ? kEmpty : kPre;  // SearchMutable: always exhaustive
         if (pl == kGraph && p.strategy == 0) {
           const double sc = std::max(sel, 1e-9);
           pparams[pi].nprobe = std::max<uint64_t>(
@@ -1202,7 +1493,8 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
         if (pl == kPre) stats_[1] += m * (b.goff[fq[fi] + 1] - b.goff[fq[fi]]);
         const size_t gi = (s0 + si) * G + fq[fi];
         b.matches[gi] = m;
-        b.strat[gi] = pl == kEmpty ? "empty" : pl == kPre ? "prefilter_exact" : pl == kGraph ? "filtered_index" : "post_filter";
+        b.strat[gi] = seg.is_mutable ? "scan_filter"
+                      : pl == kEmpty ? "empty" : pl == kPre ? "prefilter_exact" : pl == kGraph ? "filtered_index" : "post_filter";
       }
     }
 

@@ -207,7 +207,12 @@ typedef struct vdbgpu_hit {
  * the segments whose manifest position % nshards == shard are loaded (one shard per GPU).
  * A segment's persisted delete set (the manifest entry's deletes_file, a "VDBDEL01" blob holding a
  * portable roaring bitmap) is loaded as its delete bits; a value at or past the segment's rows is
- * VDBGPU_CORRUPTION, as Segment::Open. Later deletes go through vdbgpu_collection_set_deleted. */
+ * VDBGPU_CORRUPTION, as Segment::Open. The logs (wal/<n>.log from the manifest's wal_log_number)
+ * are replayed as recovery does (collection_impl.cc:160-235): records after flushed_lsn delete
+ * the old rows of their ids and append upserts to the mutable segment, which shard 0 holds and
+ * searches exhaustively (merge part 0; disk segments are parts 1..n in manifest order). Damaged
+ * logs give recovery's errors (VDBGPU_CORRUPTION); a torn tail of the newest log is ignored. The
+ * directory is not modified. Later deletes go through vdbgpu_collection_set_deleted. */
 VDBGPU_API int vdbgpu_collection_open(vdbgpu_ctx* ctx, const char* path, uint32_t shard,
                                       uint32_t nshards, vdbgpu_collection** out);
 
@@ -276,8 +281,9 @@ VDBGPU_API int vdbgpu_collection_search_grouped(vdbgpu_collection* c, const floa
  * bitmaps, the index searches, and the rest of the call. enable: 1 / 0 turns the index-search count on / off, -1 leaves it. Returns the count written. */
 VDBGPU_API int vdbgpu_collection_stats(vdbgpu_collection* c, int enable, uint64_t* out, int cap);
 
-/* Collection::Search with explain for one query: JSON array with one object per local disk
- * segment {"id", "strategy", "matches", "live_rows", "distance_computations", "results"}
+/* Collection::Search with explain for one query: JSON array with one object per local segment,
+ * the mutable segment first {"id", "kind" ("mutable" / "disk"), "strategy", "matches",
+ * "live_rows", "distance_computations", "results"}
  * (SegmentExplain, include/vdb/collection.h:45-58). Returns VDBGPU_RESOURCE_EXHAUSTED when cap
  * is too small. */
 VDBGPU_API int vdbgpu_collection_explain(vdbgpu_collection* c, const float* query, uint32_t k,

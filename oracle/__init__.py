@@ -214,10 +214,14 @@ def _engine_lib(lib_path: str = REF_ENGINE_LIB):
     sig = {
         "ref_coll_last_error": (ctypes.c_char_p, []),
         "ref_coll_create": (_P, [ctypes.c_char_p, ctypes.c_char_p, ci]),
+        "ref_coll_open": (_P, [ctypes.c_char_p, ci]),
         "ref_coll_free": (None, [_P]),
         "ref_coll_bulk_load": (ci, [_P, _P, _P, c64, _P, _P, c32]),
         "ref_coll_bulk_load_json": (ci, [_P, _P, _P, c64, ctypes.c_char_p]),
         "ref_coll_remove_flush": (ci, [_P, _P, c64, _P, _P, c64, _P]),
+        "ref_coll_upsert_json": (ci, [_P, _P, _P, c64, ctypes.c_char_p]),
+        "ref_coll_remove": (ci, [_P, _P, c64, _P]),
+        "ref_coll_flush": (ci, [_P]),
         "ref_coll_search_batch": (ci, [_P, _P, c64, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, _P, _P]),
         "ref_coll_explain": (ci, [_P, _P, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, ctypes.c_char_p,
                                   ctypes.c_size_t]),
@@ -271,6 +275,23 @@ class RefCollection:
         if not self.h:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
 
+    @classmethod
+    def open(cls, path: str, threads: int = 0, lib_path: str = REF_ENGINE_LIB) -> "RefCollection":
+        """Collection::Open of an existing directory (recovery replays its logs)."""
+        self = cls.__new__(cls)
+        self.l = _engine_lib(lib_path)
+        self.path = path
+        self.h = self.l.ref_coll_open(path.encode(), threads)
+        if not self.h:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+        import json
+        with open(os.path.join(path, "CURRENT")) as f:
+            cur = f.read().strip()
+        with open(os.path.join(path, cur), "rb") as f:
+            opts = json.loads(f.read()[24:])["options"]
+        self.dim, self.schema = opts["dim"], opts["schema"]
+        return self
+
     def bulk_load(self, ids: np.ndarray, vectors: np.ndarray, years=None, tags=None, metadata=None):
         """One on-disk segment. Metadata either as (years int64, tags uint32 word ids with
         UINT32_MAX = unused, stored as keywords "w<id>") or as a list of dicts."""
@@ -286,6 +307,28 @@ class RefCollection:
                                            _ptr(None if years is None else np.ascontiguousarray(years, np.int64)),
                                            _ptr(None if tags is None else np.ascontiguousarray(tags, np.uint32)), mt)
         if rc != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+
+    def upsert(self, ids: np.ndarray, vectors: np.ndarray, metadata=None):
+        """Collection::UpsertBatch (one log record per row); metadata a list of dicts or None."""
+        import json
+        v = np.ascontiguousarray(vectors[:, :self.dim], dtype=np.float32)
+        ids = np.ascontiguousarray(ids, dtype=np.uint64)
+        rc = self.l.ref_coll_upsert_json(self.h, _ptr(ids), _ptr(v), ids.size,
+                                         None if metadata is None else json.dumps(metadata).encode())
+        if rc != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+
+    def remove(self, ids: np.ndarray) -> int:
+        """Collection::RemoveBatch; returns how many of ids were live."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint64)
+        removed = np.zeros(1, dtype=np.uint64)
+        if self.l.ref_coll_remove(self.h, _ptr(ids), ids.size, _ptr(removed)) != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+        return int(removed[0])
+
+    def flush(self):
+        if self.l.ref_coll_flush(self.h) != 0:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
 
     def remove_flush(self, ids: np.ndarray, up_ids: np.ndarray, up_vectors: np.ndarray) -> int:

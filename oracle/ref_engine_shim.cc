@@ -66,6 +66,24 @@ ref_coll* ref_coll_create(const char* path, const char* options_json, int thread
   return h;
 }
 
+// Collection::Open of an existing directory (crash recovery: the logs are replayed into the
+// mutable segment), without background flushes or compactions.
+ref_coll* ref_coll_open(const char* path, int threads) {
+  vdb::OpenOptions oo;
+  oo.num_threads = static_cast<size_t>(threads);
+  oo.auto_compact = false;
+  oo.auto_flush = false;
+  auto c = vdb::Collection::Open(path, oo);
+  if (!c.ok()) {
+    g_err = c.status().ToString();
+    return nullptr;
+  }
+  auto* h = new ref_coll;
+  h->c = std::move(c).value();
+  h->dim = h->c->options().dim;
+  return h;
+}
+
 void ref_coll_free(ref_coll* h) {
   if (h == nullptr) return;
   if (h->c) (void)h->c->Close();
@@ -118,6 +136,56 @@ int ref_coll_bulk_load_json(ref_coll* h, const uint64_t* ids, const float* vecto
     }
   }
   vdb::Status s = h->c->BulkLoad(ids, vectors, n, meta_json != nullptr ? &md : nullptr);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  return 0;
+}
+
+// Collection::UpsertBatch of n rows with metadata as ref_coll_bulk_load_json (null = none): one
+// log record per row (src/engine/collection_impl.cc:460-540).
+int ref_coll_upsert_json(ref_coll* h, const uint64_t* ids, const float* vectors, uint64_t n,
+                         const char* meta_json) {
+  std::vector<vdb::Metadata> md;
+  if (meta_json != nullptr) {
+    auto j = nlohmann::json::parse(meta_json, nullptr, false);
+    if (j.is_discarded() || !j.is_array() || j.size() != n) {
+      g_err = "metadata must be a JSON array with one entry per row";
+      return 3;
+    }
+    md.resize(n);
+    for (uint64_t i = 0; i < n; ++i) {
+      vdb::Status s = vdb::MetadataFromJson(j[i], h->c->options().schema, &md[i]);
+      if (!s.ok()) {
+        g_err = s.ToString();
+        return static_cast<int>(s.code());
+      }
+    }
+  }
+  vdb::Status s = h->c->UpsertBatch(ids, vectors, n, meta_json != nullptr ? &md : nullptr);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  return 0;
+}
+
+// Collection::RemoveBatch; *removed = how many ids were live.
+int ref_coll_remove(ref_coll* h, const uint64_t* ids, uint64_t n, uint64_t* removed) {
+  size_t r = 0;
+  vdb::Status s = h->c->RemoveBatch(ids, n, &r);
+  if (!s.ok()) {
+    g_err = s.ToString();
+    return static_cast<int>(s.code());
+  }
+  if (removed != nullptr) *removed = r;
+  return 0;
+}
+
+// Collection::Flush (synchronous).
+int ref_coll_flush(ref_coll* h) {
+  vdb::Status s = h->c->Flush();
   if (!s.ok()) {
     g_err = s.ToString();
     return static_cast<int>(s.code());

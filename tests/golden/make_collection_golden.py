@@ -218,8 +218,77 @@ def make_deletes(name="coll_deletes", dim=4, seed=14, nq=32):
     print("wrote", name, os.path.getsize(os.path.join(OUT, name + ".npz")), "bytes")
 
 
+def make_mutable(name="coll_mutable", dim=24, seed=15, nq=24):
+    """A collection left with an unflushed write-ahead log, as after a crash or a close without
+    Flush. Disk segments: A (bulk load), B (the first upserts, flushed, with A's superseded rows as
+    a persisted delete set) and D (a later bulk load). The log then holds upserts of new ids, of
+    A's and B's ids, of one id twice, removals of disk rows, log rows and absent ids, and an id
+    upserted and removed before D's bulk load brought it back (D's row is newer than both
+    records). The fixture holds the directory as closed; searches and explains (mutable part
+    first) come from the reference's Collection::Open of it, which replays the log."""
+    rng = np.random.default_rng(seed)
+    tmp = tempfile.mkdtemp()
+    path = os.path.join(tmp, "coll")
+    coll = oracle.RefCollection(path, dim, metric="cosine", index={"type": "hnsw", "M": 8, "ef_construction": 64},
+                                schema=SCHEMA, threads=4)
+    centres = rng.standard_normal((12, dim)).astype(np.float32)
+    ids_a = np.arange(1000, 2500, dtype=np.uint64) * 3
+    coll.bulk_load(ids_a, rows_mixture(rng, ids_a.size, dim, centres), metadata=metadata(rng, ids_a.size))
+    ids_b = np.concatenate([np.arange(5000, 5300, dtype=np.uint64) * 3, ids_a[rng.choice(1500, 50, replace=False)]])
+    coll.upsert(ids_b, rows_mixture(rng, ids_b.size, dim, centres), metadata(rng, ids_b.size))
+    coll.flush()
+    new = np.arange(9000, 9200, dtype=np.uint64) * 3
+    again = new[:5]  # upserted twice in the log
+    ups = np.concatenate([new, ids_a[rng.choice(1500, 30, replace=False)], ids_b[rng.choice(350, 20, replace=False)],
+                          again])
+    coll.upsert(ups, rows_mixture(rng, ups.size, dim, centres), metadata(rng, ups.size))
+    gone = np.concatenate([ids_a[rng.choice(1500, 40, replace=False)], ids_b[rng.choice(350, 15, replace=False)],
+                           new[rng.choice(200, 25, replace=False)], np.array([1, 2], np.uint64)])
+    removed = coll.remove(gone)
+    x = np.array([777777], np.uint64)
+    coll.upsert(x, rows_mixture(rng, 1, dim, centres), metadata(rng, 1))
+    coll.remove(x)
+    ids_d = np.concatenate([x, np.arange(20000, 20299, dtype=np.uint64) * 3])
+    coll.bulk_load(ids_d, rows_mixture(rng, ids_d.size, dim, centres), metadata=metadata(rng, ids_d.size))
+    last = np.array([900001, 900002, 900003], np.uint64)  # new ids: the log ends with three upserts
+    coll.upsert(last, rows_mixture(rng, 3, dim, centres), [None, {"year": 2024}, {"tags": []}])
+    coll.close()
+    files = pack_dir_with_logs(path)  # the directory as the loader sees it
+    coll = oracle.RefCollection.open(path, threads=4)  # the reference's own recovery of it
+    q = rows_mixture(rng, nq, dim, centres)
+    filters = FILTERS[:6] + [FILTERS[11], FILTERS[13]]
+    out = {"queries": q, "dim": np.array(dim), "filters": np.array([json.dumps(f) for f in filters]),
+           "schema": np.array(json.dumps(SCHEMA)), "cases": np.array([json.dumps(c) for c in CASES]),
+           "removed_live": np.array(removed)}
+    for ci, (strategy, thr, ef, nprobe, k, alpha) in enumerate(CASES):
+        for fi, f in enumerate(filters + [None]):
+            ids, d = coll.search(q, k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
+                                 prefilter_threshold=thr, post_filter_alpha=alpha)
+            out[f"ids_{ci}_{fi}"] = ids
+            out[f"dist_{ci}_{fi}"] = d
+            ex = coll.explain(q[0], k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
+                              prefilter_threshold=thr, post_filter_alpha=alpha)
+            out[f"explain_{ci}_{fi}"] = np.array(json.dumps(ex))
+    coll.close()
+    out.update(files)
+    shutil.rmtree(tmp)
+    np.savez_compressed(os.path.join(OUT, name + ".npz"), **out)
+    print("wrote", name, os.path.getsize(os.path.join(OUT, name + ".npz")), "bytes")
+
+
+def pack_dir_with_logs(path):
+    files = {}
+    for dp, _, fns in os.walk(path):
+        for fn in fns:
+            full = os.path.join(dp, fn)
+            with open(full, "rb") as f:
+                files["file:" + os.path.relpath(full, path)] = np.frombuffer(f.read(), dtype=np.uint8)
+    return files
+
+
 def main():
     oracle.build(ref=True)
+    make_mutable()
     make_deletes()
     parse_golden()
     make("coll_hnsw", 48, "cosine", {"type": "hnsw", "M": 8, "ef_construction": 64}, [900, 1300, 700], seed=11)
