@@ -653,6 +653,25 @@ int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, uint64_t nr
 
 void vdbgpu_buffer_free(void* p) { std::free(p); }
 
+int vdbgpu_collection_inspect(const char* path, char* out_json, size_t cap) {
+  if (path == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  std::string text;
+  Status s = vdbgpu::GpuCollection::Inspect(path, &text);
+  int rc = VDBGPU_OK;
+  if (!s.ok()) {
+    rc = static_cast<int>(s.code());
+    text = s.message();
+  } else if (out_json != nullptr && text.size() + 1 > cap) {
+    rc = VDBGPU_RESOURCE_EXHAUSTED;
+  }
+  if (out_json != nullptr && cap > 0) {
+    const size_t n = std::min(cap - 1, text.size());
+    std::memcpy(out_json, text.data(), n);
+    out_json[n] = '\0';
+  }
+  return rc;
+}
+
 int vdbgpu_filter_describe(const char* schema_json, const char* filter_json, char* out, size_t cap) {
   if (schema_json == nullptr || filter_json == nullptr) return VDBGPU_INVALID_ARGUMENT;
   std::string text;

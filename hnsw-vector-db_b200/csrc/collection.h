@@ -71,6 +71,10 @@ class GpuCollection {
   // mutable segment.
   static Status Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
                      std::unique_ptr<GpuCollection>* out);
+  // The same recovery on the host only, reported as Collection::Stats (collection_impl.cc:
+  // 1168-1225): JSON {live_rows, total_rows, deleted_rows, last_lsn, flushed_lsn,
+  // recovery_records, segments: [{id, kind, index, rows, deleted, lsn}]}, the mutable segment first.
+  static Status Inspect(const std::string& path, std::string* json);
   // An empty collection with the reference's options JSON (engine/options_json.cc), to which
   // segments are added from their files' contents.
   static Status Create(std::string_view options_json, std::unique_ptr<GpuCollection>* out);

@@ -511,6 +511,9 @@ Status LoadIdsAndDeletes(SegEntry* e) {
 // delete bits.
 struct MutableRows {
   uint64_t n = 0;
+  uint64_t max_lsn = 0;   // of the rows appended (MutableSegment::max_lsn)
+  uint64_t last_lsn = 0;  // the collection's after replay
+  uint64_t records = 0;   // records replayed
   std::vector<float> rows;
   std::vector<uint64_t> ids;
   std::vector<std::string> meta;
@@ -566,6 +569,8 @@ Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, 
         return Status(Status::kCorruption, "log sequence gap: expected LSN " + std::to_string(expected) +
                                                ", found " + std::to_string(rec.lsn));
       ++expected;
+      ++mut->records;
+      mut->last_lsn = std::max(mut->last_lsn, rec.lsn);
       Reader r(rec.payload);
       uint64_t id = 0;
       if (rec.type == 2) {
@@ -584,6 +589,7 @@ Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, 
         std::memcpy(mut->rows.data() + mut->n * pd, vec.data(), vec.size());
         mut->ids.push_back(id);
         mut->meta.emplace_back(meta);
+        mut->max_lsn = std::max(mut->max_lsn, rec.lsn);
         if (mut->n % 32 == 0) mut->del.push_back(0u);
       }
       auto it = ids.find(id);
@@ -614,9 +620,21 @@ Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, 
 
 }  // namespace
 
-Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
-                           std::unique_ptr<GpuCollection>* out) {
-  if (nshards == 0 || shard >= nshards) return Status(Status::kInvalidArgument, "bad shard");
+namespace {
+
+// The directory as Collection::Open recovers it (CollectionImpl::Recover, collection_impl.cc:
+// 76-235), on the host: options, segments with their ids and delete bits (those of shard `shard`
+// of nshards, or of every segment when the logs hold records or `all`), and the mutable segment
+// replayed from the logs. Reads only.
+struct RecoveredDir {
+  CollectionOptions opt;
+  std::vector<SegEntry> segs;
+  MutableRows mut;
+  uint64_t flushed_lsn = 0;
+  uint32_t mutable_id = 0;
+};
+
+Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, bool all, RecoveredDir* d) {
   // ReadCurrentManifest (src/storage/manifest.cc:116-127).
   std::string current;
   VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/CURRENT", &current));
@@ -641,10 +659,10 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
   };
   const uint64_t flushed_lsn = u64_of("flushed_lsn"), wal_log_number = u64_of("wal_log_number");
   uint64_t next = u64_of("next_file_number");
-  auto c = std::make_unique<GpuCollection>();
-  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, &c->opt_));
-  const uint32_t pd = c->opt_.pd;
-  std::vector<SegEntry> entries(segs->arr.size());
+  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, &d->opt));
+  d->flushed_lsn = flushed_lsn;
+  std::vector<SegEntry>& entries = d->segs;
+  entries.resize(segs->arr.size());
   for (size_t i = 0; i < segs->arr.size(); ++i) {
     const JsonValue& s = segs->arr[i];
     const JsonValue* idv = s.get("id");
@@ -688,9 +706,26 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
   // Ids and delete sets: of this shard's segments, and of every segment when the logs hold
   // records (an upsert or delete may name a row of any segment).
   for (size_t i = 0; i < entries.size(); ++i)
-    if (any_records || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(LoadIdsAndDeletes(&entries[i]));
-  MutableRows mut;
-  if (any_records) VDBGPU_RETURN_IF_ERROR(ReplayLogs(logs, flushed_lsn, c->opt_, entries, &mut));
+    if (all || any_records || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(LoadIdsAndDeletes(&entries[i]));
+  d->mut.last_lsn = flushed_lsn;
+  for (const SegEntry& e : entries) d->mut.last_lsn = std::max(d->mut.last_lsn, e.lsn);
+  if (any_records) VDBGPU_RETURN_IF_ERROR(ReplayLogs(logs, flushed_lsn, d->opt, entries, &d->mut));
+  d->mutable_id = static_cast<uint32_t>(next);
+  return Status::OK();
+}
+
+}  // namespace
+
+Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
+                           std::unique_ptr<GpuCollection>* out) {
+  if (nshards == 0 || shard >= nshards) return Status(Status::kInvalidArgument, "bad shard");
+  RecoveredDir d;
+  VDBGPU_RETURN_IF_ERROR(RecoverDir(path, shard, nshards, false, &d));
+  auto c = std::make_unique<GpuCollection>();
+  c->opt_ = d.opt;
+  const uint32_t pd = c->opt_.pd;
+  std::vector<SegEntry>& entries = d.segs;
+  MutableRows& mut = d.mut;
 
   for (size_t i = 0; i < entries.size(); ++i) {
     if (i % nshards != shard) continue;
@@ -736,7 +771,7 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
     const uint32_t crc = Crc32c(flat.data(), flat.size());
     flat.append(reinterpret_cast<const char*>(&crc), 4);
     const std::string meta = mut.MetaPayload();
-    const uint32_t mid = static_cast<uint32_t>(next);
+    const uint32_t mid = d.mutable_id;
     VDBGPU_RETURN_IF_ERROR(c->AddSegment(ctx, mid, 0, mut.rows.data(), mut.n, mut.ids.data(), meta, flat));
     for (auto& s : c->segs_)
       if (s->ordinal == 0) s->is_mutable = true;
@@ -746,6 +781,38 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
   }
   c->total_segments_ = static_cast<uint32_t>(entries.size() + (mut.n > 0 ? 1 : 0));
   *out = std::move(c);
+  return Status::OK();
+}
+
+
+Status GpuCollection::Inspect(const std::string& path, std::string* json) {
+  RecoveredDir d;
+  VDBGPU_RETURN_IF_ERROR(RecoverDir(path, 0, 1, true, &d));
+  auto count = [](const std::vector<uint32_t>& bits, uint64_t rows) {
+    uint64_t c = 0;
+    for (uint64_t w = 0; w < bits.size(); ++w) {
+      const uint32_t valid = w < rows / 32 ? 0xFFFFFFFFu : (w == rows / 32 ? (1u << (rows % 32)) - 1u : 0u);
+      c += static_cast<uint64_t>(__builtin_popcount(bits[w] & valid));
+    }
+    return c;
+  };
+  std::string segs;
+  uint64_t total = 0, deleted = 0;
+  auto add = [&](uint32_t id, const char* kind, const std::string& index, uint64_t rows, uint64_t del, uint64_t lsn) {
+    if (!segs.empty()) segs += ",";
+    segs += "{\"id\":" + std::to_string(id) + ",\"kind\":\"" + kind + "\",\"index\":\"" + index +
+            "\",\"rows\":" + std::to_string(rows) + ",\"deleted\":" + std::to_string(del) +
+            ",\"lsn\":" + std::to_string(lsn) + "}";
+    total += rows;
+    deleted += del;
+  };
+  add(d.mutable_id, "mutable", "flat", d.mut.n, count(d.mut.del, d.mut.n), d.mut.max_lsn);
+  const std::string index = std::string(IndexFileName(d.opt.index_type)).substr(6);
+  for (const SegEntry& e : d.segs) add(e.id, "disk", index, e.rows, count(e.del, e.rows), e.lsn);
+  *json = "{\"live_rows\":" + std::to_string(total - deleted) + ",\"total_rows\":" + std::to_string(total) +
+          ",\"deleted_rows\":" + std::to_string(deleted) + ",\"last_lsn\":" + std::to_string(d.mut.last_lsn) +
+          ",\"flushed_lsn\":" + std::to_string(d.flushed_lsn) +
+          ",\"recovery_records\":" + std::to_string(d.mut.records) + ",\"segments\":[" + segs + "]}";
   return Status::OK();
 }
 

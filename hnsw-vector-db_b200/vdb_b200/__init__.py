@@ -120,6 +120,7 @@ _SIGNATURES = {
     "vdbgpu_buffer_free": (None, [_P]),
     "vdbgpu_filter_describe": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                               ctypes.c_size_t]),
+    "vdbgpu_collection_inspect": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 _lib = None
@@ -588,3 +589,14 @@ def filter_describe(schema, filter) -> Tuple[int, str]:
     buf = ctypes.create_string_buffer(1 << 16)
     code = lib().vdbgpu_filter_describe(st.encode(), _filter_text(filter), buf, len(buf))
     return code, buf.value.decode(errors="replace")
+
+
+def inspect_collection(path: str) -> dict:
+    """The recovery of Collection.open on the host, without a GPU (vdbgpu_collection_inspect):
+    Collection::Stats fields of the directory, the mutable segment first. Raises VdbError."""
+    import json
+    buf = ctypes.create_string_buffer(1 << 20)
+    code = lib().vdbgpu_collection_inspect(os.fspath(path).encode(), buf, len(buf))
+    if code != OK:
+        raise VdbError(code, buf.value.decode(errors="replace"))
+    return json.loads(buf.value.decode())

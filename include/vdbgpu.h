@@ -334,6 +334,14 @@ VDBGPU_API int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, 
 /* Releases a buffer returned by the library (vdbgpu_hnsw_build, vdbgpu_ivfpq_build). */
 VDBGPU_API void vdbgpu_buffer_free(void* p);
 
+/* The recovery of vdbgpu_collection_open (manifest, delete sets, log replay) on the host, without
+ * a GPU, reported as Collection::Stats (src/engine/collection_impl.cc:1168-1225): JSON
+ * {"live_rows", "total_rows", "deleted_rows", "last_lsn", "flushed_lsn", "recovery_records",
+ * "segments": [{"id", "kind", "index", "rows", "deleted", "lsn"}]}, the mutable segment first.
+ * On error out_json holds the message and the status code is returned; VDBGPU_RESOURCE_EXHAUSTED
+ * when cap is too small (out_json then holds a truncated prefix). Reads only. */
+VDBGPU_API int vdbgpu_collection_inspect(const char* path, char* out_json, size_t cap);
+
 /* FilterExpr::Parse (src/meta/filter_parser.cc) against a schema (JSON, schema.cc:246-270),
  * without a GPU: VDBGPU_OK with the parsed filter's description (FilterExpr::ToString) in out,
  * or the reference's status code with its message in out. */

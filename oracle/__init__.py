@@ -222,6 +222,7 @@ def _engine_lib(lib_path: str = REF_ENGINE_LIB):
         "ref_coll_upsert_json": (ci, [_P, _P, _P, c64, ctypes.c_char_p]),
         "ref_coll_remove": (ci, [_P, _P, c64, _P]),
         "ref_coll_flush": (ci, [_P]),
+        "ref_coll_stats": (ci, [_P, ctypes.c_char_p, ctypes.c_size_t]),
         "ref_coll_search_batch": (ci, [_P, _P, c64, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, _P, _P]),
         "ref_coll_explain": (ci, [_P, _P, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, ctypes.c_char_p,
                                   ctypes.c_size_t]),
@@ -326,6 +327,14 @@ class RefCollection:
         if self.l.ref_coll_remove(self.h, _ptr(ids), ids.size, _ptr(removed)) != 0:
             raise RuntimeError(self.l.ref_coll_last_error().decode())
         return int(removed[0])
+
+    def stats(self) -> dict:
+        """Collection::Stats (rows, deletes, LSNs, per-segment id / kind / index / rows / deleted / lsn)."""
+        import json
+        buf = ctypes.create_string_buffer(1 << 20)
+        if self.l.ref_coll_stats(self.h, buf, len(buf)) != 0:
+            raise RuntimeError(self.l.ref_coll_last_error().decode())
+        return json.loads(buf.value.decode())
 
     def flush(self):
         if self.l.ref_coll_flush(self.h) != 0:

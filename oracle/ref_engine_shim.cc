@@ -193,6 +193,26 @@ int ref_coll_flush(ref_coll* h) {
   return 0;
 }
 
+// Collection::Stats as JSON (the row and log fields, and per segment id / kind / index / rows /
+// deleted / lsn).
+int ref_coll_stats(ref_coll* h, char* out, size_t cap) {
+  const vdb::CollectionStats st = h->c->Stats();
+  nlohmann::json j = {{"live_rows", st.live_rows}, {"total_rows", st.total_rows},
+                      {"deleted_rows", st.deleted_rows}, {"last_lsn", st.last_lsn},
+                      {"flushed_lsn", st.flushed_lsn}, {"recovery_records", st.last_recovery_records}};
+  j["segments"] = nlohmann::json::array();
+  for (const auto& s : st.segments)
+    j["segments"].push_back({{"id", s.id}, {"kind", s.kind}, {"index", s.index}, {"rows", s.rows},
+                             {"deleted", s.deleted}, {"lsn", s.lsn}});
+  const std::string text = j.dump();
+  if (text.size() + 1 > cap) {
+    g_err = "stats buffer too small";
+    return 7;
+  }
+  std::memcpy(out, text.c_str(), text.size() + 1);
+  return 0;
+}
+
 // The filter bitmap of one segment: SegmentColumns::Build over the segment's meta.bin
 // (segment_reader.cc:75-95) then SegmentColumns::Evaluate (columns.cc:185-205). out receives
 // (rows + 31) / 32 words, bit r of word r / 32 set for every matching row.

@@ -213,6 +213,9 @@ def make_deletes(name="coll_deletes", dim=4, seed=14, nq=32):
     out["segment_ids"] = np.array([int(os.path.basename(s)[4:]) for s in segdirs])
     coll.close()
     out.update(pack_dir(path))
+    coll = oracle.RefCollection.open(path, threads=4)  # Collection::Stats after the reference's recovery
+    out["stats"] = np.array(json.dumps(coll.stats()))
+    coll.close()
     shutil.rmtree(tmp)
     np.savez_compressed(os.path.join(OUT, name + ".npz"), **out)
     print("wrote", name, os.path.getsize(os.path.join(OUT, name + ".npz")), "bytes")
@@ -269,6 +272,7 @@ def make_mutable(name="coll_mutable", dim=24, seed=15, nq=24):
             ex = coll.explain(q[0], k=k, ef=ef, nprobe=nprobe, strategy=strategy, filter=f,
                               prefilter_threshold=thr, post_filter_alpha=alpha)
             out[f"explain_{ci}_{fi}"] = np.array(json.dumps(ex))
+    out["stats"] = np.array(json.dumps(coll.stats()))
     coll.close()
     out.update(files)
     shutil.rmtree(tmp)
