@@ -653,6 +653,15 @@ int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, uint64_t nr
 
 void vdbgpu_buffer_free(void* p) { std::free(p); }
 
+int vdbgpu_collection_apply_log(vdbgpu_collection* c, const void* records, size_t bytes, uint64_t* applied) {
+  if (c == nullptr || (records == nullptr && bytes > 0)) return VDBGPU_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(c->ctx->c->mu());
+  cudaSetDevice(c->ctx->c->device());
+  Status s = c->c->ApplyLog(*c->ctx->c, std::string_view(static_cast<const char*>(records), bytes), applied);
+  if (!s.ok()) return Fail(c->ctx, s);
+  return VDBGPU_OK;
+}
+
 int vdbgpu_collection_inspect(const char* path, char* out_json, size_t cap) {
   if (path == nullptr) return VDBGPU_INVALID_ARGUMENT;
   std::string text;

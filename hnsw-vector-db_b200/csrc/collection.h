@@ -75,6 +75,14 @@ class GpuCollection {
   // 1168-1225): JSON {live_rows, total_rows, deleted_rows, last_lsn, flushed_lsn,
   // recovery_records, segments: [{id, kind, index, rows, deleted, lsn}]}, the mutable segment first.
   static Status Inspect(const std::string& path, std::string* json);
+  // Applies log records (the bytes the reference appends to its log for a write batch: records
+  // framed as in a log file, without the file header) as recovery replays them: deletes of old
+  // rows on this shard's disk segments, upserts appended to the mutable segment (rebuilt on shard
+  // 0). Records at or below the last applied LSN are skipped; a gap or a damaged record fails the
+  // call after the records before it were applied. *applied = records applied. Only for
+  // collections opened from a directory.
+  Status ApplyLog(Context& ctx, std::string_view records, uint64_t* applied);
+  struct LogState;
   // An empty collection with the reference's options JSON (engine/options_json.cc), to which
   // segments are added from their files' contents.
   static Status Create(std::string_view options_json, std::unique_ptr<GpuCollection>* out);
@@ -129,6 +137,7 @@ class GpuCollection {
   Status Bitmaps(Context& ctx, Batch& b, const std::vector<uint32_t>& fq, size_t s0, size_t cs,
                  std::vector<uint64_t>* matches);
   uint64_t MaxWords() const;
+  Status UploadMutable(Context& ctx);
   size_t SegmentsPerChunk(const Batch& b, size_t nfilters) const;
   uint32_t* PairBits(size_t fi, size_t si, size_t cs) const;
   Status RunIndex(Context& ctx, Batch& b, size_t s, uint32_t g, uint32_t kk, const SearchParams& p,
@@ -139,6 +148,7 @@ class GpuCollection {
   bool stats_on_ = false;
   uint64_t stats_[kStats] = {};
   std::vector<std::unique_ptr<GpuSegment>> segs_;
+  std::shared_ptr<LogState> log_;  // host recovery state (collections opened from a directory)
   // Per-batch device scratch (grow-only).
   MultiScratch multi_;
   DeviceBuffer q_raw_, perm_, prepared_, qstatus_, keys_, dc_, short_, leafbits_, pairbits_,

@@ -478,11 +478,11 @@ struct SegEntry {
   uint32_t id = 0;
   uint64_t rows = 0, lsn = 0;
   std::string deletes_file, dir;
-  std::vector<uint64_t> ids;
-  std::vector<uint32_t> del;  // (rows + 31) / 32 words
+  std::vector<uint64_t> ids;  // read for the id map, then released
+  std::vector<uint32_t> del;  // (rows + 31) / 32 words; empty until read
 };
 
-Status LoadIdsAndDeletes(SegEntry* e) {
+Status LoadIds(SegEntry* e) {
   std::string idsf;
   VDBGPU_RETURN_IF_ERROR(ReadFile(e->dir + "/ids.u64", &idsf));
   std::string_view ids_p;
@@ -491,18 +491,21 @@ Status LoadIdsAndDeletes(SegEntry* e) {
   if (ids_p.size() != e->rows * 8) return Status(Status::kCorruption, e->dir + ": ids.u64 size mismatch");
   e->ids.resize(e->rows);
   if (e->rows > 0) std::memcpy(e->ids.data(), ids_p.data(), e->rows * 8);
+  return Status::OK();
+}
+
+// The persisted delete set (segment_reader.cc:101-116): a "VDBDEL01" blob named by the manifest
+// entry's deletes_file.
+Status LoadDeletes(SegEntry* e) {
   e->del.assign((e->rows + 31) / 32, 0u);
-  // The persisted delete set (segment_reader.cc:101-116): a "VDBDEL01" blob named by the
-  // manifest entry's deletes_file.
-  if (!e->deletes_file.empty()) {
-    std::string delf;
-    VDBGPU_RETURN_IF_ERROR(ReadFile(e->dir + "/" + e->deletes_file, &delf));
-    std::string_view del_p;
-    st = DecodeBlob(delf, "VDBDEL01", &del_p);
-    if (!st.ok()) return Status(Status::kCorruption, e->dir + "/" + e->deletes_file + ": " + st.message());
-    st = DecodeDeleteSet(del_p, e->rows, &e->del);
-    if (!st.ok()) return Status(st.code(), e->dir + ": " + st.message());
-  }
+  if (e->deletes_file.empty()) return Status::OK();
+  std::string delf;
+  VDBGPU_RETURN_IF_ERROR(ReadFile(e->dir + "/" + e->deletes_file, &delf));
+  std::string_view del_p;
+  Status st = DecodeBlob(delf, "VDBDEL01", &del_p);
+  if (!st.ok()) return Status(Status::kCorruption, e->dir + "/" + e->deletes_file + ": " + st.message());
+  st = DecodeDeleteSet(del_p, e->rows, &e->del);
+  if (!st.ok()) return Status(st.code(), e->dir + ": " + st.message());
   return Status::OK();
 }
 
@@ -512,8 +515,8 @@ Status LoadIdsAndDeletes(SegEntry* e) {
 struct MutableRows {
   uint64_t n = 0;
   uint64_t max_lsn = 0;   // of the rows appended (MutableSegment::max_lsn)
-  uint64_t last_lsn = 0;  // the collection's after replay
-  uint64_t records = 0;   // records replayed
+  uint64_t last_lsn = 0;  // the collection's
+  uint64_t records = 0;   // records replayed at open
   std::vector<float> rows;
   std::vector<uint64_t> ids;
   std::vector<std::string> meta;
@@ -534,84 +537,103 @@ struct MutableRows {
 
 constexpr uint64_t kMutableMaxRows = uint64_t{1} << 26;  // MutableSegment::kDefaultMaxRows
 
-// Replays the log records after flushed_lsn: the id map is rebuilt from the segments' live rows,
-// oldest segment first (Recover step 4), then each record is applied as ApplyOp does during
-// replay: a record older than the segment holding the id's current row leaves that row alone
-// (an upserted row is then appended deleted).
-Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, uint64_t flushed_lsn,
-                  const CollectionOptions& opt, std::vector<SegEntry>& segs, MutableRows* mut) {
+// The external-id map and ApplyOp's rule for one record (collection_impl.cc:574-599, replay
+// form): the id's old row is deleted unless the segment holding it is at least as new as the
+// record, in which case an upserted row is appended already deleted.
+struct LogApplier {
   struct Loc {
     int64_t seg;  // index into segs, -1 = the mutable segment
     uint32_t row;
   };
   std::unordered_map<uint64_t, Loc> ids;
-  std::vector<size_t> order(segs.size());
-  for (size_t i = 0; i < order.size(); ++i) order[i] = i;
-  std::sort(order.begin(), order.end(), [&](size_t a, size_t b) {
-    return segs[a].lsn < segs[b].lsn || (segs[a].lsn == segs[b].lsn && segs[a].id < segs[b].id);
-  });
-  for (size_t i : order)
-    for (uint64_t r = 0; r < segs[i].rows; ++r)
-      if (!(segs[i].del[r / 32] >> (r % 32) & 1u)) ids[segs[i].ids[r]] = Loc{static_cast<int64_t>(i), static_cast<uint32_t>(r)};
-  auto mark = [&](const Loc& l) {
-    std::vector<uint32_t>& d = l.seg < 0 ? mut->del : segs[static_cast<size_t>(l.seg)].del;
-    d[l.row / 32] |= 1u << (l.row % 32);
-  };
-  const uint32_t pd = opt.pd;
-  std::vector<RowValue> row(opt.schema.size());
-  uint64_t expected = flushed_lsn + 1;
+  std::vector<bool> touched;  // disk segments whose delete bits changed
+  uint64_t expected = 1;      // the LSN the next record must carry
+
+  // Recover step 4: live rows of every segment, oldest segment first.
+  void Build(const std::vector<SegEntry>& segs) {
+    std::vector<size_t> order(segs.size());
+    for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+    std::sort(order.begin(), order.end(), [&](size_t a, size_t b) {
+      return segs[a].lsn < segs[b].lsn || (segs[a].lsn == segs[b].lsn && segs[a].id < segs[b].id);
+    });
+    for (size_t i : order)
+      for (uint64_t r = 0; r < segs[i].rows; ++r)
+        if (!(segs[i].del[r / 32] >> (r % 32) & 1u)) ids[segs[i].ids[r]] = Loc{static_cast<int64_t>(i), static_cast<uint32_t>(r)};
+    touched.assign(segs.size(), false);
+  }
+
+  // Applies one record: records at or below skip_below are skipped, any other must carry the
+  // expected LSN.
+  Status Apply(const WalRecordView& rec, uint64_t skip_below, const CollectionOptions& opt,
+               std::vector<SegEntry>& segs, MutableRows* mut) {
+    if (rec.lsn <= skip_below) return Status::OK();
+    if (rec.lsn != expected)
+      return Status(Status::kCorruption, "log sequence gap: expected LSN " + std::to_string(expected) +
+                                             ", found " + std::to_string(rec.lsn));
+    ++expected;
+    mut->last_lsn = std::max(mut->last_lsn, rec.lsn);
+    Reader r(rec.payload);
+    uint64_t id = 0;
+    std::string_view vec, meta;
+    if (rec.type == 2) {
+      if (!r.u64(&id) || r.remaining() != 0)
+        return Status(Status::kCorruption, "bad delete record at LSN " + std::to_string(rec.lsn));
+    } else {
+      uint32_t dim = 0, mlen = 0;
+      if (!r.u64(&id) || !r.u32(&dim) || dim == 0 || !r.bytes(static_cast<size_t>(dim) * 4, &vec) ||
+          !r.u32(&mlen) || !r.bytes(mlen, &meta) || r.remaining() != 0 || dim != opt.dim)
+        return Status(Status::kCorruption, "bad upsert record at LSN " + std::to_string(rec.lsn));
+      std::vector<RowValue> row(opt.schema.size());
+      if (!DecodeMetaRowValues(opt.schema, meta, &row))
+        return Status(Status::kCorruption, "bad metadata at LSN " + std::to_string(rec.lsn));
+      if (mut->n >= kMutableMaxRows) return Status(Status::kResourceExhausted, "mutable segment is full");
+    }
+    auto mark = [&](const Loc& l) {
+      if (l.seg >= 0) touched[static_cast<size_t>(l.seg)] = true;
+      std::vector<uint32_t>& d = l.seg < 0 ? mut->del : segs[static_cast<size_t>(l.seg)].del;
+      d[l.row / 32] |= 1u << (l.row % 32);
+    };
+    auto it = ids.find(id);
+    const bool old_is_newer =
+        it != ids.end() && it->second.seg >= 0 && segs[static_cast<size_t>(it->second.seg)].lsn >= rec.lsn;
+    if (it != ids.end() && !old_is_newer) mark(it->second);
+    if (rec.type == 2) {
+      if (it != ids.end() && !old_is_newer) ids.erase(it);
+      return Status::OK();
+    }
+    const uint32_t pd = opt.pd;
+    mut->rows.resize((mut->n + 1) * pd, 0.0f);
+    std::memcpy(mut->rows.data() + mut->n * pd, vec.data(), vec.size());
+    mut->ids.push_back(id);
+    mut->meta.emplace_back(meta);
+    mut->max_lsn = std::max(mut->max_lsn, rec.lsn);
+    if (mut->n % 32 == 0) mut->del.push_back(0u);
+    const Loc here{-1, static_cast<uint32_t>(mut->n)};
+    ++mut->n;
+    if (old_is_newer) {
+      mark(here);
+    } else {
+      ids[id] = here;
+    }
+    return Status::OK();
+  }
+};
+
+// Recover step 5 (collection_impl.cc:160-235): the records after flushed_lsn of every log, in
+// order; a torn tail is accepted only at the end of the newest log (recovery truncates it there;
+// this loader reads the directory without changing it).
+Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, uint64_t flushed_lsn,
+                  const CollectionOptions& opt, std::vector<SegEntry>& segs, MutableRows* mut, LogApplier* ap) {
   for (size_t li = 0; li < logs.size(); ++li) {
     const std::string& path = logs[li].first;
     bool torn = false;
     Status ps = ParseWalRecords(logs[li].second, [&](const WalRecordView& rec) -> Status {
-      if (rec.lsn <= flushed_lsn) return Status::OK();
-      if (rec.lsn != expected)
-        return Status(Status::kCorruption, "log sequence gap: expected LSN " + std::to_string(expected) +
-                                               ", found " + std::to_string(rec.lsn));
-      ++expected;
-      ++mut->records;
-      mut->last_lsn = std::max(mut->last_lsn, rec.lsn);
-      Reader r(rec.payload);
-      uint64_t id = 0;
-      if (rec.type == 2) {
-        if (!r.u64(&id) || r.remaining() != 0)
-          return Status(Status::kCorruption, "bad delete record at LSN " + std::to_string(rec.lsn));
-      } else {
-        uint32_t dim = 0, mlen = 0;
-        std::string_view vec, meta;
-        if (!r.u64(&id) || !r.u32(&dim) || dim == 0 || !r.bytes(static_cast<size_t>(dim) * 4, &vec) ||
-            !r.u32(&mlen) || !r.bytes(mlen, &meta) || r.remaining() != 0 || dim != opt.dim)
-          return Status(Status::kCorruption, "bad upsert record at LSN " + std::to_string(rec.lsn));
-        if (!DecodeMetaRowValues(opt.schema, meta, &row))
-          return Status(Status::kCorruption, "bad metadata at LSN " + std::to_string(rec.lsn));
-        if (mut->n >= kMutableMaxRows) return Status(Status::kResourceExhausted, "mutable segment is full");
-        mut->rows.resize((mut->n + 1) * pd, 0.0f);
-        std::memcpy(mut->rows.data() + mut->n * pd, vec.data(), vec.size());
-        mut->ids.push_back(id);
-        mut->meta.emplace_back(meta);
-        mut->max_lsn = std::max(mut->max_lsn, rec.lsn);
-        if (mut->n % 32 == 0) mut->del.push_back(0u);
-      }
-      auto it = ids.find(id);
-      const bool old_is_newer =
-          it != ids.end() && it->second.seg >= 0 && segs[static_cast<size_t>(it->second.seg)].lsn >= rec.lsn;
-      if (it != ids.end() && !old_is_newer) mark(it->second);
-      if (rec.type == 2) {
-        if (it != ids.end() && !old_is_newer) ids.erase(it);
-        return Status::OK();
-      }
-      const Loc here{-1, static_cast<uint32_t>(mut->n)};
-      ++mut->n;
-      if (old_is_newer) {
-        mark(here);
-      } else {
-        ids[id] = here;
-      }
+      const uint64_t before = ap->expected;
+      VDBGPU_RETURN_IF_ERROR(ap->Apply(rec, flushed_lsn, opt, segs, mut));
+      if (ap->expected != before) ++mut->records;
       return Status::OK();
     }, &torn);
     if (!ps.ok()) return Status(ps.code(), path + ": " + ps.message());
-    // A torn tail is only acceptable at the end of the newest log (Open truncates it there; this
-    // loader reads the directory without changing it).
     if (torn && li + 1 != logs.size())
       return Status(Status::kCorruption, path + ": damaged record in a log that is not the newest");
   }
@@ -620,21 +642,28 @@ Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, 
 
 }  // namespace
 
+// What a collection keeps on the host after Open: the manifest's segments (delete bits, lsn; ids
+// only while the id map is built), the mutable segment's rows, and the id map once a log record
+// has been applied.
+struct GpuCollection::LogState {
+  std::string path;
+  uint32_t shard = 0, nshards = 1;
+  uint32_t mutable_id = 0;
+  uint64_t flushed_lsn = 0;
+  std::vector<SegEntry> segs;
+  MutableRows mut;
+  LogApplier ap;
+  bool have_map = false;
+};
+
 namespace {
 
 // The directory as Collection::Open recovers it (CollectionImpl::Recover, collection_impl.cc:
-// 76-235), on the host: options, segments with their ids and delete bits (those of shard `shard`
-// of nshards, or of every segment when the logs hold records or `all`), and the mutable segment
+// 76-235), on the host: options, segments with their delete bits (those of shard `shard` of
+// nshards, or of every segment when the logs hold records or `all`), and the mutable segment
 // replayed from the logs. Reads only.
-struct RecoveredDir {
-  CollectionOptions opt;
-  std::vector<SegEntry> segs;
-  MutableRows mut;
-  uint64_t flushed_lsn = 0;
-  uint32_t mutable_id = 0;
-};
-
-Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, bool all, RecoveredDir* d) {
+Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, bool all, CollectionOptions* opt,
+                  GpuCollection::LogState* d) {
   // ReadCurrentManifest (src/storage/manifest.cc:116-127).
   std::string current;
   VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/CURRENT", &current));
@@ -659,7 +688,10 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
   };
   const uint64_t flushed_lsn = u64_of("flushed_lsn"), wal_log_number = u64_of("wal_log_number");
   uint64_t next = u64_of("next_file_number");
-  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, &d->opt));
+  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, opt));
+  d->path = path;
+  d->shard = shard;
+  d->nshards = nshards;
   d->flushed_lsn = flushed_lsn;
   std::vector<SegEntry>& entries = d->segs;
   entries.resize(segs->arr.size());
@@ -703,14 +735,24 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
     any_records |= data.size() > kWalFileHeaderSize;
     logs.emplace_back(p, std::move(data));
   }
-  // Ids and delete sets: of this shard's segments, and of every segment when the logs hold
-  // records (an upsert or delete may name a row of any segment).
+  d->mutable_id = static_cast<uint32_t>(next);
+  // Delete sets: of this shard's segments, and of every segment when the logs hold records (an
+  // upsert or delete may name a row of any segment, so the id map needs every segment's ids).
   for (size_t i = 0; i < entries.size(); ++i)
-    if (all || any_records || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(LoadIdsAndDeletes(&entries[i]));
+    if (all || any_records || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(LoadDeletes(&entries[i]));
   d->mut.last_lsn = flushed_lsn;
   for (const SegEntry& e : entries) d->mut.last_lsn = std::max(d->mut.last_lsn, e.lsn);
-  if (any_records) VDBGPU_RETURN_IF_ERROR(ReplayLogs(logs, flushed_lsn, d->opt, entries, &d->mut));
-  d->mutable_id = static_cast<uint32_t>(next);
+  // Records continue from flushed_lsn + 1 (collection_impl.cc:183); after the replay, from the
+  // last record replayed. In a directory the reference wrote this is also its next LSN: a bulk
+  // load or compaction takes the LSN of the last record, it does not advance it.
+  d->ap.expected = flushed_lsn + 1;
+  if (any_records) {
+    for (SegEntry& e : entries) VDBGPU_RETURN_IF_ERROR(LoadIds(&e));
+    d->ap.Build(entries);
+    d->have_map = true;
+    for (SegEntry& e : entries) std::vector<uint64_t>().swap(e.ids);
+    VDBGPU_RETURN_IF_ERROR(ReplayLogs(logs, flushed_lsn, *opt, entries, &d->mut, &d->ap));
+  }
   return Status::OK();
 }
 
@@ -719,17 +761,14 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
 Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard, uint32_t nshards,
                            std::unique_ptr<GpuCollection>* out) {
   if (nshards == 0 || shard >= nshards) return Status(Status::kInvalidArgument, "bad shard");
-  RecoveredDir d;
-  VDBGPU_RETURN_IF_ERROR(RecoverDir(path, shard, nshards, false, &d));
   auto c = std::make_unique<GpuCollection>();
-  c->opt_ = d.opt;
+  c->log_ = std::make_shared<LogState>();
+  LogState& d = *c->log_;
+  VDBGPU_RETURN_IF_ERROR(RecoverDir(path, shard, nshards, false, &c->opt_, &d));
   const uint32_t pd = c->opt_.pd;
-  std::vector<SegEntry>& entries = d.segs;
-  MutableRows& mut = d.mut;
-
-  for (size_t i = 0; i < entries.size(); ++i) {
+  for (size_t i = 0; i < d.segs.size(); ++i) {
     if (i % nshards != shard) continue;
-    const SegEntry& e = entries[i];
+    const SegEntry& e = d.segs[i];
     const std::string& dir = e.dir;
     // vectors.f32 header checks of Segment::Open (segment_reader.cc:36-51).
     std::string vec;
@@ -746,6 +785,8 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
         GetAt<uint64_t>(h, 32) != kSegmentHeaderSize || data_len != e.rows * pd * sizeof(float) ||
         vec.size() < kSegmentHeaderSize + data_len)
       return Status(Status::kCorruption, dir + ": header does not match the manifest");
+    SegEntry ide = e;  // this segment's ids, for the upload only
+    VDBGPU_RETURN_IF_ERROR(LoadIds(&ide));
     std::string metaf, indexf;
     VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/meta.bin", &metaf));
     VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/" + IndexFileName(c->opt_.index_type), &indexf));
@@ -755,7 +796,7 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
     // Part 0 of the merge is the mutable segment (collection_impl.cc:1056-1059); disk segments
     // follow in manifest order.
     st = c->AddSegment(ctx, e.id, static_cast<uint32_t>(i + 1), reinterpret_cast<const float*>(h + kSegmentHeaderSize),
-                       e.rows, e.ids.data(), meta_p, indexf);
+                       e.rows, ide.ids.data(), meta_p, indexf);
     if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
     bool any = false;
     for (uint32_t w : e.del) any |= w != 0;
@@ -764,30 +805,91 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
       if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
     }
   }
-  // The mutable segment lives on shard 0 and is searched exhaustively (SearchMutable,
-  // planner.cc:131-149) through a flat index over its rows.
-  if (shard == 0 && mut.n > 0) {
-    std::string flat = "VDBFLAT1";
-    const uint32_t crc = Crc32c(flat.data(), flat.size());
-    flat.append(reinterpret_cast<const char*>(&crc), 4);
-    const std::string meta = mut.MetaPayload();
-    const uint32_t mid = d.mutable_id;
-    VDBGPU_RETURN_IF_ERROR(c->AddSegment(ctx, mid, 0, mut.rows.data(), mut.n, mut.ids.data(), meta, flat));
-    for (auto& s : c->segs_)
-      if (s->ordinal == 0) s->is_mutable = true;
-    bool any = false;
-    for (uint32_t w : mut.del) any |= w != 0;
-    if (any) VDBGPU_RETURN_IF_ERROR(c->SetDeleted(ctx, mid, mut.del.data()));
-  }
-  c->total_segments_ = static_cast<uint32_t>(entries.size() + (mut.n > 0 ? 1 : 0));
+  VDBGPU_RETURN_IF_ERROR(c->UploadMutable(ctx));
   *out = std::move(c);
   return Status::OK();
 }
 
+// The mutable segment lives on shard 0 and is searched exhaustively (SearchMutable,
+// planner.cc:131-149) through a flat index over its rows; it is rebuilt whole after a change.
+Status GpuCollection::UploadMutable(Context& ctx) {
+  const LogState& d = *log_;
+  segs_.erase(std::remove_if(segs_.begin(), segs_.end(), [](const auto& s) { return s->is_mutable; }), segs_.end());
+  if (d.shard == 0 && d.mut.n > 0) {
+    std::string flat = "VDBFLAT1";
+    const uint32_t crc = Crc32c(flat.data(), flat.size());
+    flat.append(reinterpret_cast<const char*>(&crc), 4);
+    const std::string meta = d.mut.MetaPayload();
+    VDBGPU_RETURN_IF_ERROR(AddSegment(ctx, d.mutable_id, 0, d.mut.rows.data(), d.mut.n, d.mut.ids.data(), meta, flat));
+    for (auto& s : segs_)
+      if (s->ordinal == 0) s->is_mutable = true;
+    bool any = false;
+    for (uint32_t w : d.mut.del) any |= w != 0;
+    if (any) VDBGPU_RETURN_IF_ERROR(SetDeleted(ctx, d.mutable_id, d.mut.del.data()));
+  }
+  total_segments_ = static_cast<uint32_t>(d.segs.size() + (d.mut.n > 0 ? 1 : 0));
+  return Status::OK();
+}
+
+Status GpuCollection::ApplyLog(Context& ctx, std::string_view records, uint64_t* applied) {
+  if (applied != nullptr) *applied = 0;
+  if (!log_) return Status(Status::kFailedPrecondition, "the collection was not opened from a directory");
+  LogState& d = *log_;
+  if (!d.have_map) {
+    // The id map, built on first use from every segment's ids and current delete bits.
+    for (SegEntry& e : d.segs) {
+      if (e.del.empty()) VDBGPU_RETURN_IF_ERROR(LoadDeletes(&e));
+      VDBGPU_RETURN_IF_ERROR(LoadIds(&e));
+    }
+    const uint64_t expected = d.ap.expected;
+    // Rows already in the mutable segment keep their ids (later rows of an id win).
+    d.ap.Build(d.segs);
+    for (uint64_t r = 0; r < d.mut.n; ++r)
+      if (!(d.mut.del[r / 32] >> (r % 32) & 1u)) d.ap.ids[d.mut.ids[r]] = LogApplier::Loc{-1, static_cast<uint32_t>(r)};
+    d.ap.expected = expected;
+    for (SegEntry& e : d.segs) std::vector<uint64_t>().swap(e.ids);
+    d.have_map = true;
+  }
+  d.ap.touched.assign(d.segs.size(), false);
+  const uint64_t n_before = d.mut.n;
+  const uint64_t del_before = [&] {
+    uint64_t c = 0;
+    for (uint32_t w : d.mut.del) c += static_cast<uint64_t>(__builtin_popcount(w));
+    return c;
+  }();
+  // The records as the log holds them (no file header); a damaged record fails the call, after
+  // the records before it have been applied.
+  Status st = Status::OK();
+  size_t pos = 0;
+  uint64_t count = 0;
+  while (pos < records.size()) {
+    WalRecordView rec;
+    size_t len = 0;
+    if (!TryParseWalRecord(records, pos, &rec, &len)) {
+      st = Status(Status::kInvalidArgument, "bad log record at offset " + std::to_string(pos));
+      break;
+    }
+    const uint64_t before = d.ap.expected;
+    st = d.ap.Apply(rec, d.ap.expected - 1, opt_, d.segs, &d.mut);
+    if (!st.ok()) break;
+    count += d.ap.expected != before ? 1 : 0;
+    pos += len;
+  }
+  for (size_t i = 0; i < d.segs.size(); ++i) {
+    if (!d.ap.touched[i] || i % d.nshards != d.shard) continue;
+    VDBGPU_RETURN_IF_ERROR(SetDeleted(ctx, d.segs[i].id, d.segs[i].del.data()));
+  }
+  uint64_t del_after = 0;
+  for (uint32_t w : d.mut.del) del_after += static_cast<uint64_t>(__builtin_popcount(w));
+  if (d.mut.n != n_before || del_after != del_before) VDBGPU_RETURN_IF_ERROR(UploadMutable(ctx));
+  if (applied != nullptr) *applied = count;
+  return st;
+}
 
 Status GpuCollection::Inspect(const std::string& path, std::string* json) {
-  RecoveredDir d;
-  VDBGPU_RETURN_IF_ERROR(RecoverDir(path, 0, 1, true, &d));
+  LogState d;
+  CollectionOptions opt;
+  VDBGPU_RETURN_IF_ERROR(RecoverDir(path, 0, 1, true, &opt, &d));
   auto count = [](const std::vector<uint32_t>& bits, uint64_t rows) {
     uint64_t c = 0;
     for (uint64_t w = 0; w < bits.size(); ++w) {
@@ -807,7 +909,7 @@ Status GpuCollection::Inspect(const std::string& path, std::string* json) {
     deleted += del;
   };
   add(d.mutable_id, "mutable", "flat", d.mut.n, count(d.mut.del, d.mut.n), d.mut.max_lsn);
-  const std::string index = std::string(IndexFileName(d.opt.index_type)).substr(6);
+  const std::string index = std::string(IndexFileName(opt.index_type)).substr(6);
   for (const SegEntry& e : d.segs) add(e.id, "disk", index, e.rows, count(e.del, e.rows), e.lsn);
   *json = "{\"live_rows\":" + std::to_string(total - deleted) + ",\"total_rows\":" + std::to_string(total) +
           ",\"deleted_rows\":" + std::to_string(deleted) + ",\"last_lsn\":" + std::to_string(d.mut.last_lsn) +

@@ -121,6 +121,8 @@ _SIGNATURES = {
     "vdbgpu_filter_describe": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                               ctypes.c_size_t]),
     "vdbgpu_collection_inspect": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "vdbgpu_collection_apply_log": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t,
+                                                   ctypes.c_void_p]),
 }
 
 _lib = None
@@ -486,6 +488,13 @@ class Collection:
                                                               len(texts), _ptr(qf), _ptr(ids), _ptr(dists),
                                                               _ptr(hits)))
         return ids, dists
+
+    def apply_log(self, records: bytes) -> int:
+        """Applies write-ahead log records (the reference's log bytes for a write batch, without the
+        file header) as recovery replays them; returns how many were applied."""
+        n = ctypes.c_uint64(0)
+        self.ctx.check(lib().vdbgpu_collection_apply_log(self._h, bytes(records), len(records), ctypes.byref(n)))
+        return int(n.value)
 
     def explain(self, query, k: int = 10, ef: int = 64, nprobe: int = 16, rerank: int = -1, filter=None,
                 strategy: str = "auto", prefilter_threshold: int = 10000, post_filter_alpha: int = 10):

@@ -334,6 +334,18 @@ VDBGPU_API int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, 
 /* Releases a buffer returned by the library (vdbgpu_hnsw_build, vdbgpu_ivfpq_build). */
 VDBGPU_API void vdbgpu_buffer_free(void* p);
 
+/* Applies write-ahead log records to a collection opened with vdbgpu_collection_open, as recovery
+ * replays them (ApplyOp, src/engine/collection_impl.cc:574-599): `records` are the bytes the
+ * reference appends to its log for a write batch (WalWriter::append, src/storage/wal.cc: records
+ * framed as in a log file, without the 16-byte file header). Upserts are appended to the mutable
+ * segment (rebuilt on shard 0), and the old rows of upserted or deleted ids are deleted on this
+ * shard's segments. Records at or below the last applied LSN are skipped, so a batch may overlap
+ * what the directory's log already held; an LSN gap is VDBGPU_CORRUPTION and a damaged record
+ * VDBGPU_INVALID_ARGUMENT, each after the records before it were applied. *applied (nullable) =
+ * records applied. A flush of the reference (a new disk segment) is followed by reopening. */
+VDBGPU_API int vdbgpu_collection_apply_log(vdbgpu_collection* c, const void* records, size_t bytes,
+                                           uint64_t* applied);
+
 /* The recovery of vdbgpu_collection_open (manifest, delete sets, log replay) on the host, without
  * a GPU, reported as Collection::Stats (src/engine/collection_impl.cc:1168-1225): JSON
  * {"live_rows", "total_rows", "deleted_rows", "last_lsn", "flushed_lsn", "recovery_records",

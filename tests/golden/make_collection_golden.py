@@ -227,8 +227,9 @@ def make_mutable(name="coll_mutable", dim=24, seed=15, nq=24):
     a persisted delete set) and D (a later bulk load). The log then holds upserts of new ids, of
     A's and B's ids, of one id twice, removals of disk rows, log rows and absent ids, and an id
     upserted and removed before D's bulk load brought it back (D's row is newer than both
-    records). The fixture holds the directory as closed; searches and explains (mutable part
-    first) come from the reference's Collection::Open of it, which replays the log."""
+    records), then more upserts and removals after D. The fixture holds the directory as closed;
+    searches and explains (mutable part first) come from the reference's Collection::Open of it,
+    which replays the log."""
     rng = np.random.default_rng(seed)
     tmp = tempfile.mkdtemp()
     path = os.path.join(tmp, "coll")
@@ -253,6 +254,12 @@ def make_mutable(name="coll_mutable", dim=24, seed=15, nq=24):
     coll.remove(x)
     ids_d = np.concatenate([x, np.arange(20000, 20299, dtype=np.uint64) * 3])
     coll.bulk_load(ids_d, rows_mixture(rng, ids_d.size, dim, centres), metadata=metadata(rng, ids_d.size))
+    # After D: upserts of new ids and of A's and D's ids, then removals across A, D and the log.
+    more = np.concatenate([np.arange(30000, 30020, dtype=np.uint64) * 3, ids_a[rng.choice(1500, 10, replace=False)],
+                           ids_d[1 + rng.choice(299, 10, replace=False)]])
+    coll.upsert(more, rows_mixture(rng, more.size, dim, centres), metadata(rng, more.size))
+    coll.remove(np.concatenate([ids_a[rng.choice(1500, 8, replace=False)], ids_d[1 + rng.choice(299, 6, replace=False)],
+                                new[rng.choice(200, 5, replace=False)], more[:3]]))
     last = np.array([900001, 900002, 900003], np.uint64)  # new ids: the log ends with three upserts
     coll.upsert(last, rows_mixture(rng, 3, dim, centres), [None, {"year": 2024}, {"tags": []}])
     coll.close()
