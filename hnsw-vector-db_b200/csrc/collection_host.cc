@@ -44,6 +44,18 @@ Status ReadFile(const std::string& path, std::string* out) {
   return Status::OK();
 }
 
+// The first n bytes of a file (fewer if it is shorter) and its size.
+Status ReadPrefix(const std::string& path, size_t n, std::string* out, uint64_t* size) {
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f) return Status(Status::kIOError, "cannot open " + path);
+  *size = static_cast<uint64_t>(f.tellg());
+  f.seekg(0);
+  out->assign(static_cast<size_t>(std::min<uint64_t>(n, *size)), '\0');
+  if (!out->empty() && !f.read(&(*out)[0], static_cast<std::streamsize>(out->size())))
+    return Status(Status::kIOError, "cannot read " + path);
+  return Status::OK();
+}
+
 template <class T>
 T GetAt(const char* p, size_t off) {
   T v;
@@ -473,6 +485,23 @@ std::vector<std::string> ListDir(const std::string& path) {
   return names;
 }
 
+// vectors.f32 header checks of Segment::Open (segment_reader.cc:36-51) against the manifest and
+// the collection's options: the 4 KiB header and the file's size.
+Status CheckSegmentHeader(const std::string& dir, const char* h, uint64_t file_size, uint64_t rows,
+                          const CollectionOptions& opt) {
+  if (file_size < kSegmentHeaderSize) return Status(Status::kCorruption, dir + ": vectors.f32 shorter than its header");
+  if (std::memcmp(h, "VDBSEG01", 8) != 0) return Status(Status::kCorruption, dir + ": bad magic");
+  if (GetAt<uint32_t>(h, kSegmentHeaderSize - 4) != Crc32c(h, kSegmentHeaderSize - 4))
+    return Status(Status::kCorruption, dir + ": header checksum mismatch");
+  const uint64_t data_len = GetAt<uint64_t>(h, 40);
+  if (GetAt<uint32_t>(h, 8) != 1 || GetAt<uint32_t>(h, 12) != static_cast<uint32_t>(opt.metric) ||
+      GetAt<uint64_t>(h, 16) != rows || GetAt<uint32_t>(h, 24) != opt.dim || GetAt<uint32_t>(h, 28) != opt.pd ||
+      GetAt<uint64_t>(h, 32) != kSegmentHeaderSize || rows > (file_size / 4) ||
+      data_len != rows * opt.pd * sizeof(float) || file_size - kSegmentHeaderSize < data_len)
+    return Status(Status::kCorruption, dir + ": header does not match the manifest");
+  return Status::OK();
+}
+
 // One disk segment of the manifest, with its ids and delete bits once read.
 struct SegEntry {
   uint32_t id = 0;
@@ -736,6 +765,12 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
     logs.emplace_back(p, std::move(data));
   }
   d->mutable_id = static_cast<uint32_t>(next);
+  for (const SegEntry& e : entries) {
+    std::string h;
+    uint64_t size = 0;
+    VDBGPU_RETURN_IF_ERROR(ReadPrefix(e.dir + "/vectors.f32", kSegmentHeaderSize, &h, &size));
+    VDBGPU_RETURN_IF_ERROR(CheckSegmentHeader(e.dir, h.data(), size, e.rows, *opt));
+  }
   // Delete sets: of this shard's segments, and of every segment when the logs hold records (an
   // upsert or delete may name a row of any segment, so the id map needs every segment's ids).
   for (size_t i = 0; i < entries.size(); ++i)
@@ -773,18 +808,8 @@ Status GpuCollection::Open(Context& ctx, const std::string& path, uint32_t shard
     // vectors.f32 header checks of Segment::Open (segment_reader.cc:36-51).
     std::string vec;
     VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/vectors.f32", &vec));
-    if (vec.size() < kSegmentHeaderSize) return Status(Status::kCorruption, dir + ": vectors.f32 shorter than its header");
+    VDBGPU_RETURN_IF_ERROR(CheckSegmentHeader(dir, vec.data(), vec.size(), e.rows, c->opt_));
     const char* h = vec.data();
-    if (std::memcmp(h, "VDBSEG01", 8) != 0) return Status(Status::kCorruption, dir + ": bad magic");
-    if (GetAt<uint32_t>(h, kSegmentHeaderSize - 4) != Crc32c(h, kSegmentHeaderSize - 4))
-      return Status(Status::kCorruption, dir + ": header checksum mismatch");
-    const uint64_t hrows = GetAt<uint64_t>(h, 16);
-    const uint64_t data_len = GetAt<uint64_t>(h, 40);
-    if (GetAt<uint32_t>(h, 8) != 1 || GetAt<uint32_t>(h, 12) != static_cast<uint32_t>(c->opt_.metric) ||
-        hrows != e.rows || GetAt<uint32_t>(h, 24) != c->opt_.dim || GetAt<uint32_t>(h, 28) != pd ||
-        GetAt<uint64_t>(h, 32) != kSegmentHeaderSize || data_len != e.rows * pd * sizeof(float) ||
-        vec.size() < kSegmentHeaderSize + data_len)
-      return Status(Status::kCorruption, dir + ": header does not match the manifest");
     SegEntry ide = e;  // this segment's ids, for the upload only
     VDBGPU_RETURN_IF_ERROR(LoadIds(&ide));
     std::string metaf, indexf;

@@ -91,3 +91,91 @@ def test_damaged_delete_set_is_corruption(tmp_path):
     with pytest.raises(vdb_b200.VdbError) as e:
         _inspect(path)
     assert e.value.code == vdb_b200.CORRUPTION and "delete set out of range" in str(e.value)
+
+
+
+def _fuzz(tmp_path, name, pick, mutate, n, seed):
+    """Mutations of one file of a fixture directory, checksums recomputed so that the decoders
+    behind them see the damage: recovery returns a status for each (OK or one of the reference's
+    codes) and never fails otherwise (no crash, no unbounded allocation)."""
+    import vdb_b200
+    g = golden(name)
+    base = extract_collection(g, tmp_path / "base")
+    target = pick(base, g)
+    orig = open(target, "rb").read()
+    rng = np.random.default_rng(seed)
+    codes = {}
+    for _ in range(n):
+        open(target, "wb").write(mutate(orig, rng))
+        try:
+            vdb_b200.inspect_collection(base)
+            codes[0] = codes.get(0, 0) + 1
+        except vdb_b200.VdbError as e:
+            assert e.code in (vdb_b200.CORRUPTION, vdb_b200.INVALID_ARGUMENT, vdb_b200.NOT_FOUND,
+                              vdb_b200.IO_ERROR, vdb_b200.RESOURCE_EXHAUSTED), str(e)
+            codes[e.code] = codes.get(e.code, 0) + 1
+    return codes
+
+
+def _damage(p: bytes, rng) -> bytes:
+    b = bytearray(p)
+    kind = int(rng.integers(0, 3))
+    if kind == 0:
+        for _ in range(int(rng.integers(1, 6))):
+            b[int(rng.integers(0, len(b)))] ^= 1 << int(rng.integers(0, 8))
+    elif kind == 1:
+        b = b[:int(rng.integers(0, len(b)))]
+    else:
+        i = int(rng.integers(0, len(b) + 1))
+        b[i:i] = bytes(rng.integers(0, 256, int(rng.integers(1, 9)), dtype=np.uint8))
+    return bytes(b)
+
+
+def _reblob(orig, rng):
+    """A blob file (delete set, manifest) with a damaged payload and a valid checksum."""
+    return blob(orig[:8], _damage(orig[24:], rng))
+
+
+def _relog(orig, rng):
+    """A log with one record damaged after its checksum field (type, LSN, payload), checksum
+    recomputed; or the raw bytes damaged, framing included."""
+    from helpers import crc32c
+    if rng.random() < 0.25:
+        return orig[:16] + _damage(orig[16:], rng)
+    recs, pos = [], 16
+    while pos < len(orig):
+        plen = int(np.frombuffer(orig, "<u4", 1, pos + 4)[0])
+        recs.append((pos, 17 + plen))
+        pos += 17 + plen
+    off, ln = recs[int(rng.integers(0, len(recs)))]
+    r = bytearray(orig[off:off + ln])
+    for _ in range(int(rng.integers(1, 4))):
+        r[int(rng.integers(8, len(r)))] ^= 1 << int(rng.integers(0, 8))
+    r[0:4] = np.array([crc32c(bytes(r[4:]))], "<u4").tobytes()
+    return orig[:off] + bytes(r) + orig[off + ln:]
+
+
+def _manifest_path(p, g):
+    return os.path.join(p, [k for k in g if k.startswith("file:MANIFEST-")][0][5:])
+
+
+def test_fuzzed_logs_never_crash(tmp_path):
+    import vdb_b200
+    codes = _fuzz(tmp_path, "coll_mutable", lambda p, g: _log(p)[0], _relog, 250, 1)
+    assert codes.get(vdb_b200.CORRUPTION, 0) > 0 and codes.get(0, 0) > 0
+
+
+def test_fuzzed_delete_sets_never_crash(tmp_path):
+    import vdb_b200
+
+    def pick(p, g):
+        seg = json.loads(g[[k for k in g if k.startswith("file:MANIFEST-")][0]].tobytes()[24:])["segments"][0]
+        return os.path.join(p, "segments", f"seg-{seg['id']:06d}", seg["deletes_file"])
+    codes = _fuzz(tmp_path, "coll_deletes", pick, _reblob, 150, 2)
+    assert codes.get(vdb_b200.CORRUPTION, 0) > 0 and codes.get(0, 0) > 0
+
+
+def test_fuzzed_manifests_never_crash(tmp_path):
+    import vdb_b200
+    codes = _fuzz(tmp_path, "coll_mutable", _manifest_path, _reblob, 200, 3)
+    assert codes.get(vdb_b200.CORRUPTION, 0) > 0
