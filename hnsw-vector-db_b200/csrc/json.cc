@@ -299,11 +299,18 @@ std::string JsonNumber(double d) {
   if (d == 0) return std::signbit(d) ? "-0.0" : "0.0";
   std::string out = d < 0 ? "-" : "";
   d = std::fabs(d);
-  // Shortest round-trip decimal digits D.DDDe[+-]X.
+  // Shortest decimal digits D.DDDe[+-]X that identify d with room to spare: the value must lie
+  // strictly inside d's rounding interval, half-way to each neighbouring double (the boundaries
+  // themselves, reached only through round-half-even, are excluded, as in the shortest-digit
+  // search of Loitsch's Grisu2, which nlohmann::json's dump uses). The half-way points are exact
+  // in long double (64-bit significand).
+  const long double lo = (static_cast<long double>(d) + std::nextafter(d, 0.0)) / 2;
+  const long double hi = (static_cast<long double>(d) + std::nextafter(d, HUGE_VAL)) / 2;
   char buf[48];
   for (int prec = 1; prec <= 17; ++prec) {
     std::snprintf(buf, sizeof(buf), "%.*e", prec - 1, d);
-    if (std::strtod(buf, nullptr) == d) break;
+    const long double v = std::strtold(buf, nullptr);
+    if (std::strtod(buf, nullptr) == d && lo < v && v < hi) break;
   }
   std::string digits;
   const char* e = std::strchr(buf, 'e');

@@ -297,8 +297,47 @@ def pack_dir_with_logs(path):
     return files
 
 
+def fuzz_parse_golden(n=3000, seed=5):
+    """Mutated filter texts (characters and tokens inserted, deleted, replaced in the PARSE_CASES)
+    with the reference parser's code and text for each (tests/golden/filter_fuzz.npz), plus two
+    integer literals whose double sits half-way between two shorter decimals."""
+    rng = np.random.default_rng(seed)
+    tokens = list('{}[]":,0123456789.-eE ') + [
+        '"field"', '"and"', '"or"', '"not"', '"eq"', '"ne"', '"in"', '"gte"', '"lt"', '"exists"', 'true',
+        'false', 'null', '"year"', '"tags"', '"score"', '"lang"', '"flag"', '\\u00e9', '\\"', '1e400', '-0',
+        '18446744073709551616', '9223372036854775807']
+    texts = ['{"field": "year", "eq": 144744073709551615}', '{"field":"year","eq": -92337203654775808}']
+    codes, outs = [], []
+    for t in texts:
+        rc, o = oracle.ref_filter_parse(SCHEMA, t)
+        codes.append(rc)
+        outs.append(o)
+    nvalid = n // 3  # a third of the cases parse, the rest exercise the error paths
+    while len(texts) < n:
+        b = list(PARSE_CASES[int(rng.integers(0, len(PARSE_CASES)))])
+        for _ in range(int(rng.integers(1, 5))):
+            i, op = int(rng.integers(0, len(b) + 1)), int(rng.integers(0, 3))
+            if op == 0 and b:
+                del b[min(i, len(b) - 1)]
+            elif op == 1:
+                b.insert(i, tokens[int(rng.integers(0, len(tokens)))])
+            elif b:
+                b[min(i, len(b) - 1)] = tokens[int(rng.integers(0, len(tokens)))]
+        t = "".join(b)
+        rc, o = oracle.ref_filter_parse(SCHEMA, t)
+        if (rc == 0 and codes.count(0) >= nvalid) or (rc != 0 and len(codes) - codes.count(0) >= n - nvalid):
+            continue
+        texts.append(t)
+        codes.append(rc)
+        outs.append(o)
+    np.savez_compressed(os.path.join(OUT, "filter_fuzz.npz"), cases=np.array(texts), codes=np.array(codes),
+                        texts=np.array(outs), schema=np.array(json.dumps(SCHEMA)))
+    print("wrote filter_fuzz", len(texts), "cases,", sum(c == 0 for c in codes), "valid")
+
+
 def main():
     oracle.build(ref=True)
+    fuzz_parse_golden()
     make_mutable()
     make_deletes()
     parse_golden()

@@ -18,6 +18,18 @@ def test_filter_parser_matches_reference_golden():
         assert vdb_b200.filter_describe(schema, str(case)) == (int(code), str(text)), str(case)[:80]
 
 
+def test_filter_parser_matches_reference_on_fuzzed_texts():
+    """3,000 mutations of the golden texts (a third of them valid filters) with the reference
+    parser's code and text: error paths and messages, and numeric literals printed as the
+    reference prints them (shortest digits strictly inside the double's rounding interval)."""
+    import vdb_b200
+    g = golden("filter_fuzz")
+    schema = str(g["schema"])
+    bad = [str(c) for c, code, text in zip(g["cases"], g["codes"], g["texts"])
+           if vdb_b200.filter_describe(schema, str(c)) != (int(code), str(text))]
+    assert not bad, (len(bad), bad[:5])
+
+
 def test_filter_parser_matches_live_reference():
     import oracle
     import vdb_b200
