@@ -1,17 +1,19 @@
 #include "collection.h"
 
 #include <algorithm>
+#include <cerrno>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
-#include <fstream>
 #include <functional>
 #include <map>
-#include <sstream>
 #include <unordered_map>
 
 #include <dirent.h>
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include "formats.h"
 #include "hnsw.cuh"
@@ -34,26 +36,45 @@ constexpr uint32_t kScatterChunk = 16384;
 
 uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
 
-Status ReadFile(const std::string& path, std::string* out) {
-  std::ifstream f(path, std::ios::binary);
-  if (!f) return Status(Status::kIOError, "cannot open " + path);
-  std::ostringstream ss;
-  ss << f.rdbuf();
-  if (!f.good() && !f.eof()) return Status(Status::kIOError, "cannot read " + path);
-  *out = ss.str();
+// Whole-file reads as the reference's PosixEnv::read_file (src/storage/posix_env.cc:99-124):
+// errors are IOError "<call> <path>: <strerror>". With a limit, only the first `limit` bytes.
+Status ErrnoStatus(const char* what, const std::string& path, int err) {
+  return Status(Status::kIOError, std::string(what) + " " + path + ": " + std::strerror(err));
+}
+
+Status ReadFileLimit(const std::string& path, uint64_t limit, std::string* out, uint64_t* size) {
+  const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return ErrnoStatus("open", path, errno);
+  struct stat st {};
+  if (::fstat(fd, &st) != 0) {
+    const int e = errno;
+    ::close(fd);
+    return ErrnoStatus("stat", path, e);
+  }
+  if (size != nullptr) *size = static_cast<uint64_t>(st.st_size);
+  out->resize(static_cast<size_t>(std::min<uint64_t>(limit, static_cast<uint64_t>(st.st_size))));
+  size_t got = 0;
+  while (got < out->size()) {
+    const ssize_t n = ::read(fd, &(*out)[got], out->size() - got);
+    if (n < 0) {
+      if (errno == EINTR) continue;
+      const int e = errno;
+      ::close(fd);
+      return ErrnoStatus("read", path, e);
+    }
+    if (n == 0) break;
+    got += static_cast<size_t>(n);
+  }
+  out->resize(got);
+  ::close(fd);
   return Status::OK();
 }
 
+Status ReadFile(const std::string& path, std::string* out) { return ReadFileLimit(path, UINT64_MAX, out, nullptr); }
+
 // The first n bytes of a file (fewer if it is shorter) and its size.
 Status ReadPrefix(const std::string& path, size_t n, std::string* out, uint64_t* size) {
-  std::ifstream f(path, std::ios::binary | std::ios::ate);
-  if (!f) return Status(Status::kIOError, "cannot open " + path);
-  *size = static_cast<uint64_t>(f.tellg());
-  f.seekg(0);
-  out->assign(static_cast<size_t>(std::min<uint64_t>(n, *size)), '\0');
-  if (!out->empty() && !f.read(&(*out)[0], static_cast<std::streamsize>(out->size())))
-    return Status(Status::kIOError, "cannot read " + path);
-  return Status::OK();
+  return ReadFileLimit(path, n, out, size);
 }
 
 template <class T>
@@ -242,6 +263,60 @@ Status CollectionOptionsFromJson(const JsonValue& j, CollectionOptions* o) {
       return Status(Status::kInvalidArgument, "unknown index type");
   }
   if (const JsonValue* s = j.get("schema")) VDBGPU_RETURN_IF_ERROR(SchemaFromJson(*s, &o->schema));
+  return Status::OK();
+}
+
+// OptionsFromJson exactly as recovery applies it to the manifest's options
+// (src/engine/options_json.cc:10-30, 55-106): every field's type is checked, no range is (Open
+// does not run ValidateOptions); the read path keeps dim, metric, index type and schema.
+Status ManifestOptionsFromJson(const JsonValue& j, CollectionOptions* o) {
+  if (!j.is_object()) return Status(Status::kInvalidArgument, "options must be a JSON object");
+  auto unsigned_of = [](const JsonValue& obj, const char* key, uint64_t* out) -> Status {
+    const JsonValue* v = obj.get(key);
+    if (v == nullptr) return Status::OK();
+    if (v->kind != JsonValue::kUint && !(v->kind == JsonValue::kInt && v->i >= 0))
+      return Status(Status::kInvalidArgument, std::string(key) + " must be a non-negative integer");
+    if (out != nullptr) *out = v->kind == JsonValue::kUint ? v->u : static_cast<uint64_t>(v->i);
+    return Status::OK();
+  };
+  auto number_of = [](const JsonValue& obj, const char* key) -> Status {
+    const JsonValue* v = obj.get(key);
+    if (v != nullptr && !v->is_number()) return Status(Status::kInvalidArgument, std::string(key) + " must be a number");
+    return Status::OK();
+  };
+  uint64_t dim = 0;
+  VDBGPU_RETURN_IF_ERROR(unsigned_of(j, "dim", &dim));
+  o->dim = static_cast<uint32_t>(dim);
+  o->pd = PaddedDim(o->dim);
+  o->metric = 0;
+  if (const JsonValue* m = j.get("metric")) {
+    if (!m->is_string() || !ParseMetricName(m->s, &o->metric))
+      return Status(Status::kInvalidArgument, "unknown metric (use l2, ip or cosine)");
+  }
+  o->index_type = kIndexHnsw;
+  if (const JsonValue* idx = j.get("index")) {
+    if (idx->is_string()) {
+      if (!ParseIndexTypeName(idx->s, &o->index_type)) return Status(Status::kInvalidArgument, "unknown index type");
+    } else if (!idx->is_null()) {
+      if (!idx->is_object()) return Status(Status::kInvalidArgument, "index must be an object");
+      if (const JsonValue* t = idx->get("type")) {
+        if (!t->is_string() || !ParseIndexTypeName(t->s, &o->index_type))
+          return Status(Status::kInvalidArgument, "unknown index type");
+      }
+      for (const char* k : {"M", "ef_construction", "pq_m", "m", "nlist", "max_train_points_per_centroid", "seed"})
+        VDBGPU_RETURN_IF_ERROR(unsigned_of(*idx, k, nullptr));
+    }
+  }
+  o->schema.clear();
+  if (const JsonValue* s = j.get("schema")) VDBGPU_RETURN_IF_ERROR(SchemaFromJson(*s, &o->schema));
+  if (const JsonValue* s = j.get("sync")) {
+    if (!s->is_string() || (s->s != "always" && s->s != "interval" && s->s != "none"))
+      return Status(Status::kInvalidArgument, "unknown sync mode (use always, interval or none)");
+  }
+  for (const char* k : {"sync_interval_ms", "flush_bytes", "flush_age_ms", "tier_base_rows", "tier_fanout"})
+    VDBGPU_RETURN_IF_ERROR(unsigned_of(j, k, nullptr));
+  VDBGPU_RETURN_IF_ERROR(number_of(j, "merge_into_largest_ratio"));
+  VDBGPU_RETURN_IF_ERROR(number_of(j, "delete_compaction_ratio"));
   return Status::OK();
 }
 
@@ -696,52 +771,116 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
   // ReadCurrentManifest (src/storage/manifest.cc:116-127).
   std::string current;
   VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/CURRENT", &current));
-  while (!current.empty() && (current.back() == '\n' || current.back() == '\r' || current.back() == ' '))
-    current.pop_back();
-  if (current.rfind("MANIFEST-", 0) != 0) return Status(Status::kCorruption, "bad CURRENT file");
+  while (!current.empty() && (current.back() == '\n' || current.back() == '\r')) current.pop_back();
+  uint64_t number = 0;
+  if (!ParseNumberedName(current, "MANIFEST-", "", &number)) return Status(Status::kCorruption, "bad CURRENT file");
   std::string mf;
   VDBGPU_RETURN_IF_ERROR(ReadFile(path + "/" + current, &mf));
   std::string_view payload;
   VDBGPU_RETURN_IF_ERROR(DecodeBlob(mf, "VDBMAN01", &payload));
+  // DecodeManifest (manifest.cc:75-106): nlohmann::json's at() and get<T>() on every key, their
+  // exceptions reported as "bad manifest: <what()>".
   JsonValue j;
   if (!ParseJson(payload, &j) || !j.is_object()) return Status(Status::kCorruption, "manifest is not valid JSON");
-  const JsonValue* fv = j.get("format_version");
-  if (fv == nullptr || !fv->is_integer() || fv->number() != 1)
-    return Status(Status::kCorruption, "unknown manifest version");
-  const JsonValue* opts = j.get("options");
-  const JsonValue* segs = j.get("segments");
-  if (opts == nullptr || segs == nullptr || !segs->is_array()) return Status(Status::kCorruption, "bad manifest");
-  auto u64_of = [&](const char* key) -> uint64_t {
-    const JsonValue* v = j.get(key);
-    return v != nullptr && v->is_integer() ? static_cast<uint64_t>(v->number()) : 0;
+  auto type_name = [](const JsonValue& v) -> std::string {
+    switch (v.kind) {
+      case JsonValue::kNull: return "null";
+      case JsonValue::kBool: return "boolean";
+      case JsonValue::kString: return "string";
+      case JsonValue::kArray: return "array";
+      case JsonValue::kObject: return "object";
+      default: return "number";
+    }
   };
-  const uint64_t flushed_lsn = u64_of("flushed_lsn"), wal_log_number = u64_of("wal_log_number");
-  uint64_t next = u64_of("next_file_number");
-  VDBGPU_RETURN_IF_ERROR(CollectionOptionsFromJson(*opts, opt));
+  auto bad = [](const std::string& what) { return Status(Status::kCorruption, "bad manifest: " + what); };
+  auto at = [&](const JsonValue& o, const char* key, const JsonValue** out) -> Status {
+    if (!o.is_object()) return bad("[json.exception.type_error.304] cannot use at() with " + type_name(o));
+    *out = o.get(key);
+    if (*out == nullptr) return bad(std::string("[json.exception.out_of_range.403] key '") + key + "' not found");
+    return Status::OK();
+  };
+  // get<unsigned T>(): numbers and booleans convert (static_cast), anything else is a type error.
+  auto get_u64 = [&](const JsonValue& v, uint64_t* out) -> Status {
+    switch (v.kind) {
+      case JsonValue::kUint: *out = v.u; return Status::OK();
+      case JsonValue::kInt: *out = static_cast<uint64_t>(v.i); return Status::OK();
+      case JsonValue::kDouble:
+        *out = v.d >= 0 && v.d < 18446744073709551616.0 ? static_cast<uint64_t>(v.d)
+                                                          : static_cast<uint64_t>(static_cast<int64_t>(v.d));
+        return Status::OK();
+      case JsonValue::kBool: *out = v.b ? 1 : 0; return Status::OK();
+      default: return bad("[json.exception.type_error.302] type must be number, but is " + type_name(v));
+    }
+  };
+  auto key_u64 = [&](const JsonValue& o, const char* key, uint64_t* out) -> Status {
+    const JsonValue* v = nullptr;
+    VDBGPU_RETURN_IF_ERROR(at(o, key, &v));
+    return get_u64(*v, out);
+  };
+  // j.value("format_version", 0) != 1: a present value converts like get<int>().
+  int64_t version = 0;
+  if (const JsonValue* fv = j.get("format_version")) {
+    uint64_t x = 0;
+    VDBGPU_RETURN_IF_ERROR(get_u64(*fv, &x));
+    version = fv->kind == JsonValue::kDouble ? static_cast<int64_t>(fv->d) : static_cast<int64_t>(x);
+  }
+  if (version != 1) return Status(Status::kCorruption, "unknown manifest version");
+  uint64_t mnumber = 0, next = 0, flushed_lsn = 0, wal_log_number = 0;
+  VDBGPU_RETURN_IF_ERROR(key_u64(j, "number", &mnumber));
+  const JsonValue* opts = nullptr;
+  VDBGPU_RETURN_IF_ERROR(at(j, "options", &opts));
+  VDBGPU_RETURN_IF_ERROR(ManifestOptionsFromJson(*opts, opt));
+  VDBGPU_RETURN_IF_ERROR(key_u64(j, "next_file_number", &next));
+  VDBGPU_RETURN_IF_ERROR(key_u64(j, "flushed_lsn", &flushed_lsn));
+  VDBGPU_RETURN_IF_ERROR(key_u64(j, "wal_log_number", &wal_log_number));
+  const JsonValue* segs = nullptr;
+  VDBGPU_RETURN_IF_ERROR(at(j, "segments", &segs));
+  // Range-for over a JSON value: an array's elements, an object's values, nothing for null, the
+  // value itself otherwise.
+  std::vector<const JsonValue*> seg_list;
+  if (segs->is_array()) {
+    for (const auto& v : segs->arr) seg_list.push_back(&v);
+  } else if (segs->is_object()) {
+    for (const auto& kv : segs->obj) seg_list.push_back(&kv.second);
+  } else if (!segs->is_null()) {
+    seg_list.push_back(segs);
+  }
   d->path = path;
   d->shard = shard;
   d->nshards = nshards;
   d->flushed_lsn = flushed_lsn;
   std::vector<SegEntry>& entries = d->segs;
-  entries.resize(segs->arr.size());
-  for (size_t i = 0; i < segs->arr.size(); ++i) {
-    const JsonValue& s = segs->arr[i];
-    const JsonValue* idv = s.get("id");
-    const JsonValue* rv = s.get("rows");
-    const JsonValue* lv = s.get("lsn");
-    const JsonValue* dfv = s.get("deletes_file");
-    if (idv == nullptr || rv == nullptr || !idv->is_integer() || !rv->is_integer() ||
-        (dfv != nullptr && !dfv->is_string()) || (lv != nullptr && !lv->is_integer()))
-      return Status(Status::kCorruption, "bad manifest segment entry");
+  entries.resize(seg_list.size());
+  for (size_t i = 0; i < seg_list.size(); ++i) {
+    const JsonValue& s = *seg_list[i];
     SegEntry& e = entries[i];
-    e.id = static_cast<uint32_t>(idv->number());
-    e.rows = static_cast<uint64_t>(rv->number());
-    e.lsn = lv != nullptr ? static_cast<uint64_t>(lv->number()) : 0;
-    if (dfv != nullptr) e.deletes_file = dfv->s;
+    uint64_t id = 0, deleted = 0;
+    VDBGPU_RETURN_IF_ERROR(key_u64(s, "id", &id));
+    e.id = static_cast<uint32_t>(id);
+    VDBGPU_RETURN_IF_ERROR(key_u64(s, "rows", &e.rows));
+    VDBGPU_RETURN_IF_ERROR(key_u64(s, "deleted", &deleted));
+    VDBGPU_RETURN_IF_ERROR(key_u64(s, "lsn", &e.lsn));
+    const JsonValue* dfv = nullptr;
+    VDBGPU_RETURN_IF_ERROR(at(s, "deletes_file", &dfv));
+    if (!dfv->is_string()) return bad("[json.exception.type_error.302] type must be string, but is " + type_name(*dfv));
+    e.deletes_file = dfv->s;
+    const JsonValue* files = nullptr;
+    VDBGPU_RETURN_IF_ERROR(at(s, "files", &files));
+    // it.key() needs an object iterator; null and empty arrays iterate nothing.
+    if (files->is_object()) {
+      for (const auto& kv : files->obj) {
+        uint64_t x = 0;
+        VDBGPU_RETURN_IF_ERROR(key_u64(kv.second, "size", &x));
+        VDBGPU_RETURN_IF_ERROR(key_u64(kv.second, "crc", &x));
+      }
+    } else if (!files->is_null() && !(files->is_array() && files->arr.empty())) {
+      return bad("[json.exception.invalid_iterator.207] cannot use key() for non-object iterators");
+    }
     char name[32];
     std::snprintf(name, sizeof(name), "seg-%06u", e.id);
     e.dir = path + "/segments/" + name;
   }
+  if (mnumber != number) return Status(Status::kCorruption, "manifest number does not match CURRENT");
   // The next file number (Recover steps 1, 2 and 5): past every manifest, segment directory and
   // log; the mutable segment takes it.
   uint64_t num = 0;

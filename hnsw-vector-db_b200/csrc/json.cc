@@ -155,6 +155,33 @@ class Parser {
       const unsigned char c = static_cast<unsigned char>(*p_++);
       if (c == '"') return true;
       if (c < 0x20) return false;  // control characters must be escaped
+      if (c >= 0x80) {
+        // A well-formed UTF-8 sequence (the Unicode standard's table of well-formed byte
+        // sequences): no overlong forms, no surrogates, nothing above U+10FFFF.
+        int more = 0;
+        unsigned char lo = 0x80, hi = 0xBF;
+        if (c >= 0xC2 && c <= 0xDF) {
+          more = 1;
+        } else if (c >= 0xE0 && c <= 0xEF) {
+          more = 2;
+          if (c == 0xE0) lo = 0xA0;
+          if (c == 0xED) hi = 0x9F;
+        } else if (c >= 0xF0 && c <= 0xF4) {
+          more = 3;
+          if (c == 0xF0) lo = 0x90;
+          if (c == 0xF4) hi = 0x8F;
+        } else {
+          return false;
+        }
+        if (end_ - p_ < more) return false;
+        out->push_back(static_cast<char>(c));
+        for (int i = 0; i < more; ++i) {
+          const unsigned char t = static_cast<unsigned char>(*p_++);
+          if (t < (i == 0 ? lo : 0x80) || t > (i == 0 ? hi : 0xBF)) return false;
+          out->push_back(static_cast<char>(t));
+        }
+        continue;
+      }
       if (c != '\\') {
         out->push_back(static_cast<char>(c));
         continue;

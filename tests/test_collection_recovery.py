@@ -179,3 +179,43 @@ def test_fuzzed_manifests_never_crash(tmp_path):
     import vdb_b200
     codes = _fuzz(tmp_path, "coll_mutable", _manifest_path, _reblob, 200, 3)
     assert codes.get(vdb_b200.CORRUPTION, 0) > 0
+
+
+@pytest.mark.parametrize("which", ["manifest", "log"])
+def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which):
+    """Damaged copies of the mutable fixture (manifest payloads, log records; checksums
+    recomputed) recovered by the reference's own Collection::Open and by inspect: the same status
+    code class, the same message, and when both open, the same Stats. Needs the reference engine
+    (oracle/_ref), built from the reference sources where they are present."""
+    import shutil
+
+    import oracle
+    import vdb_b200
+    if not os.path.exists(oracle.REF_ENGINE_LIB):
+        pytest.skip("the reference engine is not built here")
+    g = golden("coll_mutable")
+    base = extract_collection(g, tmp_path / "base")
+    target = _manifest_path(base, g) if which == "manifest" else _log(base)[0]
+    mutate = _reblob if which == "manifest" else _relog
+    orig = open(target, "rb").read()
+    rng = np.random.default_rng(21)
+    bad = []
+    for it in range(80):
+        open(target, "wb").write(mutate(orig, rng))
+        try:
+            ours = (0, vdb_b200.inspect_collection(base))
+        except vdb_b200.VdbError as e:
+            ours = (e.code, str(e).split(": ", 1)[1])
+        copy = str(tmp_path / f"copy{it}")
+        shutil.copytree(base, copy)  # the reference's recovery writes into the directory
+        try:
+            c = oracle.RefCollection.open(copy, threads=1)
+            ref = (0, c.stats())
+            c.close()
+        except RuntimeError as e:
+            ref = (-1, str(e))
+        shutil.rmtree(copy)
+        if (ours[0] == 0) != (ref[0] == 0) or (ours[0] == 0 and ours[1] != ref[1]) or \
+                (ours[0] != 0 and ours[1].replace(base, copy) not in ref[1]):
+            bad.append((it, str(ours)[:160], str(ref)[:160]))
+    assert not bad, bad[:4]
