@@ -321,29 +321,201 @@ std::string JsonQuote(const std::string& s) {
   return o + "\"";
 }
 
+namespace {
+
+// Grisu2 (F. Loitsch, "Printing floating-point numbers quickly and accurately with integers",
+// PLDI 2010) with the parameters nlohmann::json's dump uses: alpha = -60, gamma = -32, cached
+// powers of ten every 8 decades from 1e-300, and the rounding interval shrunk by one unit on each
+// side. Its digits are shortest within that interval but not always the closest, so the last
+// digit can differ from a correctly rounded shortest form; this reproduces the reference's text.
+struct DiyFp {
+  uint64_t f;
+  int e;
+};
+
+DiyFp Mul(DiyFp x, DiyFp y) {  // the upper 64 bits of the 128-bit product, rounded half up
+  const unsigned __int128 p = static_cast<unsigned __int128>(x.f) * y.f;
+  const uint64_t h = static_cast<uint64_t>(p >> 64) + (static_cast<uint64_t>(p) >> 63);
+  return {h, x.e + y.e + 64};
+}
+
+DiyFp Normalize(DiyFp x) {
+  while ((x.f >> 63) == 0) {
+    x.f <<= 1;
+    --x.e;
+  }
+  return x;
+}
+
+struct CachedPower {
+  uint64_t f;
+  int e;
+  int k;
+};
+
+// 10^k = f * 2^e, f normalized to 64 bits and rounded to nearest, for k = -300, -292, ..., 324
+// (exact big-integer arithmetic).
+constexpr CachedPower kCachedPowers[] = {
+    {0xAB70FE17C79AC6CAull, -1060, -300},
+    {0xFF77B1FCBEBCDC4Full, -1034, -292},
+    {0xBE5691EF416BD60Cull, -1007, -284},
+    {0x8DD01FAD907FFC3Cull, -980, -276},
+    {0xD3515C2831559A83ull, -954, -268},
+    {0x9D71AC8FADA6C9B5ull, -927, -260},
+    {0xEA9C227723EE8BCBull, -901, -252},
+    {0xAECC49914078536Dull, -874, -244},
+    {0x823C12795DB6CE57ull, -847, -236},
+    {0xC21094364DFB5637ull, -821, -228},
+    {0x9096EA6F3848984Full, -794, -220},
+    {0xD77485CB25823AC7ull, -768, -212},
+    {0xA086CFCD97BF97F4ull, -741, -204},
+    {0xEF340A98172AACE5ull, -715, -196},
+    {0xB23867FB2A35B28Eull, -688, -188},
+    {0x84C8D4DFD2C63F3Bull, -661, -180},
+    {0xC5DD44271AD3CDBAull, -635, -172},
+    {0x936B9FCEBB25C996ull, -608, -164},
+    {0xDBAC6C247D62A584ull, -582, -156},
+    {0xA3AB66580D5FDAF6ull, -555, -148},
+    {0xF3E2F893DEC3F126ull, -529, -140},
+    {0xB5B5ADA8AAFF80B8ull, -502, -132},
+    {0x87625F056C7C4A8Bull, -475, -124},
+    {0xC9BCFF6034C13053ull, -449, -116},
+    {0x964E858C91BA2655ull, -422, -108},
+    {0xDFF9772470297EBDull, -396, -100},
+    {0xA6DFBD9FB8E5B88Full, -369, -92},
+    {0xF8A95FCF88747D94ull, -343, -84},
+    {0xB94470938FA89BCFull, -316, -76},
+    {0x8A08F0F8BF0F156Bull, -289, -68},
+    {0xCDB02555653131B6ull, -263, -60},
+    {0x993FE2C6D07B7FACull, -236, -52},
+    {0xE45C10C42A2B3B06ull, -210, -44},
+    {0xAA242499697392D3ull, -183, -36},
+    {0xFD87B5F28300CA0Eull, -157, -28},
+    {0xBCE5086492111AEBull, -130, -20},
+    {0x8CBCCC096F5088CCull, -103, -12},
+    {0xD1B71758E219652Cull, -77, -4},
+    {0x9C40000000000000ull, -50, 4},
+    {0xE8D4A51000000000ull, -24, 12},
+    {0xAD78EBC5AC620000ull, 3, 20},
+    {0x813F3978F8940984ull, 30, 28},
+    {0xC097CE7BC90715B3ull, 56, 36},
+    {0x8F7E32CE7BEA5C70ull, 83, 44},
+    {0xD5D238A4ABE98068ull, 109, 52},
+    {0x9F4F2726179A2245ull, 136, 60},
+    {0xED63A231D4C4FB27ull, 162, 68},
+    {0xB0DE65388CC8ADA8ull, 189, 76},
+    {0x83C7088E1AAB65DBull, 216, 84},
+    {0xC45D1DF942711D9Aull, 242, 92},
+    {0x924D692CA61BE758ull, 269, 100},
+    {0xDA01EE641A708DEAull, 295, 108},
+    {0xA26DA3999AEF774Aull, 322, 116},
+    {0xF209787BB47D6B85ull, 348, 124},
+    {0xB454E4A179DD1877ull, 375, 132},
+    {0x865B86925B9BC5C2ull, 402, 140},
+    {0xC83553C5C8965D3Dull, 428, 148},
+    {0x952AB45CFA97A0B3ull, 455, 156},
+    {0xDE469FBD99A05FE3ull, 481, 164},
+    {0xA59BC234DB398C25ull, 508, 172},
+    {0xF6C69A72A3989F5Cull, 534, 180},
+    {0xB7DCBF5354E9BECEull, 561, 188},
+    {0x88FCF317F22241E2ull, 588, 196},
+    {0xCC20CE9BD35C78A5ull, 614, 204},
+    {0x98165AF37B2153DFull, 641, 212},
+    {0xE2A0B5DC971F303Aull, 667, 220},
+    {0xA8D9D1535CE3B396ull, 694, 228},
+    {0xFB9B7CD9A4A7443Cull, 720, 236},
+    {0xBB764C4CA7A44410ull, 747, 244},
+    {0x8BAB8EEFB6409C1Aull, 774, 252},
+    {0xD01FEF10A657842Cull, 800, 260},
+    {0x9B10A4E5E9913129ull, 827, 268},
+    {0xE7109BFBA19C0C9Dull, 853, 276},
+    {0xAC2820D9623BF429ull, 880, 284},
+    {0x80444B5E7AA7CF85ull, 907, 292},
+    {0xBF21E44003ACDD2Dull, 933, 300},
+    {0x8E679C2F5E44FF8Full, 960, 308},
+    {0xD433179D9C8CB841ull, 986, 316},
+    {0x9E19DB92B4E31BA9ull, 1013, 324},
+};
+
+void Grisu2(double v, std::string* digits, int* decimal_exponent) {
+  uint64_t bits;
+  std::memcpy(&bits, &v, 8);
+  const uint64_t frac = bits & ((uint64_t{1} << 52) - 1);
+  const int bexp = static_cast<int>(bits >> 52);
+  const DiyFp w0 = bexp == 0 ? DiyFp{frac, 1 - 1075} : DiyFp{frac + (uint64_t{1} << 52), bexp - 1075};
+  // Rounding boundaries: half-way to the neighbouring doubles (closer below at a power of two).
+  const bool lower_closer = frac == 0 && bexp > 1;
+  const DiyFp m_plus{2 * w0.f + 1, w0.e - 1};
+  const DiyFp m_minus = lower_closer ? DiyFp{4 * w0.f - 1, w0.e - 2} : DiyFp{2 * w0.f - 1, w0.e - 1};
+  const DiyFp wp = Normalize(m_plus);
+  const DiyFp wm{m_minus.f << (m_minus.e - wp.e), wp.e};
+  const DiyFp w = Normalize(w0);
+  // The cached power c = 10^k that brings the exponent into [alpha, gamma]: k is the smallest
+  // tabulated decade at or above ceil((alpha - e - 1) * log10(2)).
+  constexpr int kAlpha = -60;
+  const int kk = static_cast<int>(std::ceil((kAlpha - wp.e - 1) * 0.30102999566398119521));
+  const CachedPower& c = kCachedPowers[(300 + kk + 7) / 8];
+  const DiyFp cp{c.f, c.e};
+  const DiyFp W = Mul(w, cp), Wm = Mul(wm, cp), Wp = Mul(wp, cp);
+  const DiyFp M_minus{Wm.f + 1, Wm.e}, M_plus{Wp.f - 1, Wp.e};
+  int dexp = -c.k;
+  // Digit generation within (M_minus, M_plus), then moving the last digit towards W.
+  uint64_t delta = M_plus.f - M_minus.f;
+  uint64_t dist = M_plus.f - W.f;
+  const int shift = -M_plus.e;
+  const uint64_t one = uint64_t{1} << shift;
+  uint32_t p1 = static_cast<uint32_t>(M_plus.f >> shift);
+  uint64_t p2 = M_plus.f & (one - 1);
+  auto round_last = [&](uint64_t rest, uint64_t ten_k) {
+    while (rest < dist && delta - rest >= ten_k && (rest + ten_k < dist || dist - rest > rest + ten_k - dist)) {
+      --digits->back();
+      rest += ten_k;
+    }
+  };
+  uint32_t pow10 = 1;
+  int n = 1;
+  while (pow10 <= p1 / 10) {
+    pow10 *= 10;
+    ++n;
+  }
+  digits->clear();
+  while (n > 0) {
+    digits->push_back(static_cast<char>('0' + p1 / pow10));
+    p1 %= pow10;
+    --n;
+    const uint64_t rest = (static_cast<uint64_t>(p1) << shift) + p2;
+    if (rest <= delta) {
+      *decimal_exponent = dexp + n;
+      round_last(rest, static_cast<uint64_t>(pow10) << shift);
+      return;
+    }
+    pow10 /= 10;
+  }
+  int m = 0;
+  for (;;) {
+    p2 *= 10;
+    digits->push_back(static_cast<char>('0' + (p2 >> shift)));
+    p2 &= one - 1;
+    ++m;
+    delta *= 10;
+    dist *= 10;
+    if (p2 <= delta) break;
+  }
+  *decimal_exponent = dexp - m;
+  round_last(p2, one);
+}
+
+}  // namespace
+
 std::string JsonNumber(double d) {
   if (!std::isfinite(d)) return "null";
   if (d == 0) return std::signbit(d) ? "-0.0" : "0.0";
   std::string out = d < 0 ? "-" : "";
   d = std::fabs(d);
-  // Shortest decimal digits D.DDDe[+-]X that identify d with room to spare: the value must lie
-  // strictly inside d's rounding interval, half-way to each neighbouring double (the boundaries
-  // themselves, reached only through round-half-even, are excluded, as in the shortest-digit
-  // search of Loitsch's Grisu2, which nlohmann::json's dump uses). The half-way points are exact
-  // in long double (64-bit significand).
-  const long double lo = (static_cast<long double>(d) + std::nextafter(d, 0.0)) / 2;
-  const long double hi = (static_cast<long double>(d) + std::nextafter(d, HUGE_VAL)) / 2;
-  char buf[48];
-  for (int prec = 1; prec <= 17; ++prec) {
-    std::snprintf(buf, sizeof(buf), "%.*e", prec - 1, d);
-    const long double v = std::strtold(buf, nullptr);
-    if (std::strtod(buf, nullptr) == d && lo < v && v < hi) break;
-  }
   std::string digits;
-  const char* e = std::strchr(buf, 'e');
-  for (const char* c = buf; c < e; ++c)
-    if (*c != '.') digits.push_back(*c);
-  const int exp10 = std::atoi(e + 1);
+  int dexp = 0;
+  Grisu2(d, &digits, &dexp);
+  const int exp10 = dexp + static_cast<int>(digits.size()) - 1;
   const int k = static_cast<int>(digits.size());
   const int n = exp10 + 1;  // position of the decimal point
   // Layout of nlohmann::json's number serialisation (fixed for -4 < n <= 15, else exponential).

@@ -298,9 +298,10 @@ def pack_dir_with_logs(path):
 
 
 def fuzz_parse_golden(n=3000, seed=5):
-    """Mutated filter texts (characters and tokens inserted, deleted, replaced in the PARSE_CASES)
-    with the reference parser's code and text for each (tests/golden/filter_fuzz.npz), plus two
-    integer literals whose double sits half-way between two shorter decimals."""
+    """Mutated filter texts (characters and tokens inserted, deleted, replaced in the PARSE_CASES),
+    grammar-generated filters and comparisons against doubles of every magnitude, with the
+    reference parser's code and text for each (tests/golden/filter_fuzz.npz), plus two integer
+    literals whose double sits half-way between two shorter decimals."""
     rng = np.random.default_rng(seed)
     tokens = list('{}[]":,0123456789.-eE ') + [
         '"field"', '"and"', '"or"', '"not"', '"eq"', '"ne"', '"in"', '"gte"', '"lt"', '"exists"', 'true',
@@ -327,6 +328,46 @@ def fuzz_parse_golden(n=3000, seed=5):
         rc, o = oracle.ref_filter_parse(SCHEMA, t)
         if (rc == 0 and codes.count(0) >= nvalid) or (rc != 0 and len(codes) - codes.count(0) >= n - nvalid):
             continue
+        texts.append(t)
+        codes.append(rc)
+        outs.append(o)
+    # Filters generated from the grammar (nested and / or / not over every operator and type),
+    # and single comparisons against doubles of every magnitude, random bit patterns included.
+    types = {f["name"]: f["type"] for f in SCHEMA}
+
+    def number():
+        k = int(rng.integers(0, 4))
+        if k == 0:
+            return float(np.frombuffer(np.array([int(rng.integers(0, 2**63 - 2**52, dtype=np.uint64))], "<u8").tobytes(), "<f8")[0])
+        if k == 1:
+            return float(rng.normal() * 10.0 ** int(rng.integers(-30, 30)))
+        if k == 2:
+            return int(rng.integers(-2**62, 2**62))
+        return float(np.float32(rng.normal() * 10.0 ** int(rng.integers(-10, 10))))
+
+    def leaf():
+        f = str(rng.choice(list(types)))
+        t = types[f]
+        ops = ["eq", "ne", "in", "exists"] + (["lt", "lte", "gt", "gte"] if t in ("int64", "float64") else [])
+        op = str(rng.choice(ops))
+        one = (number if t in ("int64", "float64") else
+               (lambda: str(rng.choice(["en", "t0", "", "\u00e9", "a\"b"]))) if t != "bool" else (lambda: bool(rng.random() < .5)))
+        v = bool(rng.random() < 0.5) if op == "exists" else ([one() for _ in range(int(rng.integers(1, 5)))] if op == "in" else one())
+        return {"field": f, op: v}
+
+    def node(d):
+        r = rng.random()
+        if d > 3 or r < 0.45:
+            return leaf()
+        if r < 0.85:
+            return {"and" if r < 0.65 else "or": [node(d + 1) for _ in range(int(rng.integers(1, 4)))]}
+        return {"not": node(d + 1)}
+
+    extra = [json.dumps(node(0)) for _ in range(1500)]
+    extra += ['{"field": "score", "eq": %s}' % repr(v) for v in (number() for _ in range(1500))
+              if isinstance(v, int) or np.isfinite(v)]
+    for t in extra:
+        rc, o = oracle.ref_filter_parse(SCHEMA, t)
         texts.append(t)
         codes.append(rc)
         outs.append(o)

@@ -19,9 +19,10 @@ def test_filter_parser_matches_reference_golden():
 
 
 def test_filter_parser_matches_reference_on_fuzzed_texts():
-    """3,000 mutations of the golden texts (a third of them valid filters) with the reference
-    parser's code and text: error paths and messages, and numeric literals printed as the
-    reference prints them (shortest digits strictly inside the double's rounding interval)."""
+    """6,000 texts with the reference parser's code and text: mutations of the golden texts (a
+    third of them valid), grammar-generated filters, and comparisons against doubles of every
+    magnitude. Covers error paths and messages, and numbers printed as the reference prints them
+    (Grisu2's digits, which can differ from the correctly rounded shortest form)."""
     import vdb_b200
     g = golden("filter_fuzz")
     schema = str(g["schema"])
