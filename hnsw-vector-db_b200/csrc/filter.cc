@@ -18,10 +18,13 @@ const char* FieldTypeName(FieldType t) {
 }
 
 bool ParseFieldType(std::string_view s, FieldType* out) {
+  // The names and aliases of ParseFieldType (src/util/status.cc:141-156).
   static const std::pair<const char*, FieldType> kTypes[] = {
-      {"int64", FieldType::Int64},   {"float64", FieldType::Float64},
-      {"keyword", FieldType::Keyword}, {"keyword_list", FieldType::KeywordList},
-      {"bool", FieldType::Bool}};
+      {"int64", FieldType::Int64},     {"int", FieldType::Int64},
+      {"float64", FieldType::Float64}, {"float", FieldType::Float64},
+      {"double", FieldType::Float64},  {"keyword", FieldType::Keyword},
+      {"string", FieldType::Keyword},  {"keyword_list", FieldType::KeywordList},
+      {"tags", FieldType::KeywordList}, {"bool", FieldType::Bool}};
   for (const auto& [name, t] : kTypes) {
     if (s == name) {
       *out = t;

@@ -371,8 +371,45 @@ def fuzz_parse_golden(n=3000, seed=5):
         texts.append(t)
         codes.append(rc)
         outs.append(o)
+    # Schemas: the field list with names and types changed (type aliases included), fields
+    # dropped, repeated or given extra keys, and the JSON text mutated; parsed with one filter.
+    schemas, scodes, souts = [], [], []
+    names = ["", "year", "a.b", "x" * 70, "\u00e9", "1abc", "a-b", "_x", "A"]
+    stypes = ["int", "string", "double", "float", "tags", "keyword", "bool", "", "INT64", "int32"]
+    while len(schemas) < 2000:
+        if rng.random() < 0.6:
+            sch = [dict(f) for f in SCHEMA if rng.random() < 0.8]
+            for f in sch:
+                if rng.random() < 0.15:
+                    f["type"] = str(rng.choice(stypes))
+                if rng.random() < 0.1:
+                    f["name"] = str(rng.choice(names))
+                if rng.random() < 0.05:
+                    f["extra"] = 1
+                if rng.random() < 0.05:
+                    del f["type"]
+            if rng.random() < 0.1:
+                sch = sch + sch[:1]
+            t = json.dumps(sch if rng.random() > 0.1 else {f.get("name", "?"): f.get("type", 0) for f in sch})
+        else:
+            b = list(json.dumps(SCHEMA))
+            for _ in range(int(rng.integers(1, 4))):
+                i, op = int(rng.integers(0, len(b) + 1)), int(rng.integers(0, 3))
+                if op == 0 and b:
+                    del b[min(i, len(b) - 1)]
+                elif op == 1:
+                    b.insert(i, tokens[int(rng.integers(0, len(tokens)))])
+                elif b:
+                    b[min(i, len(b) - 1)] = tokens[int(rng.integers(0, len(tokens)))]
+            t = "".join(b)
+        l = oracle._engine_lib()
+        rc = l.ref_filter_parse(t.encode(), b'{"field": "year", "gte": 1}')
+        schemas.append(t)
+        scodes.append(rc)
+        souts.append(l.ref_coll_last_error().decode())
     np.savez_compressed(os.path.join(OUT, "filter_fuzz.npz"), cases=np.array(texts), codes=np.array(codes),
-                        texts=np.array(outs), schema=np.array(json.dumps(SCHEMA)))
+                        texts=np.array(outs), schema=np.array(json.dumps(SCHEMA)), schemas=np.array(schemas),
+                        schema_codes=np.array(scodes), schema_texts=np.array(souts))
     print("wrote filter_fuzz", len(texts), "cases,", sum(c == 0 for c in codes), "valid")
 
 

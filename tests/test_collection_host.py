@@ -31,6 +31,23 @@ def test_filter_parser_matches_reference_on_fuzzed_texts():
     assert not bad, (len(bad), bad[:5])
 
 
+def test_schema_parser_matches_reference_on_fuzzed_texts():
+    """2,000 schemas (names and types changed, type aliases, dropped, repeated and extended
+    fields, mutated JSON) parsed with one filter, against the reference's SchemaFromJson and
+    FilterExpr::Parse (its schema messages carry the status name as a prefix)."""
+    import vdb_b200
+    g = golden("filter_fuzz")
+    bad = []
+    for sch, code, text in zip(g["schemas"], g["schema_codes"], g["schema_texts"]):
+        want = str(text)
+        for prefix in ("invalid_argument: ", "not_found: ", "corruption: "):
+            if int(code) != 0 and want.startswith(prefix):
+                want = want[len(prefix):]
+        if vdb_b200.filter_describe(str(sch), '{"field": "year", "gte": 1}') != (int(code), want):
+            bad.append(str(sch)[:120])
+    assert not bad, (len(bad), bad[:4])
+
+
 def test_filter_parser_matches_live_reference():
     import oracle
     import vdb_b200
