@@ -2,8 +2,8 @@
 
 The reference searches every segment of a collection and merges the per-segment top-k lists
 (CollectionImpl::Search, src/engine/collection_impl.cc:1056-1108). Segments are independent, so
-rank r holds the segments whose manifest position i has i % world == r, searches them with its
-own GPU and merges them locally (ordered by (dist, part, row), one hit per external id). The
+rank r holds the segments whose manifest position i has i % world == r (rank 0 also holds the
+mutable segment rebuilt from the log), searches them with its own GPU and merges them locally (ordered by (dist, part, row), one hit per external id). The
 only exchange is one all-gather of every rank's k merged hit records per query (24 bytes each)
 over NCCL, after which each rank (or rank 0 alone) runs the same merge over the world lists on
 its GPU. The result equals the unsharded merge: a hit among a query's global first k distinct
@@ -72,3 +72,9 @@ class ShardedCollection:
         dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
         vdb_b200.merge_hits(self.ctx, gathered.view(self.world, nq, k * HIT_BYTES), k, out=(ids, dists))
         return ids.view(torch.uint64) if hasattr(torch, "uint64") else ids, dists
+
+    def apply_log(self, records: bytes) -> int:
+        """Applies write-ahead log records on this rank (Collection.apply_log): every rank keeps the
+        id map, deletes rows of its own segments, and rank 0 rebuilds the mutable segment. Every
+        rank must be given the same records, between searches."""
+        return self.local.apply_log(records)
