@@ -219,3 +219,61 @@ def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which)
                 (ours[0] != 0 and ours[1].replace(base, copy) not in ref[1]):
             bad.append((it, str(ours)[:160], str(ref)[:160]))
     assert not bad, bad[:4]
+
+
+def test_recovery_matches_live_reference_on_random_histories(tmp_path):
+    """100 random write histories run by the reference's own Collection (bulk loads, upserts of
+    new and existing ids with and without metadata, removals of live and absent ids, flushes, on
+    flat and HNSW collections, L2 and cosine), closed, then recovered by the reference's
+    Collection::Open and by inspect: Stats identical. Needs the reference engine (oracle/_ref)."""
+    import shutil
+
+    import oracle
+    import vdb_b200
+    if not os.path.exists(oracle.REF_ENGINE_LIB):
+        pytest.skip("the reference engine is not built here")
+    bad = []
+    for sc in range(100):
+        rng = np.random.default_rng(4000 + sc)
+        path, copy = str(tmp_path / f"c{sc}"), str(tmp_path / f"r{sc}")
+        dim = 8
+        c = oracle.RefCollection(path, dim, metric=str(rng.choice(["l2", "cosine"])),
+                                 index={"type": str(rng.choice(["flat", "hnsw"])), "M": 8, "ef_construction": 32},
+                                 schema=[{"name": "year", "type": "int64"}], threads=1)
+        live, next_id = [], 1
+        for _ in range(int(rng.integers(3, 12))):
+            op = rng.random()
+            if op < 0.25:
+                m = int(rng.integers(1, 300))
+                ids = np.arange(next_id, next_id + m, dtype=np.uint64)
+                next_id += m
+                c.bulk_load(ids, rng.standard_normal((m, dim)).astype(np.float32))
+                live += ids.tolist()
+            elif op < 0.6:
+                m = int(rng.integers(1, 60))
+                if live and rng.random() < 0.5:
+                    ids = np.array([live[int(i)] for i in rng.integers(0, len(live), m)], np.uint64)
+                else:
+                    ids = np.arange(next_id, next_id + m, dtype=np.uint64)
+                    next_id += m
+                meta = [None if rng.random() < 0.5 else {"year": int(rng.integers(1990, 2030))} for _ in range(m)]
+                c.upsert(ids, rng.standard_normal((m, dim)).astype(np.float32), meta)
+                live = sorted(set(live) | set(ids.tolist()))
+            elif op < 0.85:
+                m = int(rng.integers(1, 40))
+                ids = np.array([live[int(i)] for i in rng.integers(0, len(live), m)] if live else [1], np.uint64)
+                c.remove(np.concatenate([ids, np.array([10**9], np.uint64)]))
+                live = sorted(set(live) - set(ids.tolist()))
+            else:
+                c.flush()
+        c.close()
+        shutil.copytree(path, copy)  # the reference's recovery writes into the directory
+        ours = vdb_b200.inspect_collection(path)
+        r = oracle.RefCollection.open(copy, threads=1)
+        want = r.stats()
+        r.close()
+        if ours != want:
+            bad.append((sc, ours, want))
+        shutil.rmtree(path)
+        shutil.rmtree(copy)
+    assert not bad, bad[:2]
