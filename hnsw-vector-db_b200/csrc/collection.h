@@ -63,6 +63,8 @@ struct PartExplain {
   uint64_t live_rows = 0, matches = 0, dc = 0, results = 0;
 };
 
+struct RecoveryState;  // collection_store.h
+
 class GpuCollection {
  public:
   // Opens a collection directory written by the reference (CURRENT -> MANIFEST-<n> -> segments,
@@ -82,7 +84,6 @@ class GpuCollection {
   // call after the records before it were applied. *applied = records applied. Only for
   // collections opened from a directory.
   Status ApplyLog(Context& ctx, std::string_view records, uint64_t* applied);
-  struct LogState;
   // An empty collection with the reference's options JSON (engine/options_json.cc), to which
   // segments are added from their files' contents.
   static Status Create(std::string_view options_json, std::unique_ptr<GpuCollection>* out);
@@ -148,7 +149,7 @@ class GpuCollection {
   bool stats_on_ = false;
   uint64_t stats_[kStats] = {};
   std::vector<std::unique_ptr<GpuSegment>> segs_;
-  std::shared_ptr<LogState> log_;  // host recovery state (collections opened from a directory)
+  std::shared_ptr<RecoveryState> log_;  // host recovery state (collections opened from a directory)
   // Per-batch device scratch (grow-only).
   MultiScratch multi_;
   DeviceBuffer q_raw_, perm_, prepared_, qstatus_, keys_, dc_, short_, leafbits_, pairbits_,
