@@ -277,3 +277,22 @@ def test_recovery_matches_live_reference_on_random_histories(tmp_path):
         shutil.rmtree(path)
         shutil.rmtree(copy)
     assert not bad, bad[:2]
+
+
+def test_inspect_errors_through_the_c_abi(tmp_path):
+    """A missing directory is the reference's IOError text for CURRENT; a buffer too small for the
+    JSON is VDBGPU_RESOURCE_EXHAUSTED with a truncated, terminated prefix; a null path is
+    VDBGPU_INVALID_ARGUMENT."""
+    import ctypes
+
+    import vdb_b200
+    lib = vdb_b200.lib()
+    buf = ctypes.create_string_buffer(256)
+    missing = str(tmp_path / "nope")
+    assert lib.vdbgpu_collection_inspect(missing.encode(), buf, len(buf)) == vdb_b200.IO_ERROR
+    assert buf.value.decode() == f"open {missing}/CURRENT: No such file or directory"
+    path = extract_collection(golden("coll_mutable"), tmp_path)
+    small = ctypes.create_string_buffer(16)
+    assert lib.vdbgpu_collection_inspect(path.encode(), small, len(small)) == vdb_b200.RESOURCE_EXHAUSTED
+    assert small.value.decode() == json.dumps(_inspect(path), separators=(",", ":"))[:15]
+    assert lib.vdbgpu_collection_inspect(None, buf, len(buf)) == vdb_b200.INVALID_ARGUMENT
