@@ -478,8 +478,6 @@ Status LogApplier::Apply(const WalRecordView& rec, uint64_t skip_below, const Co
   if (rec.lsn != expected)
     return Status(Status::kCorruption, "log sequence gap: expected LSN " + std::to_string(expected) +
                                            ", found " + std::to_string(rec.lsn));
-  ++expected;
-  mut->last_lsn = std::max(mut->last_lsn, rec.lsn);
   Reader r(rec.payload);
   uint64_t id = 0;
   std::string_view vec, meta;
@@ -496,6 +494,10 @@ Status LogApplier::Apply(const WalRecordView& rec, uint64_t skip_below, const Co
       return Status(Status::kCorruption, "bad metadata at LSN " + std::to_string(rec.lsn));
     if (mut->n >= kMutableMaxRows) return Status(Status::kResourceExhausted, "mutable segment is full");
   }
+  // The record is sound: it takes its LSN (a refused record leaves the expected LSN unchanged, so
+  // a live caller may send it again once corrected).
+  ++expected;
+  mut->last_lsn = std::max(mut->last_lsn, rec.lsn);
   auto mark = [&](const Loc& l) {
     if (l.seg >= 0) touched[static_cast<size_t>(l.seg)] = true;
     std::vector<uint32_t>& d = l.seg < 0 ? mut->del : segs[static_cast<size_t>(l.seg)].del;
@@ -525,11 +527,12 @@ Status LogApplier::Apply(const WalRecordView& rec, uint64_t skip_below, const Co
   }
   return Status::OK();
 }
+
 // Recover step 5 (collection_impl.cc:160-235): the records after flushed_lsn of every log, in
 // order; a torn tail is accepted only at the end of the newest log (recovery truncates it there;
 // this loader reads the directory without changing it).
 static Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>& logs, uint64_t flushed_lsn,
-                  const CollectionOptions& opt, std::vector<SegEntry>& segs, MutableRows* mut, LogApplier* ap) {
+                         const CollectionOptions& opt, std::vector<SegEntry>& segs, MutableRows* mut, LogApplier* ap) {
   for (size_t li = 0; li < logs.size(); ++li) {
     const std::string& path = logs[li].first;
     bool torn = false;
@@ -545,9 +548,6 @@ static Status ReplayLogs(const std::vector<std::pair<std::string, std::string>>&
   }
   return Status::OK();
 }
-
-
-
 
 // The directory as Collection::Open recovers it (CollectionImpl::Recover, collection_impl.cc:
 // 76-235), on the host: options, segments with their delete bits (those of shard `shard` of
@@ -716,7 +716,6 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
   }
   return Status::OK();
 }
-
 
 Status GpuCollection::Inspect(const std::string& path, std::string* json) {
   RecoveryState d;

@@ -341,8 +341,9 @@ VDBGPU_API void vdbgpu_buffer_free(void* p);
  * segment (rebuilt on shard 0), and the old rows of upserted or deleted ids are deleted on this
  * shard's segments. Records at or below the last applied LSN are skipped, so a batch may overlap
  * what the directory's log already held; an LSN gap is VDBGPU_CORRUPTION and a damaged record
- * VDBGPU_INVALID_ARGUMENT, each after the records before it were applied. *applied (nullable) =
- * records applied. A flush of the reference (a new disk segment) is followed by reopening. */
+ * VDBGPU_INVALID_ARGUMENT (or VDBGPU_CORRUPTION for a well-framed record with a bad payload), each
+ * after the records before it were applied; the refused record is not consumed and may be sent
+ * again. *applied (nullable) = records applied. A flush of the reference (a new disk segment) is followed by reopening. */
 VDBGPU_API int vdbgpu_collection_apply_log(vdbgpu_collection* c, const void* records, size_t bytes,
                                            uint64_t* applied);
 
