@@ -116,3 +116,49 @@ def decode_portable_roaring(p: bytes):
     assert at == len(p)
     v = np.concatenate(vals) if vals else np.zeros(0, np.int64)
     return v, kinds, cookie & 0xFFFF, count
+
+
+def encode_portable_roaring(values, runs=True) -> bytes:
+    """Sorted distinct uint32 values in CRoaring's portable serialization (RoaringFormatSpec):
+    per 16-bit key an array (<= 4096 values) or bitmap container, or with runs=True a run
+    container where that is smaller. Test-side writer for fixtures."""
+    v = np.unique(np.asarray(values, dtype=np.int64))
+    keys = np.unique(v >> 16)
+    conts = []
+    for key in keys:
+        lo = (v[(v >> 16) == key] & 0xFFFF).astype(np.int64)
+        starts = np.concatenate([[0], np.nonzero(np.diff(lo) != 1)[0] + 1])
+        ends = np.concatenate([starts[1:], [lo.size]]) - 1
+        kind = "bitmap" if lo.size > 4096 else "array"
+        base = 8192 if kind == "bitmap" else 2 + 2 * lo.size
+        if runs and 2 + 4 * starts.size < base:
+            kind = "run"
+        if kind == "run":
+            body = np.array([starts.size], "<u2").tobytes() + np.stack(
+                [lo[starts], lo[ends] - lo[starts]], 1).astype("<u2").tobytes()
+        elif kind == "bitmap":
+            bits = np.zeros(65536, np.uint8)
+            bits[lo] = 1
+            body = np.packbits(bits, bitorder="little").tobytes()
+        else:
+            body = lo.astype("<u2").tobytes()
+        conts.append((int(key), lo.size, kind, body))
+    n = len(conts)
+    has_runs = any(c[2] == "run" for c in conts)
+    if has_runs:
+        bits = np.zeros((n + 7) // 8, np.uint8)
+        for i, c in enumerate(conts):
+            if c[2] == "run":
+                bits[i // 8] |= 1 << (i % 8)
+        head = np.array([12347 | ((n - 1) << 16)], "<u4").tobytes() + bits.tobytes()
+    else:
+        head = np.array([12346, n], "<u4").tobytes()
+    head += np.array([[c[0], c[1] - 1] for c in conts], "<u2").reshape(-1).tobytes()
+    if not has_runs or n >= 4:
+        off = len(head) + 4 * n
+        offs = []
+        for c in conts:
+            offs.append(off)
+            off += len(c[3])
+        head += np.array(offs, "<u4").tobytes()
+    return head + b"".join(c[3] for c in conts)

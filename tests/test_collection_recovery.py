@@ -296,3 +296,54 @@ def test_inspect_errors_through_the_c_abi(tmp_path):
     assert lib.vdbgpu_collection_inspect(path.encode(), small, len(small)) == vdb_b200.RESOURCE_EXHAUSTED
     assert small.value.decode() == json.dumps(_inspect(path), separators=(",", ":"))[:15]
     assert lib.vdbgpu_collection_inspect(None, buf, len(buf)) == vdb_b200.INVALID_ARGUMENT
+
+
+def test_random_delete_sets_decode_as_the_reference(tmp_path):
+    """Random delete sets over the 200,000-row fixture segment (sparse rows, dense ranges, every
+    other row of a key, whole keys; serialized with and without run containers, so every cookie,
+    container kind and offset layout occurs) recovered by inspect: the deleted count is the set's
+    size, and where the reference engine is built, equal to its Collection::Open."""
+    import shutil
+
+    import oracle
+    import vdb_b200
+    from helpers import decode_portable_roaring, encode_portable_roaring
+    live_ref = os.path.exists(oracle.REF_ENGINE_LIB)
+    g = golden("coll_deletes")
+    path = extract_collection(g, tmp_path / "base")
+    seg = json.loads(g[[k for k in g if k.startswith("file:MANIFEST-")][0]].tobytes()[24:])["segments"][0]
+    target = os.path.join(path, "segments", f"seg-{seg['id']:06d}", seg["deletes_file"])
+    rows = seg["rows"]
+    rng = np.random.default_rng(31)
+    kinds_seen = set()
+    for it in range(40):
+        parts = []
+        for _ in range(int(rng.integers(1, 6))):
+            kind = int(rng.integers(0, 4))
+            if kind == 0:
+                parts.append(rng.choice(rows, int(rng.integers(1, 3000)), replace=False))
+            elif kind == 1:
+                a = int(rng.integers(0, rows - 1))
+                parts.append(np.arange(a, min(rows, a + int(rng.integers(1, 20000)))))
+            elif kind == 2:
+                key = int(rng.integers(0, rows >> 16))
+                parts.append(np.arange(key << 16, min(rows, (key + 1) << 16), int(rng.integers(2, 4))))
+            else:
+                key = int(rng.integers(0, (rows >> 16) + 1))
+                parts.append(np.arange(key << 16, min(rows, (key + 1) << 16)))
+        want = np.unique(np.concatenate(parts))
+        payload = encode_portable_roaring(want, runs=bool(it % 2))
+        got_vals, kinds, _, _ = decode_portable_roaring(payload)
+        assert np.array_equal(got_vals, want)
+        kinds_seen |= set(kinds)
+        open(target, "wb").write(blob(b"VDBDEL01", payload))
+        st = vdb_b200.inspect_collection(path)
+        assert st["segments"][1]["deleted"] == want.size
+        if live_ref:
+            copy = str(tmp_path / f"r{it}")
+            shutil.copytree(path, copy)
+            r = oracle.RefCollection.open(copy, threads=1)
+            assert r.stats() == st
+            r.close()
+            shutil.rmtree(copy)
+    assert kinds_seen == {"array", "bitmap", "run"}
