@@ -68,7 +68,7 @@ __device__ void keep_smallest(uint64_t* s, int n, int c) {
     const uint64_t x = i < n ? s[i] : kNoNeighbor;
     const bool keep = i < n && x <= ans;
     const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
-    if (keep) s[w + __popc(m & lt)] = x;  // every read of this round precedes the ballot
+    if (keep) s[w + __popc(m & lt)] = x;  // every read of this pass precedes the ballot
     w += __popc(m);
   }
   __syncwarp();

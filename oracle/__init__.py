@@ -25,7 +25,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REF_LIB = os.path.join(HERE, "_ref", "libvdbref.so")
 REF_ENGINE_LIB = os.path.join(HERE, "_ref", "libvdbref_engine.so")
 ORACLE_LIB = os.path.join(HERE, "liboracle.so")
-REFERENCE_SRC = os.environ.get("VDB_REFERENCE_SRC", "/root/reference")
+# The reference checkout sits beside this repository unless VDB_REFERENCE_SRC names it.
+REFERENCE_SRC = os.environ.get("VDB_REFERENCE_SRC",
+                               os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 ORDER_SCALAR, ORDER_AVX512, ORDER_AVX2 = 0, 1, 2
 L2, IP, COSINE = 0, 1, 2
