@@ -103,7 +103,7 @@ def pack_dir(path):
 
 def make(name, dim, metric, index, sizes, seed, nq=24, filters=FILTERS, cases=CASES):
     rng = np.random.default_rng(seed)
-    tmp = tempfile.mkdtemp()
+    tmp = tempfile.mkdtemp(dir=OUT)  # scratch beside the fixtures, removed below
     path = os.path.join(tmp, "coll")
     coll = oracle.RefCollection(path, dim, metric=metric, index=index, schema=SCHEMA, threads=4)
     centres = rng.standard_normal((12, dim)).astype(np.float32)
@@ -180,7 +180,7 @@ def make_deletes(name="coll_deletes", dim=4, seed=14, nq=32):
     run container (cookie 12346); segment C's is one run (cookie 12347 without offsets). Rows lie on
     a 1/16 grid to keep the fixture small; half the queries sit next to deleted rows."""
     rng = np.random.default_rng(seed)
-    tmp = tempfile.mkdtemp()
+    tmp = tempfile.mkdtemp(dir=OUT)  # scratch beside the fixtures, removed below
     path = os.path.join(tmp, "coll")
     coll = oracle.RefCollection(path, dim, metric="l2", index={"type": "flat"}, schema=[], threads=4)
     sizes = [200000, 5000, 3000]
@@ -231,7 +231,7 @@ def make_mutable(name="coll_mutable", dim=24, seed=15, nq=24):
     searches and explains (mutable part first) come from the reference's Collection::Open of it,
     which replays the log."""
     rng = np.random.default_rng(seed)
-    tmp = tempfile.mkdtemp()
+    tmp = tempfile.mkdtemp(dir=OUT)  # scratch beside the fixtures, removed below
     path = os.path.join(tmp, "coll")
     coll = oracle.RefCollection(path, dim, metric="cosine", index={"type": "hnsw", "M": 8, "ef_construction": 64},
                                 schema=SCHEMA, threads=4)
