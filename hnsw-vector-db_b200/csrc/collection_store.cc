@@ -416,16 +416,44 @@ static std::vector<std::string> ListDir(const std::string& path) {
 // the collection's options: the 4 KiB header and the file's size.
 Status CheckSegmentHeader(const std::string& dir, const char* h, uint64_t file_size, uint64_t rows,
                           const CollectionOptions& opt) {
-  if (file_size < kSegmentHeaderSize) return Status(Status::kCorruption, dir + ": vectors.f32 shorter than its header");
-  if (std::memcmp(h, "VDBSEG01", 8) != 0) return Status(Status::kCorruption, dir + ": bad magic");
+  const std::string vpath = dir + "/vectors.f32";
+  if (file_size < kSegmentHeaderSize) return Status(Status::kCorruption, vpath + ": shorter than its header");
+  if (std::memcmp(h, "VDBSEG01", 8) != 0) return Status(Status::kCorruption, vpath + ": bad magic");
   if (GetAt<uint32_t>(h, kSegmentHeaderSize - 4) != Crc32c(h, kSegmentHeaderSize - 4))
-    return Status(Status::kCorruption, dir + ": header checksum mismatch");
+    return Status(Status::kCorruption, vpath + ": header checksum mismatch");
   const uint64_t data_len = GetAt<uint64_t>(h, 40);
   if (GetAt<uint32_t>(h, 8) != 1 || GetAt<uint32_t>(h, 12) != static_cast<uint32_t>(opt.metric) ||
       GetAt<uint64_t>(h, 16) != rows || GetAt<uint32_t>(h, 24) != opt.dim || GetAt<uint32_t>(h, 28) != opt.pd ||
       GetAt<uint64_t>(h, 32) != kSegmentHeaderSize || rows > (file_size / 4) ||
       data_len != rows * opt.pd * sizeof(float) || file_size - kSegmentHeaderSize < data_len)
-    return Status(Status::kCorruption, dir + ": header does not match the manifest");
+    return Status(Status::kCorruption, vpath + ": header does not match the manifest");
+  return Status::OK();
+}
+
+// The data checksum of Segment::Open with verify_crc (its default; segment_reader.cc:51-53): the
+// crc32c of the rows after the header against the header's field at byte 48, read in chunks.
+static Status VerifySegmentData(const std::string& dir, const char* h) {
+  const std::string vpath = dir + "/vectors.f32";
+  const uint64_t data_len = GetAt<uint64_t>(h, 40);
+  const int fd = ::open(vpath.c_str(), O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return ErrnoStatus("open", vpath, errno);
+  std::vector<char> buf(std::min<uint64_t>(data_len, uint64_t{64} << 20));
+  uint32_t crc = 0;
+  uint64_t done = 0;
+  while (done < data_len) {
+    const size_t want = static_cast<size_t>(std::min<uint64_t>(buf.size(), data_len - done));
+    const ssize_t n = ::pread(fd, buf.data(), want, static_cast<off_t>(kSegmentHeaderSize + done));
+    if (n < 0 && errno == EINTR) continue;
+    if (n <= 0) {
+      const int e = n < 0 ? errno : EIO;
+      ::close(fd);
+      return ErrnoStatus("read", vpath, e);
+    }
+    crc = Crc32cExtend(crc, buf.data(), static_cast<size_t>(n));
+    done += static_cast<uint64_t>(n);
+  }
+  ::close(fd);
+  if (crc != GetAt<uint32_t>(h, 48)) return Status(Status::kCorruption, vpath + ": data checksum mismatch");
   return Status::OK();
 }
 
@@ -691,11 +719,15 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
     logs.emplace_back(p, std::move(data));
   }
   d->mutable_id = static_cast<uint32_t>(next);
-  for (const SegEntry& e : entries) {
+  // Segment::Open's header checks for every segment, and its data checksum for the segments this
+  // shard opens (each shard verifies its own).
+  for (size_t i = 0; i < entries.size(); ++i) {
+    const SegEntry& e = entries[i];
     std::string h;
     uint64_t size = 0;
     VDBGPU_RETURN_IF_ERROR(ReadPrefix(e.dir + "/vectors.f32", kSegmentHeaderSize, &h, &size));
     VDBGPU_RETURN_IF_ERROR(CheckSegmentHeader(e.dir, h.data(), size, e.rows, *opt));
+    if (all || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(VerifySegmentData(e.dir, h.data()));
   }
   // Delete sets: of this shard's segments, and of every segment when the logs hold records (an
   // upsert or delete may name a row of any segment, so the id map needs every segment's ids).

@@ -19,15 +19,33 @@ struct CrcTable {
   }
 };
 
+// The same polynomial with the x86 CRC32 instruction (SSE4.2), 8 bytes at a time.
+__attribute__((target("sse4.2"))) uint32_t Crc32cHw(const uint8_t* p, size_t n, uint32_t c) {
+  uint64_t c64 = c;
+  for (; n >= 8; n -= 8, p += 8) {
+    uint64_t w;
+    std::memcpy(&w, p, 8);
+    c64 = __builtin_ia32_crc32di(c64, w);
+  }
+  c = static_cast<uint32_t>(c64);
+  for (; n > 0; --n, ++p) c = __builtin_ia32_crc32qi(c, *p);
+  return c;
+}
+
 }  // namespace
 
-uint32_t Crc32c(const void* data, size_t n) {
+uint32_t Crc32cExtend(uint32_t crc, const void* data, size_t n) {
   static const CrcTable table;
+  static const bool hw = __builtin_cpu_supports("sse4.2");
   const auto* p = static_cast<const uint8_t*>(data);
-  uint32_t c = 0xFFFFFFFFu;
+  uint32_t c = crc ^ 0xFFFFFFFFu;
+  if (hw) return Crc32cHw(p, n, c) ^ 0xFFFFFFFFu;
   for (size_t i = 0; i < n; ++i) c = table.t[(c ^ p[i]) & 0xFFu] ^ (c >> 8);
   return c ^ 0xFFFFFFFFu;
 }
+
+uint32_t Crc32c(const void* data, size_t n) { return Crc32cExtend(0, data, n); }
+
 
 bool Reader::raw(void* v, size_t n) {
   if (static_cast<size_t>(end_ - p_) < n) return false;

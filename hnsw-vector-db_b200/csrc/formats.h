@@ -14,6 +14,8 @@ namespace vdbgpu {
 
 // CRC32C (Castagnoli, reflected polynomial 0x82F63B78), as src/util/crc32c.h computes it.
 uint32_t Crc32c(const void* data, size_t n);
+// CRC32C continued over more bytes: Crc32cExtend(Crc32c(a), b) == Crc32c(a followed by b).
+uint32_t Crc32cExtend(uint32_t crc, const void* data, size_t n);
 
 // CheckIndexFile (src/index/index.cc:46-56): 8-byte magic, body, CRC32C of everything before
 // the 4-byte footer.

@@ -155,6 +155,26 @@ def _relog(orig, rng):
     return orig[:off] + bytes(r) + orig[off + ln:]
 
 
+def _revectors(orig, rng):
+    """A segment's vectors.f32 with bytes flipped in its rows (a data checksum mismatch), or in its
+    4 KiB header with the header checksum recomputed half the time (reaching the field checks)."""
+    from helpers import crc32c
+    b = bytearray(orig)
+    if rng.random() < 0.5:
+        for _ in range(int(rng.integers(1, 4))):
+            b[4096 + int(rng.integers(0, len(b) - 4096))] ^= 1 << int(rng.integers(0, 8))
+    else:
+        b[int(rng.integers(0, 64))] ^= 1 << int(rng.integers(0, 8))
+        if rng.random() < 0.5:
+            b[4092:4096] = np.array([crc32c(bytes(b[:4092]))], "<u4").tobytes()
+    return bytes(b)
+
+
+def _vectors_path(p, g):
+    seg = json.loads(g[[k for k in g if k.startswith("file:MANIFEST-")][0]].tobytes()[24:])["segments"][1]
+    return os.path.join(p, "segments", f"seg-{seg['id']:06d}", "vectors.f32")
+
+
 def _manifest_path(p, g):
     return os.path.join(p, [k for k in g if k.startswith("file:MANIFEST-")][0][5:])
 
@@ -181,10 +201,10 @@ def test_fuzzed_manifests_never_crash(tmp_path):
     assert codes.get(vdb_b200.CORRUPTION, 0) > 0
 
 
-@pytest.mark.parametrize("which", ["manifest", "log"])
+@pytest.mark.parametrize("which", ["manifest", "log", "vectors"])
 def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which):
-    """Damaged copies of the mutable fixture (manifest payloads, log records; checksums
-    recomputed) recovered by the reference's own Collection::Open and by inspect: the same status
+    """Damaged copies of the mutable fixture (manifest payloads, log records, a segment's vectors
+    file; checksums recomputed where they would stop the damage early) recovered by the reference's own Collection::Open and by inspect: the same status
     code class, the same message, and when both open, the same Stats. Needs the reference engine
     (oracle/_ref), built from the reference sources where they are present."""
     import shutil
@@ -195,8 +215,8 @@ def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which)
         pytest.skip("the reference engine is not built here")
     g = golden("coll_mutable")
     base = extract_collection(g, tmp_path / "base")
-    target = _manifest_path(base, g) if which == "manifest" else _log(base)[0]
-    mutate = _reblob if which == "manifest" else _relog
+    target = {"manifest": _manifest_path, "log": lambda p, g: _log(p)[0], "vectors": _vectors_path}[which](base, g)
+    mutate = {"manifest": _reblob, "log": _relog, "vectors": _revectors}[which]
     orig = open(target, "rb").read()
     rng = np.random.default_rng(21)
     bad = []
