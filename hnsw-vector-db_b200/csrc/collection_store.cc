@@ -488,6 +488,45 @@ Status LoadDeletes(SegEntry* e) {
 
 
 
+// meta.bin as Segment::Open reads it (segment_reader.cc:71-90): the blob, the row count and
+// offsets, then every row decoded as SegmentColumns::Build does (columns.cc:40-50).
+static Status CheckMetaBin(const std::string& dir, uint64_t rows, const Schema& schema) {
+  std::string f;
+  VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/meta.bin", &f));
+  std::string_view p;
+  Status st = DecodeBlob(f, "VDBMETA1", &p);
+  if (!st.ok()) return Status(Status::kCorruption, dir + "/meta.bin: " + st.message());
+  Reader r(p);
+  uint64_t n = 0;
+  std::string_view offs_bytes;
+  if (!r.u64(&n) || n != rows || rows >= p.size() / 8 || !r.bytes((rows + 1) * 8, &offs_bytes))
+    return Status(Status::kCorruption, dir + ": bad meta.bin");
+  std::vector<uint64_t> offs(rows + 1);
+  std::memcpy(offs.data(), offs_bytes.data(), offs_bytes.size());
+  std::string_view bytes;
+  r.bytes(r.remaining(), &bytes);
+  for (uint64_t i = 0; i < rows; ++i)
+    if (offs[i] > offs[i + 1] || offs[i + 1] > bytes.size())
+      return Status(Status::kCorruption, dir + ": bad meta.bin offsets");
+  std::vector<RowValue> row(schema.size());
+  for (uint64_t i = 0; i < rows; ++i)
+    if (!DecodeMetaRowValues(schema, bytes.substr(offs[i], offs[i + 1] - offs[i]), &row))
+      return Status(Status::kCorruption, "bad metadata at row " + std::to_string(i));
+  return Status::OK();
+}
+
+// The index file's framing as LoadIndex checks it first (src/index/index.cc:46-87): length,
+// checksum, a known magic. The body is parsed when the index is loaded onto a GPU.
+static Status CheckIndexFraming(const std::string& dir, const char* name) {
+  std::string f;
+  VDBGPU_RETURN_IF_ERROR(ReadFile(dir + "/" + name, &f));
+  std::string_view magic, body;
+  Status st = CheckIndexFile(f, &magic, &body);
+  if (!st.ok()) return Status(st.code(), dir + ": " + st.message());
+  if (IndexTypeForMagic(magic) < 0) return Status(Status::kCorruption, dir + ": unknown index file magic");
+  return Status::OK();
+}
+
 // Recover step 4: live rows of every segment, oldest segment first.
 void LogApplier::Build(const std::vector<SegEntry>& segs) {
   std::vector<size_t> order(segs.size());
@@ -719,20 +758,27 @@ Status RecoverDir(const std::string& path, uint32_t shard, uint32_t nshards, boo
     logs.emplace_back(p, std::move(data));
   }
   d->mutable_id = static_cast<uint32_t>(next);
-  // Segment::Open's header checks for every segment, and its data checksum for the segments this
-  // shard opens (each shard verifies its own).
+  // Segment::Open's checks in its order (segment_reader.cc:20-116) for the segments this shard
+  // opens: the vectors header and data checksum, ids.u64, meta.bin, the index file's framing, the
+  // delete set. Other shards' segments get the header check here and the rest from their owner.
   for (size_t i = 0; i < entries.size(); ++i) {
-    const SegEntry& e = entries[i];
+    SegEntry& e = entries[i];
     std::string h;
     uint64_t size = 0;
     VDBGPU_RETURN_IF_ERROR(ReadPrefix(e.dir + "/vectors.f32", kSegmentHeaderSize, &h, &size));
     VDBGPU_RETURN_IF_ERROR(CheckSegmentHeader(e.dir, h.data(), size, e.rows, *opt));
-    if (all || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(VerifySegmentData(e.dir, h.data()));
+    if (!all && i % nshards != shard) continue;
+    VDBGPU_RETURN_IF_ERROR(VerifySegmentData(e.dir, h.data()));
+    VDBGPU_RETURN_IF_ERROR(LoadIds(&e));
+    std::vector<uint64_t>().swap(e.ids);
+    VDBGPU_RETURN_IF_ERROR(CheckMetaBin(e.dir, e.rows, opt->schema));
+    VDBGPU_RETURN_IF_ERROR(CheckIndexFraming(e.dir, IndexFileName(opt->index_type)));
+    VDBGPU_RETURN_IF_ERROR(LoadDeletes(&e));
   }
-  // Delete sets: of this shard's segments, and of every segment when the logs hold records (an
-  // upsert or delete may name a row of any segment, so the id map needs every segment's ids).
+  // Every segment's delete set when the logs hold records (an upsert or delete may name a row of
+  // any segment, so the id map needs every segment's ids).
   for (size_t i = 0; i < entries.size(); ++i)
-    if (all || any_records || i % nshards == shard) VDBGPU_RETURN_IF_ERROR(LoadDeletes(&entries[i]));
+    if (any_records && entries[i].del.empty()) VDBGPU_RETURN_IF_ERROR(LoadDeletes(&entries[i]));
   d->mut.last_lsn = flushed_lsn;
   for (const SegEntry& e : entries) d->mut.last_lsn = std::max(d->mut.last_lsn, e.lsn);
   // Records continue from flushed_lsn + 1 (collection_impl.cc:183); after the replay, from the

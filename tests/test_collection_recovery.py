@@ -175,6 +175,28 @@ def _vectors_path(p, g):
     return os.path.join(p, "segments", f"seg-{seg['id']:06d}", "vectors.f32")
 
 
+def _reindex(orig, rng):
+    """An index file with bytes flipped (its checksum then fails), or with its magic changed and the
+    checksum recomputed (an unknown magic). Damage to the body behind a valid checksum is found
+    when the index is loaded onto a GPU, so it is not made here."""
+    from helpers import crc32c
+    b = bytearray(orig)
+    if rng.random() < 0.6:
+        b[int(rng.integers(0, len(b)))] ^= 1 << int(rng.integers(0, 8))
+    else:
+        b[int(rng.integers(0, 8))] ^= 1 << int(rng.integers(0, 8))
+        b[-4:] = np.array([crc32c(bytes(b[:-4]))], "<u4").tobytes()
+    return bytes(b)
+
+
+def _segment_file(name):
+    def pick(p, g):
+        seg = json.loads(g[[k for k in g if k.startswith("file:MANIFEST-")][0]].tobytes()[24:])["segments"][1]
+        d = os.path.join(p, "segments", f"seg-{seg['id']:06d}")
+        return os.path.join(d, name if name != "index" else [f for f in os.listdir(d) if f.startswith("index.")][0])
+    return pick
+
+
 def _manifest_path(p, g):
     return os.path.join(p, [k for k in g if k.startswith("file:MANIFEST-")][0][5:])
 
@@ -201,7 +223,7 @@ def test_fuzzed_manifests_never_crash(tmp_path):
     assert codes.get(vdb_b200.CORRUPTION, 0) > 0
 
 
-@pytest.mark.parametrize("which", ["manifest", "log", "vectors"])
+@pytest.mark.parametrize("which", ["manifest", "log", "vectors", "ids", "meta", "index"])
 def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which):
     """Damaged copies of the mutable fixture (manifest payloads, log records, a segment's vectors
     file; checksums recomputed where they would stop the damage early) recovered by the reference's own Collection::Open and by inspect: the same status
@@ -215,8 +237,11 @@ def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which)
         pytest.skip("the reference engine is not built here")
     g = golden("coll_mutable")
     base = extract_collection(g, tmp_path / "base")
-    target = {"manifest": _manifest_path, "log": lambda p, g: _log(p)[0], "vectors": _vectors_path}[which](base, g)
-    mutate = {"manifest": _reblob, "log": _relog, "vectors": _revectors}[which]
+    target = {"manifest": _manifest_path, "log": lambda p, g: _log(p)[0], "vectors": _vectors_path,
+              "ids": _segment_file("ids.u64"), "meta": _segment_file("meta.bin"),
+              "index": _segment_file("index")}[which](base, g)
+    mutate = {"manifest": _reblob, "log": _relog, "vectors": _revectors, "ids": _reblob, "meta": _reblob,
+              "index": _reindex}[which]
     orig = open(target, "rb").read()
     rng = np.random.default_rng(21)
     bad = []
