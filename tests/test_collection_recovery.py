@@ -392,3 +392,14 @@ def test_random_delete_sets_decode_as_the_reference(tmp_path):
             r.close()
             shutil.rmtree(copy)
     assert kinds_seen == {"array", "bitmap", "run"}
+
+
+@pytest.mark.parametrize("name", ["coll_hnsw", "coll_ivfpq", "coll_flat"])
+def test_every_collection_fixture_passes_recovery(tmp_path, name):
+    """The read-path fixtures pass every recovery check that Collection.open runs before its
+    uploads (segment headers and data checksums, ids, metadata rows, index framing)."""
+    import vdb_b200
+    g = golden(name)
+    st = vdb_b200.inspect_collection(extract_collection(g, tmp_path))
+    assert [s["rows"] for s in st["segments"][1:]] == [int(x) for x in g["sizes"]]
+    assert st["live_rows"] == int(np.sum(g["sizes"]))
