@@ -171,8 +171,8 @@ Status ParseIvfPq(std::string_view body, uint64_t rows, uint32_t pd, uint32_t di
   if (!r.bytes(size_t(nl) * pd * 4, &b)) return Status(Status::kCorruption, "truncated ivf centroids");
   out->coarse.resize(size_t(nl) * pd);
   if (!b.empty()) std::memcpy(out->coarse.data(), b.data(), b.size());
-  VDBGPU_RETURN_IF_ERROR(ParsePq(r, &out->pq));
-  if (out->pq.dim != dim) return Status(Status::kCorruption, "bad pq codebook");
+  // IvfPqIndex::load (ivf_pq.cc:263) reports any codebook fault, truncation included, alike.
+  if (!ParsePq(r, &out->pq).ok() || out->pq.dim != dim) return Status(Status::kCorruption, "bad pq codebook");
   const uint32_t m = out->pq.m;
   out->list_off.assign(nl + 1, 0);
   out->ids.clear();

@@ -54,8 +54,9 @@ class HnswGpuIndex final : public GpuIndex {
       uint64_t fn = 0;
       if (!r.u64(&fn) || fn != n) return Status(Status::kCorruption, "hnsw-sq8 index does not match the segment");
       Sq8Data q;
-      VDBGPU_RETURN_IF_ERROR(ParseSq8(r, &q));
-      if (q.pd != pd) return Status(Status::kCorruption, "hnsw-sq8 index does not match the segment");
+      // HnswSq8Index::load (hnsw_index.cc:117-122) reports any quantizer fault as a mismatch.
+      if (!ParseSq8(r, &q).ok() || q.pd != pd)
+        return Status(Status::kCorruption, "hnsw-sq8 index does not match the segment");
       std::string_view codes;
       if (!r.bytes(n * pd, &codes)) return Status(Status::kCorruption, "truncated sq8 codes");
       VDBGPU_RETURN_IF_ERROR(Upload(ctx, q.vmin, &vmin_));

@@ -49,8 +49,9 @@ class IvfPqGpuIndex final : public GpuIndex {
       Reader r(body);
       uint64_t fn = 0;
       if (!r.u64(&fn) || fn != n) return Status(Status::kCorruption, "pq index does not match the segment");
-      VDBGPU_RETURN_IF_ERROR(ParsePq(r, &pq));
-      if (pq.dim != dim) return Status(Status::kCorruption, "pq index does not match the segment");
+      // PqFlatIndex::load (ivf_pq.cc:86-90) reports any codebook fault as a mismatch.
+      if (!ParsePq(r, &pq).ok() || pq.dim != dim)
+        return Status(Status::kCorruption, "pq index does not match the segment");
       if (!r.bytes(n * pq.m, &codes_view)) return Status(Status::kCorruption, "truncated pq codes");
       nlist_ = 0;
     } else {
