@@ -269,7 +269,7 @@ def test_recovery_matches_live_reference_on_damaged_directories(tmp_path, which)
 def test_recovery_matches_live_reference_on_random_histories(tmp_path):
     """100 random write histories run by the reference's own Collection (bulk loads, upserts of
     new and existing ids with and without metadata, removals of live and absent ids, flushes, on
-    flat and HNSW collections, L2 and cosine), closed, then recovered by the reference's
+    collections of every index type, L2 and cosine), closed, then recovered by the reference's
     Collection::Open and by inspect: Stats identical. Needs the reference engine (oracle/_ref)."""
     import shutil
 
@@ -282,8 +282,9 @@ def test_recovery_matches_live_reference_on_random_histories(tmp_path):
         rng = np.random.default_rng(4000 + sc)
         path, copy = str(tmp_path / f"c{sc}"), str(tmp_path / f"r{sc}")
         dim = 8
-        c = oracle.RefCollection(path, dim, metric=str(rng.choice(["l2", "cosine"])),
-                                 index={"type": str(rng.choice(["flat", "hnsw"])), "M": 8, "ef_construction": 32},
+        index = {"type": str(rng.choice(["flat", "hnsw", "hnsw_sq8", "pq", "ivf_pq"])), "M": 8,
+                 "ef_construction": 32, "pq_m": 4, "nlist": 4}
+        c = oracle.RefCollection(path, dim, metric=str(rng.choice(["l2", "cosine"])), index=index,
                                  schema=[{"name": "year", "type": "int64"}], threads=1)
         live, next_id = [], 1
         for _ in range(int(rng.integers(3, 12))):
