@@ -3,6 +3,7 @@
 #include "../../include/vdbgpu.h"
 
 #include <algorithm>
+#include <initializer_list>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -13,6 +14,7 @@
 #include "formats.h"
 #include "noalloc.h"
 #include "runtime.h"
+#include "shard.h"
 
 struct vdbgpu_ctx {
   std::unique_ptr<vdbgpu::Context> c;
@@ -29,6 +31,11 @@ struct vdbgpu_collection {
   std::unique_ptr<vdbgpu::GpuCollection> c;
 };
 
+struct vdbgpu_shard_group {
+  vdbgpu_ctx* ctx;
+  std::unique_ptr<vdbgpu::ShardGroup> g;
+};
+
 static_assert(sizeof(vdbgpu_hit) == sizeof(vdbgpu::HitRecord), "vdbgpu_hit layout");
 
 namespace {
@@ -40,14 +47,16 @@ int Fail(vdbgpu_ctx* ctx, const Status& s) {
   return static_cast<int>(s.code());
 }
 
-bool IsDevicePtr(const void* p) {
-  if (p == nullptr) return false;
-  cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    (void)cudaGetLastError();
-    return false;
-  }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+// True for memory the context's device may use directly. Callers first reject other GPUs'
+// memory (RejectForeign), so false means host memory to be staged through a copy.
+bool IsDevicePtr(const void* p, int device) {
+  return p != nullptr && vdbgpu::WherePointer(p, device) == vdbgpu::MemWhere::kDevice;
+}
+
+// kInvalidArgument when any of the caller's buffers is another GPU's memory.
+Status RejectForeign(int device, std::initializer_list<std::pair<const void*, const char*>> bufs) {
+  for (const auto& b : bufs) VDBGPU_RETURN_IF_ERROR(vdbgpu::RejectOtherDevice(b.first, device, b.second));
+  return Status::OK();
 }
 
 uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
@@ -57,6 +66,12 @@ uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
 extern "C" {
 
 int vdbgpu_abi_version(void) { return VDBGPU_ABI_VERSION; }
+
+int vdbgpu_launch_count(uint64_t* out) {
+  if (out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = vdbgpu::LaunchCount();
+  return VDBGPU_OK;
+}
 
 int vdbgpu_device_count(int* out) {
   if (out == nullptr) return VDBGPU_INVALID_ARGUMENT;
@@ -246,9 +261,13 @@ int vdbgpu_index_search(vdbgpu_index* index, const float* queries, uint64_t nq, 
   auto check = [&](const Status& x) { s = x; return x.ok(); };
   auto cuda = [&](cudaError_t e, const char* what) { return check(vdbgpu::CudaStatus(e, what)); };
 
+  if (!check(RejectForeign(c.device(), {{queries, "the query buffer"}, {allow_bits, "the filter bitset"},
+                                         {out_dist, "the distance output"}, {out_row, "the row output"},
+                                         {out_dist_comps, "the distance-count output"}})))
+    return Fail(ctx, s);
   // Queries.
   void* p = nullptr;
-  if (IsDevicePtr(queries)) {
+  if (IsDevicePtr(queries, c.device())) {
     b.queries = queries;
   } else {
     if (!check(c.workspace(vdbgpu::kWsQueries, nq * pd * sizeof(float), &p))) return Fail(ctx, s);
@@ -269,7 +288,7 @@ int vdbgpu_index_search(vdbgpu_index* index, const float* queries, uint64_t nq, 
     b.allow = static_cast<const uint32_t*>(p);
   }
   // Outputs.
-  const bool dev_out = IsDevicePtr(out_dist) && IsDevicePtr(out_row);
+  const bool dev_out = IsDevicePtr(out_dist, c.device()) && IsDevicePtr(out_row, c.device());
   if (dev_out) {
     b.out_dist = out_dist;
     b.out_row = out_row;
@@ -282,7 +301,7 @@ int vdbgpu_index_search(vdbgpu_index* index, const float* queries, uint64_t nq, 
     b.out_dist = static_cast<float*>(od);
     b.out_row = static_cast<uint32_t*>(orow);
   }
-  const bool dev_dc = out_dist_comps != nullptr && IsDevicePtr(out_dist_comps);
+  const bool dev_dc = out_dist_comps != nullptr && IsDevicePtr(out_dist_comps, c.device());
   if (out_dist_comps != nullptr) {
     if (dev_dc) {
       b.dist_comps = out_dist_comps;
@@ -326,7 +345,11 @@ int vdbgpu_index_search_noalloc(vdbgpu_index* index, const float* queries, uint6
   std::lock_guard<std::mutex> g(c.mu());
   cudaSetDevice(c.device());
   // Host buffers would need staging copies in allocated memory: only device pointers are taken.
-  if (!IsDevicePtr(queries) || !IsDevicePtr(out_dist) || !IsDevicePtr(out_row))
+  if (Status f = RejectForeign(c.device(), {{queries, "the query buffer"}, {out_dist, "the distance output"},
+                                            {out_row, "the row output"}});
+      !f.ok())
+    return Fail(ctx, f);
+  if (!IsDevicePtr(queries, c.device()) || !IsDevicePtr(out_dist, c.device()) || !IsDevicePtr(out_row, c.device()))
     return Fail(ctx, Status(Status::kInvalidArgument,
                             "the allocation-free search takes device pointers for queries and outputs"));
   vdbgpu::SearchBatch b{};
@@ -561,7 +584,10 @@ int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
   const vdbgpu_hit* in = lists;
   void* buf;
   Status s;
-  if (nrec > 0 && !IsDevicePtr(lists)) {
+  s = RejectForeign(cx.device(), {{lists, "the hit lists"}, {out_ids, "the id output"}, {out_dist, "the distance output"},
+                                  {out_hits, "the hit output"}});
+  if (!s.ok()) return Fail(ctx, s);
+  if (nrec > 0 && !IsDevicePtr(lists, cx.device())) {
     s = cx.workspace(vdbgpu::kWsScratch0, nrec * sizeof(vdbgpu_hit), &buf);
     if (!s.ok()) return Fail(ctx, s);
     if (cudaMemcpyAsync(buf, lists, nrec * sizeof(vdbgpu_hit), cudaMemcpyHostToDevice, st) != cudaSuccess)
@@ -574,8 +600,8 @@ int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
   ma.k = static_cast<int>(k);
   ma.nq = nq;
   ma.records = reinterpret_cast<const vdbgpu::HitRecord*>(in);
-  const bool ids_dev = IsDevicePtr(out_ids) && IsDevicePtr(out_dist);
-  const bool hits_dev = IsDevicePtr(out_hits);
+  const bool ids_dev = IsDevicePtr(out_ids, cx.device()) && IsDevicePtr(out_dist, cx.device());
+  const bool hits_dev = IsDevicePtr(out_hits, cx.device());
   void *ib = nullptr, *db = nullptr, *hb = nullptr;
   if (out_ids != nullptr) {
     if (ids_dev) {
@@ -603,6 +629,50 @@ int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
   }
   if (hb != nullptr) cudaMemcpyAsync(out_hits, hb, nq * k * sizeof(vdbgpu_hit), cudaMemcpyDeviceToHost, st);
   s = cx.Sync("merge hits");
+  return s.ok() ? VDBGPU_OK : Fail(ctx, s);
+}
+
+int vdbgpu_shard_id(void* out_id) {
+  if (out_id == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  return static_cast<int>(vdbgpu::ShardUniqueId(out_id).code());
+}
+
+int vdbgpu_shard_group_open(vdbgpu_ctx* ctx, const void* id, int rank, int nranks, int timeout_ms,
+                            vdbgpu_shard_group** out) {
+  if (ctx == nullptr || id == nullptr || out == nullptr) return VDBGPU_INVALID_ARGUMENT;
+  *out = nullptr;
+  std::lock_guard<std::mutex> g(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  std::unique_ptr<vdbgpu::ShardGroup> sg;
+  Status s = vdbgpu::ShardGroup::Open(*ctx->c, id, rank, nranks, timeout_ms, &sg);
+  if (!s.ok()) return Fail(ctx, s);
+  *out = new (std::nothrow) vdbgpu_shard_group{ctx, std::move(sg)};
+  return *out != nullptr ? VDBGPU_OK : VDBGPU_RESOURCE_EXHAUSTED;
+}
+
+void vdbgpu_shard_group_close(vdbgpu_shard_group* g) {
+  if (g == nullptr) return;
+  {
+    std::lock_guard<std::mutex> l(g->ctx->c->mu());
+    cudaSetDevice(g->ctx->c->device());
+    g->g.reset();
+  }
+  delete g;
+}
+
+int vdbgpu_shard_merge(vdbgpu_shard_group* g, const vdbgpu_hit* local, uint64_t nq, uint32_t k, int root,
+                       uint64_t* out_ids, float* out_dist, vdbgpu_hit* out_hits) {
+  if (g == nullptr || (nq > 0 && local == nullptr) || ((out_ids == nullptr) != (out_dist == nullptr)))
+    return VDBGPU_INVALID_ARGUMENT;
+  vdbgpu_ctx* ctx = g->ctx;
+  if (k == 0 || k > 240) return Fail(ctx, Status(Status::kInvalidArgument, "k must be in 1..240"));
+  std::lock_guard<std::mutex> l(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  Status s = RejectForeign(ctx->c->device(), {{local, "the local hit records"}, {out_ids, "the id output"},
+                                              {out_dist, "the distance output"}, {out_hits, "the hit output"}});
+  if (s.ok())
+    s = g->g->Merge(reinterpret_cast<const vdbgpu::HitRecord*>(local), nq, k, root, out_ids, out_dist,
+                    reinterpret_cast<vdbgpu::HitRecord*>(out_hits));
   return s.ok() ? VDBGPU_OK : Fail(ctx, s);
 }
 

@@ -413,6 +413,7 @@ __global__ void __launch_bounds__(kExactWarps * 32) exact_rows_kernel(const Exac
 template <int kT, int kE>
 cudaError_t LaunchExactT(const ExactArgs& a, cudaStream_t st) {
   const int blocks = (a.nitems + kExactWarps - 1) / kExactWarps;
+  NoteLaunch();
   exact_rows_kernel<kT, kE><<<blocks, kExactWarps * 32, 0, st>>>(a);
   return cudaGetLastError();
 }
@@ -563,6 +564,7 @@ cudaError_t LaunchPrepareQueries(const float* in, const uint32_t* perm, uint64_t
   if (nq == 0) return cudaSuccess;
   const int threads = 128;
   const unsigned blocks = static_cast<unsigned>((nq + threads - 1) / threads);
+  NoteLaunch();
   prepare_queries_kernel<<<blocks, threads, 0, st>>>(in, perm, nq, dim, pd, cosine ? 1 : 0, out, qstatus);
   return cudaGetLastError();
 }
@@ -571,12 +573,14 @@ cudaError_t LaunchLeafRange(const RangeTask* tasks, int ntasks, uint32_t max_wor
   if (ntasks == 0 || max_words == 0) return cudaSuccess;
   // 8 warps x 32 words per block.
   const dim3 grid((max_words + 255) / 256, ntasks);
+  NoteLaunch();
   leaf_range_kernel<<<grid, 256, 0, st>>>(tasks);
   return cudaGetLastError();
 }
 
 cudaError_t LaunchPostingScatter(const ScatterTask* tasks, int ntasks, cudaStream_t st) {
   if (ntasks == 0) return cudaSuccess;
+  NoteLaunch();
   posting_scatter_kernel<<<ntasks, 256, 0, st>>>(tasks);
   return cudaGetLastError();
 }
@@ -585,6 +589,7 @@ cudaError_t LaunchFilterProgram(const ProgramTask* tasks, int ntasks, uint32_t m
                                 cudaStream_t st) {
   if (ntasks == 0 || max_words == 0) return cudaSuccess;
   const dim3 grid((max_words + kProgChunkWords - 1) / kProgChunkWords, ntasks);
+  NoteLaunch();
   filter_program_kernel<<<grid, 256, 0, st>>>(tasks, status);
   return cudaGetLastError();
 }
@@ -592,6 +597,7 @@ cudaError_t LaunchFilterProgram(const ProgramTask* tasks, int ntasks, uint32_t m
 cudaError_t LaunchCompactRows(const CompactTask* tasks, int ntasks, uint32_t max_words, cudaStream_t st) {
   if (ntasks == 0 || max_words == 0) return cudaSuccess;
   const dim3 grid((max_words + kProgChunkWords - 1) / kProgChunkWords, ntasks);
+  NoteLaunch();
   compact_rows_kernel<<<grid, 256, 0, st>>>(tasks);
   return cudaGetLastError();
 }
@@ -607,6 +613,7 @@ cudaError_t LaunchPackHits(const PackItem* items, int nitems, uint32_t max_nq, i
                            uint64_t flag_stride, cudaStream_t st) {
   if (nitems == 0 || max_nq == 0) return cudaSuccess;
   const dim3 grid((max_nq + 127) / 128, nitems);
+  NoteLaunch();
   pack_hits_kernel<<<grid, 128, 0, st>>>(items, k, out_stride, flag_stride);
   return cudaGetLastError();
 }
@@ -619,6 +626,7 @@ cudaError_t LaunchMerge(const MergeArgs& a, cudaStream_t st) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const unsigned blocks = static_cast<unsigned>((a.nq + kMergeWarps - 1) / kMergeWarps);
+  NoteLaunch();
   merge_kernel<<<blocks, kMergeWarps * 32, smem, st>>>(a);
   return cudaGetLastError();
 }

@@ -28,14 +28,10 @@ constexpr uint32_t kScatterChunk = 16384;
 
 uint64_t RoundUp(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
 
-bool OnDevice(const void* p) {
-  if (p == nullptr) return false;
-  cudaPointerAttributes a{};
-  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+// Memory of the context's device (or managed). Search rejects other GPUs' buffers first, so
+// false means host memory, staged through a copy.
+bool OnDevice(const void* p, int device) {
+  return p != nullptr && WherePointer(p, device) == MemWhere::kDevice;
 }
 
 template <class T>
@@ -515,6 +511,10 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
   if (r.k == 0 || r.k > kMaxK) return Status(Status::kInvalidArgument, "k must be in 1..10000");
   if (r.k > kMaxGpuK) return Status(Status::kNotSupported, "k above 240 is not supported on the GPU");
   if (r.nq == 0) return Status::OK();
+  VDBGPU_RETURN_IF_ERROR(RejectOtherDevice(r.queries, ctx.device(), "the query buffer"));
+  VDBGPU_RETURN_IF_ERROR(RejectOtherDevice(r.out_ids, ctx.device(), "the id output"));
+  VDBGPU_RETURN_IF_ERROR(RejectOtherDevice(r.out_dist, ctx.device(), "the distance output"));
+  VDBGPU_RETURN_IF_ERROR(RejectOtherDevice(r.out_records, ctx.device(), "the hit output"));
   for (auto& v : stats_) v = 0;
   stats_[0] = r.nq;
   const uint64_t t_search = NowUs();
@@ -553,7 +553,7 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
   cudaStream_t st = ctx.stream();
   // PrepareQuery on the device.
   const float* qin = r.queries;
-  if (!OnDevice(r.queries)) {
+  if (!OnDevice(r.queries, ctx.device())) {
     VDBGPU_RETURN_IF_ERROR(q_raw_.ensure(b.nq * dim * sizeof(float)));
     VDBGPU_CUDA(cudaMemcpyAsync(q_raw_.get(), r.queries, b.nq * dim * sizeof(float), cudaMemcpyHostToDevice, st));
     qin = q_raw_.as<float>();
@@ -622,7 +622,8 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
   ma.part_no = static_cast<const uint32_t*>(part_dev);
   ma.ids = static_cast<const uint64_t* const*>(ids_dev);
   ma.perm = perm_.as<uint32_t>();
-  const bool rec_dev = OnDevice(r.out_records), ids_dev_ok = OnDevice(r.out_ids) && OnDevice(r.out_dist);
+  const bool rec_dev = OnDevice(r.out_records, ctx.device()),
+             ids_dev_ok = OnDevice(r.out_ids, ctx.device()) && OnDevice(r.out_dist, ctx.device());
   if (r.out_records != nullptr) {
     if (rec_dev) {
       ma.out_records = r.out_records;
@@ -680,6 +681,20 @@ Status GpuCollection::Search(Context& ctx, const Request& r) {
         uint64_t res = 0;
         for (uint32_t j = 0; j < b.k; ++j) res += keys[(s * b.nq + i) * b.k + j] != ~0ull ? 1 : 0;
         e.results = res;
+      }
+    }
+    // The reference always searches a mutable segment, empty or not (collection_impl.cc:1056-1059;
+    // SearchMutable, planner.cc:131-149): with no rows it is explained as a scan of nothing. Shard
+    // 0 of a collection opened from a directory reports it the same way.
+    const bool has_mutable = std::any_of(segs_.begin(), segs_.end(), [](const auto& x) { return x->is_mutable; });
+    if (log_ && log_->shard == 0 && !has_mutable) {
+      for (uint64_t i = 0; i < b.nq; ++i) {
+        PartExplain e;
+        e.segment_id = log_->mutable_id;
+        e.is_mutable = true;
+        e.strategy = gof[i] < b.F ? "scan_filter" : "scan";
+        auto& parts = (*r.explain)[b.perm[i]];
+        parts.insert(parts.begin(), e);
       }
     }
   }

@@ -13,6 +13,9 @@
 
 namespace vdbgpu {
 
+// Host side: counts one kernel launch of this library (runtime.cc; read by vdbgpu_launch_count).
+void NoteLaunch();
+
 // Status word codes written by kernels (0 = ok). The host maps any non-zero code to
 // kUnavailable (timeouts) or kInternal (everything else).
 enum DeviceError : int {

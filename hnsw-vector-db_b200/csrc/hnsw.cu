@@ -814,7 +814,9 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
   // Output: the k best results; HNSW-SQ8 re-ranks the best `depth` on fp32 rows first.
   int nout = nres < a.k_graph ? nres : a.k_graph;
   if (!bad && kSq8 && a.depth > 0 && nout > 0) {
-    // Rerank (src/index/index.cc:89-95): exact fp32 distances of the graph's best candidates.
+    // Rerank (src/index/index.cc:89-95): exact fp32 distances of the graph's best candidates,
+    // written back in place over res[0, nout) (nout <= k_graph <= ef slots; the candidate array
+    // of a pooled walk is only the sorted front, shorter than a deep re-rank), then sorted there.
     for (int i = 0; i < nout; i += 4) {
       uint32_t r[4];
 #pragma unroll
@@ -836,14 +838,14 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
           dl = lane == c ? d[c] : dl;
           rl = lane == c ? r[c] : rl;
         }
-        s.cand[i + lane] = pack_neighbor(dl, rl);
+        s.res[i + lane] = pack_neighbor(dl, rl);
       }
       __syncwarp();
     }
     dc += static_cast<uint64_t>(nout);
-    // Sort the re-ranked candidates (insertion into res, nout <= ef).
-    for (int i = 0; i < nout; ++i) {
-      const uint64_t key = s.cand[i];
+    // Insertion sort of res[0, nout) in place: res[0, i) is sorted, res[i] is inserted into it.
+    for (int i = 1; i < nout; ++i) {
+      const uint64_t key = s.res[i];
       __syncwarp();
       insert_sorted(s.res, 0, i, key);
     }
@@ -882,11 +884,13 @@ cudaError_t LaunchHnswSearch(const HnswArgs& a, cudaStream_t stream) {
     e = cudaFuncSetAttribute(hnsw_search_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    NoteLaunch();
     hnsw_search_kernel<true><<<blocks, warps * 32, smem, stream>>>(a);
   } else {
     e = cudaFuncSetAttribute(hnsw_search_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    NoteLaunch();
     hnsw_search_kernel<false><<<blocks, warps * 32, smem, stream>>>(a);
   }
   return cudaGetLastError();

@@ -210,12 +210,14 @@ cudaError_t LaunchSelect(const PruneArgs& a, cudaStream_t st) {
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
+  NoteLaunch();
   select_kernel<<<static_cast<unsigned>((a.n + w - 1) / w), w * 32, smem, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t LaunchReverse(const uint32_t* fwd, int stride, uint64_t n, uint32_t* cnt, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
+  NoteLaunch();
   count_reverse_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(fwd, stride, n, cnt);
   return cudaGetLastError();
 }
@@ -223,6 +225,7 @@ cudaError_t LaunchReverse(const uint32_t* fwd, int stride, uint64_t n, uint32_t*
 cudaError_t LaunchFillReverse(const uint32_t* fwd, int stride, uint64_t n, const uint64_t* off, uint32_t* cursor,
                               uint32_t* rev, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
+  NoteLaunch();
   fill_reverse_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(fwd, stride, n, off, cursor, rev);
   return cudaGetLastError();
 }
@@ -234,12 +237,14 @@ cudaError_t LaunchMergeLinks(const PruneArgs& a, cudaStream_t st) {
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
+  NoteLaunch();
   merge_kernel<<<static_cast<unsigned>((a.n + w - 1) / w), w * 32, smem, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t LaunchGatherRows(const float* rows, const uint32_t* ids, uint64_t n, int pd, float* out, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
+  NoteLaunch();
   gather_rows_kernel<<<static_cast<unsigned>(n), 128, 0, st>>>(rows, ids, n, pd, out);
   return cudaGetLastError();
 }

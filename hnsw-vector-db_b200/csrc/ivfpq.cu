@@ -434,8 +434,11 @@ cudaError_t LaunchProbeOrder(const uint32_t* probe_ids, int nq, int nprobe, uint
   cudaError_t e = cudaMemsetAsync(counts, 0, (static_cast<size_t>(nlist) + 1) * sizeof(uint32_t), stream);
   if (e != cudaSuccess) return e;
   const int blocks = (nq + 255) / 256;
+  NoteLaunch();
   probe_count_kernel<<<blocks, 256, 0, stream>>>(probe_ids, nq, nprobe, nlist, counts);
+  NoteLaunch();
   probe_scan_kernel<<<1, 1024, 0, stream>>>(counts, nlist + 1);
+  NoteLaunch();
   probe_place_kernel<<<blocks, 256, 0, stream>>>(probe_ids, nq, nprobe, nlist, counts, order);
   return cudaGetLastError();
 }
@@ -447,11 +450,13 @@ cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(ivfpq_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    NoteLaunch();
     ivfpq_kernel<8><<<a.nq, 8 * 32, smem, stream>>>(a);
   } else {
     cudaError_t e = cudaFuncSetAttribute(ivfpq_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    NoteLaunch();
     ivfpq_kernel<4><<<a.nq, 4 * 32, smem, stream>>>(a);
   }
   return cudaGetLastError();
@@ -459,6 +464,7 @@ cudaError_t LaunchIvfPq(const IvfPqArgs& a, cudaStream_t stream) {
 
 cudaError_t LaunchTerm2(const float* coarse, uint32_t nlist, int pd, const float* centroids, int m,
                         int ds, float* term2, cudaStream_t stream) {
+  NoteLaunch();
   term2_kernel<<<2048, 256, 0, stream>>>(coarse, nlist, pd, centroids, m, ds, term2);
   return cudaGetLastError();
 }

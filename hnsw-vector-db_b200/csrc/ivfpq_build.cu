@@ -174,6 +174,7 @@ cudaError_t LaunchAssignNearest(const AssignArgs& a, cudaStream_t st) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const uint64_t blocks = (a.n + kAssignThreads - 1) / kAssignThreads;
+  NoteLaunch();
   assign_kernel<<<static_cast<unsigned>(blocks), kAssignThreads, smem, st>>>(a);
   return cudaGetLastError();
 }
@@ -191,6 +192,7 @@ cudaError_t LaunchPqEncode(const PqEncodeArgs& a, cudaStream_t st) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const uint64_t blocks = (a.n + kEncodeThreads - 1) / kEncodeThreads;
+  NoteLaunch();
   pq_encode_kernel<<<static_cast<unsigned>(blocks), kEncodeThreads, smem, st>>>(a, group);
   return cudaGetLastError();
 }

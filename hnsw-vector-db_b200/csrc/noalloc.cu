@@ -13,7 +13,10 @@
 //     made on that device (with the device current). That first call should come before any
 //     stream capture;
 //   * limits: at most 128 queries per call, padded dimension at most 256, at most 16 row slices,
-//     k and the candidate depth as in the regular entry point; larger requests are rejected;
+//     k and the candidate depth as in the regular entry point; larger requests are rejected. With
+//     16 slices the scan keeps at most 16 of the GPU's 148 SMs busy: the entry point is sized for
+//     small latency-bound batches, not for throughput;
+//   * an empty index gives misses (+inf, UINT32_MAX) in every slot, as the regular search does;
 //   * every call shares the one array and keeps the previous call's contents: the per-query
 //     thresholds are reset at the start of each call, everything else is fully rewritten before it
 //     is read. Calls whose work overlaps on the GPU (on different streams, or from different
@@ -45,6 +48,14 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchEnd];
 std::mutex g_mu;
 void* g_addr[kNoAllocMaxDevices] = {};
 
+// Misses for every slot (+inf, UINT32_MAX), as the regular search returns them for an empty index.
+__global__ void fill_misses_kernel(float* dist, uint32_t* row, uint64_t n) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
+    dist[i] = __int_as_float(0x7f800000);
+    row[i] = 0xFFFFFFFFu;
+  }
+}
+
 }  // namespace
 
 const size_t kNoAllocScratchBytes = kScratchEnd;
@@ -75,7 +86,13 @@ Status ScanSearchNoAlloc(Context& ctx, const ScanOperands& op, int metric, uint3
     return Status(Status::kInvalidArgument, "the allocation-free search takes at most 128 queries per call");
   if (op.kpad > kNoAllocMaxKpad)
     return Status(Status::kInvalidArgument, "the allocation-free search supports padded dimensions up to 256");
-  if (op.rows == 0) return Status(Status::kInvalidArgument, "the allocation-free search needs a non-empty index");
+  if (op.rows == 0) {
+    const uint64_t n = b.nq * b.k;
+    NoteLaunch();
+    fill_misses_kernel<<<static_cast<unsigned>(std::min<uint64_t>((n + 255) / 256, 1024)), 256, 0, stream>>>(
+        b.out_dist, b.out_row, n);
+    return CudaStatus(cudaGetLastError(), "fill misses");
+  }
   if (cpre > kScanCap - 64) return Status(Status::kNotSupported, "candidate depth too large");
   void* base = nullptr;
   VDBGPU_RETURN_IF_ERROR(NoAllocScratch(ctx.device(), &base));

@@ -3,6 +3,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -58,6 +59,33 @@ int DetectKernelOrder() {
 
 const char* KernelOrderName(int order) {
   return order == 1 ? "avx512" : order == 2 ? "avx2" : "scalar";
+}
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}  // namespace
+
+void NoteLaunch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t LaunchCount() { return g_launches.load(std::memory_order_relaxed); }
+
+MemWhere WherePointer(const void* p, int device) {
+  if (p == nullptr) return MemWhere::kHost;
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MemWhere::kHost;
+  }
+  if (a.type == cudaMemoryTypeManaged) return MemWhere::kDevice;
+  if (a.type == cudaMemoryTypeDevice) return a.device == device ? MemWhere::kDevice : MemWhere::kOtherDevice;
+  return MemWhere::kHost;
+}
+
+Status RejectOtherDevice(const void* p, int device, const char* what) {
+  if (WherePointer(p, device) != MemWhere::kOtherDevice) return Status::OK();
+  cudaPointerAttributes a{};
+  (void)cudaPointerGetAttributes(&a, p);
+  return Status(Status::kInvalidArgument, std::string(what) + " is memory of device " + std::to_string(a.device) +
+                                              "; this index lives on device " + std::to_string(device));
 }
 
 Status Context::Open(int device, std::unique_ptr<Context>* out) {

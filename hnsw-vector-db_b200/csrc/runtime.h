@@ -89,6 +89,20 @@ class DeviceBuffer {
 int DetectKernelOrder();
 const char* KernelOrderName(int order);
 
+// Kernel launches of this library in this process (every launch site calls NoteLaunch), read by
+// vdbgpu_launch_count: a caller can count the launches of a timed region.
+void NoteLaunch();
+uint64_t LaunchCount();
+
+// Where a caller's buffer lives, seen from a context on `device`: host memory (staged through a
+// copy), memory this device's kernels may use directly (its own allocations, managed memory), or
+// another GPU's memory, which the kernels must not be given: without peer access enabled every
+// access to it is an illegal address.
+enum class MemWhere { kHost, kDevice, kOtherDevice };
+MemWhere WherePointer(const void* p, int device);
+// kInvalidArgument naming `what` when p is another GPU's memory, else OK.
+Status RejectOtherDevice(const void* p, int device, const char* what);
+
 class Context {
  public:
   static Status Open(int device, std::unique_ptr<Context>* out);

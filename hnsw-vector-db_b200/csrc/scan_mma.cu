@@ -518,6 +518,7 @@ cudaError_t LaunchScanT(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, co
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
+  NoteLaunch();
   scan_mma_kernel<kMode, kWgs><<<grid, ScanThreads(kWgs), smem, stream>>>(tmap_a, tmap_b, a);
   return cudaGetLastError();
 }

@@ -589,6 +589,7 @@ cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int blocks = (a.nq + kFinWarps - 1) / kFinWarps;
+  NoteLaunch();
   finalize_kernel<<<blocks, kFinWarps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
@@ -596,6 +597,7 @@ cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream) {
 cudaError_t LaunchScanSeed(const SeedArgs& a, cudaStream_t stream) {
   if (a.nq <= 0) return cudaSuccess;
   const int blocks = (a.nq + kSeedWarps - 1) / kSeedWarps;
+  NoteLaunch();
   scan_seed_kernel<<<blocks, kSeedWarps * 32, 0, stream>>>(a);
   return cudaGetLastError();
 }
@@ -605,6 +607,7 @@ cudaError_t LaunchScatterResults(const float* src_dist, const uint32_t* src_row,
                                  cudaStream_t stream) {
   const uint64_t total = static_cast<uint64_t>(n) * k;
   if (total == 0) return cudaSuccess;
+  NoteLaunch();
   scatter_results_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
       src_dist, src_row, list, n, k, out_dist, out_row);
   return cudaGetLastError();
@@ -613,6 +616,7 @@ cudaError_t LaunchScatterResults(const float* src_dist, const uint32_t* src_row,
 cudaError_t LaunchPrepQueries(const PrepArgs& a, cudaStream_t stream) {
   const int threads = 256;
   const int blocks = (a.nq_pad * 32 + threads - 1) / threads;
+  NoteLaunch();
   prep_queries_kernel<<<blocks, threads, 0, stream>>>(a);
   return cudaGetLastError();
 }
@@ -621,12 +625,14 @@ cudaError_t LaunchPrepRows(const float* rows, uint64_t n, int pd, int kpad, int 
                            int scale_log2, void* operand, float* norms, cudaStream_t stream) {
   const int threads = 256;
   const uint64_t blocks = (n * 32 + threads - 1) / threads;
+  NoteLaunch();
   prep_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
       rows, n, pd, kpad, ab_format, scale_log2, operand, norms);
   return cudaGetLastError();
 }
 
 cudaError_t LaunchAbsMax(const float* x, uint64_t count, uint32_t* out, cudaStream_t stream) {
+  NoteLaunch();
   absmax_kernel<<<1184, 256, 0, stream>>>(x, count, out);
   return cudaGetLastError();
 }
@@ -635,6 +641,7 @@ cudaError_t LaunchSq8MinMax(const float* rows, uint64_t n, int dim, int pd, uint
                             uint32_t* kmax, cudaStream_t stream) {
   if (dim > 1024) return cudaErrorInvalidValue;
   uint64_t blocks = n < 4096 ? (n == 0 ? 1 : n) : 4096;
+  NoteLaunch();
   sq8_minmax_kernel<<<static_cast<unsigned>(blocks), dim, 0, stream>>>(rows, n, dim, pd, kmin, kmax);
   return cudaGetLastError();
 }
@@ -644,6 +651,7 @@ cudaError_t LaunchSq8Encode(const float* rows, uint64_t n, int dim, int pd, int 
                             float* rowterm, cudaStream_t stream) {
   const int threads = 256;
   const uint64_t blocks = (n * 32 + threads - 1) / threads;
+  NoteLaunch();
   sq8_encode_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
       rows, n, dim, pd, kpad, vmin, scale, codes, operand, rowterm);
   return cudaGetLastError();
@@ -653,6 +661,7 @@ cudaError_t LaunchSq8Operand(const uint8_t* codes, uint64_t n, int pd, int kpad,
                              __half* operand, float* rowterm, cudaStream_t stream) {
   const int threads = 256;
   const uint64_t blocks = (n * 32 + threads - 1) / threads;
+  NoteLaunch();
   sq8_operand_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(codes, n, pd, kpad,
                                                                             scale, operand, rowterm);
   return cudaGetLastError();

@@ -68,6 +68,7 @@ class CollectionInfo(ctypes.Structure):
 _P = ctypes.c_void_p
 _SIGNATURES = {
     "vdbgpu_abi_version": (ctypes.c_int, []),
+    "vdbgpu_launch_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64)]),
     "vdbgpu_device_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "vdbgpu_open": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(_P)]),
     "vdbgpu_close": (None, [_P]),
@@ -111,6 +112,10 @@ _SIGNATURES = {
                                                        ctypes.POINTER(ctypes.c_uint64)]),
     "vdbgpu_merge_hits": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
                                          _P, _P, _P]),
+    "vdbgpu_shard_id": (ctypes.c_int, [_P]),
+    "vdbgpu_shard_group_open": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
+    "vdbgpu_shard_group_close": (None, [_P]),
+    "vdbgpu_shard_merge": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int, _P, _P, _P]),
     "vdbgpu_hnsw_build": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                          ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, ctypes.POINTER(_P),
                                          ctypes.POINTER(ctypes.c_size_t)]),
@@ -556,6 +561,85 @@ def merge_hits(ctx: Context, lists, k: int, out=None, hits=None):
         ids, dists = out
     ctx.check(lib().vdbgpu_merge_hits(ctx._h, _ptr(lists), nl, nq, int(k), _ptr(ids), _ptr(dists), _ptr(hits)))
     return ids, dists
+
+
+def launch_count() -> int:
+    """Kernel launches of the library in this process so far (vdbgpu_launch_count)."""
+    v = ctypes.c_uint64(0)
+    lib().vdbgpu_launch_count(ctypes.byref(v))
+    return int(v.value)
+
+
+SHARD_ID_BYTES = 128
+
+
+def _same_nccl_as_torch():
+    """Points the library at the NCCL that torch links against (the nvidia-nccl wheel), unless the
+    caller chose one (VDBGPU_NCCL_LIB). A process holds one libnccl.so.2: whichever loads first
+    serves every later user, so the library must not load an older system copy that a later
+    `import torch` would then be handed."""
+    if os.environ.get("VDBGPU_NCCL_LIB"):
+        return
+    try:
+        import nvidia.nccl
+    except ImportError:
+        return
+    for d in getattr(nvidia.nccl, "__path__", []):
+        p = os.path.join(d, "lib", "libnccl.so.2")
+        if os.path.exists(p):
+            os.environ["VDBGPU_NCCL_LIB"] = p
+            return
+
+
+def shard_id() -> bytes:
+    """A rendezvous token for one ShardGroup (ncclGetUniqueId), made on one rank and handed to
+    every rank by the caller's own channel."""
+    _same_nccl_as_torch()
+    buf = ctypes.create_string_buffer(SHARD_ID_BYTES)
+    code = lib().vdbgpu_shard_id(buf)
+    if code != OK:
+        _raise(code, "could not make a shard token (is libnccl.so.2 available?)")
+    return buf.raw
+
+
+class ShardGroup:
+    """This rank's membership in the NCCL group of a collection sharded over the GPUs of one node
+    (vdbgpu_shard_group_open): merge() exchanges every rank's merged hit records and merges them
+    on the receiving GPU(s). Every wait is bounded by timeout_ms; a failure aborts the group."""
+
+    def __init__(self, ctx: Context, token: bytes, rank: int, nranks: int, timeout_ms: int = 60000):
+        if len(token) != SHARD_ID_BYTES:
+            raise ValueError("the token must be SHARD_ID_BYTES bytes")
+        _same_nccl_as_torch()
+        self.ctx, self.rank, self.nranks = ctx, int(rank), int(nranks)
+        self._token = ctypes.create_string_buffer(token, SHARD_ID_BYTES)
+        h = _P()
+        ctx.check(lib().vdbgpu_shard_group_open(ctx._h, self._token, self.rank, self.nranks, int(timeout_ms),
+                                                ctypes.byref(h)))
+        self._h = h
+
+    def merge(self, local, nq: int, k: int, root: int = -1, out=None, hits=None):
+        """local: this rank's nq x k merged records (HIT_DTYPE numpy (nq, k), or a CUDA uint8 tensor
+        of nq*k*24 bytes). Returns (ids, dists) on receiving ranks (out, or new numpy arrays),
+        None elsewhere."""
+        receives = root < 0 or root == self.rank
+        if out is None and receives:
+            out = (np.empty((nq, k), np.uint64), np.empty((nq, k), np.float32))
+        ids, dists = out if (out is not None and receives) else (None, None)
+        self.ctx.check(lib().vdbgpu_shard_merge(self._h, _ptr(local), int(nq), int(k), int(root), _ptr(ids),
+                                                _ptr(dists), _ptr(hits) if receives else None))
+        return (ids, dists) if receives else None
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().vdbgpu_shard_group_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def build_hnsw(ctx: Context, metric, rows, dim: int, M: int = 16, candidates: int = 0, seed: int = 42) -> bytes:

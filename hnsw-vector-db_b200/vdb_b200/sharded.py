@@ -3,17 +3,19 @@
 The reference searches every segment of a collection and merges the per-segment top-k lists
 (CollectionImpl::Search, src/engine/collection_impl.cc:1056-1108). Segments are independent, so
 rank r holds the segments whose manifest position i has i % world == r (rank 0 also holds the
-mutable segment rebuilt from the log), searches them with its own GPU and merges them locally (ordered by (dist, part, row), one hit per external id). The
-only exchange is one all-gather of every rank's k merged hit records per query (24 bytes each)
-over NCCL, after which each rank (or rank 0 alone) runs the same merge over the world lists on
-its GPU. The result equals the unsharded merge: a hit among a query's global first k distinct
-ids is among the first k distinct ids of its own rank.
+mutable segment rebuilt from the log), searches them with its own GPU and merges them locally
+(ordered by (dist, part, row), one hit per external id). The only exchange is the library's
+vdbgpu_shard_merge: every rank's k merged hit records per query (24 bytes each) cross NVLink in one
+NCCL collective, and the receiving GPU(s) run the same merge over the world lists. The result
+equals the unsharded merge: a hit among a query's global first k distinct ids is among the first k
+distinct ids of its own rank.
+
+torch.distributed serves only to hand the NCCL rendezvous token from rank 0 to the other ranks
+(any backend, gloo included); the exchange itself is the C ABI's.
 """
 from __future__ import annotations
 
-from typing import Optional, Sequence
-
-import numpy as np
+from typing import Callable, Optional, Sequence
 
 import vdb_b200
 
@@ -25,34 +27,34 @@ def owner(ordinal: int, world: int) -> int:
     return ordinal % world
 
 
-def gather_hits(local, group=None):
-    """All-gathers each rank's merged hit records (a flat uint8 tensor of nq * k * 24 bytes) into
-    a (world, nq * k * 24) tensor on the same device (NCCL for CUDA tensors, gloo on the CPU)."""
-    import torch
+def share_token(group=None, make: Optional[Callable[[], bytes]] = None) -> bytes:
+    """The shard group's rendezvous token, made on rank 0 (vdb_b200.shard_id, or `make`) and
+    broadcast to every rank of the torch.distributed group."""
     import torch.distributed as dist
-    world = dist.get_world_size(group)
-    flat = local.contiguous().view(-1)
-    out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
-    dist.all_gather_into_tensor(out, flat, group=group)
-    if out.is_cuda:
-        # The collective is ordered on torch's stream only; the library launches on its own
-        # stream, so the gathered records must be complete before this returns.
-        torch.cuda.current_stream(out.device).synchronize()
-    return out.view(world, flat.numel())
+    rank = dist.get_rank(group)
+    box = [(make or vdb_b200.shard_id)() if rank == 0 else None]
+    src = 0 if group is None else dist.get_global_rank(group, 0)
+    dist.broadcast_object_list(box, src=src, group=group)
+    token = box[0]
+    if not isinstance(token, (bytes, bytearray)) or len(token) != vdb_b200.SHARD_ID_BYTES:
+        raise RuntimeError("bad shard token received from rank 0")
+    return bytes(token)
 
 
 class ShardedCollection:
     """This rank's shard of a collection directory written by the reference, searched on this
-    rank's GPU, with results merged across ranks."""
+    rank's GPU, with results merged across ranks over NCCL."""
 
     def __init__(self, path: str, rank: int, world: int, device: Optional[int] = None, group=None,
-                 ctx: Optional[vdb_b200.Context] = None, local: Optional[vdb_b200.Collection] = None):
+                 ctx: Optional[vdb_b200.Context] = None, local: Optional[vdb_b200.Collection] = None,
+                 timeout_ms: int = 60000):
         import torch
-        self.rank, self.world, self.group = rank, world, group
+        self.rank, self.world = rank, world
         self.device = torch.cuda.current_device() if device is None else device
         self.ctx = ctx if ctx is not None else vdb_b200.Context(self.device)
         self.local = local if local is not None else vdb_b200.Collection.open(self.ctx, path, shard=rank,
                                                                                nshards=world)
+        self.shards = vdb_b200.ShardGroup(self.ctx, share_token(group), rank, world, timeout_ms)
 
     def search(self, queries, filters: Sequence = (), query_filter=None, k: int = 10, on_all_ranks: bool = False,
                **params):
@@ -65,12 +67,13 @@ class ShardedCollection:
         dev = torch.device("cuda", self.device)
         hits = torch.empty(nq * k * HIT_BYTES, dtype=torch.uint8, device=dev)
         self.local.search_grouped(queries, list(filters), query_filter, k=k, out=False, hits=hits, **params)
-        gathered = gather_hits(hits, self.group)
-        if not on_all_ranks and self.rank != 0:
+        root = -1 if on_all_ranks else 0
+        receives = on_all_ranks or self.rank == 0
+        ids = torch.empty((nq, k), dtype=torch.int64, device=dev) if receives else None
+        dists = torch.empty((nq, k), dtype=torch.float32, device=dev) if receives else None
+        self.shards.merge(hits, nq, k, root=root, out=(ids, dists) if receives else None)
+        if not receives:
             return None
-        ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
-        dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
-        vdb_b200.merge_hits(self.ctx, gathered.view(self.world, nq, k * HIT_BYTES), k, out=(ids, dists))
         return ids.view(torch.uint64) if hasattr(torch, "uint64") else ids, dists
 
     def apply_log(self, records: bytes) -> int:
@@ -78,3 +81,6 @@ class ShardedCollection:
         id map, deletes rows of its own segments, and rank 0 rebuilds the mutable segment. Every
         rank must be given the same records, between searches."""
         return self.local.apply_log(records)
+
+    def close(self):
+        self.shards.close()

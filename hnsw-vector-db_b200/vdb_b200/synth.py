@@ -98,3 +98,33 @@ def zipf_tags(n, vocab=1000, zipf_s=1.1, seed=5):
     out = np.empty(n, dtype=np.uint32)
     _l().synth_zipf(n, vocab, zipf_s, seed, out.ctypes.data)
     return out
+
+
+# Config 4: 64 segments of 1,562,500 rows (normalised C0-style mixture, not rounded) with int64
+# "year" U[1990, 2024] and keyword_list "tags" (1-5 Zipf(1.1) words of 1,000), and queries with one
+# filter per distinct Zipf-drawn tag: year >= 2020 AND tags contains the tag.
+C4_DIM = 128
+
+
+def c4_segment(s, seg_rows):
+    """Segment s of config 4: rows (normalised mixture), external ids, year / tags metadata."""
+    rows = mixture(seg_rows, C4_DIM, 100, centres="uniform", lo=0.0, hi=100.0, sigma=10.0, normalize=True,
+                   seed=4, stream=10 + s)
+    ids = np.arange(s * seg_rows, (s + 1) * seg_rows, dtype=np.uint64)
+    years, tags = metadata(seg_rows, seed=1000 + s)
+    return rows, ids, years, tags
+
+
+def c4_queries(nq):
+    """Queries of config 4, their filters (JSON, one per distinct Zipf-drawn tag) and each query's
+    filter index."""
+    import json
+    qs = mixture(nq, C4_DIM, 100, centres="uniform", lo=0.0, hi=100.0, sigma=10.0, normalize=True, seed=4,
+                 stream=9)
+    qtags = zipf_tags(nq, seed=5)
+    distinct = sorted(set(qtags.tolist()))
+    pos = {t: i for i, t in enumerate(distinct)}
+    filters = [json.dumps({"and": [{"field": "year", "gte": 2020}, {"field": "tags", "eq": f"w{t}"}]})
+               for t in distinct]
+    qf = np.array([pos[t] for t in qtags.tolist()], dtype=np.int32)
+    return qs, filters, qf

@@ -84,6 +84,10 @@ typedef struct vdbgpu_index vdbgpu_index;
 /* Library version (VDBGPU_ABI_VERSION). */
 VDBGPU_API int vdbgpu_abi_version(void);
 
+/* Kernel launches this library has made in this process, on every device (no counterpart in the
+ * reference, which has no GPU): the difference across a timed region is its launch count. */
+VDBGPU_API int vdbgpu_launch_count(uint64_t* out);
+
 /* Number of visible CUDA devices (0 without a GPU). */
 VDBGPU_API int vdbgpu_device_count(int* out);
 
@@ -165,7 +169,9 @@ VDBGPU_API int vdbgpu_index_search(vdbgpu_index* index, const float* queries, ui
  * device (nq x padded_dim, nq x k, nq x k). Work is launched on `stream` (NULL: the context's
  * stream) and the call returns once it has finished. All calls share the one scratch array: calls
  * whose work overlaps on the GPU race and must be serialised by the caller. Results are those of
- * vdbgpu_index_search with the same parameters (no filter, no statistics). */
+ * vdbgpu_index_search with the same parameters (no filter, no statistics); an empty index gives
+ * misses (+inf, UINT32_MAX) in every slot. The scan runs on at most 16 SMs: the entry point is
+ * meant for small batches, where latency rather than throughput matters. */
 VDBGPU_API int vdbgpu_index_search_noalloc(vdbgpu_index* index, const float* queries, uint64_t nq,
                                            uint32_t k, const vdbgpu_search_params* params,
                                            float* out_dist, uint32_t* out_row, void* stream);
@@ -304,6 +310,43 @@ VDBGPU_API int vdbgpu_collection_filter_bitmap(vdbgpu_collection* c, const char*
 VDBGPU_API int vdbgpu_merge_hits(vdbgpu_ctx* ctx, const vdbgpu_hit* lists, uint32_t nlists,
                                  uint64_t nq, uint32_t k, uint64_t* out_ids, float* out_dist,
                                  vdbgpu_hit* out_hits);
+
+/* ------------------------------------------------------- collections sharded over GPUs
+ *
+ * The exchange step of a collection whose disk segments are spread over the GPUs of one node
+ * (vdbgpu_collection_open with shard / nshards, one process or thread per GPU). The reference has
+ * no sharding: it searches every segment and merges the per-segment lists in one process
+ * (CollectionImpl::Search, src/engine/collection_impl.cc:1056-1108). Each rank merges its own
+ * segments with vdbgpu_collection_search_grouped (out_hits); vdbgpu_shard_merge moves those k
+ * records per query between ranks with NCCL over NVLink and runs the same merge on the receiving
+ * GPU, which gives the unsharded result. NCCL (libnccl.so.2) is loaded on first use; without it
+ * these calls return VDBGPU_UNAVAILABLE. */
+
+#define VDBGPU_SHARD_ID_BYTES 128
+
+typedef struct vdbgpu_shard_group vdbgpu_shard_group;
+
+/* A rendezvous token (ncclGetUniqueId) for one group: made on one rank, handed to every rank by the
+ * host's own channel, VDBGPU_SHARD_ID_BYTES bytes. */
+VDBGPU_API int vdbgpu_shard_id(void* out_id);
+
+/* Joins the group as `rank` of `nranks` on the context's device (every rank calls it with the same
+ * token). Every wait of the group (this rendezvous, each exchange) is bounded by timeout_ms (<= 0:
+ * 60 s); a wait that runs out aborts the group and returns VDBGPU_UNAVAILABLE, as does an NCCL
+ * failure. */
+VDBGPU_API int vdbgpu_shard_group_open(vdbgpu_ctx* ctx, const void* id, int rank, int nranks,
+                                       int timeout_ms, vdbgpu_shard_group** out);
+VDBGPU_API void vdbgpu_shard_group_close(vdbgpu_shard_group* g);
+
+/* The exchange: every rank's local nq x k merged records (host or device memory of the context's
+ * device) go to every rank (root < 0, an all-gather) or to `root` alone (a gather), and the
+ * receiving ranks merge the nranks lists as vdbgpu_merge_hits does (out_ids / out_dist / out_hits
+ * host or device, nullable; ignored on ranks that do not receive). Every rank must call it with
+ * the same nq, k and root, in the same order. After a failure the group is aborted and further
+ * calls return VDBGPU_FAILED_PRECONDITION. */
+VDBGPU_API int vdbgpu_shard_merge(vdbgpu_shard_group* g, const vdbgpu_hit* local, uint64_t nq,
+                                  uint32_t k, int root, uint64_t* out_ids, float* out_dist,
+                                  vdbgpu_hit* out_hits);
 
 /* Index::build for HNSW (HnswIndex, src/index/hnsw/hnsw_index.h:12-41) on the GPU: a graph over
  * nrows rows (nrows x padded_dim floats, host or device; cosine rows already normalised) with

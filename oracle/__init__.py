@@ -24,6 +24,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_LIB = os.path.join(HERE, "_ref", "libvdbref.so")
 REF_ENGINE_LIB = os.path.join(HERE, "_ref", "libvdbref_engine.so")
+REF_GPUINDEX_LIB = os.path.join(HERE, "_ref", "libvdbref_gpuindex.so")
 ORACLE_LIB = os.path.join(HERE, "liboracle.so")
 # The reference checkout sits beside this repository unless VDB_REFERENCE_SRC names it.
 REFERENCE_SRC = os.environ.get("VDB_REFERENCE_SRC",
@@ -35,10 +36,13 @@ _P = ctypes.c_void_p
 
 
 def build(ref: bool = True) -> None:
-    """Builds liboracle.so, and _ref/libvdbref.so when the reference sources are present."""
+    """Builds liboracle.so, and the reference's own libraries under _ref/ when the reference
+    sources are present (the vdb::GpuIndex harness too once lib/libvdbgpu.so exists)."""
     targets = ["oracle"]
     if ref and os.path.isdir(os.path.join(REFERENCE_SRC, "src")):
         targets += ["ref", "engine"]
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "hnsw-vector-db_b200", "lib", "libvdbgpu.so")):
+            targets += ["gpuindex"]
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REFERENCE_SRC}", "-j8"] + targets, check=True)
 
 
@@ -236,6 +240,57 @@ def _engine_lib(lib_path: str = REF_ENGINE_LIB):
         f.restype = res
         f.argtypes = args
     return l
+
+
+class GpuIndexHarness:
+    """The reference's SearchDiskSegment over a collection directory's disk segments, opened by
+    Segment::Open with their CPU indexes (use_gpu False) or with vdb::GpuIndex as each segment's
+    prebuilt index (use_gpu True): oracle/_ref/libvdbref_gpuindex.so (ref_gpuindex_shim.cc)."""
+
+    def __init__(self, path: str, use_gpu: bool, device: int = 0, lib_path: str = REF_GPUINDEX_LIB):
+        if not os.path.exists(lib_path):
+            raise ImportError(f"{lib_path} is missing (build with `make -C oracle gpuindex`)")
+        l = ctypes.CDLL(lib_path)
+        c64, c32, ci = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int
+        for name, res, args in (("gi_last_error", ctypes.c_char_p, []),
+                                ("gi_open", _P, [ctypes.c_char_p, ci, ci]),
+                                ("gi_close", None, [_P]),
+                                ("gi_segments", c32, [_P]),
+                                ("gi_search", ci, [_P, _P, c32, c64, c64, ci, ci, c64, c64, ctypes.c_char_p, _P, _P,
+                                                   _P, ctypes.c_char_p, ctypes.c_size_t])):
+            f = getattr(l, name)
+            f.restype, f.argtypes = res, args
+        self.l = l
+        self.h = l.gi_open(path.encode(), int(use_gpu), device)
+        if not self.h:
+            raise RuntimeError(l.gi_last_error().decode())
+        self.nseg = l.gi_segments(self.h)
+
+    def search(self, q: np.ndarray, k=10, ef=64, nprobe=16, rerank=-1, strategy="auto", filter=None,
+               prefilter_threshold=10000, post_filter_alpha=10):
+        """Per segment (segment-local rows, dists, hit counts) and the explain list of one query."""
+        import json
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        d = np.empty((self.nseg, k), np.float32)
+        r = np.empty((self.nseg, k), np.uint32)
+        c = np.empty(self.nseg, np.uint32)
+        buf = ctypes.create_string_buffer(1 << 16)
+        rc = self.l.gi_search(self.h, _ptr(q), k, ef, nprobe, rerank, STRATEGIES[strategy], prefilter_threshold,
+                              post_filter_alpha, _fj(filter), _ptr(d), _ptr(r), _ptr(c), buf, len(buf))
+        if rc != 0:
+            raise RuntimeError(self.l.gi_last_error().decode())
+        return r, d, c, json.loads(buf.value.decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.l.gi_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def ref_filter_parse(schema: list, filter_json: str, lib_path: str = REF_ENGINE_LIB):

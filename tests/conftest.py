@@ -31,6 +31,8 @@ def built_libraries():
     if not (os.path.exists(os.path.join(PKG, "lib", "libvdbgpu.so"))
             and os.path.exists(os.path.join(PKG, "lib", "libvdbsynth.so"))):
         _make(["-C", PKG])
+    if not os.path.exists(oracle.REF_GPUINDEX_LIB) and os.path.isdir(os.path.join(oracle.REFERENCE_SRC, "src")):
+        oracle.build(ref=True)
     yield
 
 

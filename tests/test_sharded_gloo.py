@@ -1,7 +1,8 @@
-"""The cross-rank step of the sharded collection on the CPU: two gloo ranks all-gather their
-merged hit records with vdb_b200.sharded.gather_hits (the same call the GPU ranks make over
-NCCL), and merging the gathered per-rank lists gives the merge of all segments at once
-(CollectionImpl::Search's order and dedupe, restated in oracle.merge_hits_py)."""
+"""The host side of the sharded collection on the CPU, with two gloo ranks:
+* the NCCL rendezvous token is made on rank 0 and reaches every rank (vdb_b200.sharded.share_token);
+* each rank's merged records, laid out rank-major as vdbgpu_shard_merge exchanges them, merge into
+  the merge of all segments at once (CollectionImpl::Search's order and dedupe, restated in
+  oracle.merge_hits_py), whatever segments each rank owns (sharded.owner)."""
 import datetime
 import os
 import socket
@@ -59,8 +60,12 @@ def _worker(rank, world, port, nq, k, result_q):
             _records(oracle.merge_hits_py([c for p, lst in enumerate(parts) if sharded.owner(p, world) == rank
                                            for c in lst], k), k, vdb_b200.HIT_DTYPE)
             for parts in cands])
+        token = sharded.share_token(make=lambda: bytes(range(128)))
+        assert token == bytes(range(128))
+        # The rank-major exchange of vdbgpu_shard_merge (an all-gather), done here with gloo.
         t = torch.from_numpy(local.view(np.uint8).reshape(-1).copy())
-        g = sharded.gather_hits(t)
+        g = torch.empty(world * t.numel(), dtype=torch.uint8)
+        dist.all_gather_into_tensor(g, t)
         result_q.put((rank, g.numpy().tobytes()))
       except Exception as e:  # report instead of leaving the parent waiting
         result_q.put((rank, "error: %r" % (e,)))
