@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--c2-rows", type=int, default=10_000_000,
                    help="config 2 rows (smaller only for profiling captures)")
+    p.add_argument("--c3-ef", default="64,128,256", help="config 3 beam widths (comma-separated)")
+    p.add_argument("--c3-variants", default="fp32,sq8", help="config 3 distance variants (fp32, sq8)")
     return p.parse_args()
 
 
@@ -444,7 +446,12 @@ def run_c4_ours(args):
     for _ in range(max(3, args.warmup)):
         step(q_dev, ids_dev, d_dev)
     coll.stats(enable=True)
+    ctx.set_timing(True)
     step(q_dev, ids_dev, d_dev)
+    # Graph-walk counters of that step: walks, expansions, front refills, pool slots scanned by
+    # refills, merges into the front, result inserts, most expansions of one walk.
+    wc = ctx.stage_counters()[:7]
+    ctx.set_timing(False)
     st = coll.stats(enable=False)
     if world > 1:
         torch.distributed.barrier()
@@ -552,6 +559,10 @@ def run_c4_ours(args):
             "plan_per_step": {"prefilter_pairs": w[3], "graph_pairs": w[4], "empty_pairs": w[5]},
             "stage_ms_busiest_rank": {"bitmaps_plan": ph[0], "exact": ph[1], "graph_walks": ph[2],
                                       "merge_other": ph[3], "search_call": search_ms, "exchange": exchange_ms},
+            "walk_counters_per_walk_rank0": ({"walks": wc[0], "expansions": wc[1] / wc[0],
+                                              "front_refills": wc[2] / wc[0], "pool_slots_scanned": wc[3] / wc[0],
+                                              "front_merges": wc[4] / wc[0], "result_inserts": wc[5] / wc[0],
+                                              "max_expansions": wc[6]} if len(wc) >= 7 and wc[0] else None),
             "recall_at_10_vs_exact_filtered": recall,
             "e2e": {"value": nq / (float(te.item()) / 1000.0), "unit": "queries/s",
                     "h2d_bytes_per_step": nq * DIM * 4, "d2h_bytes_per_step": nq * K * 12},
@@ -784,11 +795,12 @@ def run_c3(args, ctx, stream, local, ref, hbm, src):
     flat.search(q_dev, k=K, out=(gt_ids, gt_d))
     gt = gt_ids.cpu().numpy().view(np.uint32)
     flat.free()
-    for type_, variant in ((1, "fp32"), (2, "sq8")):
+    variants = [v for v in ((1, "fp32"), (2, "sq8")) if v[1] in args.c3_variants.split(",")]
+    for type_, variant in variants:
         data, build_s = reference_graph(ref, type_, base, 0)
         idx = vdb_b200.Index.load(ctx, data, "l2", b_dev, DIM)
         rref = ref.load_index(data, oracle.L2, base, DIM)
-        for ef in (64, 128, 256):
+        for ef in (int(x) for x in args.c3_ef.split(",")):
             ids_dev = torch.empty((nq, K), dtype=torch.int32, device="cuda")
             d_dev = torch.empty((nq, K), dtype=torch.float32, device="cuda")
             ctx.set_timing(True)
@@ -798,6 +810,9 @@ def run_c3(args, ctx, stream, local, ref, hbm, src):
                 idx.search(q_dev, k=K, ef=ef, out=(ids_dev, d_dev))
                 walk_ms.append(ctx.stage_times()[1])
             ms, clk = _timed(step, args.steps, args.warmup, stream, local)
+            # Walk counters of the last step: walks, expansions, front refills, pool slots scanned,
+            # merges into the front, result inserts, most expansions of one walk.
+            wc = ctx.stage_counters()[:7]
             ctx.set_timing(False)
             gpu_ids = ids_dev.cpu().numpy().view(np.uint32).copy()
             gpu_d = d_dev.cpu().numpy().copy()
@@ -830,6 +845,10 @@ def run_c3(args, ctx, stream, local, ref, hbm, src):
                                 "unit": "GB/s", "frac": achieved / hbm, "peak_kind": f"{src} copy bandwidth",
                                 "kernel_ms": kernel_ms, "traffic": hnsw_traffic_per_launch(variant, ef, nq),
                                 "algorithmic": formula},
+                   "walk_counters_per_query": ({"expansions": wc[1] / nq, "front_refills": wc[2] / nq,
+                                                "pool_slots_scanned": wc[3] / nq, "front_merges": wc[4] / nq,
+                                                "result_inserts": wc[5] / nq, "max_expansions": wc[6]}
+                                               if len(wc) >= 7 and wc[0] else None),
                    "recall_at_10_vs_exact": _recall(gpu_ids, gt),
                    "recall_at_10_reference_vs_exact": _recall(r_ids, gt),
                    "identical_ids_vs_reference_same_graph": float(np.mean(same)),

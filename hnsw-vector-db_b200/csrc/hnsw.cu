@@ -330,29 +330,58 @@ __device__ bool pool_merge(uint64_t key, bool want, uint64_t* front, int& chead,
   npool += np;
   const uint32_t mf = __ballot_sync(0xFFFFFFFFu, to_front);
   if (mf == 0) return true;
-  uint64_t x[4];
+  // Merge path: only the m <= 32 new keys are sorted; every key's place in the merged order is
+  // its index in its own sorted run plus the number of keys of the other run below it (keys are
+  // unique: a fresh node's id is in neither run). The front occupies [chead, chead + ncand) within
+  // [0, kPoolFront), so front[kPoolFront, kPoolFront + 32) holds the sorted new keys for searching.
+  uint64_t b[1] = {to_front ? key : ~0ull};
+  warp_sort<1>(b);
+  uint64_t* bs = front + kPoolFront;
+  bs[lane] = b[0];
+  uint64_t av[3];
 #pragma unroll
   for (int e = 0; e < 3; ++e) {
     const int i = e * 32 + lane;
-    x[e] = i < ncand ? front[chead + i] : ~0ull;
+    av[e] = i < ncand ? front[chead + i] : ~0ull;
   }
-  x[3] = to_front ? key : ~0ull;
   __syncwarp();
-  warp_sort<4>(x);
-  const int total = ncand + __popc(mf);
+  const int m = __popc(mf);
+  int pos_b = 0;
+  if (lane < m) {  // new key: its rank plus the front keys below it
+    int lo = 0, hi = ncand;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (front[chead + mid] < b[0]) lo = mid + 1; else hi = mid;
+    }
+    pos_b = lane + lo;
+  }
+  int pos_a[3];
+#pragma unroll
+  for (int e = 0; e < 3; ++e) {  // front key: its rank plus the new keys below it
+    int lo = 0, hi = m;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (bs[mid] < av[e]) lo = mid + 1; else hi = mid;
+    }
+    pos_a[e] = e * 32 + lane + lo;
+  }
+  __syncwarp();
+  const int total = ncand + m;
   const int keep = total < kPoolFront ? total : kPoolFront;
   const int nover = total - keep;  // <= 32: room was reserved above
   uint64_t over_min = ~0ull;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int i = e * 32 + lane;
-    if (i < keep) {
-      front[i] = x[e];
-    } else if (i < total) {
-      pool[npool + (i - keep)] = x[e];
-      over_min = x[e] < over_min ? x[e] : over_min;
+  auto place = [&](int pos, uint64_t v) {
+    if (pos < keep) {
+      front[pos] = v;
+    } else {
+      pool[npool + (pos - keep)] = v;
+      over_min = v < over_min ? v : over_min;
     }
-  }
+  };
+  if (lane < m) place(pos_b, b[0]);
+#pragma unroll
+  for (int e = 0; e < 3; ++e)
+    if (e * 32 + lane < ncand) place(pos_a[e], av[e]);
   if (nover > 0) pmin = warp_min_u64(over_min);  // overflow keys lie below the old pmin
   npool += nover;
   chead = 0;
@@ -672,7 +701,7 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
         // themselves are merged afterwards (their order of insertion does not matter).
         uint64_t mykey = ~0ull;
         bool mywant = false;
-        for (int i = 0; i < nf; ++i) {
+        auto consider = [&](int i) {
           const uint32_t id = s.nb_id[i];
           const float de = s.nb_d[i];
           if (nres < ef || de < lower) {
@@ -692,6 +721,17 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
               }
               lower = neighbor_dist(s.res[nres - 1]);
             }
+          }
+        };
+        int i0 = 0;
+        for (; i0 < nf && nres < ef; ++i0) consider(i0);
+        if (i0 < nf) {
+          // The result set is full: `lower` can only fall from here, so a neighbour at or beyond
+          // it now is refused at its turn too. Only the others are taken in list order.
+          uint32_t maybe = __ballot_sync(0xFFFFFFFFu, lane >= i0 && lane < nf && s.nb_d[lane] < lower);
+          while (maybe != 0u) {
+            consider(__ffs(maybe) - 1);
+            maybe &= maybe - 1u;
           }
         }
         c_merge += __any_sync(0xFFFFFFFFu, mywant && mykey < pmin) ? 1 : 0;

@@ -125,6 +125,10 @@ class HnswGpuIndex final : public GpuIndex {
     a.out_row = b.out_row;
     a.out_dc = b.dist_comps;
     a.status = ctx.status_word();
+    // Work counters of the walk while timing is on (HnswArgs::counters).
+    a.counters = ctx.timing() ? ctx.counters() : nullptr;
+    if (a.counters != nullptr)
+      VDBGPU_CUDA(cudaMemsetAsync(a.counters, 0, 8 * sizeof(unsigned long long), ctx.stream()));
     // Unfiltered walks keep their state in shared memory: a visited hash and a candidate array
     // sized for the walk; one that overflows reruns the batch with that structure doubled (and
     // fewer queries per block once four no longer fit). Filtered walks keep every reached node
