@@ -698,6 +698,51 @@ int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows, uint64_t n
   return VDBGPU_OK;
 }
 
+int vdbgpu_hnsw_extend(vdbgpu_ctx* ctx, int metric, const void* file_bytes, size_t nbytes, const float* rows,
+                       uint64_t nrows, uint32_t dim, uint32_t padded_dim, void** out_file, size_t* out_bytes) {
+  if (ctx == nullptr || file_bytes == nullptr || out_file == nullptr || out_bytes == nullptr ||
+      (nrows > 0 && rows == nullptr))
+    return VDBGPU_INVALID_ARGUMENT;
+  *out_file = nullptr;
+  *out_bytes = 0;
+  if (metric < 0 || metric > 2 || dim == 0 || dim > padded_dim || padded_dim % 16 != 0)
+    return Fail(ctx, Status(Status::kInvalidArgument, "bad geometry or metric"));
+  std::string_view magic, body;
+  Status s = vdbgpu::CheckIndexFile(std::string_view(static_cast<const char*>(file_bytes), nbytes), &magic, &body);
+  if (!s.ok()) return Fail(ctx, s);
+  if (magic != "VDBHNSW1") {
+    const int t = vdbgpu::IndexTypeForMagic(magic);
+    static const char* kNames[] = {"flat", "hnsw", "hnsw_sq8", "pq", "ivf_pq"};
+    return Fail(ctx, Status(Status::kNotSupported, std::string("extend is not supported by ") +
+                                                       (t >= 0 && t <= 4 ? kNames[t] : "this index file")));
+  }
+  // index.hnsw: padded dim, then the graph, whose capacity is its row count.
+  vdbgpu::Reader peek(body);
+  uint32_t fpd = 0;
+  uint64_t cap = 0;
+  if (!peek.u32(&fpd) || !peek.u64(&cap)) return Fail(ctx, Status(Status::kCorruption, "truncated hnsw header"));
+  if (fpd != padded_dim) return Fail(ctx, Status(Status::kCorruption, "hnsw dim mismatch"));
+  if (nrows < cap) return Fail(ctx, Status(Status::kInvalidArgument, "extend needs a superset of the indexed rows"));
+  vdbgpu::Reader r(body);
+  r.u32(&fpd);
+  vdbgpu::HnswGraphData g;
+  s = vdbgpu::ParseHnswGraph(r, cap, &g);
+  if (!s.ok()) return Fail(ctx, s);
+  if (g.size != g.cap) return Fail(ctx, Status(Status::kNotSupported, "extend needs a complete graph"));
+  std::lock_guard<std::mutex> lk(ctx->c->mu());
+  cudaSetDevice(ctx->c->device());
+  s = RejectForeign(ctx->c->device(), {{rows, "the rows"}});
+  std::string file;
+  if (s.ok()) s = vdbgpu::ExtendHnswFile(*ctx->c, metric, g, padded_dim, rows, nrows, dim, &file);
+  if (!s.ok()) return Fail(ctx, s);
+  void* p = std::malloc(file.size());
+  if (p == nullptr) return Fail(ctx, Status(Status::kResourceExhausted, "host allocation"));
+  std::memcpy(p, file.data(), file.size());
+  *out_file = p;
+  *out_bytes = file.size();
+  return VDBGPU_OK;
+}
+
 int vdbgpu_ivfpq_build(vdbgpu_ctx* ctx, int type, const float* rows, uint64_t nrows, uint32_t dim,
                        uint32_t padded_dim, uint32_t nlist, uint32_t pq_m, uint32_t max_train_ppc,
                        uint64_t seed, void** out_file, size_t* out_bytes) {

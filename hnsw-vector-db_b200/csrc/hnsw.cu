@@ -40,6 +40,11 @@ struct WarpSmem {
   float* nb_d;        // their distances
 };
 
+// Brings a line into L2 without waiting for it (no register is written).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ uint32_t hash_slot(uint32_t id, int bits) {
   return (id * 2654435761u) >> (32 - bits);
 }
@@ -303,14 +308,23 @@ __device__ void pool_compact(uint64_t* pool, int& npool) {
   const int lane = threadIdx.x & 31;
   const uint32_t lt = (1u << lane) - 1u;
   int nkeep = 0;
-  for (int base = 0; base < npool; base += 32) {
-    const int i = base + lane;
-    const uint64_t k = i < npool ? pool[i] : ~0ull;
-    const bool kp = k != ~0ull;
-    const uint32_t mk = __ballot_sync(0xFFFFFFFFu, kp);
+  // Four chunks of 32 are read before any is written (loads in flight together); a chunk's
+  // entries move to nkeep <= its own start, never ahead of unread entries.
+  for (int base = 0; base < npool; base += 128) {
+    uint64_t kk[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + 32 * u + lane;
+      kk[u] = i < npool ? pool[i] : ~0ull;
+    }
     __syncwarp();
-    if (kp) pool[nkeep + __popc(mk & lt)] = k;  // nkeep <= base: never ahead of unread entries
-    nkeep += __popc(mk);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const bool kp = kk[u] != ~0ull;
+      const uint32_t mk = __ballot_sync(0xFFFFFFFFu, kp);
+      if (kp) pool[nkeep + __popc(mk & lt)] = kk[u];
+      nkeep += __popc(mk);
+    }
     __syncwarp();
   }
   npool = nkeep;
@@ -402,14 +416,25 @@ __device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* p
   const int lane = threadIdx.x & 31;
   const uint32_t lt = (1u << lane) - 1u;
   auto live = [&](uint64_t k) { return k != ~0ull && (!prune || !(neighbor_dist(k) > lower)); };
+  // Every pool scan reads four chunks of 32 keys per step, so a lane has four loads in flight.
+  auto load4 = [&](int base, uint64_t (&kk)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + 32 * u + lane;
+      kk[u] = i < npool ? pool[i] : ~0ull;
+    }
+  };
   uint64_t m = ~0ull;
   int nlive = 0;
-  for (int i = lane; i < npool; i += 32) {
-    const uint64_t k = pool[i];
-    if (live(k)) {
-      ++nlive;
-      m = k < m ? k : m;
-    }
+  for (int base = 0; base < npool; base += 128) {
+    uint64_t kk[4];
+    load4(base, kk);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (live(kk[u])) {
+        ++nlive;
+        m = kk[u] < m ? kk[u] : m;
+      }
   }
   m = warp_min_u64(m);
   nlive = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(nlive)));
@@ -426,13 +451,17 @@ __device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* p
     bool found = false;
     for (int attempt = 0; attempt < 4 && !found; ++attempt) {
       int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int i = lane; i < npool; i += 32) {
-        const uint64_t k = pool[i];
-        if (!live(k)) continue;
-        const float d = neighbor_dist(k);
-        float t = base + delta;
+      for (int b0 = 0; b0 < npool; b0 += 128) {
+        uint64_t kk[4];
+        load4(b0, kk);
 #pragma unroll
-        for (int j = 0; j < 8; ++j, t = base + (t - base) * 4.f) c[j] += d <= t ? 1 : 0;
+        for (int u = 0; u < 4; ++u) {
+          if (!live(kk[u])) continue;
+          const float d = neighbor_dist(kk[u]);
+          float t = base + delta;
+#pragma unroll
+          for (int j = 0; j < 8; ++j, t = base + (t - base) * 4.f) c[j] += d <= t ? 1 : 0;
+        }
       }
       int best = -1;
       float t = base + delta;
@@ -490,23 +519,28 @@ __device__ void pool_refill(uint64_t* front, int& chead, int& ncand, uint64_t* p
   int nsel = 0;
   uint64_t kmin = ~0ull;
   bool any_left = false;
-  for (int base = 0; base < npool; base += 32) {
-    const int i = base + lane;
-    const uint64_t k = i < npool ? pool[i] : ~0ull;
-    const bool lv = i < npool && live(k);
-    const bool sel = lv && k <= thr;
-    const uint32_t ms = __ballot_sync(0xFFFFFFFFu, sel);
-    if (sel) {
-      const int at = nsel + __popc(ms & lt);
-      if (at < 128) front[at] = k;
+  for (int b0 = 0; b0 < npool; b0 += 128) {
+    uint64_t kk[4];
+    load4(b0, kk);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = b0 + 32 * u + lane;
+      const uint64_t k = kk[u];
+      const bool lv = i < npool && live(k);
+      const bool sel = lv && k <= thr;
+      const uint32_t ms = __ballot_sync(0xFFFFFFFFu, sel);
+      if (sel) {
+        const int at = nsel + __popc(ms & lt);
+        if (at < 128) front[at] = k;
+      }
+      if (i < npool && !lv && k != ~0ull) pool[i] = ~0ull;  // pruned: dead
+      if (sel) pool[i] = ~0ull;                              // moved to the front
+      if (lv && !sel) {
+        kmin = k < kmin ? k : kmin;
+        any_left = true;
+      }
+      nsel += __popc(ms);
     }
-    if (i < npool && !lv && k != ~0ull) pool[i] = ~0ull;  // pruned: dead
-    if (sel) pool[i] = ~0ull;                              // moved to the front
-    if (lv && !sel) {
-      kmin = k < kmin ? k : kmin;
-      any_left = true;
-    }
-    nsel += __popc(ms);
   }
   __syncwarp();
   kmin = warp_min_u64(kmin);
@@ -670,6 +704,10 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
         // The list's count and its slots load together (a block always holds M0 slots).
         const uint32_t cnt = ll[0];
         const uint32_t e_raw = lane < static_cast<int>(a.M0) ? ll[1 + lane] : 0u;
+        // The next expansion most often takes the current front head: its link block starts
+        // towards L2 now and lands while this expansion runs.
+        if (ncand > 0 && lane < 2)
+          prefetch_l2(a.links0 + static_cast<size_t>(neighbor_id(s.cand[chead])) * (1 + a.M0) + 32 * lane);
         uint32_t e = 0;
         bool fresh = false, al = false;
         if (lane < static_cast<int>(cnt)) {
@@ -677,6 +715,18 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
           if (e >= n) {
             bad = true;
           } else {
+            // Unfiltered walks: the neighbour's vector starts towards L2 beside its visited mark,
+            // so the distance pass below finds it there (a visited neighbour's vector is fetched
+            // for nothing). Filtered walks revisit most neighbours, so they skip this.
+            if (!filtered) {
+              if (kSq8) {
+                const uint8_t* cp = a.codes + static_cast<size_t>(e) * pd;
+                for (int o = 0; o < pd; o += 128) prefetch_l2(cp + o);
+              } else {
+                const float* rp = a.rows + static_cast<size_t>(e) * pd;
+                for (int o = 0; o < pd; o += 32) prefetch_l2(rp + o);
+              }
+            }
             const uint32_t bit = 1u << (e & 31);
             fresh = (atomicOr(&vis[e >> 5], bit) & bit) == 0u;
             al = allowed(e);  // the filter bit loads beside the visited mark

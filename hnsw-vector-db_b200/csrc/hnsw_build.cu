@@ -84,8 +84,10 @@ __device__ PruneSmem carve(uint8_t* base, int pd, int maxm) {
 __global__ void select_kernel(const PruneArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t node = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
-  if (node >= a.n) return;
+  const uint64_t local = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  const uint64_t nsel = a.n_select != 0 ? a.n_select : a.n;
+  if (local >= nsel) return;
+  const uint64_t node = a.node_base + local;  // the node's position in the layer
   PruneSmem s = carve(sm + static_cast<size_t>(warp) * PruneWarpBytes(a.pd, a.maxm), a.pd, a.maxm);
   // Candidates arrive sorted by (dist, id); keep order, drop self and misses.
   int nc = 0;
@@ -94,8 +96,8 @@ __global__ void select_kernel(const PruneArgs a) {
     uint32_t id = UINT32_MAX;
     float d = 0.f;
     if (j < a.kc) {
-      id = a.cand_ids[node * a.kc + j];
-      d = a.cand_d[node * a.kc + j];
+      id = a.cand_ids[local * a.kc + j];
+      d = a.cand_d[local * a.kc + j];
     }
     const bool ok = id != UINT32_MAX && id != static_cast<uint32_t>(node) && id < a.n;
     const uint32_t m = __ballot_sync(0xFFFFFFFFu, ok);
@@ -104,7 +106,7 @@ __global__ void select_kernel(const PruneArgs a) {
   }
   __syncwarp();
   const int kept = heuristic(a, s, nc, a.maxm);
-  uint32_t* out = a.out + node * a.out_stride;
+  uint32_t* out = a.out + local * a.out_stride;
   for (int i = lane; i < kept; i += 32) out[1 + i] = s.kept[i];
   if (lane == 0) out[0] = static_cast<uint32_t>(kept);
 }
@@ -116,14 +118,15 @@ __global__ void count_reverse_kernel(const uint32_t* fwd, int stride, uint64_t n
   for (uint32_t j = 0; j < l[0]; ++j) atomicAdd(&cnt[l[1 + j]], 1u);
 }
 
+// Source u's back links name it as src_base + u (its position in the layer).
 __global__ void fill_reverse_kernel(const uint32_t* fwd, int stride, uint64_t n, const uint64_t* off,
-                                    uint32_t* cursor, uint32_t* rev) {
+                                    uint32_t* cursor, uint32_t* rev, uint32_t src_base) {
   const uint64_t u = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
   if (u >= n) return;
   const uint32_t* l = fwd + u * stride;
   for (uint32_t j = 0; j < l[0]; ++j) {
     const uint32_t v = l[1 + j];
-    rev[off[v] + atomicAdd(&cursor[v], 1u)] = static_cast<uint32_t>(u);
+    rev[off[v] + atomicAdd(&cursor[v], 1u)] = src_base + static_cast<uint32_t>(u);
   }
 }
 
@@ -211,7 +214,8 @@ cudaError_t LaunchSelect(const PruneArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   NoteLaunch();
-  select_kernel<<<static_cast<unsigned>((a.n + w - 1) / w), w * 32, smem, st>>>(a);
+  const uint64_t nsel = a.n_select != 0 ? a.n_select : a.n;
+  select_kernel<<<static_cast<unsigned>((nsel + w - 1) / w), w * 32, smem, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -223,10 +227,11 @@ cudaError_t LaunchReverse(const uint32_t* fwd, int stride, uint64_t n, uint32_t*
 }
 
 cudaError_t LaunchFillReverse(const uint32_t* fwd, int stride, uint64_t n, const uint64_t* off, uint32_t* cursor,
-                              uint32_t* rev, cudaStream_t st) {
+                              uint32_t* rev, cudaStream_t st, uint32_t src_base) {
   if (n == 0) return cudaSuccess;
   NoteLaunch();
-  fill_reverse_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(fwd, stride, n, off, cursor, rev);
+  fill_reverse_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(fwd, stride, n, off, cursor, rev,
+                                                                              src_base);
   return cudaGetLastError();
 }
 

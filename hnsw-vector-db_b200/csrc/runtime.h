@@ -277,6 +277,11 @@ Status BuildIvfPqFile(Context& ctx, int type, const float* rows, uint64_t n, uin
                       uint32_t nlist, uint32_t pq_m, uint32_t max_train_ppc, uint64_t seed, std::string* file);
 Status BuildHnswFile(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim, uint32_t pd, uint32_t M,
                      uint32_t kcand, uint64_t seed, std::string* file);
+// HnswIndex::extend (src/index/hnsw/hnsw_index.cc:50-58) on the GPU: graph g (parsed from an
+// index.hnsw over its first g.cap rows) with rows [g.cap, n) inserted, as a complete index file.
+struct HnswGraphData;
+Status ExtendHnswFile(Context& ctx, int metric, const HnswGraphData& g, uint32_t pd, const float* rows, uint64_t n,
+                      uint32_t dim, std::string* file);
 
 // Shared by flat and SQ8-flat search: a tensor-core pre-rank of every row followed by the exact
 // finalize. Declared here so the HNSW/IVF indexes can reuse it for exact fallbacks.

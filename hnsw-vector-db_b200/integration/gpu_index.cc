@@ -34,7 +34,7 @@ StatusOr<std::unique_ptr<Index>> GpuIndex::Load(vdbgpu_ctx* ctx, std::string_vie
     vdbgpu_last_error(ctx, msg, sizeof(msg));
     return rc == VDBGPU_CORRUPTION ? Status::Corruption(msg) : Status::Internal(msg);
   }
-  return std::unique_ptr<Index>(new GpuIndex(ctx, h, view, static_cast<IndexType>(type), std::string(file)));
+  return std::unique_ptr<Index>(new GpuIndex(ctx, h, view, static_cast<IndexType>(type), metric, std::string(file)));
 }
 
 GpuIndex::~GpuIndex() { vdbgpu_index_free(h_); }
@@ -52,6 +52,23 @@ Status GpuIndex::save(WritableFile& f) const {
   std::string_view magic, body;
   VDB_RETURN_IF_ERROR(CheckIndexFile(file_, &magic, &body));
   return WriteIndexFile(f, magic, std::string(body));
+}
+
+StatusOr<std::unique_ptr<Index>> GpuIndex::extend(const VectorView& vectors, ThreadPool*) const {
+  if (vectors.rows < view_.rows || vectors.padded_dim != view_.padded_dim)
+    return Status::InvalidArgument("extend needs a superset of the indexed rows");
+  if (type_ == IndexType::Flat) return Load(ctx_, file_, metric_, vectors);  // a flat index has no state
+  if (type_ != IndexType::Hnsw)
+    return Status::NotSupported(std::string("extend is not supported by ") + IndexTypeName(type_));
+  void* out = nullptr;
+  size_t nbytes = 0;
+  const int rc = vdbgpu_hnsw_extend(ctx_, static_cast<int>(metric_), file_.data(), file_.size(), vectors.data,
+                                    vectors.rows, static_cast<uint32_t>(vectors.dim),
+                                    static_cast<uint32_t>(vectors.padded_dim), &out, &nbytes);
+  if (rc != VDBGPU_OK) return Error(rc);
+  std::string file(static_cast<const char*>(out), nbytes);
+  vdbgpu_buffer_free(out);
+  return Load(ctx_, file, metric_, vectors);
 }
 
 Status GpuIndex::search_batch(const float* q, size_t nq, size_t k, const SearchParams& p, const RowFilter* filter,

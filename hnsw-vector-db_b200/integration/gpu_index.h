@@ -40,15 +40,20 @@ class GpuIndex final : public Index {
   size_t memory_bytes() const override;
   // Writes back the file it was loaded from (magic, body, CRC32C footer).
   Status save(WritableFile& f) const override;
+  // Index::extend (src/index/index.h:53-54): Flat is rebuilt over `vectors`; an HNSW graph gets
+  // the new rows inserted on the GPU (vdbgpu_hnsw_extend); other types are not extendable, as in
+  // the reference. The new index lives on the same device.
+  StatusOr<std::unique_ptr<Index>> extend(const VectorView& vectors, ThreadPool* pool) const override;
 
  private:
-  GpuIndex(vdbgpu_ctx* ctx, vdbgpu_index* h, const VectorView& view, IndexType type, std::string file)
-      : ctx_(ctx), h_(h), view_(view), type_(type), file_(std::move(file)) {}
+  GpuIndex(vdbgpu_ctx* ctx, vdbgpu_index* h, const VectorView& view, IndexType type, Metric metric, std::string file)
+      : ctx_(ctx), h_(h), view_(view), type_(type), metric_(metric), file_(std::move(file)) {}
   Status Error(int rc) const;
   vdbgpu_ctx* ctx_;
   vdbgpu_index* h_;
   VectorView view_;
   IndexType type_;
+  Metric metric_;
   std::string file_;
 };
 

@@ -119,6 +119,8 @@ _SIGNATURES = {
     "vdbgpu_hnsw_build": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                          ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, ctypes.POINTER(_P),
                                          ctypes.POINTER(ctypes.c_size_t)]),
+    "vdbgpu_hnsw_extend": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_size_t, _P, ctypes.c_uint64, ctypes.c_uint32,
+                                          ctypes.c_uint32, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t)]),
     "vdbgpu_ivfpq_build": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                           ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64,
                                           ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t)]),
@@ -651,6 +653,23 @@ def build_hnsw(ctx: Context, metric, rows, dim: int, M: int = 16, candidates: in
     nb = ctypes.c_size_t(0)
     ctx.check(lib().vdbgpu_hnsw_build(ctx._h, m, _ptr(rows), n, int(dim), pd, int(M), int(candidates), int(seed),
                                       ctypes.byref(p), ctypes.byref(nb)))
+    try:
+        return ctypes.string_at(p, nb.value)
+    finally:
+        lib().vdbgpu_buffer_free(p)
+
+
+def extend_hnsw(ctx: Context, metric, file_bytes: bytes, rows, dim: int) -> bytes:
+    """HnswIndex::extend on the GPU: the index.hnsw `file_bytes` (a graph over the first rows of
+    `rows`) with the remaining rows inserted, as a new index file in the same format. rows is
+    (n, padded_dim) float32, numpy or a CUDA tensor."""
+    m = METRICS[metric] if isinstance(metric, str) else int(metric)
+    n, pd = int(rows.shape[0]), int(rows.shape[1])
+    buf = np.frombuffer(file_bytes, dtype=np.uint8)
+    p = _P()
+    nb = ctypes.c_size_t(0)
+    ctx.check(lib().vdbgpu_hnsw_extend(ctx._h, m, buf.ctypes.data, buf.size, _ptr(rows), n, int(dim), pd,
+                                       ctypes.byref(p), ctypes.byref(nb)))
     try:
         return ctypes.string_at(p, nb.value)
     finally:

@@ -361,6 +361,21 @@ VDBGPU_API int vdbgpu_hnsw_build(vdbgpu_ctx* ctx, int metric, const float* rows,
                                  uint32_t dim, uint32_t padded_dim, uint32_t M, uint32_t candidates,
                                  uint64_t seed, void** out_file, size_t* out_bytes);
 
+/* HnswIndex::extend (src/index/hnsw/hnsw_index.cc:50-58) on the GPU: the index.hnsw file
+ * (file_bytes, the graph over the first rows) with the remaining rows of `rows` (nrows x
+ * padded_dim floats, host or device, nrows >= the graph's rows) inserted, as a complete index
+ * file in the same format (the graph's M, seed and ef_construction field kept). New nodes take
+ * level_for's levels with the graph's seed; each links to select_neighbors of its exact nearest
+ * neighbours among the old nodes and the new nodes inserted up to its round, and back links
+ * re-prune full lists with the heuristic, as vdbgpu_hnsw_build does. The reference's extend
+ * inserts one node at a time on host threads (order-dependent); this graph is valid in the same
+ * format, not the same graph. Only HNSW files (not HNSW-SQ8, PQ or IVF-PQ, which the reference
+ * cannot extend either: VDBGPU_NOT_SUPPORTED). *out_file is malloc'd; release it with
+ * vdbgpu_buffer_free. */
+VDBGPU_API int vdbgpu_hnsw_extend(vdbgpu_ctx* ctx, int metric, const void* file_bytes, size_t nbytes,
+                                  const float* rows, uint64_t nrows, uint32_t dim, uint32_t padded_dim,
+                                  void** out_file, size_t* out_bytes);
+
 /* Index::build + save for IVF-PQ (type VDBGPU_INDEX_IVF_PQ) and PQ-flat (VDBGPU_INDEX_PQ_FLAT) on
  * the GPU (IvfPqIndex::build, src/index/quant/ivf_pq.cc:106-150; PqFlatIndex::build, :45-58):
  * the reference's seeded k-means (kmeans.cc:55-174) replayed exactly (host RNG and sums, GPU

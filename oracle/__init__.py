@@ -95,6 +95,7 @@ class Ref:
             "ref_index_load": (_P, [_P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64, ctypes.c_uint32,
                                     ctypes.c_uint32, ctypes.c_uint32]),
             "ref_index_free": (None, [_P]),
+            "ref_index_extend": (_P, [_P, _P, ctypes.c_uint64, ctypes.c_int]),
             "ref_index_type": (ctypes.c_int, [_P]),
             "ref_index_save": (ctypes.c_size_t, [_P, ctypes.POINTER(_P)]),
             "ref_free": (None, [_P]),
@@ -191,6 +192,13 @@ class RefIndex:
         data = ctypes.string_at(p, size)
         self.ref.l.ref_free(p)
         return data
+
+    def extend(self, rows: np.ndarray, threads=0) -> "RefIndex":
+        """Index::extend over `rows` (the index's rows first): a new index."""
+        h = self.ref.l.ref_index_extend(self.h, _ptr(rows), rows.shape[0], threads)
+        if not h:
+            raise RuntimeError(self.ref.l.ref_last_error().decode())
+        return RefIndex(self.ref, h, rows.shape[0], rows.shape[1])
 
     def search(self, q, k=10, ef=64, nprobe=16, rerank=-1, allow=None, threads=0):
         nq = q.shape[0]

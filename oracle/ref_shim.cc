@@ -158,6 +158,28 @@ ref_index* ref_index_load(const void* bytes, size_t nbytes, int metric, const fl
   return h;
 }
 
+// Index::extend (src/index/index.h:53-54) over a copy of `rows` (n rows, the first ones the
+// index's own); threads as in ref_index_build. A new handle, or null with ref_last_error.
+ref_index* ref_index_extend(const ref_index* h, const float* rows, uint64_t n, int threads) {
+  ref_index* e = MakeHandle(static_cast<int>(h->metric), rows, n, static_cast<uint32_t>(h->view.dim),
+                            static_cast<uint32_t>(h->view.padded_dim));
+  e->opts = h->opts;
+  vdb::StatusOr<std::unique_ptr<vdb::Index>> r = vdb::Status::Internal("unreached");
+  if (threads == 1) {
+    r = h->index->extend(e->view, nullptr);
+  } else {
+    vdb::ThreadPool pool(static_cast<size_t>(threads));
+    r = h->index->extend(e->view, &pool);
+  }
+  if (!r.ok()) {
+    g_error = r.status().ToString();
+    delete e;
+    return nullptr;
+  }
+  e->index = std::move(r).value();
+  return e;
+}
+
 void ref_index_free(ref_index* h) { delete h; }
 
 int ref_index_type(const ref_index* h) { return static_cast<int>(h->index->type()); }
