@@ -40,13 +40,6 @@ struct WarpSmem {
   float* nb_d;        // their distances
 };
 
-// A relaxed GPU-scope load: reads past L1, and is ordered with the atomics that made the marks.
-__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Brings a line into L2 without waiting for it (no register is written).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
@@ -686,12 +679,6 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
       ncand = 1;
       __syncwarp();
       int steps = 0;
-      // Speculation on the next expansion: after this expansion's visit marks are in place, the
-      // front head's link list and its neighbours' visited words are read. The head rarely
-      // changes before it is popped (only a new candidate below it displaces it); when it is the
-      // next node expanded, its freshness is known without a round trip to the visited bitmap:
-      // no visit happens between the read and that expansion, so the words are exact.
-      uint32_t spec_id = 0xFFFFFFFFu, spec_cnt = 0, spec_e = 0, spec_w = 0;
       while (!bad) {
         if (ncand == 0) {
           if (npool == 0) break;
@@ -713,37 +700,20 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
           break;
         }
         const uint32_t cid = neighbor_id(c);
-        const bool known = cid == spec_id;  // warp-uniform
-        uint32_t cnt, e_raw;
-        if (known) {
-          cnt = spec_cnt;
-          e_raw = spec_e;
-        } else {
-          const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
-          // The list's count and its slots load together (a block always holds M0 slots).
-          cnt = ll[0];
-          e_raw = lane < static_cast<int>(a.M0) ? ll[1 + lane] : 0u;
-        }
-        // The next expansion most often takes the current front head: its link list is read now
-        // and lands while this expansion runs.
-        const uint32_t nxt = ncand > 0 ? neighbor_id(s.cand[chead]) : 0xFFFFFFFFu;
-        uint32_t nxt_cnt = 0, nxt_e = 0;
-        if (nxt != 0xFFFFFFFFu) {
-          const uint32_t* nl = a.links0 + static_cast<size_t>(nxt) * (1 + a.M0);
-          nxt_cnt = nl[0];
-          nxt_e = lane < static_cast<int>(a.M0) ? nl[1 + lane] : 0u;
-        }
+        const uint32_t* ll = a.links0 + static_cast<size_t>(cid) * (1 + a.M0);
+        // The list's count and its slots load together (a block always holds M0 slots).
+        const uint32_t cnt = ll[0];
+        const uint32_t e_raw = lane < static_cast<int>(a.M0) ? ll[1 + lane] : 0u;
+        // The next expansion most often takes the current front head: its link block starts
+        // towards L2 now and lands while this expansion runs.
+        if (ncand > 0 && lane < 2)
+          prefetch_l2(a.links0 + static_cast<size_t>(neighbor_id(s.cand[chead])) * (1 + a.M0) + 32 * lane);
         uint32_t e = 0;
         bool fresh = false, al = false;
         if (lane < static_cast<int>(cnt)) {
           e = e_raw;
           if (e >= n) {
             bad = true;
-          } else if (known) {
-            const uint32_t bit = 1u << (e & 31);
-            fresh = (spec_w & bit) == 0u;
-            if (fresh) atomicOr(&vis[e >> 5], bit);  // the mark; its old value is already known
-            al = allowed(e);
           } else {
             // Unfiltered walks: the neighbour's vector starts towards L2 beside its visited mark,
             // so the distance pass below finds it there (a visited neighbour's vector is fetched
@@ -770,8 +740,6 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
         const uint32_t fm = __ballot_sync(0xFFFFFFFFu, fresh);
         const int nf = __popc(fm);
         if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
-        // This expansion's marks reach the bitmap before any lane reads it again below.
-        __threadfence_block();
         __syncwarp();
         // The filter bits in the compacted (list) order of the fresh neighbours.
         const int src = lane < nf ? static_cast<int>(__fns(fm, 0, lane + 1)) : 0;
@@ -779,13 +747,6 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
         const uint32_t amask = __ballot_sync(0xFFFFFFFFu, lane < nf && al_c != 0);
         dists_of<kSq8>(a, s.q, s.nb_id, s.nb_d, nf, l2);
         dc += static_cast<uint64_t>(nf);
-        // The next head's visited words, read past L1 (the marks are made in L2). A link out of
-        // range reads nothing (the expansion that uses it reports the corrupt graph).
-        spec_id = nxt;
-        spec_cnt = nxt_cnt;
-        spec_e = nxt_e;
-        spec_w = 0;
-        if (nxt != 0xFFFFFFFFu && lane < static_cast<int>(nxt_cnt) && nxt_e < n) spec_w = ld_relaxed(&vis[nxt_e >> 5]);
         // Result updates in list order decide which neighbours become candidates; the candidates
         // themselves are merged afterwards (their order of insertion does not matter).
         uint64_t mykey = ~0ull;
