@@ -40,11 +40,6 @@ struct WarpSmem {
   float* nb_d;        // their distances
 };
 
-// Brings a line into L2 without waiting for it (no register is written).
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
-}
-
 __device__ __forceinline__ uint32_t hash_slot(uint32_t id, int bits) {
   return (id * 2654435761u) >> (32 - bits);
 }
