@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "hnsw_build.cuh"
+#include "ivfpq.cuh"
 #include "kernels.cuh"
 #include "runtime.h"
 #include "scan_mma.cuh"
@@ -132,6 +133,7 @@ class FlatGpuIndex final : public GpuIndex {
     VDBGPU_RETURN_IF_ERROR(
         ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, op_.ab_format));
     VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, sample_rowterm_));
+    VDBGPU_RETURN_IF_ERROR(BuildQueryGrouping(ctx, &op_, metric, dim, pd, &pivots_));
     return ctx.Sync("flat index build");
   }
 
@@ -162,6 +164,7 @@ class FlatGpuIndex final : public GpuIndex {
   DeviceBuffer rows_, operand_, norms_;
   DeviceBuffer sample_rowterm_[2];
   ScanOperands op_;
+  std::unique_ptr<GpuIndex> pivots_;
 };
 
 class Sq8FlatGpuIndex final : public GpuIndex {
@@ -239,6 +242,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
     op_.scale = scale_.as<float>();
     VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&op_.b_map, operand_.get(), npad, kpad, kScanBN, 0));
     VDBGPU_RETURN_IF_ERROR(BuildScanSample(ctx, &op_, sample_rowterm_));
+    VDBGPU_RETURN_IF_ERROR(BuildQueryGrouping(ctx, &op_, metric, dim, pd, &pivots_));
     return ctx.Sync("sq8 index build");
   }
 
@@ -295,6 +299,7 @@ class Sq8FlatGpuIndex final : public GpuIndex {
   DeviceBuffer rows_, codes_, operand_, rowterm_, vmin_, scale_;
   DeviceBuffer sample_rowterm_[2];
   ScanOperands op_;
+  std::unique_ptr<GpuIndex> pivots_;
 };
 
 }  // namespace
@@ -329,12 +334,107 @@ Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer (&rowterm_s)
   return Status::OK();
 }
 
+constexpr uint64_t kGroupPivots = 1024;      // query-grouping pivots
+constexpr uint64_t kGroupSample = 4096;      // sample rows the pivots are chosen from (about)
+constexpr uint64_t kGroupMinQueries = 2048;  // batches below this are scanned as given
+
+bool GroupingEnabled() {
+  const char* v = std::getenv("VDB_SCAN_GROUP");
+  return v == nullptr || *v == 0 || std::strcmp(v, "0") != 0;
+}
+
+namespace {
+
+// L2 for metric 0, else minus the dot product; four partial sums (pd is a multiple of 16).
+float GroupKey(const float* a, const float* b, uint32_t pd, bool l2) {
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  for (uint32_t i = 0; i < pd; i += 4) {
+    for (int j = 0; j < 4; ++j) {
+      if (l2) {
+        const float d = a[i + j] - b[i + j];
+        s[j] += d * d;
+      } else {
+        s[j] += a[i + j] * b[i + j];
+      }
+    }
+  }
+  const float t = (s[0] + s[1]) + (s[2] + s[3]);
+  return l2 ? t : -t;
+}
+
+// The grouping pivots, `want` rows of the n-row sample: farthest-point selection (each new pivot
+// the sample row whose nearest chosen pivot is farthest, first maximum, starting at sample row 0),
+// which on clustered rows takes one pivot in every cluster before a second in any, then ordered
+// by a greedy nearest-neighbour chain from the first (nearest unvisited next, first minimum), so
+// pivots that share a region sit next to each other in the scan order.
+std::vector<float> ChooseGroupPivots(const std::vector<float>& s, uint64_t n, uint32_t pd, bool l2,
+                                     uint64_t want) {
+  std::vector<uint64_t> sel{0};
+  std::vector<float> near(n);
+  for (uint64_t i = 0; i < n; ++i) near[i] = GroupKey(&s[0], &s[i * pd], pd, l2);
+  while (sel.size() < want) {
+    uint64_t far = 0;
+    for (uint64_t i = 1; i < n; ++i)
+      if (near[i] > near[far]) far = i;
+    sel.push_back(far);
+    for (uint64_t i = 0; i < n; ++i) near[i] = std::min(near[i], GroupKey(&s[far * pd], &s[i * pd], pd, l2));
+  }
+  const uint64_t p = sel.size();
+  std::vector<char> used(p, 0);
+  std::vector<float> out(p * pd);
+  uint64_t cur = 0;
+  used[0] = 1;
+  for (uint64_t o = 0; o < p; ++o) {
+    std::memcpy(&out[o * pd], &s[sel[cur] * pd], pd * sizeof(float));
+    uint64_t next = p;
+    float best = 0.f;
+    for (uint64_t j = 0; j < p; ++j) {
+      if (used[j]) continue;
+      const float k = GroupKey(&s[sel[cur] * pd], &s[sel[j] * pd], pd, l2);
+      if (next == p || k < best) {
+        best = k;
+        next = j;
+      }
+    }
+    if (next == p) break;
+    used[next] = 1;
+    cur = next;
+  }
+  return out;
+}
+
+}  // namespace
+
+Status BuildQueryGrouping(Context& ctx, ScanOperands* op, int metric, uint32_t dim, uint32_t pd,
+                          std::unique_ptr<GpuIndex>* pivots) {
+  op->group_index = nullptr;
+  pivots->reset();
+  if (op->rows < kSampleMinRows || op->rows_f32 == nullptr || !GroupingEnabled()) return Status::OK();
+  const uint64_t stride = std::max<uint64_t>(1, op->rows / kGroupSample);
+  const uint64_t n = op->rows / stride;
+  std::vector<float> sample(n * pd);
+  VDBGPU_CUDA(cudaMemcpy2DAsync(sample.data(), pd * sizeof(float), op->rows_f32, stride * pd * sizeof(float),
+                                pd * sizeof(float), n, cudaMemcpyDeviceToHost, ctx.stream()));
+  VDBGPU_RETURN_IF_ERROR(ctx.Sync("grouping sample"));
+  const uint64_t want = std::min<uint64_t>(kGroupPivots, n / 4);
+  const std::vector<float> rows = ChooseGroupPivots(sample, n, pd, metric == 0, want);
+  DeviceBuffer prow;
+  VDBGPU_RETURN_IF_ERROR(prow.alloc(rows.size() * sizeof(float)));
+  VDBGPU_CUDA(cudaMemcpyAsync(prow.get(), rows.data(), rows.size() * sizeof(float), cudaMemcpyHostToDevice,
+                              ctx.stream()));
+  VDBGPU_RETURN_IF_ERROR(CreateFlatIndex(ctx, metric, prow.as<float>(), want, dim, pd, pivots));
+  op->group_index = pivots->get();
+  return Status::OK();
+}
+
 namespace {
 
 // One scan (plus its seed) and finalize over b; seeded scans rescan the queries finalize
-// returns (fewer than cpre keys below their bound) without a seed.
+// returns (fewer than cpre keys below their bound) without a seed. mark0 = false: the caller
+// recorded stage mark 0 already.
 Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
-                      const SearchBatch& b, int cpre, int depth, bool top) {
+                      const SearchBatch& b, int cpre, int depth, bool top, bool mark0 = true,
+                      bool nearest = false) {
   if (b.nq == 0) return Status::OK();
   if (op.rows == 0) {
     // Nothing to scan: every slot is a miss.
@@ -355,7 +455,7 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsQTau, nq * sizeof(uint32_t), &qtau));
   VDBGPU_CUDA(cudaMemsetAsync(qtau, 0xFF, nq * sizeof(uint32_t), ctx.stream()));
 
-  if (top) ctx.Mark(0);
+  if (top && mark0) ctx.Mark(0);
   PrepArgs pa{};
   pa.nq = static_cast<int>(nq);
   pa.nq_pad = static_cast<int>(nq_pad);
@@ -387,7 +487,7 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   // One candidate list per (unit, epilogue warpgroup, query). Two warpgroups split each tile's
   // columns and halve the time an accumulator waits for its epilogue, but double the lists: a
   // win once seeding keeps the lists short.
-  const uint64_t wgs = static_cast<uint64_t>(ctx.scan_wgs() > 0 ? ctx.scan_wgs() : (seeded ? 2 : 1));
+  const uint64_t wgs = nearest ? 1 : static_cast<uint64_t>(ctx.scan_wgs() > 0 ? ctx.scan_wgs() : (seeded ? 2 : 1));
   // Sample levels, coarsest first: each starts from the bound the previous one seeded.
   const int levels = seeded ? (op.nsamples > 1 && op.samples[1].rows >= 4u * static_cast<uint64_t>(
                                                        SeedKeep(cpre, op.samples[0].stride)) ? 2 : 1)
@@ -426,6 +526,13 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
   sa.cand_count = static_cast<int*>(cnt);
   sa.qtau = static_cast<uint32_t*>(qtau);
   sa.status = ctx.status_word();
+  if (nearest) {
+    // Only each query's nearest row is wanted: each 32-row chunk offers its best key with that
+    // key's row, and lists compact to one entry.
+    sa.keep = 1;
+    sa.chunk_best = 2;
+    sa.compact_at = 96;
+  }
   for (int lv = levels - 1; lv >= 0; --lv) {
     const ScanOperands::Sample& smp = op.samples[lv];
     const uint64_t nu = qtiles * static_cast<uint64_t>(upq_s[lv]);
@@ -524,7 +631,46 @@ Status ScanSearchImpl(Context& ctx, const ScanOperands& op, int metric, uint32_t
 
 Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
                   const SearchBatch& b, int cpre, int depth) {
-  return ScanSearchImpl(ctx, op, metric, pd, b, cpre, depth, true);
+  if (op.group_index == nullptr || b.nq < kGroupMinQueries || b.allow != nullptr || op.rows == 0)
+    return ScanSearchImpl(ctx, op, metric, pd, b, cpre, depth, true);
+  // Query grouping (stage 0 includes it): each query's nearest pivot (a tensor-core scan of the
+  // pivots in which each 32-row chunk offers its best row, then that row's exact distance), the queries ordered by pivot (a counting sort), the scan
+  // over the reordered batch, and its results written back to the caller's query order. Every
+  // query's result is its own, whatever order the batch is scanned in.
+  ctx.Mark(0);
+  const uint64_t nq = b.nq;
+  const uint32_t cells = static_cast<uint32_t>(op.group_index->rows());
+  void *pid, *pdist, *ord, *qp, *od, *orow;
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsGroupIds, nq * 4, &pid));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsGroupDist, nq * 4, &pdist));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsGroupOrder, (nq + cells + 1) * 4, &ord));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsGroupQueries, nq * pd * sizeof(float), &qp));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsGroupOutDist, nq * b.k * sizeof(float), &od));
+  VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsGroupOutRow, nq * b.k * sizeof(uint32_t), &orow));
+  SearchBatch pb{};
+  pb.queries = b.queries;
+  pb.nq = nq;
+  pb.k = 1;
+  pb.out_dist = static_cast<float*>(pdist);
+  pb.out_row = static_cast<uint32_t*>(pid);
+  const ScanOperands* pop = nullptr;
+  int pcpre = 0, pdepth = 0;
+  VDBGPU_RETURN_IF_ERROR(op.group_index->ScanPlan(pb, &pop, &pcpre, &pdepth));
+  VDBGPU_RETURN_IF_ERROR(ScanSearchImpl(ctx, *pop, metric, pd, pb, 1, 0, false, false, true));
+  uint32_t* order = static_cast<uint32_t*>(ord);
+  VDBGPU_CUDA(LaunchProbeOrder(static_cast<const uint32_t*>(pid), static_cast<int>(nq), 1, cells, order + nq, order,
+                               ctx.stream()));
+  VDBGPU_CUDA(LaunchGatherRows(b.queries, order, nq, static_cast<int>(pd), static_cast<float*>(qp), ctx.stream()));
+  SearchBatch sub = b;
+  sub.queries = static_cast<const float*>(qp);
+  sub.out_dist = static_cast<float*>(od);
+  sub.out_row = static_cast<uint32_t*>(orow);
+  sub.dist_comps = nullptr;
+  VDBGPU_RETURN_IF_ERROR(ScanSearchImpl(ctx, op, metric, pd, sub, cpre, depth, true, false));
+  VDBGPU_CUDA(LaunchScatterResults(static_cast<const float*>(od), static_cast<const uint32_t*>(orow), order,
+                                   static_cast<uint32_t>(nq), static_cast<int>(b.k), b.out_dist, b.out_row,
+                                   ctx.stream()));
+  return Status::OK();
 }
 
 Status CreateFlatIndex(Context& ctx, int metric, const float* rows, uint64_t n, uint32_t dim,

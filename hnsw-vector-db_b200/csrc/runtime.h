@@ -187,6 +187,12 @@ enum WorkspaceSlot : int {
   kWsFbQueries,
   kWsFbDist,
   kWsFbRow,
+  kWsGroupIds,
+  kWsGroupDist,
+  kWsGroupOrder,
+  kWsGroupQueries,
+  kWsGroupOutDist,
+  kWsGroupOutRow,
 };
 
 enum IndexKind : int {
@@ -310,10 +316,20 @@ struct ScanOperands {
   };
   Sample samples[2];
   int nsamples = 0;
+  // Query grouping: a flat index over up to 1024 pivot rows chosen from a row sample. Large
+  // batches are scanned in the order of each query's nearest pivot, so the 32 queries an epilogue
+  // warp serves tend to share their candidate rows and fewer 32-row chunks hold a candidate for
+  // any of them. Null = no grouping.
+  const GpuIndex* group_index = nullptr;
 };
 // Attaches the seeding samples to `op` (after b_map / rowterm are set). rowterm_s[0..1] receive
 // the sampled row terms. Small operands (and VDB_SCAN_SAMPLE=0) get none.
 Status BuildScanSample(Context& ctx, ScanOperands* op, DeviceBuffer (&rowterm_s)[2]);
+// Chooses the query-grouping pivots of `op` from about 4096 of its fp32 rows (index_flat.cc),
+// builds their flat index into `pivots` (index metric) and attaches it. Small operands (and
+// VDB_SCAN_GROUP=0) get none.
+Status BuildQueryGrouping(Context& ctx, ScanOperands* op, int metric, uint32_t dim, uint32_t pd,
+                          std::unique_ptr<GpuIndex>* pivots);
 Status ScanSearch(Context& ctx, const ScanOperands& op, int metric, uint32_t pd,
                   const SearchBatch& b, int cpre, int depth);
 

@@ -440,14 +440,26 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
           uint32_t hits = vote(cbest);
           if (a.chunk_best) {
             // A seeding sample scan needs an estimate of the keep-th key only: each chunk's best
-            // key (a real row's) stands for the chunk, and nothing is read again.
+            // key (a real row's) stands for the chunk, filed under the chunk's first row, and
+            // nothing is read again. A nearest-row scan (chunk_best 2, one warpgroup) reloads the
+            // chunk to file the key under its own row (the first column holding it).
 #pragma unroll
             for (int ch = 0; ch < kChunks; ++ch) {
               if ((hits >> ch) & 1u) {
                 const float sc = cbest[ch];
+                int col = 0;
+                if (kWgs == 1 && a.chunk_best == 2) {
+                  __syncwarp();
+                  tmem_ld_32x32b_x32(t_addr + ch * 32, va);
+                  tmem_ld_wait_regs(va);
+                  scores(va, c_base + ch * 32);
+#pragma unroll
+                  for (int j = 31; j >= 0; --j)
+                    if (__uint_as_float(va[j]) == sc) col = j;
+                }
                 if (kMin ? (sc < tau) : (sc > tau_acc)) {
                   const float key = kMin ? sc : qs * sc;
-                  buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c_base + ch * 32));
+                  buf[count] = make_uint2(__float_as_uint(key), static_cast<uint32_t>(c_base + ch * 32 + col));
                   ++count;
                   ++n_ins;
                 }

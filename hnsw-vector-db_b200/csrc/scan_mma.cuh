@@ -35,7 +35,9 @@ struct ScanArgs {
   int keep;             // candidates kept per compaction (C), < kScanCap - 32
   int compact_at;       // list length that triggers a compaction, <= kScanCap - 32 (0 = that)
   int stages;           // B k-block stages in flight, 1..kScanMaxStages (0 = kScanStages)
-  int chunk_best;       // 1: each 32-row chunk contributes only its best key (seeding sample scans)
+  int chunk_best;       // 1: each 32-row chunk contributes only its best key, filed under the chunk's
+                        // first row (seeding sample scans); 2: under the key's own row (nearest rows;
+                        // one epilogue warpgroup)
   int units_per_qtile;  // row slices per 128-query tile
   int rows_per_unit;    // multiple of kScanBN
   int nunits;           // qtiles * units_per_qtile

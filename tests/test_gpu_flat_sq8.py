@@ -116,6 +116,44 @@ def test_sq8_scan_full_size_config1(ctx):
     assert np.all(np.diff(d, axis=1) >= 0)
 
 
+@pytest.mark.parametrize("metric", [0, 1])
+def test_grouped_scan_is_the_ungrouped_scan(ctx, monkeypatch, metric):
+    """Batches of at least 2048 queries over operands of 64k rows and more are scanned in the
+    order of each query's nearest pivot (up to 1024 rows picked from a row sample), and the
+    results written back in the caller's order. Ids (tie order included) and distances equal those of the same
+    index built without grouping (VDB_SCAN_GROUP=0), for the batch and for a shuffled copy of it,
+    and the oracle's on a sample (integer rows: tensor-core keys are exact). On clustered rows the
+    grouped scan finds candidates in fewer 32-query x 32-row chunks."""
+    import vdb_b200
+    from vdb_b200 import synth
+    base, qs = synth.flat_int(100_000, 4000, dim=128, seed=21)
+    idx = vdb_b200.Index.create(ctx, "flat", metric, base, 128)
+    ctx.set_timing(True)
+    ids, d = idx.search(qs, k=10)
+    grouped_chunks = ctx.stage_counters()[1]
+    ctx.set_timing(False)
+    perm = np.random.default_rng(5).permutation(len(qs))
+    ids2, d2 = idx.search(np.ascontiguousarray(qs[perm]), k=10)
+    np.testing.assert_array_equal(ids2, ids[perm])
+    np.testing.assert_array_equal(d2, d[perm])
+    monkeypatch.setenv("VDB_SCAN_GROUP", "0")
+    plain = vdb_b200.Index.create(ctx, "flat", metric, base, 128)
+    ctx.set_timing(True)
+    pi, pdist = plain.search(qs, k=10)
+    plain_chunks = ctx.stage_counters()[1]
+    ctx.set_timing(False)
+    np.testing.assert_array_equal(ids, pi)
+    np.testing.assert_array_equal(d, pdist)
+    if metric == 0:
+        assert grouped_chunks < 0.8 * plain_chunks, (grouped_chunks, plain_chunks)
+    sample = np.arange(0, len(qs), 200)
+    oi, od = oracle.Oracle().flat_search(metric, base, qs[sample], 10)
+    np.testing.assert_array_equal(ids[sample], oi)
+    np.testing.assert_array_equal(d[sample], od)
+    plain.free()
+    idx.free()
+
+
 @pytest.mark.parametrize("keep", [None, 1, 6])
 def test_seeded_scan_is_exact(ctx, monkeypatch, keep):
     """Batches of at least 5e7 (query, row) pairs over operands of 64k rows and more start every
