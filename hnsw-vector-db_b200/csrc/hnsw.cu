@@ -188,82 +188,24 @@ __device__ __forceinline__ float group_dist(const HnswArgs& a, const float* q_s,
   return l2 ? r : -r;
 }
 
-// Packed fp32 pairs (Blackwell's two-wide FP32 instructions): each half is one IEEE fp32 operation
-// with round-to-nearest, exactly as the scalar instruction.
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
-__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
-
-// pd == 128, AVX-512 order, float rows: 8 rows per pass, two per quarter-warp, every load issued
-// before any arithmetic. The AVX-512 kernel keeps two 16-wide accumulators, acc0 over elements
-// 32t + l and acc1 over 32t + 16 + l (t = 0..3), then reduces acc0 + acc1 by halves (+8, +4, +2,
-// +1). Lane j of a quarter-warp holds slots 2j and 2j + 1 of both, as packed pairs: its loads are
-// 8-byte pairs and its arithmetic two-wide; the reduction adds the same pairs in the same tree
-// (slots +8 sit four lanes away, +4 two lanes, +2 one lane, +1 in the lane), so every distance is
-// bit-identical to the reference's.
+// pd == 128, AVX-512 order: 8 rows per pass, packed pairs (warp_ops.cuh).
 __device__ __forceinline__ void dists_of_128(const HnswArgs& a, const float* q_s, const uint32_t* ids, float* d,
                                              int n, bool l2) {
-  const int lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
-  const uint64_t* q2 = reinterpret_cast<const uint64_t*>(q_s);
-  for (int i = 0; i < n; i += 8) {
-    uint64_t x[2][8];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int my = i + 4 * h + g;
-      const uint64_t* xp = reinterpret_cast<const uint64_t*>(a.rows + static_cast<size_t>(ids[my < n ? my : i]) * 128);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        x[h][2 * t] = __ldg(&xp[16 * t + j]);          // elements 32t + 2j, +1 (acc0)
-        x[h][2 * t + 1] = __ldg(&xp[16 * t + 8 + j]);  // elements 32t + 16 + 2j, +1 (acc1)
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint64_t A0 = 0, A1 = 0;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const uint64_t qa = q2[16 * t + j], qb = q2[16 * t + 8 + j];
-        if (l2) {
-          const uint64_t da = f2_sub(qa, x[h][2 * t]), db = f2_sub(qb, x[h][2 * t + 1]);
-          A0 = f2_fma(da, da, A0);
-          A1 = f2_fma(db, db, A1);
-        } else {
-          A0 = f2_fma(qa, x[h][2 * t], A0);
-          A1 = f2_fma(qb, x[h][2 * t + 1], A1);
-        }
-      }
-      uint64_t v = f2_add(A0, A1);                        // s[2j], s[2j + 1]
-      v = f2_add(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));  // + s[l + 8]
-      v = f2_add(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));  // + v[l + 4]
-      v = f2_add(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));  // + w[l + 2]
-      const float t3 = __fadd_rn(f2_lo(v), f2_hi(v));      // x[0] + x[1]
-      const int my = i + 4 * h + g;
-      if (j == 0 && my < n) d[my] = l2 ? t3 : -t3;
-    }
-  }
-  __syncwarp();
+  warp_dists128_f32(a.rows, q_s, n, l2, [&](int i) { return ids[i]; }, [&](int i, float v) { d[i] = v; });
+}
+__device__ __forceinline__ void sq8_dists_of_128(const HnswArgs& a, const float* q_s, const uint32_t* ids, float* d,
+                                                 int n, bool l2) {
+  warp_dists128_sq8(a.codes, q_s, a.vmin, a.scale, n, l2, [&](int i) { return ids[i]; },
+                    [&](int i, float v) { d[i] = v; });
 }
 
 // Distances of ids[0..n) (n <= 32) into d[0..n), four rows per pass.
 template <bool kSq8>
 __device__ void dists_of(const HnswArgs& a, const float* q_s, const uint32_t* ids, float* d, int n,
                          bool l2) {
-  if (!kSq8 && a.pd == 128 && a.order == kOrderAvx512) {
-    dists_of_128(a, q_s, ids, d, n, l2);
+  if (a.pd == 128 && a.order == kOrderAvx512) {
+    if (kSq8) sq8_dists_of_128(a, q_s, ids, d, n, l2);
+    else dists_of_128(a, q_s, ids, d, n, l2);
     return;
   }
   const int lane = threadIdx.x & 31, g = lane >> 3;

@@ -279,7 +279,13 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   // 2. Exact distances of the candidates (stored back as packed (dist, row)).
   const bool l2 = a.metric == 0;
   // Exact fp32 distances of surv[0..n) on the float rows, 4 gathers in flight at a time.
+  const bool packed128 = pd == 128 && a.order == kOrderAvx512;
   auto exact_rows = [&](int n) {
+    if (packed128) {
+      warp_dists128_f32(a.rows, q_s, n, l2, [&](int i) { return neighbor_id(surv[i]); },
+                        [&](int i, float v) { surv[i] = pack_neighbor(v, neighbor_id(surv[i])); });
+      return;
+    }
     for (int i = 0; i < n; i += 4) {
       uint32_t r[4];
 #pragma unroll
@@ -309,6 +315,16 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   if (a.codes == nullptr) {
     exact_rows(ncand);
     sort_small(surv, ncand);
+  } else if (packed128) {
+    warp_dists128_sq8(a.codes, q_s, vmin_s, scale_s, ncand, l2, [&](int i) { return neighbor_id(surv[i]); },
+                      [&](int i, float v) { surv[i] = pack_neighbor(v, neighbor_id(surv[i])); });
+    sort_small(surv, ncand);
+    if (a.depth > 0) {
+      const int nr = ncand < a.depth ? ncand : a.depth;
+      exact_rows(nr);
+      ncand = nr;
+      sort_small(surv, ncand);
+    }
   } else {
     for (int i = 0; i < ncand; i += 8) {
       // Four pairs of codes per iteration: half-warp h takes candidates i+2c+h, c = 0..3.

@@ -280,4 +280,129 @@ __device__ __forceinline__ void warp_exact_dist4_avx512(const float* q_s, const 
   }
 }
 
+// Packed fp32 pairs (Blackwell's two-wide FP32 instructions): each half is one IEEE fp32 operation
+// with round-to-nearest, exactly as the scalar instruction.
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+
+// The AVX-512 reduction of 16 lanes (+8, +4, +2, +1) over packed pairs: lane j of a quarter-warp
+// holds slots 2j and 2j + 1, so slots +8 sit four lanes away, +4 two lanes, +2 one lane and +1
+// in the lane. Every lane of the quarter-warp returns the sum.
+__device__ __forceinline__ float f2_reduce16(uint64_t v) {
+  v = f2_add(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+  v = f2_add(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+  v = f2_add(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+  return __fadd_rn(f2_lo(v), f2_hi(v));
+}
+
+// Exact distances (L2, or minus the dot product) of n rows of 128 floats in the AVX-512 kernel's
+// order, 8 rows per pass, two per quarter-warp, every load of a pass issued before any
+// arithmetic. The AVX-512 kernel keeps two 16-wide accumulators, acc0 over elements 32t + l and
+// acc1 over 32t + 16 + l (t = 0..3), and reduces acc0 + acc1 by halves. Lane j of a quarter-warp
+// holds slots 2j and 2j + 1 of both as packed pairs: its loads are 8-byte pairs and its arithmetic
+// two-wide, so every distance is bit-identical to warp_exact_dist's. id_at(i) gives row i's id;
+// put(i, dist) is called once per row, by one lane. q_s: 128 floats, 8-byte aligned.
+template <class IdAt, class Put>
+__device__ __forceinline__ void warp_dists128_f32(const float* __restrict__ rows, const float* q_s, int n, bool l2,
+                                                  IdAt id_at, Put put) {
+  const int lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
+  const uint64_t* q2 = reinterpret_cast<const uint64_t*>(q_s);
+  for (int i = 0; i < n; i += 8) {
+    uint64_t x[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int my = i + 4 * h + g;
+      const uint64_t* xp = reinterpret_cast<const uint64_t*>(rows + static_cast<size_t>(id_at(my < n ? my : i)) * 128);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        x[h][2 * t] = __ldg(&xp[16 * t + j]);          // elements 32t + 2j, +1 (acc0)
+        x[h][2 * t + 1] = __ldg(&xp[16 * t + 8 + j]);  // elements 32t + 16 + 2j, +1 (acc1)
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint64_t A0 = 0, A1 = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint64_t qa = q2[16 * t + j], qb = q2[16 * t + 8 + j];
+        if (l2) {
+          const uint64_t da = f2_sub(qa, x[h][2 * t]), db = f2_sub(qb, x[h][2 * t + 1]);
+          A0 = f2_fma(da, da, A0);
+          A1 = f2_fma(db, db, A1);
+        } else {
+          A0 = f2_fma(qa, x[h][2 * t], A0);
+          A1 = f2_fma(qb, x[h][2 * t + 1], A1);
+        }
+      }
+      const float t3 = f2_reduce16(f2_add(A0, A1));  // s[l] = acc0[l] + acc1[l], then the tree
+      const int my = i + 4 * h + g;
+      if (j == 0 && my < n) put(my, l2 ? t3 : -t3);
+    }
+  }
+  __syncwarp();
+}
+
+// Exact SQ8 distances of n code rows of 128 bytes in the AVX-512 kernel's order: one 16-wide
+// accumulator over elements 16t + l (t = 0..7) of x = fma(code, scale, vmin), reduced by halves.
+// Layout as warp_dists128_f32: lane j of a quarter-warp holds slots 2j and 2j + 1 (a 2-byte load
+// per t), 8 rows per pass; bit-identical to halfwarp_sq8_dist. vmin / scale / q_s: 128 floats,
+// 8-byte aligned.
+template <class IdAt, class Put>
+__device__ __forceinline__ void warp_dists128_sq8(const uint8_t* __restrict__ codes, const float* q_s,
+                                                  const float* vmin, const float* scale, int n, bool l2,
+                                                  IdAt id_at, Put put) {
+  const int lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
+  const uint64_t* q2 = reinterpret_cast<const uint64_t*>(q_s);
+  const uint64_t* v2 = reinterpret_cast<const uint64_t*>(vmin);
+  const uint64_t* s2 = reinterpret_cast<const uint64_t*>(scale);
+  for (int i = 0; i < n; i += 8) {
+    uint32_t c[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int my = i + 4 * h + g;
+      const uint16_t* cp = reinterpret_cast<const uint16_t*>(codes + static_cast<size_t>(id_at(my < n ? my : i)) * 128);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) c[h][t] = __ldg(&cp[8 * t + j]);  // elements 16t + 2j, +1
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint64_t A = 0;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const uint64_t cv = f2_pack(static_cast<float>(c[h][t] & 255u), static_cast<float>(c[h][t] >> 8));
+        const uint64_t xv = f2_fma(cv, s2[8 * t + j], v2[8 * t + j]);
+        const uint64_t qv = q2[8 * t + j];
+        if (l2) {
+          const uint64_t dv = f2_sub(qv, xv);
+          A = f2_fma(dv, dv, A);
+        } else {
+          A = f2_fma(qv, xv, A);
+        }
+      }
+      const float r = f2_reduce16(A);
+      const int my = i + 4 * h + g;
+      if (j == 0 && my < n) put(my, l2 ? r : -r);
+    }
+  }
+  __syncwarp();
+}
+
 }  // namespace vdbgpu
