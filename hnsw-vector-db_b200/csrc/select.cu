@@ -48,18 +48,71 @@ __device__ void sort_small(uint64_t* s, int n) {
   else sort_into_smem<8>(s, n);
 }
 
+// The c-th smallest (1-based) of the n distinct packed keys s[0..n), c <= n: the c-th smallest
+// 32-bit key K by a bitwise search from the top bit over keys held in registers (E per lane),
+// then, only when the entries whose key is K do not all fit, the row among them by a search on
+// the low word.
+template <int E>
+__device__ uint64_t kth_packed_regs(const uint64_t* s, int n, int c) {
+  const int lane = threadIdx.x & 31;
+  uint32_t k[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    k[e] = i < n ? static_cast<uint32_t>(s[i] >> 32) : 0xFFFFFFFFu;
+  }
+  uint32_t key = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = key | (1u << bit);
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) cnt += k[e] < cand ? 1 : 0;
+    if (__reduce_add_sync(0xFFFFFFFFu, cnt) < c) key = cand;
+  }
+  // key = the largest value with fewer than c keys below it, so the c-th key itself.
+  int below = 0, at = 0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    below += k[e] < key ? 1 : 0;
+    at += (k[e] == key && e * 32 + lane < n) ? 1 : 0;
+  }
+  below = __reduce_add_sync(0xFFFFFFFFu, below);
+  at = __reduce_add_sync(0xFFFFFFFFu, at);
+  const int r = c - below;  // rank among the entries whose key is K
+  if (r == at) return (static_cast<uint64_t>(key) << 32) | 0xFFFFFFFFull;
+  uint32_t row = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = row | (1u << bit);
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = e * 32 + lane;
+      cnt += (k[e] == key && i < n && static_cast<uint32_t>(s[i]) < cand) ? 1 : 0;
+    }
+    if (__reduce_add_sync(0xFFFFFFFFu, cnt) < r) row = cand;
+  }
+  return (static_cast<uint64_t>(key) << 32) | row;
+}
+
 // Keeps the c smallest of the n distinct packed keys s[0..n) (c < n <= kMaxSurvivors) in
-// s[0..c), unordered: the c-th smallest by a bitwise search from the top bit, then a stable
-// in-place compaction of the keys at or below it.
+// s[0..c), unordered: the c-th smallest (in registers up to 512 keys, else by a bitwise search
+// over shared memory from the top bit), then a stable in-place compaction of the keys at or
+// below it.
 __device__ void keep_smallest(uint64_t* s, int n, int c) {
   const int lane = threadIdx.x & 31;
   uint64_t ans = 0;
-  for (int bit = 63; bit >= 0; --bit) {
-    const uint64_t cand = ans | (1ull << bit);
-    int cnt = 0;
-    for (int i = lane; i < n; i += 32) cnt += s[i] < cand ? 1 : 0;
-    cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
-    if (cnt < c) ans = cand;
+  if (n <= 256) {
+    ans = kth_packed_regs<8>(s, n, c);
+  } else if (n <= 512) {
+    ans = kth_packed_regs<16>(s, n, c);
+  } else {
+    for (int bit = 63; bit >= 0; --bit) {
+      const uint64_t cand = ans | (1ull << bit);
+      int cnt = 0;
+      for (int i = lane; i < n; i += 32) cnt += s[i] < cand ? 1 : 0;
+      cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+      if (cnt < c) ans = cand;
+    }
   }
   const uint32_t lt = (1u << lane) - 1u;
   int w = 0;
@@ -196,42 +249,40 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   const uint32_t thr = a.qtau[q];  // keep key < thr (ordered); 0xFFFFFFFF keeps all
   const uint32_t lt = (1u << lane) - 1u;
 
-  // 1. Gather the entries that can still be among the C best. All list counts come in one
-  // load (lane p: list p of each group of 32); the first 32 entries of four lists at a time are
-  // loaded before any of them is filed, so the loads overlap.
+  // 1. Gather the entries that can still be among the C best: lane p reads list p of each group
+  // of 32, eight entries at a time in 16-byte loads (a list's slots are 16-byte aligned and
+  // kScanCap is even, so the pair past an odd count stays inside the list), all issued before
+  // any entry is filed.
   int nsurv = 0;
   const int lists = a.wgs * a.units_per_qtile;
-  auto file = [&](uint2 v, bool valid) {
-    const bool pass = valid && float_key(__uint_as_float(v.x)) < thr;
+  auto file = [&](uint32_t kx, uint32_t row, bool valid) {
+    const uint32_t key = float_key(__uint_as_float(kx));
+    const bool pass = valid && key < thr;
     const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
     const int pos = nsurv + __popc(m & lt);
-    if (pass && pos < kMaxSurvivors)
-      surv[pos] = (static_cast<uint64_t>(float_key(__uint_as_float(v.x))) << 32) | v.y;
+    if (pass && pos < kMaxSurvivors) surv[pos] = (static_cast<uint64_t>(key) << 32) | row;
     nsurv += __popc(m);
   };
+  static_assert(kScanCap % 2 == 0, "pairs of list slots");
   for (int p0 = 0; p0 < lists; p0 += 32) {
-    const int np = lists - p0 < 32 ? lists - p0 : 32;
-    const int my_cnt = lane < np ? a.cand_count[unit_slot(a, qtile, p0 + lane, row_in_tile)] : 0;
-    for (int j0 = 0; j0 < np; j0 += 4) {
-      uint2 v[4];
-      int n[4];
+    const int p = p0 + lane;
+    int my_cnt = 0;
+    const uint4* lp = nullptr;
+    if (p < lists) {
+      const size_t slot = unit_slot(a, qtile, p, row_in_tile);
+      my_cnt = a.cand_count[slot];
+      lp = reinterpret_cast<const uint4*>(a.cand + slot * kScanCap);
+    }
+    const int maxc = __reduce_max_sync(0xFFFFFFFFu, static_cast<uint32_t>(my_cnt));
+    for (int e0 = 0; e0 < maxc; e0 += 8) {
+      uint4 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        w[u] = e0 + 2 * u < my_cnt ? __ldg(&lp[(e0 >> 1) + u]) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        n[u] = j0 + u < np ? __shfl_sync(0xFFFFFFFFu, my_cnt, j0 + u) : 0;
-        v[u] = make_uint2(0, 0);
-        if (lane < n[u]) v[u] = a.cand[unit_slot(a, qtile, p0 + j0 + u, row_in_tile) * kScanCap + lane];
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (n[u] == 0) continue;
-        file(v[u], lane < n[u]);
-        if (n[u] > 32) {
-          const uint2* b = a.cand + unit_slot(a, qtile, p0 + j0 + u, row_in_tile) * kScanCap;
-          for (int e0 = 32; e0 < n[u]; e0 += 32) {
-            const int e = e0 + lane;
-            file(e < n[u] ? b[e] : make_uint2(0, 0), e < n[u]);
-          }
-        }
+        file(w[u].x, w[u].y, e0 + 2 * u < my_cnt);
+        file(w[u].z, w[u].w, e0 + 2 * u + 1 < my_cnt);
       }
     }
   }
