@@ -936,6 +936,20 @@ def run_c2(args):
         idx.search(q_dev, k=K, nprobe=C2_NPROBE, out=(ids_dev, d_dev))
     ms, clk = _timed(step, args.steps, args.warmup, stream, local)
     gpu_ids = ids_dev.cpu().numpy().view(np.uint32).copy()
+    # Launches per step, and the stages of the tensor-core path (marks: after the coarse probe,
+    # after the nearest-list pass, after the scan of all probed lists, after the exact stage), from
+    # separate timed steps.
+    launches0 = vdb_b200.launch_count()
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = vdb_b200.launch_count() - launches0
+    ctx.set_timing(True)
+    st = np.zeros(3)
+    for _ in range(3):
+        step()
+        st += np.array(ctx.stage_times()[:3])
+    ctx.set_timing(False)
+    st /= 3
     # End to end through the C ABI from pinned host buffers.
     q_host = torch.from_numpy(qs).pin_memory()
     ids_host = torch.empty((nq, K), dtype=torch.int32).pin_memory()
@@ -990,9 +1004,9 @@ def run_c2(args):
                                        f"(coarse probe included)"},
            "e2e": {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": nq * C2_DIM * 4,
                    "d2h_bytes_per_step": nq * K * 8},
-           # per step: the coarse probe (a flat search over the 4096 centroids: prep, scan, finalize)
-           # and the list scan with its re-rank
-           "gpu_launches": 4 * args.steps,
+           "stage_ms": {"nearest_list_pass": float(st[0]), "probed_lists_scan": float(st[1]),
+                        "exact_stage": float(st[2])},
+           "gpu_launches": int(launches_per_step) * args.steps,
            "recall_at_10_vs_exact": _recall(gpu_ids, gt),
            "identical_ids_vs_reference_same_index": float(np.mean(np.all(gpu_ids[:sample] == r_ids, axis=1))),
            "cpu_baseline": {"value": sample / cpu_s, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",

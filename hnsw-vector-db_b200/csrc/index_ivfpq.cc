@@ -3,12 +3,15 @@
 // PqFlatIndex::save, ivf_pq.cc:78-84).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
 #include "formats.h"
 #include "ivfpq.cuh"
+#include "kernels.cuh"
 #include "runtime.h"
+#include "scan_mma.cuh"
 
 namespace vdbgpu {
 namespace {
@@ -20,6 +23,17 @@ Status Upload(Context& ctx, const T* p, size_t count, DeviceBuffer* out) {
     VDBGPU_CUDA(cudaMemcpyAsync(out->get(), p, count * sizeof(T), cudaMemcpyDefault, ctx.stream()));
   return Status::OK();
 }
+
+uint64_t Up(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
+
+// VDB_IVF_TENSOR=0 keeps every IVF-PQ search on the per-query kernel.
+bool TensorEnabled() {
+  const char* v = std::getenv("VDB_IVF_TENSOR");
+  return v == nullptr || *v == 0 || std::strcmp(v, "0") != 0;
+}
+
+// Batches of at least this many queries (no filter, L2) take the tensor-core pre-rank.
+constexpr uint64_t kIvfTensorMinQueries = 512;
 
 // RerankDepth (src/index/quant/ivf_pq.cc:16-19).
 uint32_t RerankDepth(int32_t rerank, uint32_t k) {
@@ -34,7 +48,8 @@ class IvfPqGpuIndex final : public GpuIndex {
   const float* device_rows() const override { return rows_.as<float>(); }
   uint64_t device_bytes() const override {
     return rows_.size() + coarse_.size() + cents_.size() + term2_.size() + off_.size() + ids_.size() +
-           codes_.size() + (coarse_index_ ? coarse_index_->device_bytes() : 0);
+           codes_.size() + poff_.size() + resid_.size() + resid_term_.size() +
+           (coarse_index_ ? coarse_index_->device_bytes() : 0);
   }
 
   Status Load(Context& ctx, std::string_view body, const float* rows, uint64_t n) {
@@ -87,22 +102,217 @@ class IvfPqGpuIndex final : public GpuIndex {
       // (the reference computes dist_(q, coarse_l) for every list, ivf_pq.cc:176-181).
       if (nlist_ > 0)
         VDBGPU_RETURN_IF_ERROR(CreateFlatIndex(ctx, metric, coarse.data(), nlist_, dim, pd, &coarse_index_));
+      VDBGPU_RETURN_IF_ERROR(BuildListOperand(ctx, off));
     }
     return ctx.Sync("ivf-pq index load");
   }
 
-  Status Search(Context& ctx, const SearchBatch& b) override {
-    const uint32_t k = b.k;
-    const uint32_t depth = RerankDepth(b.params.rerank, k);
-    if (std::max(depth, k) > 256)
-      return Status(Status::kNotSupported, "re-rank depth or k above 256 is not supported on the GPU");
-    if (!pqflat_ && nlist_ == 0) {
-      std::vector<float> d(b.nq * k, INFINITY);
-      std::vector<uint32_t> r(b.nq * k, UINT32_MAX);
-      VDBGPU_CUDA(cudaMemcpyAsync(b.out_dist, d.data(), d.size() * 4, cudaMemcpyHostToDevice, ctx.stream()));
-      VDBGPU_CUDA(cudaMemcpyAsync(b.out_row, r.data(), r.size() * 4, cudaMemcpyHostToDevice, ctx.stream()));
-      return ctx.Sync("empty ivf search");
+  // The list-mode operand (ivf_mma.cu): decoded residuals in fp16, lists on 32-row boundaries.
+  // L2 only, lists below 2^24 rows, fp16-range codebooks; otherwise none and every search takes
+  // the per-query kernel.
+  Status BuildListOperand(Context& ctx, const std::vector<uint64_t>& off) {
+    kpad_ = static_cast<uint32_t>(Up(pd, kScanBK));
+    if (metric != 0 || nlist_ == 0 || kpad_ > kScanMaxKB * kScanBK || m_ * dsub_ != dim) return Status::OK();
+    std::vector<uint64_t> poff(nlist_ + 1, 0);
+    for (uint32_t l = 0; l < nlist_; ++l) {
+      const uint64_t size = off[l + 1] - off[l];
+      if (size >= (uint64_t{1} << 24)) return Status::OK();
+      poff[l + 1] = poff[l] + Up(size, 32);
     }
+    if (poff[nlist_] >= (uint64_t{1} << 31) - 512) return Status::OK();
+    DeviceBuffer amax;
+    VDBGPU_RETURN_IF_ERROR(amax.alloc(sizeof(uint32_t)));
+    VDBGPU_CUDA(cudaMemsetAsync(amax.get(), 0, sizeof(uint32_t), ctx.stream()));
+    VDBGPU_CUDA(LaunchAbsMax(cents_.as<float>(), static_cast<uint64_t>(m_) * 256 * dsub_, amax.as<uint32_t>(),
+                             ctx.stream()));
+    uint32_t bits = 0;
+    VDBGPU_CUDA(cudaMemcpyAsync(&bits, amax.get(), 4, cudaMemcpyDeviceToHost, ctx.stream()));
+    VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    float mx;
+    std::memcpy(&mx, &bits, 4);
+    if (!std::isfinite(mx) || mx > 60000.f) return Status::OK();
+    resid_scale_log2_ = mx > 0.f ? 14 - std::ilogb(mx) : 0;
+    const uint64_t npad = Up(std::max<uint64_t>(poff[nlist_], 1), kScanBN);
+    VDBGPU_RETURN_IF_ERROR(Upload(ctx, poff.data(), poff.size(), &poff_));
+    VDBGPU_RETURN_IF_ERROR(resid_.alloc(npad * kpad_ * 2));
+    VDBGPU_CUDA(cudaMemsetAsync(resid_.get(), 0, npad * kpad_ * 2, ctx.stream()));
+    VDBGPU_RETURN_IF_ERROR(resid_term_.alloc((npad + kScanBN) * sizeof(float)));
+    VDBGPU_CUDA(cudaMemsetAsync(resid_term_.get(), 0, (npad + kScanBN) * sizeof(float), ctx.stream()));
+    IvfDecodeArgs da{};
+    da.codes = codes_.as<uint8_t>();
+    da.list_off = off_.as<uint64_t>();
+    da.poff = poff_.as<uint64_t>();
+    da.nlist = nlist_;
+    da.m = static_cast<int>(m_);
+    da.dsub = static_cast<int>(dsub_);
+    da.kpad = static_cast<int>(kpad_);
+    da.cstride = static_cast<int>(pd);
+    da.centroids = cents_.as<float>();
+    da.coarse = coarse_.as<float>();
+    da.scale_log2 = resid_scale_log2_;
+    da.operand = static_cast<__half*>(resid_.get());
+    da.rowterm = resid_term_.as<float>();
+    VDBGPU_CUDA(LaunchIvfDecode(da, ctx.stream()));
+    VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&resid_map_, resid_.get(), npad, kpad_, kScanBN, 0));
+    list_mode_ = true;
+    return Status::OK();
+  }
+
+  // One list-mode scan over the pairs (query, probe < np): tiles, gathered query operand, scan.
+  // Returns the tile count.
+  Status ListScan(Context& ctx, const SearchBatch& b, const void* a_op, const float* qscale, const uint32_t* pid,
+                  const float* pdist, int nprobe, int np, int cpre, uint32_t* qtau, uint32_t* pair_slot,
+                  uint32_t* ntiles) {
+    const uint64_t nq = b.nq;
+    const uint64_t max_tiles = nq * static_cast<uint64_t>(np) / 128 + nlist_;
+    void *tiles, *sq, *so, *units, *ag, *qg, *cand, *cnt;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfTiles, 3 * (static_cast<uint64_t>(nlist_) + 1) * 4, &tiles));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfSlotQuery, max_tiles * 128 * 4, &sq));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfSlotOffset, max_tiles * 128 * 4, &so));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfUnits, max_tiles * sizeof(int2), &units));
+    uint32_t* counts = static_cast<uint32_t*>(tiles);
+    uint32_t* cursor = counts + nlist_ + 1;
+    uint32_t* tstart = cursor + nlist_ + 1;
+    VDBGPU_CUDA(cudaMemsetAsync(sq, 0xFF, max_tiles * 128 * 4, ctx.stream()));
+    IvfTileArgs ta{};
+    ta.nq = static_cast<int>(nq);
+    ta.nprobe = nprobe;
+    ta.np = np;
+    ta.nlist = nlist_;
+    ta.probe_ids = pid;
+    ta.probe_dist = pdist;
+    ta.list_off = off_.as<uint64_t>();
+    ta.poff = poff_.as<uint64_t>();
+    ta.cursor = cursor;
+    ta.tile_start = tstart;
+    ta.slot_query = static_cast<uint32_t*>(sq);
+    ta.slot_offset = static_cast<float*>(so);
+    ta.pair_slot = pair_slot;
+    ta.unit_rows = static_cast<int2*>(units);
+    VDBGPU_CUDA(LaunchIvfTiles(ta, counts, ctx.stream()));
+    uint32_t nt = 0;
+    VDBGPU_CUDA(cudaMemcpyAsync(&nt, tstart + nlist_, 4, cudaMemcpyDeviceToHost, ctx.stream()));
+    VDBGPU_CUDA(cudaStreamSynchronize(ctx.stream()));
+    if (nt > max_tiles) return Status(Status::kInternal, "ivf tiles: count out of range");
+    *ntiles = nt;
+    if (nt == 0) return Status::OK();
+    const uint64_t nslots = static_cast<uint64_t>(nt) * 128;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfAg, nslots * kpad_ * 2, &ag));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfQScaleG, nslots * 4, &qg));
+    VDBGPU_CUDA(LaunchIvfGather(a_op, qscale, static_cast<const uint32_t*>(sq), static_cast<uint32_t>(nslots),
+                                static_cast<int>(kpad_), ag, static_cast<float*>(qg), ctx.stream()));
+    CUtensorMap amap;
+    VDBGPU_RETURN_IF_ERROR(ctx.EncodeOperandMap(&amap, ag, nslots, kpad_, kScanBM, 0));
+    const int wgs = 2;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCand, static_cast<uint64_t>(nt) * wgs * kScanBM * kScanCap * sizeof(uint2), &cand));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, static_cast<uint64_t>(nt) * wgs * kScanBM * sizeof(int), &cnt));
+    ScanArgs sa{};
+    sa.nq = static_cast<int>(nslots);
+    sa.nrows = 0;
+    sa.kblocks = static_cast<int>(kpad_ / kScanBK);
+    sa.mode = kKeyList;
+    sa.ab_format = 0;
+    sa.keep = cpre;
+    sa.stages = ScanMaxStagesFor(sa.kblocks);
+    if (ctx.scan_stages() > 0) sa.stages = std::min(sa.stages, ctx.scan_stages());
+    sa.units_per_qtile = 1;
+    sa.rows_per_unit = kScanBN;
+    sa.nunits = static_cast<int>(nt);
+    sa.qscale = static_cast<const float*>(qg);
+    sa.rowterm = resid_term_.as<float>();
+    sa.wgs = wgs;
+    sa.cand = static_cast<uint2*>(cand);
+    sa.cand_count = static_cast<int*>(cnt);
+    sa.qtau = qtau;
+    sa.status = ctx.status_word();
+    sa.unit_rows = static_cast<const int2*>(units);
+    sa.slot_query = static_cast<const uint32_t*>(sq);
+    sa.slot_offset = static_cast<const float*>(so);
+    const int grid = static_cast<int>(std::min<uint64_t>(nt, static_cast<uint64_t>(ctx.sm_count())));
+    VDBGPU_CUDA(LaunchScan(amap, resid_map_, sa, grid, ctx.stream()));
+    return Status::OK();
+  }
+
+  // IVF-PQ search with the tensor-core pre-rank: the probe, a first list-mode scan of every
+  // query's nearest list (which publishes each query's cpre-th key there as its bound), the scan
+  // of all probed lists under those bounds, and the exact stage (reference ADC of the cpre best by
+  // pre-rank key, TopK, re-rank).
+  Status ListSearch(Context& ctx, const SearchBatch& b, uint32_t k, uint32_t depth, int nprobe, const uint32_t* pid,
+                    const float* pdist) {
+    const uint64_t nq = b.nq;
+    const uint32_t R = std::max(depth, k);
+    uint32_t c = 64;
+    while (c < 2 * R && c < 256) c <<= 1;
+    const int cpre = static_cast<int>(c);
+    const uint64_t nq_pad = Up(nq, kScanBM);
+    void *a_op, *qscale, *qtau, *ps;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfA, nq_pad * kpad_ * 2, &a_op));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfQScale, nq * 4, &qscale));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsQTau, nq * 4, &qtau));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsIvfPairSlot, nq * nprobe * 4, &ps));
+    PrepArgs pa{};
+    pa.nq = static_cast<int>(nq);
+    pa.nq_pad = static_cast<int>(nq_pad);
+    pa.pd = static_cast<int>(pd);
+    pa.kpad = static_cast<int>(kpad_);
+    pa.kind = kPrepFlat;
+    pa.ab_format = 0;
+    pa.key_factor = 2;
+    pa.row_scale_log2 = resid_scale_log2_;
+    pa.queries = b.queries;
+    pa.operand = a_op;
+    pa.qscale = static_cast<float*>(qscale);
+    VDBGPU_CUDA(LaunchPrepQueries(pa, ctx.stream()));
+    VDBGPU_CUDA(cudaMemsetAsync(qtau, 0xFF, nq * 4, ctx.stream()));
+    uint32_t nt = 0;
+    VDBGPU_RETURN_IF_ERROR(ListScan(ctx, b, a_op, static_cast<const float*>(qscale), pid, pdist, nprobe, 1, cpre,
+                                    static_cast<uint32_t*>(qtau), nullptr, &nt));
+    ctx.Mark(1);
+    VDBGPU_RETURN_IF_ERROR(ListScan(ctx, b, a_op, static_cast<const float*>(qscale), pid, pdist, nprobe, nprobe,
+                                    cpre, static_cast<uint32_t*>(qtau), static_cast<uint32_t*>(ps), &nt));
+    ctx.Mark(2);
+    void *cand, *cnt;
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCand, 0, &cand));
+    VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsCandCount, 0, &cnt));
+    IvfFinalizeArgs fa{};
+    fa.nq = static_cast<int>(nq);
+    fa.nprobe = nprobe;
+    fa.pd = static_cast<int>(pd);
+    fa.dim = static_cast<int>(dim);
+    fa.m = static_cast<int>(m_);
+    fa.dsub = static_cast<int>(dsub_);
+    fa.k = static_cast<int>(k);
+    fa.depth = static_cast<int>(depth);
+    fa.cpre = cpre;
+    fa.order = ctx.order();
+    fa.mode = term2_.get() != nullptr ? kIvfPrecomputed : kIvfResidual;
+    fa.wgs = 2;
+    fa.nlist = nlist_;
+    fa.pair_slot = static_cast<const uint32_t*>(ps);
+    fa.cand = static_cast<const uint2*>(cand);
+    fa.cand_count = static_cast<const int*>(cnt);
+    fa.qtau = static_cast<const uint32_t*>(qtau);
+    fa.probe_ids = pid;
+    fa.probe_dist = pdist;
+    fa.list_off = off_.as<uint64_t>();
+    fa.poff = poff_.as<uint64_t>();
+    fa.ids = ids_.as<uint32_t>();
+    fa.codes = codes_.as<uint8_t>();
+    fa.centroids = cents_.as<float>();
+    fa.term2 = term2_.as<float>();
+    fa.coarse = coarse_.as<float>();
+    fa.queries = b.queries;
+    fa.rows = rows_.as<float>();
+    fa.out_dist = b.out_dist;
+    fa.out_row = b.out_row;
+    fa.out_dc = b.dist_comps;
+    VDBGPU_CUDA(LaunchIvfFinalize(fa, ctx.stream()));
+    ctx.Mark(3);
+    return Status::OK();
+  }
+
+  // The fields of the per-query kernel's arguments that do not depend on the probe.
+  IvfPqArgs BaseArgs(const SearchBatch& b, uint32_t k, uint32_t depth) const {
     IvfPqArgs a{};
     a.nq = static_cast<int>(b.nq);
     a.pd = static_cast<int>(pd);
@@ -112,7 +322,6 @@ class IvfPqGpuIndex final : public GpuIndex {
     a.k = static_cast<int>(k);
     a.depth = static_cast<int>(depth);
     a.metric = metric;
-    a.order = ctx.order();
     a.nlist = nlist_;
     a.n = n_;
     a.queries = b.queries;
@@ -127,6 +336,23 @@ class IvfPqGpuIndex final : public GpuIndex {
     a.out_dist = b.out_dist;
     a.out_row = b.out_row;
     a.out_dc = b.dist_comps;
+    return a;
+  }
+
+  Status Search(Context& ctx, const SearchBatch& b) override {
+    const uint32_t k = b.k;
+    const uint32_t depth = RerankDepth(b.params.rerank, k);
+    if (std::max(depth, k) > 256)
+      return Status(Status::kNotSupported, "re-rank depth or k above 256 is not supported on the GPU");
+    if (!pqflat_ && nlist_ == 0) {
+      std::vector<float> d(b.nq * k, INFINITY);
+      std::vector<uint32_t> r(b.nq * k, UINT32_MAX);
+      VDBGPU_CUDA(cudaMemcpyAsync(b.out_dist, d.data(), d.size() * 4, cudaMemcpyHostToDevice, ctx.stream()));
+      VDBGPU_CUDA(cudaMemcpyAsync(b.out_row, r.data(), r.size() * 4, cudaMemcpyHostToDevice, ctx.stream()));
+      return ctx.Sync("empty ivf search");
+    }
+    IvfPqArgs a = BaseArgs(b, k, depth);
+    a.order = ctx.order();
     a.status = ctx.status_word();
     if (pqflat_) {
       a.mode = kPqFlat;
@@ -148,6 +374,13 @@ class IvfPqGpuIndex final : public GpuIndex {
       VDBGPU_RETURN_IF_ERROR(coarse_index_->Search(ctx, cb));
       a.probe_ids = static_cast<const uint32_t*>(pid);
       a.probe_dist = static_cast<const float*>(pdist);
+      // The exact stage takes the 256 best pre-rank keys: at least twice TopK's depth.
+      if (list_mode_ && TensorEnabled() && b.allow == nullptr && b.nq >= kIvfTensorMinQueries &&
+          std::max(depth, k) <= 128 &&
+          (a.mode == kIvfPrecomputed || a.mode == kIvfResidual)) {
+        ctx.Mark(0);
+        return ListSearch(ctx, b, k, depth, a.nprobe, a.probe_ids, a.probe_dist);
+      }
       void* ord;
       VDBGPU_RETURN_IF_ERROR(ctx.workspace(kWsScratch3, (b.nq + nlist_ + 1) * sizeof(uint32_t), &ord));
       uint32_t* counts = static_cast<uint32_t*>(ord) + b.nq;
@@ -172,6 +405,12 @@ class IvfPqGpuIndex final : public GpuIndex {
   uint32_t nlist_ = 0, m_ = 0, dsub_ = 0;
   DeviceBuffer rows_, coarse_, cents_, term2_, off_, ids_, codes_;
   std::unique_ptr<GpuIndex> coarse_index_;
+  // List mode (tensor-core pre-rank).
+  bool list_mode_ = false;
+  uint32_t kpad_ = 0;
+  int resid_scale_log2_ = 0;
+  DeviceBuffer poff_, resid_, resid_term_;
+  CUtensorMap resid_map_;
 };
 
 }  // namespace

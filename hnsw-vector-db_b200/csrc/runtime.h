@@ -193,6 +193,15 @@ enum WorkspaceSlot : int {
   kWsGroupQueries,
   kWsGroupOutDist,
   kWsGroupOutRow,
+  kWsIvfA,
+  kWsIvfQScale,
+  kWsIvfTiles,
+  kWsIvfSlotQuery,
+  kWsIvfSlotOffset,
+  kWsIvfPairSlot,
+  kWsIvfUnits,
+  kWsIvfAg,
+  kWsIvfQScaleG,
 };
 
 enum IndexKind : int {

@@ -58,8 +58,17 @@ struct __align__(8) ScanBarriers {
 // Units are ordered slice-major: the CTAs running at the same time cover one or two row slices
 // for every query tile, so each slice is read from HBM about once and served from L2, and the
 // later slices of a query start from the threshold its earlier slices published.
+template <int kMode>
 __device__ __forceinline__ void unit_rows(const ScanArgs& a, int unit, int* qtile, int* r0,
                                           int* r1) {
+  if constexpr (kMode == kKeyList) {
+    // List mode: unit u is query tile u against its own row range.
+    const int2 u = a.unit_rows[unit];
+    *qtile = unit;
+    *r0 = u.x;
+    *r1 = u.y;
+    return;
+  }
   const int qtiles = a.nunits / a.units_per_qtile;
   const int part = unit / qtiles;
   *qtile = unit - part * qtiles;
@@ -171,7 +180,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       bool first = true;
       for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
         int qtile, r0, r1;
-        unit_rows(a, unit, &qtile, &r0, &r1);
+        unit_rows<kMode>(a, unit, &qtile, &r0, &r1);
         if (!first) {
           if (!mbar_wait(&bars->a_empty, a_phase, a.status, kDevTimeoutEmpty)) break;
           a_phase ^= 1u;
@@ -218,7 +227,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       const uint32_t a_base = smem_u32(smem_a), b_base = smem_u32(smem_b);
       for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
         int qtile, r0, r1;
-        unit_rows(a, unit, &qtile, &r0, &r1);
+        unit_rows<kMode>(a, unit, &qtile, &r0, &r1);
         if (!mbar_wait(&bars->a_full, a_phase, a.status, kDevTimeoutFull)) break;
         a_phase ^= 1u;
         tc_fence_after();
@@ -278,9 +287,16 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
     bool ok = true;
     for (int unit = blockIdx.x; ok && unit < a.nunits; unit += gridDim.x) {
       int qtile, r0, r1;
-      unit_rows(a, unit, &qtile, &r0, &r1);
+      unit_rows<kMode>(a, unit, &qtile, &r0, &r1);
+      // q: the query's operand row (list mode: a slot of the gathered tiles, serving query qid).
       const int q = qtile * kScanBM + row_in_tile;
-      const bool valid_q = q < a.nq;
+      uint32_t qid = static_cast<uint32_t>(q);
+      float qoff = 0.f;
+      if constexpr (kMode == kKeyList) {
+        qid = q < a.nq ? a.slot_query[q] : 0xFFFFFFFFu;
+        if (qid != 0xFFFFFFFFu) qoff = a.slot_offset[q];
+      }
+      const bool valid_q = kMode == kKeyList ? qid != 0xFFFFFFFFu : q < a.nq;
       // key = qs * acc (+ row term); qs is minus a power of two, so key < tau <=> acc > tau / qs
       // holds exactly and the scaled-key fast path compares raw accumulators.
       const float qs = valid_q ? a.qscale[q] : -1.f;
@@ -289,7 +305,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       // A bound present before the unit starts (a seeded estimate, or the C-th key another
       // slice of this query published) applies from the first row on.
       if (valid_q) {
-        const uint32_t g0 = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
+        const uint32_t g0 = *reinterpret_cast<volatile uint32_t*>(&a.qtau[qid]);
         if (g0 != 0xFFFFFFFFu) tau = key_float(g0);
       }
       float tau_acc = tau * qs_inv;
@@ -317,7 +333,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
             tau = fminf(tau, key_float(kth));
             tau_acc = tau * qs_inv;
             // Other units of this query may drop keys above the keep-th key of this one.
-            atomicMin(&a.qtau[q], kth + 1u);
+            atomicMin(&a.qtau[qid], kth + 1u);
           }
         }
       };
@@ -325,7 +341,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
       // Scores of one chunk of 32 accumulator columns starting at row c0, in place: raw
       // accumulators (larger is closer, scaled-key mode) or keys (smaller is closer, row-term
       // mode); masked columns get the worst score.
-      constexpr bool kMin = kMode == kKeyRowTerm;
+      constexpr bool kMin = kMode != kKeyScaled;
       auto better = [](float x, float y) { return kMin ? fminf(x, y) : fmaxf(x, y); };
       auto scores = [&](uint32_t (&v)[32], int c0) {
         uint32_t allow_bits = 0xFFFFFFFFu;
@@ -342,6 +358,18 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
             v[4 * j + 1] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 1]), x.y));
             v[4 * j + 2] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 2]), x.z));
             v[4 * j + 3] = __float_as_uint(fmaf(qs, __uint_as_float(v[4 * j + 3]), x.w));
+          }
+        } else if constexpr (kMode == kKeyList) {
+          // The row term plus the query's per-list offset (rows of a list start on 32-row
+          // boundaries, so the row terms load in 16-byte steps).
+          const float4* rt4 = reinterpret_cast<const float4*>(a.rowterm + c0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = __ldg(&rt4[j]);
+            v[4 * j + 0] = __float_as_uint(__fadd_rn(fmaf(qs, __uint_as_float(v[4 * j + 0]), x.x), qoff));
+            v[4 * j + 1] = __float_as_uint(__fadd_rn(fmaf(qs, __uint_as_float(v[4 * j + 1]), x.y), qoff));
+            v[4 * j + 2] = __float_as_uint(__fadd_rn(fmaf(qs, __uint_as_float(v[4 * j + 2]), x.z), qoff));
+            v[4 * j + 3] = __float_as_uint(__fadd_rn(fmaf(qs, __uint_as_float(v[4 * j + 3]), x.w), qoff));
           }
         }
         if (!full) {
@@ -396,7 +424,7 @@ __global__ void __launch_bounds__(ScanThreads(kWgs), 1)
         const int accb = static_cast<int>(tcount & 1u);
         // The shared threshold is read now and applied after pass 1 (hides latency).
         uint32_t g = 0xFFFFFFFFu;
-        if (valid_q) g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[q]);
+        if (valid_q) g = *reinterpret_cast<volatile uint32_t*>(&a.qtau[qid]);
         if (!mbar_wait(&bars->acc_full[accb], (tcount >> 1) & 1u, a.status, kDevTimeoutAcc)) {
           ok = false;
           break;
@@ -537,6 +565,13 @@ cudaError_t LaunchScanT(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, co
 
 cudaError_t LaunchScan(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const ScanArgs& a,
                        int grid, cudaStream_t stream) {
+  if (a.mode == kKeyList) {
+    if (a.unit_rows == nullptr || a.slot_query == nullptr || a.slot_offset == nullptr || a.rowterm == nullptr ||
+        a.allow != nullptr || a.chunk_best != 0)
+      return cudaErrorInvalidValue;
+    return a.wgs == 2 ? LaunchScanT<kKeyList, 2>(tmap_a, tmap_b, a, grid, stream)
+                      : LaunchScanT<kKeyList, 1>(tmap_a, tmap_b, a, grid, stream);
+  }
   if (a.mode == kKeyRowTerm)
     return a.wgs == 2 ? LaunchScanT<kKeyRowTerm, 2>(tmap_a, tmap_b, a, grid, stream)
                       : LaunchScanT<kKeyRowTerm, 1>(tmap_a, tmap_b, a, grid, stream);

@@ -23,8 +23,12 @@ constexpr int ScanThreads(int wgs) { return 64 + 128 * wgs; }
 // Key transform applied to the fp32 accumulator acc = sum_i A[q,i] * B[r,i]:
 //   kKeyScaled:  key = qscale[q] * acc
 //   kKeyRowTerm: key = fma(qscale[q], acc, rowterm[r])
+//   kKeyList:    key = fma(qscale[s], acc, rowterm[r]) + slot_offset[s], list mode: unit u is
+//                query tile u (operand rows s = 128 u + i, serving query slot_query[s]) against
+//                rows unit_rows[u] = [x, y), x a multiple of 32 (IVF lists, each query tile
+//                gathered from the queries probing one list)
 // Smaller key = closer. Keys of one query are comparable across rows and units.
-enum ScanKeyMode : int { kKeyScaled = 0, kKeyRowTerm = 1 };
+enum ScanKeyMode : int { kKeyScaled = 0, kKeyRowTerm = 1, kKeyList = 2 };
 
 struct ScanArgs {
   int nq;               // valid queries
@@ -50,6 +54,10 @@ struct ScanArgs {
   unsigned long long* counters;  // optional: chunks, triggered chunks, inserts, compactions
   uint32_t* qtau;       // [nq] shared per-query threshold (ordered-key space), 0xFFFFFFFF = none
   int* status;          // device status word
+  // List mode (kKeyList) only.
+  const int2* unit_rows;       // [nunits] row range of each unit
+  const uint32_t* slot_query;  // [nq] query served by each operand row (0xFFFFFFFF: none)
+  const float* slot_offset;    // [nq] key offset of each operand row
 };
 
 // Launches the scan on `stream`. tmap_a: queries operand [qpad x kpad] K-major, box {64, 128};

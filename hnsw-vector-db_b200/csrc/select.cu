@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "ivfpq.cuh"
 #include "kernels.cuh"
 #include "scan_mma.cuh"
 #include "warp_ops.cuh"
@@ -420,6 +421,249 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   }
 }
 
+// ------------------------------------------------------------------ IVF-PQ exact stage (list mode)
+
+constexpr int kIvfFinWarps = 4;
+
+// L2SqAny(q - c, b) over d elements with the residual formed on the fly: l2_any's arithmetic on
+// the values the reference stores first (r = q - c, src/index/quant/ivf_pq.cc:206-208).
+__device__ __forceinline__ float l2_any_resid(const float* q, const float* c, const float* b, int d) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= d; i += 4) {
+    const float t0 = __fsub_rn(__fsub_rn(q[i], c[i]), b[i]);
+    const float t1 = __fsub_rn(__fsub_rn(q[i + 1], c[i + 1]), b[i + 1]);
+    const float t2 = __fsub_rn(__fsub_rn(q[i + 2], c[i + 2]), b[i + 2]);
+    const float t3 = __fsub_rn(__fsub_rn(q[i + 3], c[i + 3]), b[i + 3]);
+    s0 = __fadd_rn(s0, __fmul_rn(t0, t0));
+    s1 = __fadd_rn(s1, __fmul_rn(t1, t1));
+    s2 = __fadd_rn(s2, __fmul_rn(t2, t2));
+    s3 = __fadd_rn(s3, __fmul_rn(t3, t3));
+  }
+  for (; i < d; ++i) {
+    const float t = __fsub_rn(__fsub_rn(q[i], c[i]), b[i]);
+    s0 = __fadd_rn(s0, __fmul_rn(t, t));
+  }
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+__global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const IvfFinalizeArgs a) {
+  extern __shared__ __align__(16) uint8_t ivsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pd = a.pd;
+  uint8_t* wbase = ivsm + warp * (pd * sizeof(float) + kMaxSurvivors * sizeof(uint64_t));
+  float* q_s = reinterpret_cast<float*>(wbase);
+  uint64_t* surv = reinterpret_cast<uint64_t*>(wbase + pd * sizeof(float));
+  const int q = static_cast<int>(blockIdx.x) * kIvfFinWarps + warp;
+  if (q >= a.nq) return;
+  for (int i = lane; i < pd; i += 32) q_s[i] = a.queries[static_cast<size_t>(q) * pd + i];
+  const uint32_t thr = a.qtau[q];
+  const uint32_t lt = (1u << lane) - 1u;
+  __syncwarp();
+
+  // 1. The entries below the bound: lane j reads list j (probe j / wgs, epilogue warpgroup
+  // j % wgs of the probe's tile), eight entries at a time; each entry is offered as (ordered
+  // pre-rank key, probe << 24 | row within the list). walk(f) calls f(key, tag, valid) in lockstep
+  // over the warp.
+  const int lists = a.nprobe * a.wgs;
+  uint32_t scanned = 0;  // rows of the probed lists
+  auto walk = [&](auto&& f, bool count_rows) {
+    for (int j0 = 0; j0 < lists; j0 += 32) {
+      const int j = j0 + lane;
+      int cnt = 0;
+      const uint4* lp = nullptr;
+      uint32_t p = 0;
+      uint64_t pb = 0;
+      if (j < lists) {
+        p = static_cast<uint32_t>(j / a.wgs);
+        const int wg = j % a.wgs;
+        const size_t pair = static_cast<size_t>(q) * a.nprobe + p;
+        const uint32_t l = a.probe_ids[pair];
+        const uint32_t slot = a.pair_slot[pair];
+        const size_t cs = (static_cast<size_t>(slot / 128) * a.wgs + wg) * 128 + slot % 128;
+        cnt = a.cand_count[cs];
+        lp = reinterpret_cast<const uint4*>(a.cand + cs * kScanCap);
+        pb = a.poff[l];
+        if (count_rows && wg == 0) scanned += static_cast<uint32_t>(a.list_off[l + 1] - a.list_off[l]);
+      }
+      const int maxc = static_cast<int>(__reduce_max_sync(0xFFFFFFFFu, static_cast<uint32_t>(cnt)));
+      for (int e0 = 0; e0 < maxc; e0 += 8) {
+        uint4 w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) w[u] = e0 + 2 * u < cnt ? __ldg(&lp[(e0 >> 1) + u]) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          f(float_key(__uint_as_float(w[u].x)), (p << 24) | static_cast<uint32_t>(w[u].y - pb), e0 + 2 * u < cnt);
+          f(float_key(__uint_as_float(w[u].z)), (p << 24) | static_cast<uint32_t>(w[u].w - pb), e0 + 2 * u + 1 < cnt);
+        }
+      }
+    }
+  };
+  int nsurv = 0;
+  auto file = [&](uint32_t key, uint32_t tag, bool valid) {
+    const bool pass = valid && key < thr;
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, pass);
+    const int pos = nsurv + __popc(m & lt);
+    if (pass && pos < kMaxSurvivors) surv[pos] = (static_cast<uint64_t>(key) << 32) | tag;
+    nsurv += __popc(m);
+  };
+  walk(file, true);
+  scanned = __reduce_add_sync(0xFFFFFFFFu, scanned);
+  __syncwarp();
+  if (nsurv > kMaxSurvivors) {
+    // More entries below the bound than shared memory holds: the cpre-th (key, tag) over the
+    // lists by a radix select on the key (8-bit digits, a per-warp histogram in the survivors'
+    // last 1 KB) and, when the entries at that key do not all fit, a search on the tag; then
+    // exactly the cpre entries at or below it are gathered.
+    uint32_t* hist = reinterpret_cast<uint32_t*>(surv + kMaxSurvivors - 128);
+    uint32_t prefix = 0, mask = 0, at_k = 0;
+    int r = a.cpre;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll
+      for (int bb = 0; bb < 8; ++bb) hist[lane * 8 + bb] = 0;
+      __syncwarp();
+      walk([&](uint32_t key, uint32_t, bool valid) {
+        if (valid && key < thr && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }, false);
+      __syncwarp();
+      uint32_t h[8], tot = 0;
+#pragma unroll
+      for (int bb = 0; bb < 8; ++bb) {
+        h[bb] = hist[lane * 8 + bb];
+        tot += h[bb];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const uint32_t excl = incl - tot;
+      const uint32_t owner =
+          __ballot_sync(0xFFFFFFFFu, excl < static_cast<uint32_t>(r) && static_cast<uint32_t>(r) <= incl);
+      const int src = __ffs(owner) - 1;
+      uint32_t digit = 0, before = 0, cnt = 0;
+      if (lane == src) {
+        uint32_t run = excl;
+#pragma unroll
+        for (int bb = 0; bb < 8; ++bb) {
+          if (cnt == 0 && static_cast<uint32_t>(r) <= run + h[bb]) {
+            digit = static_cast<uint32_t>(lane * 8 + bb);
+            before = run;
+            cnt = h[bb];
+          }
+          run += h[bb];
+        }
+      }
+      digit = __shfl_sync(0xFFFFFFFFu, digit, src);
+      before = __shfl_sync(0xFFFFFFFFu, before, src);
+      at_k = __shfl_sync(0xFFFFFFFFu, cnt, src);
+      r -= static_cast<int>(before);
+      prefix |= digit << shift;
+      mask |= 255u << shift;
+      __syncwarp();
+    }
+    uint32_t tag_cut = 0xFFFFFFFFu;
+    if (static_cast<uint32_t>(r) != at_k) {
+      tag_cut = 0;
+      for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = tag_cut | (1u << bit);
+        int c = 0;
+        walk([&](uint32_t key, uint32_t tag, bool valid) { c += (valid && key == prefix && tag < cand) ? 1 : 0; },
+             false);
+        if (__reduce_add_sync(0xFFFFFFFFu, static_cast<uint32_t>(c)) < static_cast<uint32_t>(r)) tag_cut = cand;
+      }
+    }
+    const uint64_t kth = (static_cast<uint64_t>(prefix) << 32) | tag_cut;
+    nsurv = 0;
+    walk([&](uint32_t key, uint32_t tag, bool valid) {
+      file(key, tag, valid && ((static_cast<uint64_t>(key) << 32) | tag) <= kth);
+    }, false);
+    __syncwarp();
+  }
+  int ncand = nsurv < a.cpre ? nsurv : a.cpre;
+  if (nsurv > a.cpre) keep_smallest(surv, nsurv, a.cpre);
+
+  // 2. The reference's ADC of each candidate (one lane per candidate): its table entries
+  // term2 + 2 * (-<q_j, C_j[c]>) (precomputed) or L2SqAny(q_j - c_j, C_j[c]) (residual), summed in
+  // four partial sums, plus the coarse distance.
+  const int m = a.m, ds = a.dsub;
+  const size_t ts = static_cast<size_t>(m) * 256;
+  for (int i = lane; i < ncand; i += 32) {
+    const uint32_t tag = static_cast<uint32_t>(surv[i]);
+    const uint32_t p = tag >> 24;
+    const size_t pair = static_cast<size_t>(q) * a.nprobe + p;
+    const uint32_t l = a.probe_ids[pair];
+    const uint64_t pos = a.list_off[l] + (tag & 0xFFFFFFu);
+    const uint8_t* code = a.codes + pos * m;
+    const float* t2 = a.term2 + l * ts;
+    const float* cl = a.coarse + static_cast<size_t>(l) * pd;
+    auto entry = [&](int j) {
+      const int c = code[j];
+      const float* cen = a.centroids + (static_cast<size_t>(j) * 256 + c) * ds;
+      if (a.mode == kIvfPrecomputed)
+        return __fadd_rn(__ldg(&t2[j * 256 + c]), __fmul_rn(-dot_any(q_s + j * ds, cen, ds), 2.f));
+      return l2_any_resid(q_s + j * ds, cl + j * ds, cen, ds);
+    };
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int j = 0;
+    for (; j + 4 <= m; j += 4) {
+      s0 = __fadd_rn(s0, entry(j));
+      s1 = __fadd_rn(s1, entry(j + 1));
+      s2 = __fadd_rn(s2, entry(j + 2));
+      s3 = __fadd_rn(s3, entry(j + 3));
+    }
+    for (; j < m; ++j) s0 = __fadd_rn(s0, entry(j));
+    const float d = __fadd_rn(a.probe_dist[pair], __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+    surv[i] = pack_neighbor(d, __ldg(&a.ids[pos]));
+  }
+  __syncwarp();
+  // 3. TopK(R) by (dist, id), then the re-rank on fp32 rows (exact, reference kernel-set order).
+  sort_small(surv, ncand);
+  const int R = a.depth > a.k ? a.depth : a.k;
+  ncand = ncand < R ? ncand : R;
+  uint32_t dc = static_cast<uint32_t>(a.nlist) + scanned;
+  if (a.depth > 0) {
+    for (int i = 0; i < ncand; i += 4) {
+      uint32_t r[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) r[c] = neighbor_id(surv[i + c < ncand ? i + c : i]);
+      float d[4];
+      if (a.order == kOrderAvx512 && pd <= 8 * 32 + 16) {
+        warp_exact_dist4_avx512<8>(q_s, a.rows, r, ncand - i, pd, true, d);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) d[c] = warp_exact_dist(q_s, a.rows + static_cast<size_t>(r[c]) * pd, pd, true, a.order);
+      }
+      __syncwarp();
+      if (lane < 4 && i + lane < ncand) {
+        float dl = d[0];
+        uint32_t rl = r[0];
+#pragma unroll
+        for (int c = 1; c < 4; ++c) {
+          dl = lane == c ? d[c] : dl;
+          rl = lane == c ? r[c] : rl;
+        }
+        surv[i + lane] = pack_neighbor(dl, rl);
+      }
+      __syncwarp();
+    }
+    sort_small(surv, ncand);
+    dc += static_cast<uint32_t>(ncand);
+  }
+  for (int i = lane; i < a.k; i += 32) {
+    const size_t o = static_cast<size_t>(q) * a.k + i;
+    if (i < ncand) {
+      a.out_dist[o] = neighbor_dist(surv[i]);
+      a.out_row[o] = neighbor_id(surv[i]);
+    } else {
+      a.out_dist[o] = INFINITY;
+      a.out_row[o] = UINT32_MAX;
+    }
+  }
+  if (lane == 0 && a.out_dc != nullptr) a.out_dc[q] = dc;
+}
+
 // ------------------------------------------------------------------ seeded scans
 
 // One warp per query: the m-th smallest ordered key over the query's lists. Keys at or above the
@@ -658,6 +902,19 @@ cudaError_t LaunchFinalize(const FinalizeArgs& a, cudaStream_t stream) {
   const int blocks = (a.nq + kFinWarps - 1) / kFinWarps;
   NoteLaunch();
   finalize_kernel<<<blocks, kFinWarps * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t LaunchIvfFinalize(const IvfFinalizeArgs& a, cudaStream_t stream) {
+  if (a.nq <= 0) return cudaSuccess;
+  if (a.cpre > 256 || a.k > 256 || a.depth > 256 || a.nprobe > 128 || a.pd > 8 * 32 + 16)
+    return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(kIvfFinWarps) * (a.pd * sizeof(float) + kMaxSurvivors * sizeof(uint64_t));
+  cudaError_t e = cudaFuncSetAttribute(ivf_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  NoteLaunch();
+  ivf_finalize_kernel<<<(a.nq + kIvfFinWarps - 1) / kIvfFinWarps, kIvfFinWarps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
