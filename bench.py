@@ -948,6 +948,7 @@ def run_c2(args):
     for _ in range(3):
         step()
         st += np.array(ctx.stage_times()[:3])
+    fc = ctx.stage_counters()
     ctx.set_timing(False)
     st /= 3
     # End to end through the C ABI from pinned host buffers.
@@ -1006,6 +1007,9 @@ def run_c2(args):
                    "d2h_bytes_per_step": nq * K * 8},
            "stage_ms": {"nearest_list_pass": float(st[0]), "probed_lists_scan": float(st[1]),
                         "exact_stage": float(st[2])},
+           "exact_stage_per_query": {"entries_below_bound": fc[0] / nq, "radix_cut_fraction": fc[1] / nq,
+                                     "warp_cycles_gather": fc[2] / nq, "warp_cycles_adc": fc[3] / nq,
+                                     "warp_cycles_topk_rerank": fc[4] / nq} if len(fc) >= 5 else None,
            "gpu_launches": int(launches_per_step) * args.steps,
            "recall_at_10_vs_exact": _recall(gpu_ids, gt),
            "identical_ids_vs_reference_same_index": float(np.mean(np.all(gpu_ids[:sample] == r_ids, axis=1))),

@@ -32,6 +32,16 @@ bool TensorEnabled() {
   return v == nullptr || *v == 0 || std::strcmp(v, "0") != 0;
 }
 
+// The first list-mode pass covers at most the first SeedRows(cpre) rows of each query's nearest
+// list (VDB_IVF_SEED_ROWS; 0 = the whole list). Its cpre-th key there bounds the query: at least
+// cpre rows of a probed list lie below it, so the bound is exact, only looser than the whole
+// list's.
+uint32_t SeedRows(int cpre) {
+  const char* v = std::getenv("VDB_IVF_SEED_ROWS");
+  if (v != nullptr && *v != 0) return static_cast<uint32_t>(std::strtoul(v, nullptr, 10));
+  return static_cast<uint32_t>(4 * cpre);
+}
+
 // Batches of at least this many queries (no filter, L2) take the tensor-core pre-rank.
 constexpr uint64_t kIvfTensorMinQueries = 512;
 
@@ -161,8 +171,8 @@ class IvfPqGpuIndex final : public GpuIndex {
   // One list-mode scan over the pairs (query, probe < np): tiles, gathered query operand, scan.
   // Returns the tile count.
   Status ListScan(Context& ctx, const SearchBatch& b, const void* a_op, const float* qscale, const uint32_t* pid,
-                  const float* pdist, int nprobe, int np, int cpre, uint32_t* qtau, uint32_t* pair_slot,
-                  uint32_t* ntiles) {
+                  const float* pdist, int nprobe, int np, uint32_t row_cap, int cpre, uint32_t* qtau,
+                  uint32_t* pair_slot, uint32_t* ntiles) {
     const uint64_t nq = b.nq;
     const uint64_t max_tiles = nq * static_cast<uint64_t>(np) / 128 + nlist_;
     void *tiles, *sq, *so, *units, *ag, *qg, *cand, *cnt;
@@ -189,6 +199,7 @@ class IvfPqGpuIndex final : public GpuIndex {
     ta.slot_offset = static_cast<float*>(so);
     ta.pair_slot = pair_slot;
     ta.unit_rows = static_cast<int2*>(units);
+    ta.row_cap = row_cap;
     VDBGPU_CUDA(LaunchIvfTiles(ta, counts, ctx.stream()));
     uint32_t nt = 0;
     VDBGPU_CUDA(cudaMemcpyAsync(&nt, tstart + nlist_, 4, cudaMemcpyDeviceToHost, ctx.stream()));
@@ -265,10 +276,10 @@ class IvfPqGpuIndex final : public GpuIndex {
     VDBGPU_CUDA(LaunchPrepQueries(pa, ctx.stream()));
     VDBGPU_CUDA(cudaMemsetAsync(qtau, 0xFF, nq * 4, ctx.stream()));
     uint32_t nt = 0;
-    VDBGPU_RETURN_IF_ERROR(ListScan(ctx, b, a_op, static_cast<const float*>(qscale), pid, pdist, nprobe, 1, cpre,
-                                    static_cast<uint32_t*>(qtau), nullptr, &nt));
+    VDBGPU_RETURN_IF_ERROR(ListScan(ctx, b, a_op, static_cast<const float*>(qscale), pid, pdist, nprobe, 1,
+                                    SeedRows(cpre), cpre, static_cast<uint32_t*>(qtau), nullptr, &nt));
     ctx.Mark(1);
-    VDBGPU_RETURN_IF_ERROR(ListScan(ctx, b, a_op, static_cast<const float*>(qscale), pid, pdist, nprobe, nprobe,
+    VDBGPU_RETURN_IF_ERROR(ListScan(ctx, b, a_op, static_cast<const float*>(qscale), pid, pdist, nprobe, nprobe, 0,
                                     cpre, static_cast<uint32_t*>(qtau), static_cast<uint32_t*>(ps), &nt));
     ctx.Mark(2);
     void *cand, *cnt;
@@ -306,6 +317,9 @@ class IvfPqGpuIndex final : public GpuIndex {
     fa.out_dist = b.out_dist;
     fa.out_row = b.out_row;
     fa.out_dc = b.dist_comps;
+    fa.counters = ctx.timing() ? ctx.counters() : nullptr;
+    if (fa.counters != nullptr)
+      VDBGPU_CUDA(cudaMemsetAsync(fa.counters, 0, 8 * sizeof(unsigned long long), ctx.stream()));
     VDBGPU_CUDA(LaunchIvfFinalize(fa, ctx.stream()));
     ctx.Mark(3);
     return Status::OK();

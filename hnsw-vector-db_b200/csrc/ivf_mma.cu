@@ -101,7 +101,9 @@ __global__ void ivf_place_kernel(const IvfTileArgs a) {
   if (a.pair_slot != nullptr) a.pair_slot[pair] = slot;
   if (r % 128 == 0) {
     const uint64_t b = a.poff[l];
-    a.unit_rows[tile] = make_int2(static_cast<int>(b), static_cast<int>(b + (a.list_off[l + 1] - a.list_off[l])));
+    uint64_t size = a.list_off[l + 1] - a.list_off[l];
+    if (a.row_cap != 0 && size > a.row_cap) size = a.row_cap;
+    a.unit_rows[tile] = make_int2(static_cast<int>(b), static_cast<int>(b + size));
   }
 }
 

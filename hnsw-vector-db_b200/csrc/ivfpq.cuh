@@ -86,6 +86,7 @@ struct IvfTileArgs {
   float* slot_offset;
   uint32_t* pair_slot;        // nq x nprobe, or null
   int2* unit_rows;
+  uint32_t row_cap;           // a tile covers at most its list's first row_cap rows (0: all)
 };
 // counts: nlist words of scratch. Tiles number at most nq * np / 128 + nlist.
 cudaError_t LaunchIvfTiles(const IvfTileArgs& a, uint32_t* counts, cudaStream_t st);
@@ -96,9 +97,9 @@ cudaError_t LaunchIvfGather(const void* operand, const float* qscale, const uint
 // The exact stage after the list-mode scan, one warp per query: the entries of the query's
 // nprobe x wgs candidate lists below its bound, the cpre best of them by pre-rank key, their
 // reference ADC distances (precomputed or residual L2 tables, four partial sums, plus the coarse
-// distance), TopK(R = max(depth, k)) by (dist, id), the re-rank on fp32 rows when depth > 0, and
-// the k best. Entries below the bound beyond shared memory's room are cut to the cpre best by a
-// radix select over the lists.
+// distance with the precomputed ones), TopK(R = max(depth, k)) by (dist, id), the re-rank on fp32
+// rows when depth > 0, and the k best. Entries below the bound beyond shared memory's room are
+// cut to the cpre best by a radix select over the lists.
 struct IvfFinalizeArgs {
   int nq, nprobe, pd, dim, m, dsub, k, depth, cpre, order, mode, wgs;
   uint64_t nlist;
@@ -120,6 +121,9 @@ struct IvfFinalizeArgs {
   float* out_dist;
   uint32_t* out_row;
   uint64_t* out_dc;
+  // Optional (stage timing): [0] entries below the bounds, [1] queries cut by the radix select,
+  // [2..4] warp cycles in the gather / ADC / TopK and re-rank, summed over queries.
+  unsigned long long* counters;
 };
 cudaError_t LaunchIvfFinalize(const IvfFinalizeArgs& a, cudaStream_t st);
 

@@ -460,6 +460,13 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
   const uint32_t thr = a.qtau[q];
   const uint32_t lt = (1u << lane) - 1u;
   __syncwarp();
+  long long t_mark = clock64();
+  auto stage = [&](int i) {
+    if (a.counters == nullptr) return;
+    const long long t = clock64();
+    if (lane == 0) atomicAdd(&a.counters[i], static_cast<unsigned long long>(t - t_mark));
+    t_mark = t;
+  };
 
   // 1. The entries below the bound: lane j reads list j (probe j / wgs, epilogue warpgroup
   // j % wgs of the probe's tile), eight entries at a time; each entry is offered as (ordered
@@ -510,6 +517,10 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
   walk(file, true);
   scanned = __reduce_add_sync(0xFFFFFFFFu, scanned);
   __syncwarp();
+  if (a.counters != nullptr && lane == 0) {
+    atomicAdd(&a.counters[0], static_cast<unsigned long long>(nsurv));
+    if (nsurv > kMaxSurvivors) atomicAdd(&a.counters[1], 1ull);
+  }
   if (nsurv > kMaxSurvivors) {
     // More entries below the bound than shared memory holds: the cpre-th (key, tag) over the
     // lists by a radix select on the key (8-bit digits, a per-warp histogram in the survivors'
@@ -584,11 +595,14 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
   int ncand = nsurv < a.cpre ? nsurv : a.cpre;
   if (nsurv > a.cpre) keep_smallest(surv, nsurv, a.cpre);
 
+  stage(2);
   // 2. The reference's ADC of each candidate (one lane per candidate): its table entries
   // term2 + 2 * (-<q_j, C_j[c]>) (precomputed) or L2SqAny(q_j - c_j, C_j[c]) (residual), summed in
-  // four partial sums, plus the coarse distance.
+  // four partial sums, plus the coarse distance (precomputed tables).
   const int m = a.m, ds = a.dsub;
   const size_t ts = static_cast<size_t>(m) * 256;
+  const bool fast_adc = a.mode == kIvfPrecomputed && ds == 2 && m % 16 == 0 && m <= 64 &&
+                        (reinterpret_cast<uintptr_t>(a.codes) & 15u) == 0;
   for (int i = lane; i < ncand; i += 32) {
     const uint32_t tag = static_cast<uint32_t>(surv[i]);
     const uint32_t p = tag >> 24;
@@ -596,7 +610,7 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
     const uint32_t l = a.probe_ids[pair];
     const uint64_t pos = a.list_off[l] + (tag & 0xFFFFFFu);
     const uint8_t* code = a.codes + pos * m;
-    const float* t2 = a.term2 + l * ts;
+    const float* t2 = a.mode == kIvfPrecomputed ? a.term2 + l * ts : nullptr;
     const float* cl = a.coarse + static_cast<size_t>(l) * pd;
     auto entry = [&](int j) {
       const int c = code[j];
@@ -605,19 +619,60 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
         return __fadd_rn(__ldg(&t2[j * 256 + c]), __fmul_rn(-dot_any(q_s + j * ds, cen, ds), 2.f));
       return l2_any_resid(q_s + j * ds, cl + j * ds, cen, ds);
     };
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int j = 0;
-    for (; j + 4 <= m; j += 4) {
-      s0 = __fadd_rn(s0, entry(j));
-      s1 = __fadd_rn(s1, entry(j + 1));
-      s2 = __fadd_rn(s2, entry(j + 2));
-      s3 = __fadd_rn(s3, entry(j + 3));
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    if (fast_adc) {
+      // The code in registers (16-byte loads), then per chunk of 8 sub-quantizers every term2
+      // entry and centroid pair requested before any is used; entries are added to the partial
+      // sums in ascending j, as the reference's loop does.
+      uint32_t w[16];
+      const uint4* cp = reinterpret_cast<const uint4*>(code);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint4 v = t * 16 < m ? __ldg(&cp[t]) : make_uint4(0, 0, 0, 0);
+        w[4 * t] = v.x;
+        w[4 * t + 1] = v.y;
+        w[4 * t + 2] = v.z;
+        w[4 * t + 3] = v.w;
+      }
+      const float2* cen2 = reinterpret_cast<const float2*>(a.centroids);
+#pragma unroll
+      for (int j0 = 0; j0 < 64; j0 += 8) {
+        if (j0 < m) {
+          float tv[8];
+          float2 cv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int j = j0 + u;
+            const uint32_t c = (w[j >> 2] >> (8 * (j & 3))) & 255u;
+            tv[u] = __ldg(&t2[j * 256 + c]);
+            cv[u] = __ldg(&cen2[j * 256 + c]);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int j = j0 + u;
+            const float dq = dot_any(q_s + 2 * j, reinterpret_cast<const float*>(&cv[u]), 2);
+            s[j & 3] = __fadd_rn(s[j & 3], __fadd_rn(tv[u], __fmul_rn(-dq, 2.f)));
+          }
+        }
+      }
+    } else {
+      int j = 0;
+      for (; j + 4 <= m; j += 4) {
+        s[0] = __fadd_rn(s[0], entry(j));
+        s[1] = __fadd_rn(s[1], entry(j + 1));
+        s[2] = __fadd_rn(s[2], entry(j + 2));
+        s[3] = __fadd_rn(s[3], entry(j + 3));
+      }
+      for (; j < m; ++j) s[0] = __fadd_rn(s[0], entry(j));
     }
-    for (; j < m; ++j) s0 = __fadd_rn(s0, entry(j));
-    const float d = __fadd_rn(a.probe_dist[pair], __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+    // The coarse distance is the offset of the precomputed tables only (the residual tables
+    // already measure from the query).
+    const float off = a.mode == kIvfPrecomputed ? a.probe_dist[pair] : 0.f;
+    const float d = __fadd_rn(off, __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3])));
     surv[i] = pack_neighbor(d, __ldg(&a.ids[pos]));
   }
   __syncwarp();
+  stage(3);
   // 3. TopK(R) by (dist, id), then the re-rank on fp32 rows (exact, reference kernel-set order).
   sort_small(surv, ncand);
   const int R = a.depth > a.k ? a.depth : a.k;
@@ -662,6 +717,7 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
     }
   }
   if (lane == 0 && a.out_dc != nullptr) a.out_dc[q] = dc;
+  stage(4);
 }
 
 // ------------------------------------------------------------------ seeded scans
