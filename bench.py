@@ -970,6 +970,7 @@ def run_c2(args):
     scanned = float(dc.mean()) - C2_NLIST - DEPTH
     bytes_per_q = scanned * (C2_M + 4) + C2_NPROBE * C2_M * 1024 + DEPTH * C2_DIM * 4
     achieved = bytes_per_q * nq / (ms / 1000.0) / 1e9
+    tflops = 2.0 * C2_DIM * scanned * nq / (max(float(st[1]), 1e-6) / 1000.0) / 1e12
     # Exact ground truth on the GPU (flat index over the same rows).
     flat = vdb_b200.Index.create(ctx, "flat", "l2", b_dev, C2_DIM)
     gt_ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
@@ -997,12 +998,18 @@ def run_c2(args):
                       "rows": n_rows, "dim": C2_DIM, "batch": nq, "k": K,
                       "nlist": C2_NLIST, "pq_m": C2_M, "nprobe": C2_NPROBE, "rerank": DEPTH,
                       "l2": "inputs larger than L2: 520 MB of codes and ids + 3.8 GB rows"},
-           "roofline": {"bound": "hbm", "kernel": "ivfpq_kernel", "achieved": achieved, "peak": hbm,
-                        "unit": "GB/s", "frac": achieved / hbm, "peak_kind": f"{src} copy bandwidth",
-                        "traffic": None,
-                        "algorithmic": f"scanned x (m + 4) + nprobe x m x 1 KB + 100 x pd x 4 B per query, "
-                                       f"scanned = {scanned:.0f} codes (mean), over the whole step "
-                                       f"(coarse probe included)"},
+           # The dominant kernel is the list-mode scan of the probed lists (tensor-core pre-rank):
+           # 2 x d FLOP per (query, probed row), over that stage's CUDA-event time. Beside it, the
+           # bytes the reference's per-query ADC would read, over the whole step.
+           "roofline": {"bound": "tensor", "kernel": "scan_mma_kernel<kKeyList> (scan of the probed lists)",
+                        "achieved": tflops, "peak": burst, "unit": "TFLOP/s", "frac": tflops / burst,
+                        "peak_kind": f"{src} bf16 dense, burst", "traffic": None,
+                        "algorithmic": f"2 x {C2_DIM} x scanned FLOP per query, scanned = {scanned:.0f} rows "
+                                       f"(mean), over the probed-lists stage ({st[1]:.3f} ms)",
+                        "whole_step_reference_algorithm": {
+                            "achieved_gbs": achieved, "frac_of_hbm": achieved / hbm,
+                            "bytes": "scanned x (m + 4) + nprobe x m x 1 KB + 100 x pd x 4 B per query: the "
+                                     "per-query ADC's reads; list tiles share each list's rows instead"}},
            "e2e": {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": nq * C2_DIM * 4,
                    "d2h_bytes_per_step": nq * K * 8},
            "stage_ms": {"nearest_list_pass": float(st[0]), "probed_lists_scan": float(st[1]),
