@@ -252,8 +252,9 @@ class IvfPqGpuIndex final : public GpuIndex {
                     const float* pdist) {
     const uint64_t nq = b.nq;
     const uint32_t R = std::max(depth, k);
-    uint32_t c = 64;
-    while (c < 2 * R && c < 256) c <<= 1;
+    // cpre: R + R / 4 rounded up to a power of two, as the SQ8 scan's pre-rank (128 for R = 100).
+    uint32_t c = 32;
+    while (c < R + R / 4 && c < 256) c <<= 1;
     const int cpre = static_cast<int>(c);
     const uint64_t nq_pad = Up(nq, kScanBM);
     void *a_op, *qscale, *qtau, *ps;
@@ -388,9 +389,9 @@ class IvfPqGpuIndex final : public GpuIndex {
       VDBGPU_RETURN_IF_ERROR(coarse_index_->Search(ctx, cb));
       a.probe_ids = static_cast<const uint32_t*>(pid);
       a.probe_dist = static_cast<const float*>(pdist);
-      // The exact stage takes the 256 best pre-rank keys: at least twice TopK's depth.
+      // The exact stage takes at most 256 pre-rank keys, at least 1.25 times TopK's depth.
       if (list_mode_ && TensorEnabled() && b.allow == nullptr && b.nq >= kIvfTensorMinQueries &&
-          std::max(depth, k) <= 128 &&
+          std::max(depth, k) <= 204 &&
           (a.mode == kIvfPrecomputed || a.mode == kIvfResidual)) {
         ctx.Mark(0);
         return ListSearch(ctx, b, k, depth, a.nprobe, a.probe_ids, a.probe_dist);

@@ -23,11 +23,11 @@ def _data(n, nq, seed):
     return rows, qs
 
 
-# (rows, nlist, queries, nprobe, rerank). 512 lists of about 195 rows: a query's nearest list holds
-# fewer rows than the exact stage takes, so no bound is published before the full scan, every row
-# of the probed lists stays a candidate, and the exact stage cuts them to its 256 by a radix select
-# over the lists.
-CASES = [(200_000, 256, 1500, 16, -1), (200_000, 256, 1500, 32, 0), (100_000, 512, 600, 16, -1)]
+# (rows, nlist, queries, nprobe, rerank). 1,024 lists of about 98 rows: a query's nearest list
+# holds fewer rows than the exact stage takes (128 for re-rank depth 100), so no bound is published
+# before the full scan, every row of the probed lists stays a candidate, and the exact stage cuts
+# them to its 128 by a radix select over the lists.
+CASES = [(200_000, 256, 1500, 16, -1), (200_000, 256, 1500, 32, 0), (100_000, 1024, 600, 16, -1)]
 
 
 @pytest.mark.parametrize("case", CASES, ids=["np16_r100", "np32_r0", "small_lists"])
@@ -68,4 +68,25 @@ def test_tensor_prerank_device_buffers_and_k(ctx):
         rids, rd, _ = rindex.search(qs, k=k, nprobe=8)
         np.testing.assert_array_equal(ids_dev.cpu().numpy().view(np.uint32), rids)
         np.testing.assert_array_equal(d_dev.cpu().numpy(), rd)
+    idx.free()
+
+
+def test_config2_full_size_matches_reference(ctx):
+    """Config 2 at full size: 10,000,000 x 96 rows (the benchmark's mixture), nlist 4096, M = 48,
+    nprobe 32, re-rank depth 100, the 10,000-query batch. The index is the GPU builder's (the
+    reference's own file); ids, distances and distance computations equal the reference's
+    IvfPqIndex on every query."""
+    import vdb_b200
+    from vdb_b200 import synth
+    rows = synth.mixture(10_000_000, DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=0)
+    qs = synth.mixture(10_000, DIM, 1000, centres="uniform", lo=-1.0, hi=1.0, sigma=0.15, seed=2, stream=1)
+    data = vdb_b200.build_ivfpq(ctx, rows, DIM, nlist=4096, pq_m=PQ_M, max_train_points_per_centroid=122, seed=42)
+    idx = vdb_b200.Index.load(ctx, data, "l2", rows, DIM)
+    ids, d, dc = idx.search(qs, k=10, nprobe=32, stats=True)
+    rindex = oracle.Ref().load_index(data, oracle.L2, rows, DIM, pq_m=PQ_M)
+    rids, rd, rdc = rindex.search(qs, k=10, nprobe=32)
+    bad = np.nonzero(~np.all(ids == rids, axis=1))[0]
+    assert bad.size == 0, (bad.size, bad[:5].tolist())
+    np.testing.assert_array_equal(d, rd)
+    np.testing.assert_array_equal(dc, rdc)
     idx.free()
