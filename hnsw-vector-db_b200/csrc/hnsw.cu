@@ -700,6 +700,17 @@ __global__ void __launch_bounds__(kHnswWarps * 32, 6) hnsw_search_kernel(const H
         const uint32_t fm = __ballot_sync(0xFFFFFFFFu, fresh);
         const int nf = __popc(fm);
         if (fresh) s.nb_id[__popc(fm & ((1u << lane) - 1u))] = e;
+        // Filtered walks: the fresh neighbours' vectors start towards L2 together now, so the
+        // distance passes below (8 rows each) wait on one HBM round trip, not one per pass.
+        if (filtered && fresh) {
+          if (kSq8) {
+            const uint8_t* cp = a.codes + static_cast<size_t>(e) * pd;
+            for (int o = 0; o < pd; o += 128) prefetch_l2(cp + o);
+          } else {
+            const float* rp = a.rows + static_cast<size_t>(e) * pd;
+            for (int o = 0; o < pd; o += 32) prefetch_l2(rp + o);
+          }
+        }
         __syncwarp();
         // The filter bits in the compacted (list) order of the fresh neighbours.
         const int src = lane < nf ? static_cast<int>(__fns(fm, 0, lane + 1)) : 0;
