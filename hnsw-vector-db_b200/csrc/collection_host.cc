@@ -1097,8 +1097,14 @@ Status GpuCollection::SearchGroups(Context& ctx, Batch& b) {
         hnsw = hnsw && (t == kIndexHnsw || t == kIndexHnswSq8);
       }
       if (hnsw) {
+        // Walks of the rarest filters first: a filtered walk runs until it holds ef allowed rows,
+        // so the fewer rows a filter allows the longer its walks are, and starting the long walks
+        // first keeps them out of the launch's tail. Each walk writes its own slot, so the order
+        // changes no result.
+        std::vector<size_t> order(graph);
+        std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return matches[x] < matches[y]; });
         std::vector<HnswItem> items;
-        for (size_t pi : graph) {
+        for (size_t pi : order) {
           const size_t fi = pi / cs, si = pi % cs;
           const uint32_t f = fq[fi];
           const uint32_t need = p.strategy == 0 ? static_cast<uint32_t>(std::min<uint64_t>(b.k, matches[pi])) : 0u;
