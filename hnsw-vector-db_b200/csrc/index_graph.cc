@@ -283,15 +283,20 @@ Status HnswSearchMulti(Context& ctx, const std::vector<const GpuIndex*>& indexes
   if (a.counters != nullptr)
     VDBGPU_CUDA(cudaMemsetAsync(a.counters, 0, 8 * sizeof(unsigned long long), ctx.stream()));
   a.warps = 4;
-  // Walks per launch: their visited bitmaps and candidate pools within ~16 GiB.
+  // Walks per launch: their visited bitmaps and candidate pools within the scratch budget below.
   // Filtered walks at a few percent selectivity reach ~10^4 candidates: size the pools for that so
   // a launch rarely reruns.
   int pool_cap = static_cast<int>(std::max<uint64_t>(32768, 64 * ef));
+  // Scratch for the walks of one launch: half the free device memory, between 16 and 64 GiB. The
+  // fewer launches, the fewer launch tails (each launch waits for its longest walk).
+  size_t free_b = 0, total_b = 0;
+  VDBGPU_CUDA(cudaMemGetInfo(&free_b, &total_b));
+  const uint64_t budget = std::clamp<uint64_t>(free_b / 2 + sc->visited.size() + sc->pool.size(), 16ull << 30,
+                                               64ull << 30);
   size_t done = 0;
   while (done < nitems) {
     const uint64_t per = a.vwords * 4 + static_cast<uint64_t>(pool_cap) * 8;
-    const size_t chunk = static_cast<size_t>(std::max<uint64_t>(
-        1, std::min<uint64_t>(nitems - done, (16ull << 30) / per)));
+    const size_t chunk = static_cast<size_t>(std::max<uint64_t>(1, std::min<uint64_t>(nitems - done, budget / per)));
     VDBGPU_RETURN_IF_ERROR(sc->items.ensure(chunk * sizeof(HnswItem)));
     VDBGPU_RETURN_IF_ERROR(sc->visited.ensure(chunk * a.vwords * 4));
     VDBGPU_RETURN_IF_ERROR(sc->pool.ensure(chunk * static_cast<uint64_t>(pool_cap) * 8));
