@@ -10,8 +10,7 @@
 //   * g_scratch below is a file-scope __device__ array of kNoAllocScratchBytes (about 8.4 MB);
 //     every GPU that loads the library holds it until the process exits;
 //   * its device address is looked up once per device with cudaGetSymbolAddress, on the first call
-//     made on that device (with the device current). That first call should come before any
-//     stream capture;
+//     made on that device (with the device current);
 //   * limits: at most 128 queries per call, padded dimension at most 256, at most 16 row slices,
 //     k and the candidate depth as in the regular entry point; larger requests are rejected. With
 //     16 slices the scan keeps at most 16 of the GPU's 148 SMs busy: the entry point is sized for

@@ -163,7 +163,7 @@ VDBGPU_API int vdbgpu_index_search(vdbgpu_index* index, const float* queries, ui
  * cannot afford cudaMalloc's synchronisation or its failure under memory pressure).
  * Scratch comes from a fixed array of about 8.4 MB compiled into the library, which every GPU that
  * loads the library holds until the process exits; its device address is looked up on the first
- * call on each device, so make that first call before any stream capture.
+ * call on each device.
  * Limits: nq <= 128 queries per call, padded_dim <= 256; larger requests fail with
  * VDBGPU_INVALID_ARGUMENT. queries, out_dist and out_row must be device memory of the index's
  * device (nq x padded_dim, nq x k, nq x k). Work is launched on `stream` (NULL: the context's
