@@ -391,7 +391,7 @@ class IvfPqGpuIndex final : public GpuIndex {
       a.probe_dist = static_cast<const float*>(pdist);
       // The exact stage takes at most 256 pre-rank keys, at least 1.25 times TopK's depth.
       if (list_mode_ && TensorEnabled() && b.allow == nullptr && b.nq >= kIvfTensorMinQueries &&
-          std::max(depth, k) <= 204 &&
+          b.nq * a.nprobe <= (uint64_t{1} << 30) && std::max(depth, k) <= 204 &&
           (a.mode == kIvfPrecomputed || a.mode == kIvfResidual)) {
         ctx.Mark(0);
         return ListSearch(ctx, b, k, depth, a.nprobe, a.probe_ids, a.probe_dist);
