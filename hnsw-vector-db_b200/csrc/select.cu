@@ -678,7 +678,14 @@ __global__ void __launch_bounds__(kIvfFinWarps * 32) ivf_finalize_kernel(const I
   const int R = a.depth > a.k ? a.depth : a.k;
   ncand = ncand < R ? ncand : R;
   uint32_t dc = static_cast<uint32_t>(a.nlist) + scanned;
-  if (a.depth > 0) {
+  if (a.depth > 0 && a.order == kOrderAvx512 && (pd == 96 || pd == 128)) {
+    auto id_at = [&](int i) { return neighbor_id(surv[i]); };
+    auto put = [&](int i, float v) { surv[i] = pack_neighbor(v, neighbor_id(surv[i])); };
+    if (pd == 96) warp_dists_f32x2<3>(a.rows, q_s, ncand, true, id_at, put);
+    else warp_dists_f32x2<4>(a.rows, q_s, ncand, true, id_at, put);
+    sort_small(surv, ncand);
+    dc += static_cast<uint32_t>(ncand);
+  } else if (a.depth > 0) {
     for (int i = 0; i < ncand; i += 4) {
       uint32_t r[4];
 #pragma unroll

@@ -313,26 +313,27 @@ __device__ __forceinline__ float f2_reduce16(uint64_t v) {
   return __fadd_rn(f2_lo(v), f2_hi(v));
 }
 
-// Exact distances (L2, or minus the dot product) of n rows of 128 floats in the AVX-512 kernel's
-// order, 8 rows per pass, two per quarter-warp, every load of a pass issued before any
-// arithmetic. The AVX-512 kernel keeps two 16-wide accumulators, acc0 over elements 32t + l and
-// acc1 over 32t + 16 + l (t = 0..3), and reduces acc0 + acc1 by halves. Lane j of a quarter-warp
-// holds slots 2j and 2j + 1 of both as packed pairs: its loads are 8-byte pairs and its arithmetic
-// two-wide, so every distance is bit-identical to warp_exact_dist's. id_at(i) gives row i's id;
-// put(i, dist) is called once per row, by one lane. q_s: 128 floats, 8-byte aligned.
-template <class IdAt, class Put>
-__device__ __forceinline__ void warp_dists128_f32(const float* __restrict__ rows, const float* q_s, int n, bool l2,
-                                                  IdAt id_at, Put put) {
+// Exact distances (L2, or minus the dot product) of n rows of 32 kT floats (pd = 96 or 128) in
+// the AVX-512 kernel's order, 8 rows per pass, two per quarter-warp, every load of a pass issued
+// before any arithmetic. The AVX-512 kernel keeps two 16-wide accumulators, acc0 over elements
+// 32t + l and acc1 over 32t + 16 + l (t < kT), and reduces acc0 + acc1 by halves. Lane j of a
+// quarter-warp holds slots 2j and 2j + 1 of both as packed pairs: its loads are 8-byte pairs and its
+// arithmetic two-wide, so every distance is bit-identical to warp_exact_dist's. id_at(i) gives
+// row i's id; put(i, dist) is called once per row, by one lane. q_s: 32 kT floats, 8-byte aligned.
+template <int kT, class IdAt, class Put>
+__device__ __forceinline__ void warp_dists_f32x2(const float* __restrict__ rows, const float* q_s, int n, bool l2,
+                                                 IdAt id_at, Put put) {
   const int lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
   const uint64_t* q2 = reinterpret_cast<const uint64_t*>(q_s);
   for (int i = 0; i < n; i += 8) {
-    uint64_t x[2][8];
+    uint64_t x[2][2 * kT];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int my = i + 4 * h + g;
-      const uint64_t* xp = reinterpret_cast<const uint64_t*>(rows + static_cast<size_t>(id_at(my < n ? my : i)) * 128);
+      const uint64_t* xp =
+          reinterpret_cast<const uint64_t*>(rows + static_cast<size_t>(id_at(my < n ? my : i)) * (32 * kT));
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < kT; ++t) {
         x[h][2 * t] = __ldg(&xp[16 * t + j]);          // elements 32t + 2j, +1 (acc0)
         x[h][2 * t + 1] = __ldg(&xp[16 * t + 8 + j]);  // elements 32t + 16 + 2j, +1 (acc1)
       }
@@ -341,7 +342,7 @@ __device__ __forceinline__ void warp_dists128_f32(const float* __restrict__ rows
     for (int h = 0; h < 2; ++h) {
       uint64_t A0 = 0, A1 = 0;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < kT; ++t) {
         const uint64_t qa = q2[16 * t + j], qb = q2[16 * t + 8 + j];
         if (l2) {
           const uint64_t da = f2_sub(qa, x[h][2 * t]), db = f2_sub(qb, x[h][2 * t + 1]);
@@ -358,6 +359,12 @@ __device__ __forceinline__ void warp_dists128_f32(const float* __restrict__ rows
     }
   }
   __syncwarp();
+}
+
+template <class IdAt, class Put>
+__device__ __forceinline__ void warp_dists128_f32(const float* __restrict__ rows, const float* q_s, int n, bool l2,
+                                                  IdAt id_at, Put put) {
+  warp_dists_f32x2<4>(rows, q_s, n, l2, id_at, put);
 }
 
 // Exact SQ8 distances of n code rows of 128 bytes in the AVX-512 kernel's order: one 16-wide
